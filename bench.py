@@ -1,0 +1,407 @@
+"""Benchmark of the low-bit decode hot path on B200.
+
+Default workload (M=1 points; the metric's "W4/W3
+dequant-GEMV GB/s vs HBM peak"): y = W x with W packed int4 (and int3),
+K=4096, N=12288, group 128 along K, fp16 scales, zero-point at mid-range
+(unsigned-code reading), fp32 x ~N(0,1), fp32 y.  A *step* is one GEMV over
+each of R distinct weight copies (R*26 MB > 4x L2), captured once as a CUDA
+graph and replayed, so every timed launch streams its weights from HBM.
+
+  value      W4 GEMV algorithmic GB/s, inputs resident in HBM, whole job
+  e2e        same metric through the reference-facing host-pointer ABI
+             (vspec_cuda_fused_linear_int4_cached_bridge: x uploaded and y
+             downloaded on every call)
+  roofline   dominant kernel (the W4 GEMV) vs measured HBM copy bandwidth
+  cpu_baseline  the oracle restatement (group-wise), one host thread
+
+`--impl reference` times the reference's own CPU implementation
+(vspec_int4_matmul_ref_f32_q4_with_zero_points from oracle/_ref, compiled from
+the reference sources) on the same shape with all host threads.
+
+Multi-GPU: one process per GPU (torchrun); every rank runs the same
+independent workload (data-parallel replicas, weak scaling); timing is the
+max over ranks of CUDA-event time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vspec-engine_b200", "python"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+K_DIM, N_DIM, GROUP = 4096, 12288, 128
+METRIC = "W4 dequant-GEMV GB/s (K=4096 N=12288 M=1 group128 fp16 scales)"
+
+
+def gemv_bytes(bits: int, n: int = N_DIM, k: int = K_DIM, m: int = 1, sz_bytes: int = 2, zp: bool = False) -> int:
+    groups = k // GROUP
+    return n * ((k * bits + 7) // 8) + n * groups * sz_bytes * (2 if zp else 1) + m * k * 4 + m * n * 4
+
+
+def load_peaks() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic() -> float | None:
+    """DRAM bytes per W4 GEMV launch from the committed ncu summary (one capture)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemv_w4_k4096_n12288_traffic.json")) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index: int):
+        self.gpu = str(gpu_index)
+        try:
+            import torch
+            uuid = getattr(torch.cuda.get_device_properties(gpu_index), "uuid", None)
+            if uuid is not None:
+                self.gpu = "GPU-" + str(uuid)
+        except Exception:
+            pass
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(gpus: int):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world <= 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ GPU arm
+def make_rotation(torch, bits: int, copies: int, seed: int):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    rb = (K_DIM * bits + 7) // 8
+    ws = [torch.randint(0, 256, (N_DIM, rb), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+    ss = [(torch.rand((N_DIM, K_DIM // GROUP), device="cuda", generator=g) * 0.015 + 0.005).half()
+          for _ in range(copies)]
+    return ws, ss
+
+
+def time_gemv_graph(torch, V, bits: int, copies: int, steps: int, warmup: int, world: int, sampler=None):
+    ws, ss = make_rotation(torch, bits, copies, seed=1234 + bits)
+    x = torch.randn((1, K_DIM), device="cuda", dtype=torch.float32)
+    ys = [torch.empty((1, N_DIM), device="cuda", dtype=torch.float32) for _ in range(copies)]
+    stream = torch.cuda.Stream()
+    flags = V.F_UNSIGNED | V.F_SZ_F16
+
+    def step(st):
+        for w, s, y in zip(ws, ss, ys):
+            V.lowbit_linear(x.data_ptr(), w.data_ptr(), s.data_ptr(), None, y.data_ptr(), 1, N_DIM, K_DIM,
+                            K_DIM // GROUP, bits, flags=flags, stream=st)
+
+    with torch.cuda.stream(stream):
+        step(stream.cuda_stream)          # configures kernel attributes before capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(stream.cuda_stream)
+    torch.cuda.synchronize()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.start()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    if sampler:
+        clocks = sampler.stop()
+    else:
+        clocks = None
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    del graph
+    return ms, clocks
+
+
+def time_e2e_bridge(torch, V, copies: int, steps: int, warmup: int, world: int):
+    """Reference host-pointer ABI: registered int4 weights (fp32 s + zp, the
+    bridge's formats), host x -> host y on every call."""
+    import ctypes
+    rng = np.random.default_rng(77)
+    n, k, g = N_DIM, K_DIM, K_DIM // GROUP
+    handles, keep = [], []
+    for i in range(copies):
+        w = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+        s = rng.uniform(0.005, 0.02, size=(n, g)).astype(np.float32)
+        zp = np.full((n, g), 8.0, dtype=np.float32)
+        h = V.lib.vspec_cuda_fused_linear_int4_register_weight_bridge(w.ctypes.data, s.ctypes.data, zp.ctypes.data,
+                                                                       k, n, g)
+        if h <= 0:
+            raise RuntimeError("register_weight_bridge failed: " + V.last_error())
+        handles.append(h)
+        keep.append((w, s, zp))
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    y = np.zeros((1, n), dtype=np.float32)
+    fn = V.lib.vspec_cuda_fused_linear_int4_cached_bridge
+
+    def step():
+        for h in handles:
+            if fn(x.ctypes.data, 1, k, h, n, y.ctypes.data) != 1:
+                raise RuntimeError("cached_bridge failed: " + V.last_error())
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) * 1e3
+    barrier(world)
+    ms = max_over_ranks(dt, world)
+    bytes_per_call = n * k // 2 + 2 * n * g * 4 + k * 4 + n * 4
+    del keep
+    return ms, bytes_per_call, k * 4, n * 4
+
+
+# ------------------------------------------------------------------ CPU legs
+def cpu_oracle_sample(seconds: float = 10.0) -> dict:
+    """The oracle restatement (group-wise int4, one thread) on a bounded sample
+    of the workload: the first R rows of the N=12288 x K=4096 matrix."""
+    import oracle as O
+    rng = np.random.default_rng(5)
+    rows = 256
+    w = rng.integers(0, 256, size=(rows, K_DIM // 2), dtype=np.uint8)
+    s = rng.uniform(0.005, 0.02, size=(rows, K_DIM // GROUP)).astype(np.float16)
+    x = rng.standard_normal((1, K_DIM)).astype(np.float32)
+    t0 = time.perf_counter()
+    calls = 0
+    while True:
+        O.lowbit_matmul(x, w ^ np.uint8(0x88), rows, K_DIM, 4, s, None, K_DIM // GROUP)
+        calls += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    frac = rows / N_DIM
+    gbs = calls * gemv_bytes(4) * frac / dt / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{calls} x oracle_lowbit_matmul_f16sz on {rows} of {N_DIM} rows (K=4096, W4, group 128), "
+                      f"{dt:.1f} s, bytes scaled to the rows computed"}
+
+
+def reference_arm(args) -> None:
+    """Times the reference's own CPU implementation with all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import concurrent.futures as cf
+    import oracle as O
+    if O.REF is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libvspec_ref.so was not built"}))
+        return
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(6)
+    n, k = N_DIM, K_DIM
+    # bounded sample per step: a slice of rows sized so one step is ~0.25 s of CPU work
+    rows = min(n, max(threads, 32 * threads))
+    w = rng.integers(0, 256, size=(rows, k // 2), dtype=np.uint8)
+    s = rng.uniform(0.005, 0.02, size=rows).astype(np.float32)
+    zp = np.full(rows, 8.0, dtype=np.float32)
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    y = np.zeros((1, rows), dtype=np.float32)
+    fn = O.REF.vspec_int4_matmul_ref_f32_q4_with_zero_points
+    bounds = np.linspace(0, rows, threads + 1).astype(int)
+
+    def part(i):
+        a, b = bounds[i], bounds[i + 1]
+        if b > a:
+            yy = np.zeros((1, b - a), dtype=np.float32)
+            fn(x.ctypes.data, 1, k, w[a:b].ctypes.data, b - a, s[a:].ctypes.data, zp[a:].ctypes.data, yy.ctypes.data)
+            y[0, a:b] = yy[0]
+
+    with cf.ThreadPoolExecutor(threads) as ex:
+        for _ in range(args.warmup):
+            list(ex.map(part, range(threads)))
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            list(ex.map(part, range(threads)))
+        dt = time.perf_counter() - t0
+    frac = rows / n
+    gbs = args.steps * gemv_bytes(4) * frac / dt / 1e9
+    ms_step = dt * 1e3 / args.steps / frac
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes, fp32 math", "data": "synthetic",
+        "config": {"workload": "config 2: W4 GEMV K=4096 N=12288 M=1 (reference per-row-scale CPU function)",
+                   "parallelism": f"{threads} host threads, disjoint output rows"},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "reference",
+                         "sample": f"vspec_int4_matmul_ref_f32_q4_with_zero_points over {rows} of {n} rows per "
+                                   f"step (the reference has no group-wise CPU matmul), bytes scaled to rows"},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--copies", type=int, default=24)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import torch
+
+    import vspec_b200 as V
+    rank, world, local = dist_setup(args.gpus)
+    peak, peak_kind = load_peaks()
+    sampler = ClockSampler(local) if rank == 0 else None
+
+    ms4, clocks = time_gemv_graph(torch, V, 4, args.copies, args.steps, args.warmup, world, sampler)
+    ms3, _ = time_gemv_graph(torch, V, 3, args.copies, args.steps, args.warmup, world)
+    e2e_steps = max(3, args.steps // 5)
+    e2e_ms, e2e_bytes_call, h2d_call, d2h_call = time_e2e_bridge(torch, V, args.copies, e2e_steps, 2, world)
+
+    launches = args.steps * args.copies
+    b4, b3 = gemv_bytes(4), gemv_bytes(3)
+    gbs4 = world * launches * b4 / (ms4 * 1e-3) / 1e9
+    gbs3 = world * launches * b3 / (ms3 * 1e-3) / 1e9
+    per_launch_s = ms4 * 1e-3 / launches
+    achieved = b4 / per_launch_s / 1e9
+    e2e_gbs = world * e2e_steps * args.copies * e2e_bytes_call / (e2e_ms * 1e-3) / 1e9
+    traffic = load_traffic()
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        cpu = cpu_oracle_sample(args.cpu_seconds)
+    if world > 1:
+        import torch.distributed as dist
+        barrier(world)
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(gbs4, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms4 / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes -> f16 pairs, fp32 accumulate",
+        "data": "synthetic (seeded uniform codes, fp16 scales ~U(0.005,0.02), x ~N(0,1))",
+        "config": {"workload": "config 2 (BASELINE.json configs[1]) M=1 points: W4 and W3 GEMV, K=4096, N=12288, "
+                               "group 128, fp16 scales, zero-point mid-range",
+                   "step": f"{args.copies} GEMVs over distinct weight copies in one CUDA graph",
+                   "l2": f"inputs larger than L2: {args.copies} copies x {b4 / 1e6:.1f} MB rotating",
+                   "parallelism": f"dp{world} replicas (independent weights per GPU)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} hbm_gbs (copy read+write)",
+                     "bytes_per_launch": b4, "launch_us": round(per_launch_s * 1e6, 3)},
+        "w3": {"value": round(gbs3, 2), "unit": "GB/s", "bytes_per_launch": b3,
+               "frac": round(b3 / (ms3 * 1e-3 / launches) / 1e9 / peak, 4)},
+        "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d_call * args.copies,
+                "d2h_bytes_per_step": d2h_call * args.copies,
+                "api": "vspec_cuda_fused_linear_int4_cached_bridge (host x / host y per call, fp32 s+zp)"},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": launches * 2,
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,177 @@
+/*
+ * vspec_b200.h -- native C ABI of libvspec_b200.so, the B200 (sm_100a)
+ * implementation of Vspec-Engine's low-bit decode hot path.
+ *
+ * All pointers named d_* are device pointers; `stream` is a cudaStream_t
+ * passed as void* (NULL = legacy default stream).  Every function returns a
+ * VSPEC_B200_* status; on failure vspec_b200_last_error() describes why.
+ * Launches are asynchronous unless stated otherwise.
+ *
+ * The reference-named entry points (include/vspec/kernel/cuda_fused.h,
+ * src/python/cuda_bridge.c, include/vspec/kernel/backend.h) are declared in
+ * vspec_b200_compat.h and are thin wrappers over these functions.
+ */
+#ifndef VSPEC_B200_H
+#define VSPEC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+#define VSPEC_B200_OK 0
+#define VSPEC_B200_ERR_ARG 1          /* invalid argument (checked on the host before launch) */
+#define VSPEC_B200_ERR_CUDA 2         /* a CUDA runtime call failed */
+#define VSPEC_B200_ERR_UNSUPPORTED 3  /* valid but not supported by this build */
+#define VSPEC_B200_ERR_NOMEM 4        /* device or host allocation failed */
+#define VSPEC_B200_ERR_TIMEOUT 5      /* a bounded device wait gave up */
+
+/* Thread-local description of the last failure (never NULL). */
+const char* vspec_b200_last_error(void);
+/* Library version string. */
+const char* vspec_b200_version(void);
+
+/* ------------------------------------------------------ low-bit linear */
+/* Flags of VspecB200LinearArgs.flags */
+#define VSPEC_B200_F_SZ_F16 0x1     /* scales / zero-points are fp16 (default fp32) */
+#define VSPEC_B200_F_UNSIGNED 0x2   /* codes are unsigned offsets u - 2^(bits-1) instead of two's complement */
+#define VSPEC_B200_F_RESIDUAL 0x4   /* y = residual + W.x  (residual may alias y) */
+#define VSPEC_B200_F_RMSNORM 0x8    /* x := x / sqrt(mean(x^2) + eps) * norm_weight before the product */
+#define VSPEC_B200_F_SWIGLU 0x10    /* rows [0,n/2) are gate, [n/2,n) up; y[m][n/2] = silu(gate) * up */
+
+/*
+ * Group-wise dequant-matmul (GEMV for m <= 8, GEMM beyond):
+ *   y[i][j] = sum_t x[i][t] * (code(j,t) - zp[j][g(t)]) * s[j][g(t)]
+ *
+ * Layouts are the reference's: w is [n][ceil(k*bits/8)] bytes, each row the
+ * LSB-first bitstream of src/quant/pack.c:30-74 (bits 4: two codes per byte,
+ * low nibble first, src/quant/int4.c:25-45); s / zp are row-major
+ * [n][n_groups]; g(t) = min(G-1, t*G/k) (src/kernel/cuda/fused_linear_int4.cu:391-396).
+ * zero_points == NULL uses zero_point_const for every group.
+ *
+ * Generalizes vspec_cuda_fused_linear_int4_device / _int3_device /
+ * _int2_device (include/vspec/kernel/cuda_fused.h:34-75) with an explicit
+ * stream, group-wise scales for every bit width, fp16 scale storage and the
+ * fused RMSNorm-input / residual / SwiGLU epilogues of the Qwen decode step
+ * (Vspec-chat/python/runtime_inference.py:1245-1499).
+ */
+typedef struct VspecB200LinearArgs {
+    const float* d_x;            /* [m][k] fp32 */
+    const uint8_t* d_w;          /* [n][ceil(k*bits/8)] */
+    const void* d_scales;        /* [n][n_groups] fp32, or fp16 with VSPEC_B200_F_SZ_F16 */
+    const void* d_zero_points;   /* same layout/dtype, or NULL */
+    float zero_point_const;
+    float* d_y;                  /* [m][n], or [m][n/2] with VSPEC_B200_F_SWIGLU */
+    const float* d_residual;     /* [m][n] with VSPEC_B200_F_RESIDUAL */
+    const float* d_norm_weight;  /* [k] with VSPEC_B200_F_RMSNORM */
+    float norm_eps;
+    size_t m, n, k, n_groups;
+    int bits;                    /* 2, 3 or 4 */
+    int flags;
+} VspecB200LinearArgs;
+
+int vspec_b200_lowbit_linear(const VspecB200LinearArgs* args, void* stream);
+
+/* Same contraction through the any-shape path only (testing / odd shapes). */
+int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* args, void* stream);
+
+/* Decode every code of a packed [n][k] matrix into int8 [n][k] (bit-exact
+ * parity hook for vspec_quant_get_signed, src/quant/pack.c:53-74).
+ * use_fast_decoder = 1 runs the register decoder of the GEMV fast path
+ * (k % 32 == 0), 0 the generic per-field decoder. */
+int vspec_b200_unpack_codes(const uint8_t* d_w, size_t n, size_t k, int bits, int unsigned_codes,
+                            int8_t* d_codes, int use_fast_decoder, void* stream);
+
+/* Dequantize a packed [n][k] matrix to fp32: (code - zp) * s, s == NULL -> 1,
+ * zp == NULL -> zp_const (src/kernel/cuda/fused_linear_int4.cu:418-470,
+ * src/kernel/cuda/fused_linear_int2.cu:97-135). */
+int vspec_b200_dequant_f32(const uint8_t* d_w, const float* d_s, const float* d_zp, float zp_const, int bits,
+                           int unsigned_codes, size_t n, size_t k, size_t n_groups, float* d_out, void* stream);
+
+/* Clamp each row of an fp32 [rows][cols] matrix to +-alpha*std(row)
+ * (src/kernel/cuda/fused_linear_int3.cu:20-53). */
+int vspec_b200_clamp_rows_std(const float* d_in, float* d_out, size_t rows, size_t cols, float alpha, void* stream);
+
+/* The reference int3 kernel's arithmetic: per-row scale, 32-wide block-abs
+ * normalization, optional hash-seeded stochastic rounding to 1/16 steps
+ * (src/kernel/cuda/fused_linear_int3.cu:68-147). */
+int vspec_b200_int3_blocknorm_linear(const float* d_a, const uint8_t* d_w, const float* d_s, float* d_c, size_t m,
+                                     size_t n, size_t k, int stochastic, void* stream);
+
+/* Per-row mean code zero-points (src/quant/int4.c:69-89, src/quant/int3.c:28-48). */
+int vspec_b200_mean_code_zero_points(const uint8_t* d_w, size_t n, size_t k, int bits, float* d_zp, void* stream);
+
+/* ------------------------------------------------- paged decode attention */
+#define VSPEC_B200_KV_F32 0
+#define VSPEC_B200_KV_F16 1
+
+/*
+ * GQA decode attention of one query token per sequence over a paged K/V
+ * cache (the fused paged attention the reference runs head by head on
+ * contiguous host copies, src/kernel/cuda/attention_fused.cu:353-445,
+ * Vspec-chat/python/runtime_inference.py:1413-1433):
+ *   out[b][h] = softmax(q[b][h] . K_b^T * scale) V_b,  kv head = h / (Hq/Hkv)
+ * Pages are [num_pages][page_tokens][num_kv_heads][head_dim] -- the layout of
+ * VspecKVPagedCache pages (include/vspec/attention/kv_paged_cache.h:21-27) --
+ * in fp16 or fp32; the page table row of a sequence is its session pages[]
+ * widened to int32.  Token t is slot t % page_tokens of page
+ * table[t / page_tokens] (all pages but the last are full).  ctx_len 0
+ * yields zeros.  Page ids outside [0, num_pages) are redirected to page 0 and
+ * reported by vspec_b200_paged_attention_page_fault().
+ */
+typedef struct VspecB200PagedAttnArgs {
+    const float* d_q;             /* [batch][num_q_heads][head_dim] */
+    const void* d_k_pages;
+    const void* d_v_pages;
+    const int32_t* d_page_table;  /* [batch][max_pages_per_seq] */
+    const int32_t* d_ctx_len;     /* [batch] */
+    float* d_out;                 /* [batch][num_q_heads][head_dim] */
+    size_t batch, num_q_heads, num_kv_heads, head_dim;
+    size_t page_tokens, max_pages_per_seq, num_pages;
+    size_t max_ctx;               /* host-side upper bound of ctx_len (sizes the split grid) */
+    float scale;
+    int kv_dtype;                 /* VSPEC_B200_KV_F16 or VSPEC_B200_KV_F32 */
+    void* d_workspace;            /* NULL = library-managed device scratch */
+    size_t workspace_bytes;
+} VspecB200PagedAttnArgs;
+
+/* Scratch bytes the split-context merge needs for these sizes. */
+size_t vspec_b200_paged_attention_workspace_bytes(size_t batch, size_t num_q_heads, size_t num_kv_heads,
+                                                  size_t head_dim, size_t max_ctx);
+int vspec_b200_paged_attention(const VspecB200PagedAttnArgs* args, void* stream);
+/* Reads and clears the out-of-range page id flag (1 = seen since last call). */
+int vspec_b200_paged_attention_page_fault(int* out_flag);
+
+/* Bit-exact gather of one sequence's K and V rows in token order into
+ * [ctx][num_kv_heads][head_dim] (parity hook for vspec_kv_paged_get_token_ptr,
+ * src/attention/kv_paged_cache.c:312-356). */
+int vspec_b200_paged_gather(const void* d_k_pages, const void* d_v_pages, const int32_t* d_page_table, size_t ctx,
+                            size_t page_tokens, size_t num_kv_heads, size_t head_dim, int kv_dtype, void* d_k_out,
+                            void* d_v_out, void* stream);
+
+/* ------------------------------------------------------ fp32 helpers */
+/* y = x / sqrt(mean(x^2) + eps) * w per row (src/kernel/cuda/cuda_rmsnorm_f32.cu:9-36). */
+int vspec_b200_rmsnorm_f32(const float* d_x, const float* d_w, float eps, size_t rows, size_t dim, float* d_y,
+                           void* stream);
+/* y[m][n] = x[m][k] . W[n][k]^T in fp32 (src/kernel/cuda/cuda_linear_f32.cu:10-34). */
+int vspec_b200_linear_f32(const float* d_x, const float* d_w, size_t m, size_t k, size_t n, float* d_y, void* stream);
+/* data = silu(data) (src/kernel/cuda/cuda_elemwise_f32.cu:6-13) */
+int vspec_b200_silu_f32(float* d_data, size_t count, void* stream);
+/* data = data * other (src/kernel/cuda/cuda_elemwise_f32.cu:15-21) */
+int vspec_b200_mul_f32(float* d_data, const float* d_other, size_t count, void* stream);
+
+/* Test hook: the next `n` device allocations of the host C layer succeed and
+ * the one after fails (n < 0 disables). */
+int vspec_b200_debug_fail_alloc_after(int n);
+
+/* Device properties used by the dispatch (filled on first use). */
+int vspec_b200_device_info(int* sm_count, int* cc_major, int* cc_minor, size_t* smem_per_block_optin);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VSPEC_B200_H */

@@ -1,0 +1,339 @@
+/*
+ * oracle.c -- CPU restatement of Vspec-Engine's low-bit dequant-matmul and
+ * paged GQA decode attention.  TEST INFRASTRUCTURE ONLY (see oracle.h):
+ * the shipped library never links or calls it.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+size_t oracle_row_bytes(size_t k, int bits) {
+    /* src/quant/pack.c:11-16 */
+    return (k * (size_t)bits + 7U) / 8U;
+}
+
+int8_t oracle_get_code(const uint8_t* row, size_t t, int bits) {
+    /* src/quant/pack.c:53-74: LSB-first field of `bits` bits at bit t*bits,
+     * possibly spanning two bytes, read as two's complement. */
+    const size_t bit = t * (size_t)bits;
+    const size_t byte = bit >> 3;
+    const unsigned shift = (unsigned)(bit & 7U);
+    unsigned v = (unsigned)row[byte] >> shift;
+    if (8U - shift < (unsigned)bits) {
+        v |= (unsigned)row[byte + 1U] << (8U - shift);
+    }
+    v &= (1U << bits) - 1U;
+    if (v & (1U << (bits - 1))) {
+        return (int8_t)((int)v - (1 << bits));
+    }
+    return (int8_t)v;
+}
+
+void oracle_pack_rows(const int8_t* codes, size_t n, size_t k, int bits, uint8_t* out) {
+    /* src/quant/pack.c:30-51, applied per row so rows stay byte aligned
+     * (Vspec-chat/python/runtime_inference.py:679-705 packs row by row). */
+    const size_t rb = oracle_row_bytes(k, bits);
+    const int lo = -(1 << (bits - 1));
+    const int hi = (1 << (bits - 1)) - 1;
+    const unsigned mask = (1U << bits) - 1U;
+    memset(out, 0, n * rb);
+    for (size_t j = 0; j < n; ++j) {
+        uint8_t* row = out + j * rb;
+        for (size_t t = 0; t < k; ++t) {
+            int v = codes[j * k + t];
+            if (v < lo) v = lo;
+            if (v > hi) v = hi;
+            const unsigned u = (unsigned)v & mask;
+            const size_t bit = t * (size_t)bits;
+            const size_t byte = bit >> 3;
+            const unsigned shift = (unsigned)(bit & 7U);
+            row[byte] |= (uint8_t)(u << shift);
+            if (8U - shift < (unsigned)bits) {
+                row[byte + 1U] |= (uint8_t)(u >> (8U - shift));
+            }
+        }
+    }
+}
+
+void oracle_unpack_rows(const uint8_t* packed, size_t n, size_t k, int bits, int8_t* out) {
+    const size_t rb = oracle_row_bytes(k, bits);
+    for (size_t j = 0; j < n; ++j) {
+        for (size_t t = 0; t < k; ++t) {
+            out[j * k + t] = oracle_get_code(packed + j * rb, t, bits);
+        }
+    }
+}
+
+size_t oracle_group_of(size_t t, size_t k, size_t n_groups) {
+    /* src/kernel/cuda/fused_linear_int4.cu:391-392 */
+    if (n_groups <= 1U) return 0U;
+    size_t g = (t * n_groups) / k;
+    return g < n_groups ? g : n_groups - 1U;
+}
+
+void oracle_lowbit_matmul_f32(const float* a, size_t m, size_t k,
+                              const uint8_t* w, size_t n, int bits,
+                              const float* s, const float* zp, size_t n_groups,
+                              float* c) {
+    /* src/quant/int4.c:107-132 with the group indexing of
+     * src/kernel/cuda/fused_linear_int4.cu:391-396: one fp32 accumulator per
+     * output, terms added in t order, each term a[t] * ((q - zp) * s). */
+    if (n_groups == 0U) n_groups = 1U;
+    const size_t rb = oracle_row_bytes(k, bits);
+    for (size_t i = 0; i < m; ++i) {
+        const float* arow = a + i * k;
+        for (size_t j = 0; j < n; ++j) {
+            const uint8_t* wrow = w + j * rb;
+            float acc = 0.0f;
+            for (size_t t = 0; t < k; ++t) {
+                const size_t idx = j * n_groups + oracle_group_of(t, k, n_groups);
+                const float scale = s[idx];
+                const float z = zp ? zp[idx] : 0.0f;
+                const float q = (float)oracle_get_code(wrow, t, bits);
+                acc += arow[t] * ((q - z) * scale);
+            }
+            c[i * n + j] = acc;
+        }
+    }
+}
+
+float oracle_half_to_float(uint16_t h) {
+    /* IEEE 754 binary16: 1 sign, 5 exponent (bias 15), 10 fraction bits. */
+    const int sign = (h >> 15) & 1;
+    const int exp = (h >> 10) & 0x1F;
+    const int frac = h & 0x3FF;
+    float v;
+    if (exp == 0) {
+        v = ldexpf((float)frac, -24);              /* subnormal: frac * 2^-24 */
+    } else if (exp == 31) {
+        v = frac ? NAN : INFINITY;
+    } else {
+        v = ldexpf((float)(frac | 0x400), exp - 25); /* (1.frac) * 2^(exp-15) */
+    }
+    return sign ? -v : v;
+}
+
+void oracle_lowbit_matmul_f16sz(const float* a, size_t m, size_t k,
+                                const uint8_t* w, size_t n, int bits,
+                                const uint16_t* s16, const uint16_t* zp16, size_t n_groups,
+                                float* c) {
+    if (n_groups == 0U) n_groups = 1U;
+    const size_t cnt = n * n_groups;
+    float* s = (float*)malloc(cnt * sizeof(float));
+    float* z = zp16 ? (float*)malloc(cnt * sizeof(float)) : NULL;
+    for (size_t i = 0; i < cnt; ++i) {
+        s[i] = oracle_half_to_float(s16[i]);
+        if (z) z[i] = oracle_half_to_float(zp16[i]);
+    }
+    oracle_lowbit_matmul_f32(a, m, k, w, n, bits, s, z, n_groups, c);
+    free(s);
+    free(z);
+}
+
+void oracle_lowbit_matmul_f64acc(const float* a, size_t m, size_t k,
+                                 const uint8_t* w, size_t n, int bits,
+                                 const float* s, const float* zp, size_t n_groups,
+                                 double* c) {
+    if (n_groups == 0U) n_groups = 1U;
+    const size_t rb = oracle_row_bytes(k, bits);
+    for (size_t i = 0; i < m; ++i) {
+        const float* arow = a + i * k;
+        for (size_t j = 0; j < n; ++j) {
+            const uint8_t* wrow = w + j * rb;
+            double acc = 0.0;
+            for (size_t t = 0; t < k; ++t) {
+                const size_t idx = j * n_groups + oracle_group_of(t, k, n_groups);
+                const double z = zp ? (double)zp[idx] : 0.0;
+                const double q = (double)oracle_get_code(wrow, t, bits);
+                acc += (double)arow[t] * ((q - z) * (double)s[idx]);
+            }
+            c[i * n + j] = acc;
+        }
+    }
+}
+
+void oracle_paged_gather_f32(const float* k_pages, const float* v_pages,
+                             const int32_t* page_table, size_t ctx,
+                             size_t page_tokens, size_t num_kv_heads, size_t head_dim,
+                             float* k_out, float* v_out) {
+    /* Token t lives in page page_table[t / page_tokens] at slot t % page_tokens
+     * (kv_paged_cache.c:332-354 walks full pages in order). */
+    const size_t stride = num_kv_heads * head_dim;      /* kv_paged_cache.c:5-7 */
+    const size_t span = page_tokens * stride;           /* kv_paged_cache.c:9-11 */
+    for (size_t t = 0; t < ctx; ++t) {
+        const size_t page = (size_t)page_table[t / page_tokens];
+        const size_t off = page * span + (t % page_tokens) * stride;
+        memcpy(k_out + t * stride, k_pages + off, stride * sizeof(float));
+        memcpy(v_out + t * stride, v_pages + off, stride * sizeof(float));
+    }
+}
+
+static const float* token_row(const float* pages, const int32_t* table, size_t t,
+                              size_t page_tokens, size_t num_kv_heads, size_t head_dim,
+                              size_t kv_h) {
+    const size_t stride = num_kv_heads * head_dim;
+    const size_t page = (size_t)table[t / page_tokens];
+    return pages + page * page_tokens * stride + (t % page_tokens) * stride + kv_h * head_dim;
+}
+
+void oracle_paged_gqa_attention_f32(const float* q, const float* k_pages, const float* v_pages,
+                                    const int32_t* page_table, size_t max_pages_per_seq,
+                                    const int32_t* ctx_len, size_t batch,
+                                    size_t num_q_heads, size_t num_kv_heads, size_t head_dim,
+                                    size_t page_tokens, float scale, float* out) {
+    const size_t group = num_q_heads / num_kv_heads;
+    for (size_t b = 0; b < batch; ++b) {
+        const size_t ctx = (size_t)ctx_len[b];
+        const int32_t* table = page_table + b * max_pages_per_seq;
+        float* scores = (float*)malloc((ctx ? ctx : 1) * sizeof(float));
+        for (size_t h = 0; h < num_q_heads; ++h) {
+            /* runtime_inference.py:151 */
+            size_t kv_h = h / (group ? group : 1);
+            if (kv_h > num_kv_heads - 1) kv_h = num_kv_heads - 1;
+            const float* qh = q + (b * num_q_heads + h) * head_dim;
+            float* oh = out + (b * num_q_heads + h) * head_dim;
+            for (size_t d = 0; d < head_dim; ++d) oh[d] = 0.0f;
+            if (ctx == 0) continue;
+            /* flash_stub.c:21-32 */
+            float max_score = -1.0e30f;
+            for (size_t t = 0; t < ctx; ++t) {
+                const float* kt = token_row(k_pages, table, t, page_tokens, num_kv_heads, head_dim, kv_h);
+                float acc = 0.0f;
+                for (size_t d = 0; d < head_dim; ++d) acc += qh[d] * kt[d];
+                scores[t] = acc * scale;
+                if (scores[t] > max_score) max_score = scores[t];
+            }
+            /* flash_stub.c:34-41 */
+            float sum = 0.0f;
+            for (size_t t = 0; t < ctx; ++t) {
+                scores[t] = expf(scores[t] - max_score);
+                sum += scores[t];
+            }
+            if (sum < 1e-12f) sum = 1e-12f;
+            /* flash_stub.c:43-52 */
+            for (size_t t = 0; t < ctx; ++t) {
+                const float p = scores[t] / sum;
+                const float* vt = token_row(v_pages, table, t, page_tokens, num_kv_heads, head_dim, kv_h);
+                for (size_t d = 0; d < head_dim; ++d) oh[d] += p * vt[d];
+            }
+        }
+        free(scores);
+    }
+}
+
+void oracle_paged_gqa_attention_f64(const float* q, const float* k_pages, const float* v_pages,
+                                    const int32_t* page_table, size_t max_pages_per_seq,
+                                    const int32_t* ctx_len, size_t batch,
+                                    size_t num_q_heads, size_t num_kv_heads, size_t head_dim,
+                                    size_t page_tokens, float scale, double* out) {
+    const size_t group = num_q_heads / num_kv_heads;
+    for (size_t b = 0; b < batch; ++b) {
+        const size_t ctx = (size_t)ctx_len[b];
+        const int32_t* table = page_table + b * max_pages_per_seq;
+        double* scores = (double*)malloc((ctx ? ctx : 1) * sizeof(double));
+        for (size_t h = 0; h < num_q_heads; ++h) {
+            size_t kv_h = h / (group ? group : 1);
+            if (kv_h > num_kv_heads - 1) kv_h = num_kv_heads - 1;
+            const float* qh = q + (b * num_q_heads + h) * head_dim;
+            double* oh = out + (b * num_q_heads + h) * head_dim;
+            for (size_t d = 0; d < head_dim; ++d) oh[d] = 0.0;
+            if (ctx == 0) continue;
+            double max_score = -1.0e300;
+            for (size_t t = 0; t < ctx; ++t) {
+                const float* kt = token_row(k_pages, table, t, page_tokens, num_kv_heads, head_dim, kv_h);
+                double acc = 0.0;
+                for (size_t d = 0; d < head_dim; ++d) acc += (double)qh[d] * (double)kt[d];
+                scores[t] = acc * (double)scale;
+                if (scores[t] > max_score) max_score = scores[t];
+            }
+            double sum = 0.0;
+            for (size_t t = 0; t < ctx; ++t) {
+                scores[t] = exp(scores[t] - max_score);
+                sum += scores[t];
+            }
+            for (size_t t = 0; t < ctx; ++t) {
+                const double p = scores[t] / sum;
+                const float* vt = token_row(v_pages, table, t, page_tokens, num_kv_heads, head_dim, kv_h);
+                for (size_t d = 0; d < head_dim; ++d) oh[d] += p * (double)vt[d];
+            }
+        }
+        free(scores);
+    }
+}
+
+/* Row clamp to +-alpha*std, fp32 mean/variance accumulated in order
+ * (src/kernel/cuda/fused_linear_int3.cu:20-53). */
+void oracle_clamp_rows_std(const float* in, size_t rows, size_t cols, float alpha, float* out) {
+    for (size_t r = 0; r < rows; ++r) {
+        const float* x = in + r * cols;
+        float mean = 0.0f;
+        for (size_t i = 0; i < cols; ++i) mean += x[i];
+        mean /= (float)cols;
+        float var = 0.0f;
+        for (size_t i = 0; i < cols; ++i) {
+            const float d = x[i] - mean;
+            var += d * d;
+        }
+        var /= (float)cols;
+        const float sd = sqrtf(var > 0.0f ? var : 0.0f);
+        float th = fabsf(alpha) * sd;
+        if (th < 1e-6f) th = 1e-6f;
+        for (size_t i = 0; i < cols; ++i) {
+            float v = x[i];
+            if (v < -th) v = -th;
+            if (v > th) v = th;
+            out[r * cols + i] = v;
+        }
+    }
+}
+
+static float sr_uniform01(uint32_t state) {
+    /* xorshift32 -> 24-bit uniform (src/kernel/cuda/fused_linear_int3.cu:68-73) */
+    state ^= state << 13;
+    state ^= state >> 17;
+    state ^= state << 5;
+    return (float)(state & 0x00FFFFFFu) / 16777216.0f;
+}
+
+/* The reference int3 CUDA kernel's arithmetic (src/kernel/cuda/fused_linear_int3.cu:82-147):
+ * per-row scale, 32-wide blocks normalized by max(|a|, |w|), optional stochastic rounding of
+ * the normalized weight to 1/16 steps seeded by (i, j, t), block sums rescaled by bs^2. */
+void oracle_int3_blocknorm_f32(const float* a, size_t m, size_t k, const uint8_t* w, size_t n,
+                               const float* s, int stochastic, float* c) {
+    const size_t rb = oracle_row_bytes(k, 3);
+    for (size_t i = 0; i < m; ++i) {
+        for (size_t j = 0; j < n; ++j) {
+            const uint8_t* row = w + j * rb;
+            const float scale = s[j];
+            float acc = 0.0f;
+            for (size_t base = 0; base < k; base += 32) {
+                const size_t end = base + 32 < k ? base + 32 : k;
+                float babs = 0.0f;
+                for (size_t t = base; t < end; ++t) {
+                    const float av = fabsf(a[i * k + t]);
+                    const float wv = fabsf((float)oracle_get_code(row, t, 3) * scale);
+                    if (av > babs) babs = av;
+                    if (wv > babs) babs = wv;
+                }
+                const float bs = babs > 1e-6f ? babs : 1e-6f;
+                float bacc = 0.0f;
+                for (size_t t = base; t < end; ++t) {
+                    const float an = a[i * k + t] / bs;
+                    float wn = ((float)oracle_get_code(row, t, 3) * scale) / bs;
+                    if (stochastic) {
+                        const uint32_t seed = (uint32_t)((uint32_t)(i * 2654435761u) ^ (uint32_t)(j * 2246822519u) ^
+                                                         (uint32_t)(t * 3266489917u) ^ 0x9E3779B9u);
+                        const float steps = wn * 16.0f;
+                        const float lo = floorf(steps);
+                        wn = ((sr_uniform01(seed) < steps - lo) ? (lo + 1.0f) : lo) / 16.0f;
+                    }
+                    bacc += an * wn;
+                }
+                acc += bacc * bs * bs;
+            }
+            c[i * n + j] = acc;
+        }
+    }
+}

@@ -1,0 +1,181 @@
+"""ctypes loader for the CPU checker libraries.
+
+TEST INFRASTRUCTURE ONLY: used by tests/, __graft_entry__.smoke() and the
+CPU-baseline legs of bench.py, never by the shipped library.
+
+  ORACLE -- liboracle.so, this project's C restatement (oracle.c)
+  REF    -- _ref/libvspec_ref.so, Vspec-Engine's own CPU sources compiled from
+            the reference tree (None when it was never built)
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_double, c_float, c_int, c_size_t, c_uint64, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libvspec_ref.so")
+
+ORACLE = ctypes.CDLL(ORACLE_PATH)
+REF = ctypes.CDLL(REF_PATH) if os.path.exists(REF_PATH) else None
+
+_o = {
+    "oracle_row_bytes": ([c_size_t, c_int], c_size_t),
+    "oracle_get_code": ([c_void_p, c_size_t, c_int], ctypes.c_int8),
+    "oracle_pack_rows": ([c_void_p, c_size_t, c_size_t, c_int, c_void_p], None),
+    "oracle_unpack_rows": ([c_void_p, c_size_t, c_size_t, c_int, c_void_p], None),
+    "oracle_group_of": ([c_size_t, c_size_t, c_size_t], c_size_t),
+    "oracle_lowbit_matmul_f32": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_int, c_void_p, c_void_p, c_size_t,
+                                  c_void_p], None),
+    "oracle_lowbit_matmul_f16sz": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_int, c_void_p, c_void_p,
+                                    c_size_t, c_void_p], None),
+    "oracle_lowbit_matmul_f64acc": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_int, c_void_p, c_void_p,
+                                     c_size_t, c_void_p], None),
+    "oracle_half_to_float": ([ctypes.c_uint16], c_float),
+    "oracle_paged_gather_f32": ([c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p,
+                                 c_void_p], None),
+    "oracle_paged_gqa_attention_f32": ([c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_size_t,
+                                        c_size_t, c_size_t, c_size_t, c_float, c_void_p], None),
+    "oracle_clamp_rows_std": ([c_void_p, c_size_t, c_size_t, c_float, c_void_p], None),
+    "oracle_int3_blocknorm_f32": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_int, c_void_p], None),
+    "oracle_paged_gqa_attention_f64": ([c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_size_t,
+                                        c_size_t, c_size_t, c_size_t, c_float, c_void_p], None),
+}
+for _n, (_a, _r) in _o.items():
+    _f = getattr(ORACLE, _n)
+    _f.argtypes = _a
+    _f.restype = _r
+
+if REF is not None:
+    _r = {
+        "vspec_quant_packed_bytes": ([c_size_t, ctypes.c_uint8], c_size_t),
+        "vspec_quant_pack_signed": ([c_void_p, c_size_t, ctypes.c_uint8, c_void_p], None),
+        "vspec_quant_unpack_signed": ([c_void_p, c_size_t, ctypes.c_uint8, c_void_p], None),
+        "vspec_quant_get_signed": ([c_void_p, c_size_t, ctypes.c_uint8], ctypes.c_int8),
+        "vspec_int4_pack": ([c_void_p, c_size_t, c_void_p], None),
+        "vspec_int4_get": ([c_void_p, c_size_t], ctypes.c_int8),
+        "vspec_int4_matmul_ref_f32_q4": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_void_p], None),
+        "vspec_int4_compute_zero_points": ([c_void_p, c_size_t, c_size_t, c_void_p], None),
+        "vspec_int4_matmul_ref_f32_q4_with_zero_points": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p,
+                                                           c_void_p, c_void_p], None),
+        "vspec_int3_matmul_ref_f32_q3": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_void_p], None),
+        "vspec_int3_compute_zero_points": ([c_void_p, c_size_t, c_size_t, c_void_p], None),
+        "vspec_int3_matmul_ref_f32_q3_with_zero_points": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p,
+                                                           c_void_p, c_void_p], None),
+        "vspec_flash_attention_stub": ([c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_void_p], None),
+        "ref_cpu_backend_linear_int4": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_void_p], None),
+        "ref_cpu_backend_attention": ([c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_void_p], c_int),
+        "ref_paged_create": ([c_size_t, c_size_t, c_size_t, c_size_t], c_void_p),
+        "ref_paged_destroy": ([c_void_p], None),
+        "ref_paged_key_pool": ([c_void_p], c_void_p),
+        "ref_paged_value_pool": ([c_void_p], c_void_p),
+        "ref_paged_session_pages": ([c_void_p, c_uint64, c_void_p, c_size_t], c_size_t),
+        "ref_paged_page_used": ([c_void_p, c_size_t], c_size_t),
+        "ref_paged_gather": ([c_void_p, c_uint64, c_void_p, c_void_p], c_int),
+        "vspec_kv_paged_open_session": ([c_void_p, c_uint64], c_int),
+        "vspec_kv_paged_close_session": ([c_void_p, c_uint64], c_int),
+        "vspec_kv_paged_reuse_prefix": ([c_void_p, c_uint64, c_uint64, c_size_t], c_int),
+        "vspec_kv_paged_append": ([c_void_p, c_uint64, c_void_p, c_void_p], c_int),
+        "vspec_kv_paged_get_token_ptr": ([c_void_p, c_uint64, c_size_t, c_size_t, POINTER(c_void_p),
+                                          POINTER(c_void_p)], c_int),
+        "vspec_kv_paged_session_tokens": ([c_void_p, c_uint64], c_size_t),
+        "vspec_kv_paged_stats": ([c_void_p, c_void_p], None),
+    }
+    for _n, (_a, _rt) in _r.items():
+        _f = getattr(REF, _n)
+        _f.argtypes = _a
+        _f.restype = _rt
+    for _n in ["ref_sizeof_kernel_context", "ref_sizeof_quant_meta", "ref_sizeof_exec_config", "ref_sizeof_kv_cache",
+               "ref_sizeof_kv_paged_cache", "ref_sizeof_backend", "ref_offsetof_ctx_qmeta", "ref_offsetof_ctx_config",
+               "ref_offsetof_qmeta_scales", "ref_offsetof_qmeta_scale_count", "ref_offsetof_kv_current_tokens",
+               "ref_offsetof_kv_int3", "ref_offsetof_paged_sessions", "ref_offsetof_paged_page_meta"]:
+        getattr(REF, _n).restype = c_size_t
+
+
+def p(a: np.ndarray | None) -> int | None:
+    if a is None:
+        return None
+    assert a.flags.c_contiguous
+    return a.ctypes.data
+
+
+def row_bytes(k: int, bits: int) -> int:
+    return (k * bits + 7) // 8
+
+
+# ---------------------------------------------------------------- helpers
+def pack_rows(codes: np.ndarray, bits: int) -> np.ndarray:
+    """Pack int8 codes [n][k] row by row (reference bitstream)."""
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    n, k = codes.shape
+    out = np.zeros((n, row_bytes(k, bits)), dtype=np.uint8)
+    ORACLE.oracle_pack_rows(p(codes), n, k, bits, p(out))
+    return out
+
+
+def unpack_rows(packed: np.ndarray, n: int, k: int, bits: int) -> np.ndarray:
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    out = np.zeros((n, k), dtype=np.int8)
+    ORACLE.oracle_unpack_rows(p(packed), n, k, bits, p(out))
+    return out
+
+
+def unpack_rows_np(packed: np.ndarray, n: int, k: int, bits: int, unsigned: bool = False) -> np.ndarray:
+    """Vectorized numpy decode of the same bitstream (for large matrices)."""
+    packed = np.ascontiguousarray(packed, dtype=np.uint8).reshape(n, row_bytes(k, bits))
+    bitpos = np.arange(k, dtype=np.int64) * bits
+    byte = bitpos >> 3
+    shift = (bitpos & 7).astype(np.uint16)
+    lo = packed[:, byte].astype(np.uint16)
+    hi_idx = np.minimum(byte + 1, packed.shape[1] - 1)
+    hi = packed[:, hi_idx].astype(np.uint16)
+    v = ((lo | (hi << 8)) >> shift) & ((1 << bits) - 1)
+    v = v.astype(np.int16)
+    if unsigned:
+        return (v - (1 << (bits - 1))).astype(np.int8)
+    return np.where(v >= (1 << (bits - 1)), v - (1 << bits), v).astype(np.int8)
+
+
+def lowbit_matmul(a: np.ndarray, w: np.ndarray, n: int, k: int, bits: int, s: np.ndarray,
+                  zp: np.ndarray | None, n_groups: int) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    m = a.shape[0]
+    out = np.zeros((m, n), dtype=np.float32)
+    if s.dtype == np.float16:
+        ORACLE.oracle_lowbit_matmul_f16sz(p(a), m, k, p(np.ascontiguousarray(w)), n, bits,
+                                          p(np.ascontiguousarray(s)),
+                                          p(np.ascontiguousarray(zp)) if zp is not None else None, n_groups, p(out))
+    else:
+        ORACLE.oracle_lowbit_matmul_f32(p(a), m, k, p(np.ascontiguousarray(w)), n, bits,
+                                        p(np.ascontiguousarray(s, dtype=np.float32)),
+                                        p(np.ascontiguousarray(zp, dtype=np.float32)) if zp is not None else None,
+                                        n_groups, p(out))
+    return out
+
+
+def lowbit_matmul_f64(a: np.ndarray, w: np.ndarray, n: int, k: int, bits: int, s: np.ndarray,
+                      zp: np.ndarray | None, n_groups: int) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    m = a.shape[0]
+    out = np.zeros((m, n), dtype=np.float64)
+    ORACLE.oracle_lowbit_matmul_f64acc(p(a), m, k, p(np.ascontiguousarray(w)), n, bits,
+                                       p(np.ascontiguousarray(s, dtype=np.float32)),
+                                       p(np.ascontiguousarray(zp, dtype=np.float32)) if zp is not None else None,
+                                       n_groups, p(out))
+    return out
+
+
+def paged_attention(q, k_pages, v_pages, table, ctx_len, hq, hkv, d, pt, scale, f64=False) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    kp = np.ascontiguousarray(k_pages, dtype=np.float32)
+    vp = np.ascontiguousarray(v_pages, dtype=np.float32)
+    table = np.ascontiguousarray(table, dtype=np.int32)
+    ctx = np.ascontiguousarray(ctx_len, dtype=np.int32)
+    b = ctx.shape[0]
+    out = np.zeros((b, hq, d), dtype=np.float64 if f64 else np.float32)
+    fn = ORACLE.oracle_paged_gqa_attention_f64 if f64 else ORACLE.oracle_paged_gqa_attention_f32
+    fn(p(q), p(kp), p(vp), p(table), table.shape[1], p(ctx), b, hq, hkv, d, pt, scale, p(out))
+    return out

@@ -1,0 +1,116 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+include/*.h declares, its structs are layout-identical to the reference's,
+and host-side argument validation rejects bad calls before any CUDA work."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle as O
+import vspec_b200 as V
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for fn in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if not fn.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", fn)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        text = re.sub(r"//[^\n]*", "", text)
+        text = re.sub(r"typedef\s+struct.*?\}\s*\w+\s*;", "", text, flags=re.S)
+        text = re.sub(r"typedef\s+enum.*?\}\s*\w+\s*;", "", text, flags=re.S)
+        for m in re.finditer(r"\b(vspec_\w+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_loads_and_versions():
+    assert V.lib.vspec_b200_version().decode().startswith("vspec_b200")
+
+
+def test_every_declared_symbol_is_exported():
+    names = declared_functions()
+    assert len(names) > 50
+    missing = [n for n in sorted(names) if not hasattr(V.lib, n)]
+    assert not missing, missing
+
+
+@pytest.mark.skipif(O.REF is None, reason="reference CPU library not built")
+def test_struct_layouts_match_reference_headers():
+    R = O.REF
+    assert ctypes.sizeof(V.KernelContext) == R.ref_sizeof_kernel_context()
+    assert ctypes.sizeof(V.QuantMeta) == R.ref_sizeof_quant_meta()
+    assert ctypes.sizeof(V.ExecConfig) == R.ref_sizeof_exec_config()
+    assert ctypes.sizeof(V.KVCache) == R.ref_sizeof_kv_cache()
+    assert ctypes.sizeof(V.Backend) == R.ref_sizeof_backend()
+    assert V.KernelContext.qmeta.offset == R.ref_offsetof_ctx_qmeta()
+    assert V.KernelContext.config.offset == R.ref_offsetof_ctx_config()
+    assert V.QuantMeta.scales.offset == R.ref_offsetof_qmeta_scales()
+    assert V.QuantMeta.scale_count.offset == R.ref_offsetof_qmeta_scale_count()
+    assert V.KVCache.current_tokens.offset == R.ref_offsetof_kv_current_tokens()
+    assert V.KVCache.int3_compressed.offset == R.ref_offsetof_kv_int3()
+    # VspecKVPagedCache is 332,904 bytes in the reference headers
+    assert R.ref_sizeof_kv_paged_cache() == 332904
+
+
+def test_c_header_compiles_against_reference_headers(tmp_path):
+    """vspec_b200_compat.h must coexist with the reference's own headers (it
+    reuses their struct definitions when they are included first)."""
+    ref_inc = "/root/reference/include"
+    if not os.path.isdir(ref_inc):
+        pytest.skip("reference headers not present")
+    src = tmp_path / "t.c"
+    src.write_text('#include "vspec/kernel/backend.h"\n#include "vspec/attention/kv_cache.h"\n'
+                   '#include "vspec_b200_compat.h"\n#include "vspec_b200.h"\n'
+                   'int main(void){VspecBackend b = vspec_make_cuda_backend(); return b.name == 0;}\n')
+    rc = os.system(f"gcc -std=gnu11 -Wall -Werror -c -I{ref_inc} -I{ROOT}/include {src} -o {tmp_path}/t.o")
+    assert rc == 0
+
+
+def _args(**kw):
+    base = dict(d_x=None, d_w=None, d_scales=None, d_zero_points=None, zero_point_const=0.0, d_y=None,
+                d_residual=None, d_norm_weight=None, norm_eps=0.0, m=1, n=16, k=128, n_groups=1, bits=4, flags=0)
+    base.update(kw)
+    return V.LinearArgs(**base)
+
+
+@pytest.mark.parametrize("kw,expect", [
+    (dict(), V.OK + 1),                                   # NULL pointers
+    (dict(d_x=16, d_w=16, d_y=16, m=0), 1),               # zero dimension
+    (dict(d_x=16, d_w=16, d_y=16, bits=5), 1),            # bad bit width
+    (dict(d_x=16, d_w=16, d_y=16, flags=V.F_RESIDUAL), 1),  # residual flag without residual
+    (dict(d_x=16, d_w=16, d_y=16, flags=V.F_RMSNORM), 1),   # norm flag without weight
+    (dict(d_x=16, d_w=16, d_y=16, n_groups=1000), 1),       # more groups than k
+    (dict(d_x=16, d_w=16, d_y=16, n=15, flags=V.F_SWIGLU), 1),  # SwiGLU needs even n
+])
+def test_linear_rejects_bad_arguments_on_host(kw, expect):
+    a = _args(**kw)
+    rc = V.lib.vspec_b200_lowbit_linear(ctypes.byref(a), None)
+    assert rc == V.OK + 1 == expect
+    assert V.last_error() != "ok"
+
+
+def test_attention_rejects_bad_arguments_on_host():
+    a = V.PagedAttnArgs()
+    assert V.lib.vspec_b200_paged_attention(ctypes.byref(a), None) == 1
+    a = V.PagedAttnArgs(16, 16, 16, 16, 16, 16, 1, 6, 4, 128, 16, 4, 4, 64, 0.1, V.KV_F16, None, 0)
+    assert V.lib.vspec_b200_paged_attention(ctypes.byref(a), None) == 1   # 6 % 4 != 0
+    a = V.PagedAttnArgs(16, 16, 16, 16, 16, 16, 1, 8, 4, 128, 16, 4, 4, 65, 0.1, V.KV_F16, None, 0)
+    assert V.lib.vspec_b200_paged_attention(ctypes.byref(a), None) == 1   # max_ctx > 4 pages * 16
+    assert "exceeds" in V.last_error()
+
+
+def test_reference_bridges_fail_closed_on_bad_input():
+    # cuda_bridge.c contract: 0 on invalid input, caller falls back
+    assert V.lib.vspec_cuda_fused_linear_int4_register_weight_bridge(None, None, None, 128, 16, 1) == 0
+    assert V.lib.vspec_cuda_fused_linear_int4_cached_bridge(None, 1, 128, 1, 16, None) == 0
+    assert V.lib.vspec_cuda_fused_linear_int4_bridge(None, None, None, None, 1, 128, 16, 1, None) == 0
+    assert V.lib.vspec_cuda_gemm_dispatch_bridge(None, None, None, None, None, 0, 0, 0, 0, 4, None, None, None) == 0
+    stats = [ctypes.c_uint64() for _ in range(6)]
+    assert V.lib.vspec_cuda_int4_cached_stats_bridge(*[ctypes.byref(s) for s in stats]) == 1
+    assert stats[2].value >= 1   # the failed cached call counted as a miss

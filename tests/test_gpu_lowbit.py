@@ -1,0 +1,214 @@
+"""GPU parity of the low-bit dequant-matmul (fast tensor-core path and the
+any-shape path) against the oracle, through the C ABI."""
+import numpy as np
+import pytest
+
+import oracle as O
+import vspec_b200 as V
+from gpu_util import RTOL_F32, dequant_np, empty_dev, make_lowbit, rel_err, to_dev, torch_cuda
+
+pytestmark = pytest.mark.gpu
+
+
+def run_linear(x, w, s, zp, n, k, bits, n_groups, flags=0, zp_const=0.0, residual=None, norm_w=None, eps=1e-6,
+               generic=False, out_cols=None):
+    torch = torch_cuda()
+    m = x.shape[0]
+    dx, dw = to_dev(x), to_dev(w)
+    ds = to_dev(s) if s is not None else None
+    dzp = to_dev(zp) if zp is not None else None
+    if s is not None and s.dtype == np.float16:
+        flags |= V.F_SZ_F16
+    dy = empty_dev((m, out_cols or n), torch.float32)
+    dres = to_dev(residual) if residual is not None else None
+    dnw = to_dev(norm_w) if norm_w is not None else None
+    V.lowbit_linear(dx.data_ptr(), dw.data_ptr(), ds.data_ptr() if ds is not None else None,
+                    dzp.data_ptr() if dzp is not None else None, dy.data_ptr(), m, n, k, n_groups, bits, flags=flags,
+                    zp_const=zp_const, residual=dres.data_ptr() if dres is not None else None,
+                    norm_weight=dnw.data_ptr() if dnw is not None else None, eps=eps, generic=generic)
+    torch.cuda.synchronize()
+    return dy.cpu().numpy()
+
+
+# ---------------------------------------------------------------- decode
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("fast", [True, False])
+def test_unpack_codes_bit_exact(bits, fast):
+    torch = torch_cuda()
+    rng = np.random.default_rng(bits)
+    n, k = 37, 512
+    w = rng.integers(0, 256, size=(n, O.row_bytes(k, bits)), dtype=np.uint8)
+    dw = to_dev(w)
+    out = empty_dev((n, k), torch.int8)
+    for unsigned in (False, True):
+        V.unpack_codes(dw.data_ptr(), n, k, bits, out.data_ptr(), unsigned=unsigned, fast=fast)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        expect = O.unpack_rows(w, n, k, bits)
+        if unsigned:
+            expect = O.unpack_rows_np(w, n, k, bits, unsigned=True)
+        assert np.array_equal(got, expect)
+
+
+def test_numpy_dequant_matches_oracle():
+    rng = np.random.default_rng(5)
+    for bits in (2, 3, 4):
+        n, k, g = 9, 384, 3
+        w, s, zp = make_lowbit(rng, n, k, bits, g)
+        x = rng.standard_normal((2, k)).astype(np.float32)
+        y64 = x.astype(np.float64) @ dequant_np(w, n, k, bits, s, zp, g).T
+        assert np.max(np.abs(O.lowbit_matmul_f64(x, w, n, k, bits, s, zp, g) - y64)) < 1e-9
+
+
+# ------------------------------------------------------------- config 1
+@pytest.mark.parametrize("reading", ["literal", "unsigned"])
+def test_config1_w4_gemv(reading):
+    """x ~N(0,1) [1x4096]; 4096x4096 uniform codes 0..15 in the int4
+    layout; fp32 group-128 scales ~U(0.005,0.02); zero-point 8; seed 0."""
+    rng = np.random.default_rng(0)
+    n = k = 4096
+    g = k // 128
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    w = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+    s = rng.uniform(0.005, 0.02, size=(n, g)).astype(np.float32)
+    if reading == "literal":   # signed decode, zp tensor = 8 (what ..._with_zero_points computes)
+        zp = np.full((n, g), 8.0, dtype=np.float32)
+        y = run_linear(x, w, s, zp, n, k, 4, g)
+        ref = O.lowbit_matmul(x, w, n, k, 4, s, zp, g)
+    else:                      # unsigned codes u - 8  ==  signed decode of (bytes ^ 0x88), zp = 0
+        y = run_linear(x, w, s, None, n, k, 4, g, flags=V.F_UNSIGNED)
+        ref = O.lowbit_matmul(x, w ^ np.uint8(0x88), n, k, 4, s, None, g)
+    err = rel_err(y, ref)
+    print(f"config1 {reading}: rel err {err:.3e}")
+    assert err <= RTOL_F32
+
+
+# ------------------------------------------------------------- config 2 (sweep)
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("n", [4096, 12288])
+@pytest.mark.parametrize("m", [1, 8, 64])
+def test_config2_sweep(bits, n, m):
+    """K=4096, N in {4096,12288}, M in {1,8,64}; group 128 fp16 scales ~U(0.005,0.02);
+    zero-point at mid-range (unsigned reading); fp32 activations ~N(0,1)."""
+    rng = np.random.default_rng(1000 * bits + n + m)
+    k, g = 4096, 32
+    w = rng.integers(0, 256, size=(n, O.row_bytes(k, bits)), dtype=np.uint8)
+    s = rng.uniform(0.005, 0.02, size=(n, g)).astype(np.float16)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = run_linear(x, w, s, None, n, k, bits, g, flags=V.F_UNSIGNED)
+    ref = x.astype(np.float64) @ dequant_np(w, n, k, bits, s.astype(np.float32), None, g, unsigned=True).T
+    err = rel_err(y, ref)
+    print(f"sweep bits={bits} n={n} m={m}: rel err {err:.3e}")
+    assert err <= RTOL_F32
+
+
+# ------------------------------------------------------------- shapes / options
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("m,n,k,g", [(1, 48, 256, 2), (3, 50, 384, 1), (8, 16, 1024, 8), (5, 33, 640, 5),
+                                     (2, 40, 200, 1), (1, 7, 100, 4), (4, 24, 96, 3)])
+def test_shapes_fp32_scales(bits, m, n, k, g):
+    rng = np.random.default_rng(m * 7 + n * 11 + k + g + bits)
+    w, s, zp = make_lowbit(rng, n, k, bits, g)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    ref = O.lowbit_matmul(x, w, n, k, bits, s, zp, g)
+    for generic in (False, True):
+        y = run_linear(x, w, s, zp, n, k, bits, g, generic=generic)
+        assert rel_err(y, ref) <= RTOL_F32, (generic, rel_err(y, ref))
+
+
+@pytest.mark.parametrize("bits", [3, 4])
+def test_fp16_scales_and_null_zero_points(bits):
+    rng = np.random.default_rng(bits + 40)
+    m, n, k, g = 2, 64, 512, 4
+    w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=True)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    assert rel_err(run_linear(x, w, s, zp, n, k, bits, g), O.lowbit_matmul(x, w, n, k, bits, s, zp, g)) <= RTOL_F32
+    assert rel_err(run_linear(x, w, s, None, n, k, bits, g), O.lowbit_matmul(x, w, n, k, bits, s, None, g)) <= RTOL_F32
+
+
+def test_activation_scale_extremes():
+    """Per-row power-of-two rescale keeps fp32 accuracy for huge and tiny rows."""
+    rng = np.random.default_rng(9)
+    n, k, g = 64, 1024, 8
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    x = rng.standard_normal((4, k)).astype(np.float32)
+    x[0] *= 3e4
+    x[1] *= 1e-6
+    x[2, ::7] *= 1e3
+    x[3] = 0.0
+    y = run_linear(x, w, s, zp, n, k, 4, g)
+    ref = O.lowbit_matmul_f64(x, w, n, k, 4, s, zp, g)
+    for i in range(3):
+        assert rel_err(y[i], ref[i]) <= RTOL_F32
+    assert np.all(y[3] == 0.0)
+
+
+def test_fused_epilogues_residual_rmsnorm_swiglu():
+    rng = np.random.default_rng(21)
+    m, k, g = 3, 1024, 8
+    # residual
+    n = 96
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    y = run_linear(x, w, s, zp, n, k, 4, g, flags=V.F_RESIDUAL, residual=res)
+    assert rel_err(y, O.lowbit_matmul_f64(x, w, n, k, 4, s, zp, g) + res) <= RTOL_F32
+    # RMSNorm input (src/kernel/cuda/cuda_rmsnorm_f32.cu:9-36 semantics)
+    nw = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    eps = 1e-6
+    xh = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + eps) * nw
+    y = run_linear(x, w, s, zp, n, k, 4, g, flags=V.F_RMSNORM, norm_w=nw, eps=eps)
+    assert rel_err(y, xh @ dequant_np(w, n, k, 4, s, zp, g).T) <= RTOL_F32
+    # SwiGLU: rows [0,n/2) gate, [n/2,n) up
+    n = 128
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    full = O.lowbit_matmul_f64(x, w, n, k, 4, s, zp, g)
+    gate, up = full[:, : n // 2], full[:, n // 2:]
+    ref = gate / (1.0 + np.exp(-gate)) * up
+    y = run_linear(x, w, s, zp, n, k, 4, g, flags=V.F_SWIGLU, out_cols=n // 2)
+    assert rel_err(y, ref) <= RTOL_F32
+
+
+def test_reference_named_device_launchers():
+    """vspec_cuda_fused_linear_int{4,3,2}_device (cuda_fused.h:34-75) and the dequant /
+    expand kernels keep the reference semantics."""
+    torch = torch_cuda()
+    rng = np.random.default_rng(31)
+    m, n, k = 2, 40, 256
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    dx = to_dev(x)
+    dy = empty_dev((m, n), torch.float32)
+    # int4, group-wise with zp
+    g = 2
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    V.lib.vspec_cuda_fused_linear_int4_device(dx.data_ptr(), to_dev(w).data_ptr(), to_dev(s).data_ptr(),
+                                              to_dev(zp).data_ptr(), dy.data_ptr(), m, n, k, g)
+    torch.cuda.synchronize()
+    assert rel_err(dy.cpu().numpy(), O.lowbit_matmul(x, w, n, k, 4, s, zp, g)) <= RTOL_F32
+    # int3 without stochastic rounding == per-row plain contraction
+    w3, s3, _ = make_lowbit(rng, n, k, 3, 1, zp_mode="none")
+    V.lib.vspec_cuda_fused_linear_int3_device(dx.data_ptr(), to_dev(w3).data_ptr(), to_dev(s3).data_ptr(),
+                                              dy.data_ptr(), m, n, k, 0)
+    torch.cuda.synchronize()
+    assert rel_err(dy.cpu().numpy(), O.lowbit_matmul(x, w3, n, k, 3, s3, None, 1)) <= RTOL_F32
+    # int2: unsigned codes, (q - 1.5) * s[row]
+    w2, s2, _ = make_lowbit(rng, n, k, 2, 1, zp_mode="none")
+    V.lib.vspec_cuda_fused_linear_int2_device(dx.data_ptr(), to_dev(w2).data_ptr(), to_dev(s2).data_ptr(),
+                                              dy.data_ptr(), m, n, k)
+    torch.cuda.synchronize()
+    ref2 = x.astype(np.float64) @ (((O.unpack_rows_np(w2, n, k, 2, unsigned=True) + 2).astype(np.float64) - 1.5)
+                                   * s2.astype(np.float64)).T
+    assert rel_err(dy.cpu().numpy(), ref2) <= RTOL_F32
+    # dequant int4 -> f32 (bit-exact: one fp32 multiply per element)
+    dwf = empty_dev((n, k), torch.float32)
+    V.lib.vspec_cuda_dequant_int4_to_f32_device(to_dev(w).data_ptr(), to_dev(s).data_ptr(), to_dev(zp).data_ptr(),
+                                                dwf.data_ptr(), n, k, g)
+    torch.cuda.synchronize()
+    expect = ((O.unpack_rows(w, n, k, 4).astype(np.float32) - np.repeat(zp, k // g, axis=1))
+              * np.repeat(s, k // g, axis=1))
+    assert np.array_equal(dwf.cpu().numpy(), expect)
+    # int3 -> int4 storage expansion: decoded codes identical
+    d4 = empty_dev((n, (k + 1) // 2), torch.uint8)
+    V.lib.vspec_cuda_expand_int3_to_int4_device(to_dev(w3).data_ptr(), d4.data_ptr(), n, k)
+    torch.cuda.synchronize()
+    assert np.array_equal(O.unpack_rows(d4.cpu().numpy(), n, k, 4), O.unpack_rows(w3, n, k, 3))

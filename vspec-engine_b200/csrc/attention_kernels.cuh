@@ -1,0 +1,36 @@
+// attention_kernels.cuh -- internal interface of the paged attention kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace vb200 {
+
+constexpr int kKvF32 = 0;
+constexpr int kKvF16 = 1;
+
+struct AttnParams {
+    const float* q;             // [batch][hq][d]
+    const void* k_pages;        // [pages][page_tokens][hkv][d]
+    const void* v_pages;
+    const int32_t* page_table;  // [batch][max_pages]
+    const int32_t* ctx_len;     // [batch]
+    float* out;                 // [batch][hq][d]
+    float* part_o;              // [batch][hq][max_splits][d]
+    float* part_ml;             // [batch][hq][max_splits][2]
+    float scale;
+    int batch, hq, hkv, d, page_tokens, max_pages;
+    int split_tokens, max_splits, head_groups;
+    int num_pages;              // valid page ids are [0, num_pages)
+};
+
+int attn_read_and_clear_page_fault(int* out);
+
+int attn_choose_split(int batch, int hkv, int max_ctx, int sms);
+size_t attn_workspace_bytes(int batch, int hq, int d, int max_splits);
+int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st);
+int paged_gather_launch(const void* kp, const void* vp, const int32_t* table, int ctx, int pt, int hkv, int d,
+                        int kv_dtype, void* kout, void* vout, cudaStream_t st);
+
+}  // namespace vb200

@@ -1,0 +1,711 @@
+// lowbit_gemv.cu -- packed int2/int3/int4 dequant-GEMV for decode (M <= 8) on sm_100a.
+//
+// Contraction (reference semantics, src/quant/int4.c:107-132 with the group
+// indexing of src/kernel/cuda/fused_linear_int4.cu:391-396):
+//     y[i][j] = sum_t x[i][t] * (code(j,t) - zp[j][g(t)]) * s[j][g(t)]
+// with code() the signed LSB-first b-bit field of the reference bitstream
+// (src/quant/pack.c:53-74), or the unsigned-offset reading u - 2^(b-1) used by
+// the reference int2 kernel (src/kernel/cuda/fused_linear_int2.cu:8-12).
+//
+// Fast path (K % 128 == 0 and every group a multiple of 128 codes):
+//   * Each warp owns a 16-row tile of W and a strided subset of the 128-code
+//     k-blocks.  A thread (g = lane/4, c = lane%4) streams one 32-code chunk of
+//     rows g and g+8 per k-block with 128/96/64-bit read-only loads, software
+//     pipelined PIPE k-blocks deep.
+//   * Codes are decoded in registers straight into fp16 pairs (magic-number
+//     LOP3 + one f16x2 FMA per pair; exact small integers), which are the A
+//     fragments of mma.m16n8k16 -- no shared memory traffic for weights.
+//   * The fp32 activation is split into fp16 hi + lo parts (after an exact
+//     per-row power-of-two rescale), so the tensor-core product keeps ~22
+//     significant bits: each x row occupies two B columns.  The B fragments
+//     are staged once per CTA in shared memory, already in fragment order.
+//   * Each k-block's fp32 partial is scaled on the fly:
+//         acc += s * (dot(x, code) - zp * sum(x over the block)).
+//   * Warps reduce through shared memory in a fixed order: deterministic.
+#include "common.cuh"
+#include "lowbit_kernels.cuh"
+
+#include <stdio.h>
+
+namespace vb200 {
+
+// -------------------------------------------------------------------------
+// Code-order tables: fp16 pair q (0..15) of a decoded 32-code chunk holds
+// codes (lo_code(q), hi_code(q)).
+// -------------------------------------------------------------------------
+template <int BITS>
+__host__ __device__ __forceinline__ int lo_code(int q) {
+    if (BITS == 4) return 8 * (q >> 2) + (q & 3);
+    if (BITS == 2) return 16 * (q >> 3) + (q & 7);
+    // BITS == 3: window w = q/2 starts at code j(w) in {0,2,8,10,16,18,24,26}
+    const int w = q >> 1;
+    const int j = 8 * (w >> 1) + 2 * (w & 1);
+    return j + (q & 1);
+}
+template <int BITS>
+__host__ __device__ __forceinline__ int hi_code(int q) {
+    if (BITS == 4) return lo_code<4>(q) + 4;
+    if (BITS == 2) return lo_code<2>(q) + 8;
+    return lo_code<3>(q) + 4;
+}
+
+template <int BITS> struct Chunk { uint32_t w[BITS]; };  // 32 codes = 4*BITS bytes
+
+template <int BITS>
+__device__ __forceinline__ void load_chunk(Chunk<BITS>& c, const uint8_t* p) {
+    if constexpr (BITS == 4) {
+        uint4 v = ldg_stream_v4(p);
+        c.w[0] = v.x; c.w[1] = v.y; c.w[2] = v.z; c.w[3] = v.w;
+    } else if constexpr (BITS == 2) {
+        uint2 v = ldg_stream_v2(p);
+        c.w[0] = v.x; c.w[1] = v.y;
+    } else {
+        c.w[0] = ldg_stream_u32(p);
+        c.w[1] = ldg_stream_u32(p + 4);
+        c.w[2] = ldg_stream_u32(p + 8);
+    }
+}
+
+constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
+
+// Decode one 32-code chunk into 16 fp16 pairs of exact signed codes.
+template <int BITS, bool UNSIGNED>
+__device__ __forceinline__ void unpack_chunk(const Chunk<BITS>& c, uint32_t h[16]) {
+    if constexpr (BITS == 4) {
+        // signed(n) = (n ^ 8) - 8; unsigned-offset(u) = u - 8.
+        constexpr uint32_t kSub = f16x2_bits(1032.0, 1032.0);
+        constexpr uint32_t kMul = f16x2_bits(1.0 / 16, 1.0 / 16);
+        constexpr uint32_t kAdd = f16x2_bits(-72.0, -72.0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint32_t q = UNSIGNED ? c.w[i] : (c.w[i] ^ 0x88888888u);
+            h[4 * i + 0] = hsub2_bits(lop3_and_or(q, 0x000F000Fu, kMagic), kSub);
+            h[4 * i + 1] = hfma2_bits(lop3_and_or(q, 0x00F000F0u, kMagic), kMul, kAdd);
+            q >>= 8;
+            h[4 * i + 2] = hsub2_bits(lop3_and_or(q, 0x000F000Fu, kMagic), kSub);
+            h[4 * i + 3] = hfma2_bits(lop3_and_or(q, 0x00F000F0u, kMagic), kMul, kAdd);
+        }
+    } else if constexpr (BITS == 2) {
+        // signed(u) = (u ^ 2) - 2; unsigned-offset(u) = u - 2.
+        constexpr uint32_t kSub0 = f16x2_bits(1026.0, 1026.0);
+        constexpr uint32_t kMul1 = f16x2_bits(1.0 / 4, 1.0 / 4);
+        constexpr uint32_t kAdd1 = f16x2_bits(-258.0, -258.0);
+        constexpr uint32_t kMul2 = f16x2_bits(1.0 / 16, 1.0 / 16);
+        constexpr uint32_t kAdd2 = f16x2_bits(-66.0, -66.0);
+        constexpr uint32_t kMul3 = f16x2_bits(1.0 / 64, 1.0 / 64);
+        constexpr uint32_t kAdd3 = f16x2_bits(-18.0, -18.0);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            uint32_t q = UNSIGNED ? c.w[i] : (c.w[i] ^ 0xAAAAAAAAu);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int b = 8 * i + 4 * half;
+                h[b + 0] = hsub2_bits(lop3_and_or(q, 0x00030003u, kMagic), kSub0);
+                h[b + 1] = hfma2_bits(lop3_and_or(q, 0x000C000Cu, kMagic), kMul1, kAdd1);
+                h[b + 2] = hfma2_bits(lop3_and_or(q, 0x00300030u, kMagic), kMul2, kAdd2);
+                h[b + 3] = hfma2_bits(lop3_and_or(q, 0x00C000C0u, kMagic), kMul3, kAdd3);
+                q >>= 8;
+            }
+        }
+    } else {
+        // 32 three-bit codes in 96 bits; code j at bits [3j, 3j+3).
+        // signed(u) = (u ^ 4) - 4: flip every code's top bit, then subtract 4.
+        uint32_t w0 = c.w[0], w1 = c.w[1], w2 = c.w[2];
+        if (!UNSIGNED) {
+            w0 ^= 0x24924924u;
+            w1 ^= 0x49249249u;
+            w2 ^= 0x92492492u;
+        }
+        // Window R(j) = bits [3j-4, 3j+28) of the chunk: codes j, j+1 land at
+        // bits 4 and 7 (low half), codes j+4, j+5 at bits 16 and 19 (high half).
+        uint32_t R[8];
+        R[0] = w0 << 4;                 // j = 0
+        R[1] = w0 >> 2;                 // j = 2
+        R[2] = funnel_r(w0, w1, 20);    // j = 8
+        R[3] = funnel_r(w0, w1, 26);    // j = 10
+        R[4] = funnel_r(w1, w2, 12);    // j = 16
+        R[5] = funnel_r(w1, w2, 18);    // j = 18
+        R[6] = w2 >> 4;                 // j = 24
+        R[7] = w2 >> 10;                // j = 26
+        constexpr uint32_t kMul0 = f16x2_bits(1.0 / 16, 1.0);
+        constexpr uint32_t kAdd0 = f16x2_bits(-68.0, -1028.0);
+        constexpr uint32_t kMul1 = f16x2_bits(1.0 / 128, 1.0 / 8);
+        constexpr uint32_t kAdd1 = f16x2_bits(-12.0, -132.0);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            h[2 * w + 0] = hfma2_bits(lop3_and_or(R[w], 0x00070070u, kMagic), kMul0, kAdd0);
+            h[2 * w + 1] = hfma2_bits(lop3_and_or(R[w], 0x03800380u, kMagic), kMul1, kAdd1);
+        }
+    }
+}
+
+// Decode only fp16 pairs 2*mm and 2*mm+1 of a chunk (the A registers of MMA
+// number mm): the arithmetic of unpack_chunk, evaluated lazily so that only
+// four decoded registers per tile are live at a time.  mm is a constant
+// after loop unrolling, so every branch below folds away.
+template <int BITS, bool UNSIGNED>
+__device__ __forceinline__ void unpack_mm(const Chunk<BITS>& c, const int mm, uint32_t& h0, uint32_t& h1) {
+    if constexpr (BITS == 4) {
+        uint32_t q = UNSIGNED ? c.w[mm >> 1] : (c.w[mm >> 1] ^ 0x88888888u);
+        if (mm & 1) q >>= 8;
+        constexpr uint32_t kSub = f16x2_bits(1032.0, 1032.0);
+        constexpr uint32_t kMul = f16x2_bits(1.0 / 16, 1.0 / 16);
+        constexpr uint32_t kAdd = f16x2_bits(-72.0, -72.0);
+        h0 = hsub2_bits(lop3_and_or(q, 0x000F000Fu, kMagic), kSub);
+        h1 = hfma2_bits(lop3_and_or(q, 0x00F000F0u, kMagic), kMul, kAdd);
+    } else if constexpr (BITS == 2) {
+        uint32_t q = UNSIGNED ? c.w[mm >> 2] : (c.w[mm >> 2] ^ 0xAAAAAAAAu);
+        const int p0 = 2 * (mm & 3);  // pair index inside the word: 0, 2, 4, 6
+        if (p0 >= 4) q >>= 8;
+        constexpr uint32_t kSub0 = f16x2_bits(1026.0, 1026.0);
+        constexpr uint32_t kMul1 = f16x2_bits(1.0 / 4, 1.0 / 4);
+        constexpr uint32_t kAdd1 = f16x2_bits(-258.0, -258.0);
+        constexpr uint32_t kMul2 = f16x2_bits(1.0 / 16, 1.0 / 16);
+        constexpr uint32_t kAdd2 = f16x2_bits(-66.0, -66.0);
+        constexpr uint32_t kMul3 = f16x2_bits(1.0 / 64, 1.0 / 64);
+        constexpr uint32_t kAdd3 = f16x2_bits(-18.0, -18.0);
+        if ((p0 & 3) == 0) {
+            h0 = hsub2_bits(lop3_and_or(q, 0x00030003u, kMagic), kSub0);
+            h1 = hfma2_bits(lop3_and_or(q, 0x000C000Cu, kMagic), kMul1, kAdd1);
+        } else {
+            h0 = hfma2_bits(lop3_and_or(q, 0x00300030u, kMagic), kMul2, kAdd2);
+            h1 = hfma2_bits(lop3_and_or(q, 0x00C000C0u, kMagic), kMul3, kAdd3);
+        }
+    } else {
+        uint32_t w0 = c.w[0], w1 = c.w[1], w2 = c.w[2];
+        if (!UNSIGNED) {
+            w0 ^= 0x24924924u;
+            w1 ^= 0x49249249u;
+            w2 ^= 0x92492492u;
+        }
+        uint32_t R;
+        switch (mm) {
+            case 0: R = w0 << 4; break;
+            case 1: R = w0 >> 2; break;
+            case 2: R = funnel_r(w0, w1, 20); break;
+            case 3: R = funnel_r(w0, w1, 26); break;
+            case 4: R = funnel_r(w1, w2, 12); break;
+            case 5: R = funnel_r(w1, w2, 18); break;
+            case 6: R = w2 >> 4; break;
+            default: R = w2 >> 10; break;
+        }
+        constexpr uint32_t kMul0 = f16x2_bits(1.0 / 16, 1.0);
+        constexpr uint32_t kAdd0 = f16x2_bits(-68.0, -1028.0);
+        constexpr uint32_t kMul1 = f16x2_bits(1.0 / 128, 1.0 / 8);
+        constexpr uint32_t kAdd1 = f16x2_bits(-12.0, -132.0);
+        h0 = hfma2_bits(lop3_and_or(R, 0x00070070u, kMagic), kMul0, kAdd0);
+        h1 = hfma2_bits(lop3_and_or(R, 0x03800380u, kMagic), kMul1, kAdd1);
+    }
+}
+
+// -------------------------------------------------------------------------
+// Shared-memory plan of the fast kernel.
+// -------------------------------------------------------------------------
+struct SmemPlan {
+    int lanes;        // lanes holding B columns per n-tile (8*min(8,2m)/2 ... = 4 * columns)
+    int nt;           // n8 tiles (2 columns per x row)
+    size_t frag_bytes, xs_bytes, red_bytes, total;
+};
+
+__host__ __device__ __forceinline__ int gemv_nt(int m) { return (2 * m + 7) / 8; }
+__host__ __device__ __forceinline__ int gemv_lanes(int m) { return 4 * (2 * m < 8 ? 2 * m : 8); }
+
+static SmemPlan smem_plan(int m, int kb_total, int rt, int nwarps) {
+    SmemPlan p;
+    p.nt = gemv_nt(m);
+    p.lanes = gemv_lanes(m);
+    p.frag_bytes = (size_t)kb_total * 4 * p.nt * p.lanes * 16;
+    p.xs_bytes = (size_t)kb_total * m * sizeof(float);
+    p.red_bytes = (size_t)nwarps * rt * m * 16 * sizeof(float);
+    p.total = p.frag_bytes + p.xs_bytes + p.red_bytes + 2 * 16 * sizeof(float);
+    return p;
+}
+
+constexpr int kGemvWarps = 8;
+constexpr int kGemvThreads = kGemvWarps * 32;
+
+template <int BITS, int NT, int RT, bool UNSIGNED, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 2)
+lowbit_gemv_mma_kernel(const GemvParams p) {
+    constexpr int PIPE = (RT == 1) ? 4 : (NT == 1 ? 3 : 2);  // k-blocks in flight per warp
+    constexpr int CHUNK_BYTES = 4 * BITS;        // 32 codes
+    constexpr int KBLOCK_BYTES = 16 * BITS;      // 128 codes
+
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int m = p.m;
+    const int kbt = p.kb_total;
+    const int lanes = gemv_lanes(m);
+    uint4* frag = reinterpret_cast<uint4*>(smem_raw);
+    float* xs = reinterpret_cast<float*>(smem_raw + (size_t)kbt * 4 * NT * lanes * 16);
+    float* red = xs + (size_t)kbt * m;
+    float* row_scale = red + kGemvWarps * RT * m * 16;   // [16]: 2^-e per x row
+    float* row_norm = row_scale + 16;                      // [16]: RMSNorm inverse rms per row
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int g = lane >> 2;
+    const int c = lane & 3;
+
+    // Row bases of this CTA's tiles.
+    int tile_row0[RT];
+#pragma unroll
+    for (int tt = 0; tt < RT; ++tt) {
+        if (EPI == kEpiSwiGLU) tile_row0[tt] = blockIdx.x * 16 + tt * (p.n >> 1);
+        else tile_row0[tt] = (blockIdx.x * RT + tt) * 16;
+    }
+
+    // ---- issue the first weight loads before the activation prologue ----
+    Chunk<BITS> buf[PIPE][RT][2];
+    float sz[PIPE][RT][4];   // s(g), zp(g), s(g+8), zp(g+8)
+    const int my_kb = (kbt - warp + kGemvWarps - 1) / kGemvWarps;  // k-blocks of this warp
+
+    auto issue = [&](int stage_it, Chunk<BITS> (&b)[RT][2], float (&s)[RT][4]) {
+        const int kb = warp + stage_it * kGemvWarps;
+        const int grp = kb / p.kb_per_group;
+#pragma unroll
+        for (int tt = 0; tt < RT; ++tt) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                int row = tile_row0[tt] + g + 8 * h;
+                row = row < p.n ? row : p.n - 1;
+                const uint8_t* src = p.w + (size_t)row * p.row_bytes + (size_t)kb * KBLOCK_BYTES + c * CHUNK_BYTES;
+                load_chunk<BITS>(b[tt][h], src);
+                const size_t sidx = (size_t)row * p.n_groups + grp;
+                float sv, zv;
+                if (p.flags & VSPEC_B200_F_SZ_F16) {
+                    sv = p.s ? __half2float(reinterpret_cast<const __half*>(p.s)[sidx]) : 1.0f;
+                    zv = p.zp ? __half2float(reinterpret_cast<const __half*>(p.zp)[sidx]) : p.zp_const;
+                } else {
+                    sv = p.s ? reinterpret_cast<const float*>(p.s)[sidx] : 1.0f;
+                    zv = p.zp ? reinterpret_cast<const float*>(p.zp)[sidx] : p.zp_const;
+                }
+                s[tt][2 * h] = sv;
+                s[tt][2 * h + 1] = zv;
+            }
+        }
+    };
+
+#pragma unroll
+    for (int st = 0; st < PIPE; ++st)
+        if (st < my_kb) issue(st, buf[st], sz[st]);
+
+    // ---- activation prologue ----
+    const int K = p.k;
+    // (1) RMSNorm inverse rms per row (optional).
+    if (EPI_HAS_RMSNORM(p.flags)) {
+        for (int r = warp; r < m; r += kGemvWarps) {
+            const float* xr = p.x + (size_t)r * K;
+            float ss = 0.f;
+            for (int t = lane; t < K; t += 32) { float v = xr[t]; ss += v * v; }
+            ss = warp_sum(ss);
+            if (lane == 0) row_norm[r] = 1.0f / sqrtf(ss / (float)K + p.eps);
+        }
+        __syncthreads();
+    }
+    // (2) per (k-block, row) sums and per-row max |x|.
+    {
+        float* maxbuf = red;  // reuse the reduction area: [kGemvWarps][m]
+        for (int r = 0; r < m; ++r) {
+            const float* xr = p.x + (size_t)r * K;
+            const float nr = EPI_HAS_RMSNORM(p.flags) ? row_norm[r] : 1.0f;
+            float mx = 0.f;
+            for (int kb = warp; kb < kbt; kb += kGemvWarps) {
+                const int t = kb * 128 + lane * 4;
+                float4 v = *reinterpret_cast<const float4*>(xr + t);
+                if (EPI_HAS_RMSNORM(p.flags)) {
+                    float4 wn = *reinterpret_cast<const float4*>(p.norm_w + t);
+                    v.x = v.x * nr * wn.x; v.y = v.y * nr * wn.y; v.z = v.z * nr * wn.z; v.w = v.w * nr * wn.w;
+                }
+                float sum = (v.x + v.y) + (v.z + v.w);
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                sum = warp_sum(sum);
+                if (lane == 0) xs[kb * m + r] = sum;
+            }
+            mx = warp_max(mx);
+            if (lane == 0) maxbuf[warp * m + r] = mx;
+        }
+        __syncthreads();
+        if (tid < m) {
+            float mx = 0.f;
+            for (int w = 0; w < kGemvWarps; ++w) mx = fmaxf(mx, maxbuf[w * m + tid]);
+            // Exact power-of-two rescale so that max|x| lands in [2^13, 2^14):
+            // fp16 hi never overflows and lo keeps full precision.
+            int ex = 0;
+            if (mx > 0.f && isfinite(mx)) { (void)frexpf(mx, &ex); ex -= 14; }
+            row_scale[tid] = ldexpf(1.0f, -ex);
+        }
+        __syncthreads();
+        for (int i = tid; i < kbt * m; i += kGemvThreads) xs[i] *= row_scale[i % m];
+    }
+    // (3) B fragments in fragment order: slot (kb, mp, nt, lane) = 16 bytes.
+    {
+        const int slots = kbt * 4 * NT * lanes;
+        for (int z = tid; z < slots; z += kGemvThreads) {
+            const int ln = z % lanes;
+            const int nt = (z / lanes) % NT;
+            const int mp = (z / (lanes * NT)) & 3;
+            const int kb = z / (lanes * NT * 4);
+            const int gc = ln >> 2, cc = ln & 3;
+            const int col = 8 * nt + gc;
+            const int r = col >> 1;
+            uint32_t out[4] = {0u, 0u, 0u, 0u};
+            if (r < m) {
+                const float* xr = p.x + (size_t)r * K;
+                const float nr = EPI_HAS_RMSNORM(p.flags) ? row_norm[r] : 1.0f;
+                const float sc = row_scale[r];
+                const int base = kb * 128 + 32 * cc;
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) {
+                    const int q = 4 * mp + qq;
+                    const int t0 = base + lo_code<BITS>(q);
+                    const int t1 = base + hi_code<BITS>(q);
+                    float v0 = xr[t0], v1 = xr[t1];
+                    if (EPI_HAS_RMSNORM(p.flags)) { v0 = v0 * nr * p.norm_w[t0]; v1 = v1 * nr * p.norm_w[t1]; }
+                    v0 *= sc; v1 *= sc;
+                    __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+                    if (col & 1) {  // lo part: residual after the hi part
+                        h0 = __float2half_rn(v0 - __half2float(h0));
+                        h1 = __float2half_rn(v1 - __half2float(h1));
+                    }
+                    out[qq] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+                }
+            }
+            frag[z] = make_uint4(out[0], out[1], out[2], out[3]);
+        }
+    }
+    __syncthreads();
+
+    // ---- main loop ----
+    float acc[RT][NT][2];
+#pragma unroll
+    for (int tt = 0; tt < RT; ++tt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[tt][nt][0] = acc[tt][nt][1] = 0.f;
+
+    const bool lane_has_b = lane < lanes;
+    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+
+    for (int base_it = 0; base_it < my_kb; base_it += PIPE) {
+#pragma unroll
+        for (int st = 0; st < PIPE; ++st) {
+            const int it = base_it + st;
+            if (it < my_kb) {
+                const int kb = warp + it * kGemvWarps;
+                float d[RT][NT][4];
+                const uint4* fb = frag + (size_t)kb * 4 * NT * lanes;
+#pragma unroll
+                for (int mp = 0; mp < 4; ++mp) {
+                    uint4 bb[NT];
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        bb[nt] = make_uint4(0u, 0u, 0u, 0u);
+                        if (lane_has_b) bb[nt] = fb[(mp * NT + nt) * lanes + lane];
+                    }
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const int mm = 2 * mp + half;
+#pragma unroll
+                        for (int tt = 0; tt < RT; ++tt) {
+                            // A fragment: rows g / g+8, k-slots {2c,2c+1} and {2c+8,2c+9}
+                            uint32_t a[4];
+                            unpack_mm<BITS, UNSIGNED>(buf[st][tt][0], mm, a[0], a[2]);
+                            unpack_mm<BITS, UNSIGNED>(buf[st][tt][1], mm, a[1], a[3]);
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt) {
+                                const uint32_t b0 = half ? bb[nt].z : bb[nt].x;
+                                const uint32_t b1 = half ? bb[nt].w : bb[nt].y;
+                                mma_16816_f16(d[tt][nt], a, b0, b1, mm == 0 ? zero4 : d[tt][nt]);
+                            }
+                        }
+                    }
+                }
+                float szc[RT][4];
+#pragma unroll
+                for (int tt = 0; tt < RT; ++tt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) szc[tt][i] = sz[st][tt][i];
+                // refill this stage: the loads land while the next stages compute
+                if (it + PIPE < my_kb) issue(it + PIPE, buf[st], sz[st]);
+                // per-k-block scale / zero-point epilogue
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int r = 4 * nt + c;
+                    if (r < m) {
+                        const float xsum = xs[kb * m + r];
+#pragma unroll
+                        for (int tt = 0; tt < RT; ++tt) {
+                            acc[tt][nt][0] = fmaf(szc[tt][0], (d[tt][nt][0] + d[tt][nt][1]) - szc[tt][1] * xsum, acc[tt][nt][0]);
+                            acc[tt][nt][1] = fmaf(szc[tt][2], (d[tt][nt][2] + d[tt][nt][3]) - szc[tt][3] * xsum, acc[tt][nt][1]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- cross-warp reduction (fixed order) and epilogue ----
+    __syncthreads();  // xs/frag no longer needed; red may overlap nothing else
+#pragma unroll
+    for (int tt = 0; tt < RT; ++tt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int r = 4 * nt + c;
+            if (r < m) {
+                red[((warp * RT + tt) * m + r) * 16 + g] = acc[tt][nt][0];
+                red[((warp * RT + tt) * m + r) * 16 + g + 8] = acc[tt][nt][1];
+            }
+        }
+    __syncthreads();
+    if (EPI == kEpiSwiGLU) {
+        // rows [0, n/2) gate, [n/2, n) up; output row blockIdx.x*16 + i
+        for (int z = tid; z < m * 16; z += kGemvThreads) {
+            const int r = z >> 4, i = z & 15;
+            const int orow = blockIdx.x * 16 + i;
+            if (orow < (p.n >> 1)) {
+                float gsum = 0.f, usum = 0.f;
+                for (int w = 0; w < kGemvWarps; ++w) {
+                    gsum += red[((w * RT + 0) * m + r) * 16 + i];
+                    usum += red[((w * RT + 1) * m + r) * 16 + i];
+                }
+                const float inv = 1.0f / row_scale[r];
+                gsum *= inv; usum *= inv;
+                const float silu = gsum / (1.0f + expf(-gsum));
+                p.y[(size_t)r * (p.n >> 1) + orow] = silu * usum;
+            }
+        }
+    } else {
+        for (int z = tid; z < RT * m * 16; z += kGemvThreads) {
+            const int tt = z / (m * 16);
+            const int r = (z >> 4) % m;
+            const int i = z & 15;
+            const int orow = tile_row0[tt] + i;
+            if (orow < p.n) {
+                float sum = 0.f;
+                for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * RT + tt) * m + r) * 16 + i];
+                sum *= 1.0f / row_scale[r];
+                const size_t o = (size_t)r * p.n + orow;
+                if (p.flags & VSPEC_B200_F_RESIDUAL) sum += p.residual[o];
+                p.y[o] = sum;
+            }
+        }
+    }
+}
+
+// -------------------------------------------------------------------------
+// Generic path: any k, any group count, any alignment.  One warp per output
+// row; lanes stride the reduction; fp32 FMA; fixed-order warp reduction.
+// -------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+lowbit_gemv_generic_kernel(const GemvParams p, int bits, int unsigned_codes, int n_rows_total) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= n_rows_total) return;
+    const int j = warp;  // weight row
+    const size_t K = (size_t)p.k;
+    const uint8_t* wrow = p.w + (size_t)j * p.row_bytes;
+    for (int i = 0; i < p.m; ++i) {
+        const float* xr = p.x + (size_t)i * K;
+        float nr = 1.0f;
+        if (EPI_HAS_RMSNORM(p.flags)) {
+            float ss = 0.f;
+            for (size_t t = lane; t < K; t += 32) ss += xr[t] * xr[t];
+            ss = warp_sum(ss);
+            nr = 1.0f / sqrtf(ss / (float)K + p.eps);
+        }
+        float acc = 0.f;
+        for (size_t t = lane; t < K; t += 32) {
+            const size_t idx = (size_t)j * p.n_groups + group_of(t, K, (size_t)p.n_groups);
+            float sv, zv;
+            if (p.flags & VSPEC_B200_F_SZ_F16) {
+                sv = p.s ? __half2float(reinterpret_cast<const __half*>(p.s)[idx]) : 1.0f;
+                zv = p.zp ? __half2float(reinterpret_cast<const __half*>(p.zp)[idx]) : p.zp_const;
+            } else {
+                sv = p.s ? reinterpret_cast<const float*>(p.s)[idx] : 1.0f;
+                zv = p.zp ? reinterpret_cast<const float*>(p.zp)[idx] : p.zp_const;
+            }
+            float xv = xr[t];
+            if (EPI_HAS_RMSNORM(p.flags)) xv = xv * nr * p.norm_w[t];
+            const float q = (float)decode_code_generic(wrow, t, bits, unsigned_codes);
+            acc = fmaf(xv, (q - zv) * sv, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            const size_t o = (size_t)i * p.n + j;
+            if (p.flags & VSPEC_B200_F_RESIDUAL) acc += p.residual[o];
+            p.y[o] = acc;
+        }
+    }
+}
+
+// SwiGLU combine for the generic path: y_act[i][j] = silu(y[i][j]) * y[i][n/2 + j].
+__global__ void swiglu_combine_kernel(const float* y_full, float* y_act, int m, int half_n) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= m * half_n) return;
+    const int i = idx / half_n, j = idx % half_n;
+    const float gt = y_full[(size_t)i * 2 * half_n + j];
+    const float up = y_full[(size_t)i * 2 * half_n + half_n + j];
+    y_act[idx] = gt / (1.0f + expf(-gt)) * up;
+}
+
+// -------------------------------------------------------------------------
+// Debug/parity kernel: decode every code of a packed matrix with the exact
+// device routine the fast GEMV uses (fast layout) or the generic decoder.
+// -------------------------------------------------------------------------
+template <int BITS, bool UNSIGNED>
+__global__ void unpack_codes_fast_kernel(const uint8_t* w, int n, int k, int row_bytes, int8_t* out) {
+    const size_t chunk = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t chunks_per_row = (size_t)k / 32;
+    if (chunk >= (size_t)n * chunks_per_row) return;
+    const size_t row = chunk / chunks_per_row, ci = chunk % chunks_per_row;
+    Chunk<BITS> cbuf;
+    const uint8_t* src = w + row * row_bytes + ci * (4 * BITS);
+    // byte-wise gather (no alignment assumption) into the chunk words
+    uint8_t tmp[4 * BITS];
+    for (int i = 0; i < 4 * BITS; ++i) tmp[i] = src[i];
+    for (int i = 0; i < BITS; ++i)
+        cbuf.w[i] = (uint32_t)tmp[4 * i] | ((uint32_t)tmp[4 * i + 1] << 8) | ((uint32_t)tmp[4 * i + 2] << 16) |
+                    ((uint32_t)tmp[4 * i + 3] << 24);
+    uint32_t h[16];
+    unpack_chunk<BITS, UNSIGNED>(cbuf, h);
+    int8_t* o = out + row * (size_t)k + ci * 32;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+        const __half2 v = *reinterpret_cast<const __half2*>(&h[q]);
+        o[lo_code<BITS>(q)] = (int8_t)__half2float(__low2half(v));
+        o[hi_code<BITS>(q)] = (int8_t)__half2float(__high2half(v));
+    }
+}
+
+__global__ void unpack_codes_generic_kernel(const uint8_t* w, int n, int k, int row_bytes, int bits, int unsigned_codes,
+                                            int8_t* out) {
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)n * k) return;
+    const size_t row = idx / k, t = idx % k;
+    out[idx] = (int8_t)decode_code_generic(w + row * row_bytes, t, bits, unsigned_codes);
+}
+
+// -------------------------------------------------------------------------
+// Host-side dispatch
+// -------------------------------------------------------------------------
+static bool fast_path_ok(const GemvParams& p, int bits) {
+    if (p.m < 1 || p.m > kGemvMaxM) return false;
+    if (p.k % 128 != 0) return false;
+    if (p.n_groups < 1 || p.k % p.n_groups != 0) return false;
+    const int gsize = p.k / p.n_groups;
+    if (gsize % 128 != 0) return false;
+    if ((size_t)p.row_bytes != row_bytes_for((size_t)p.k, bits)) return false;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p.w);
+    const int need = bits == 4 ? 16 : (bits == 2 ? 8 : 4);
+    if (a % need != 0) return false;
+    if (reinterpret_cast<uintptr_t>(p.x) % 16 != 0) return false;
+    if ((p.flags & VSPEC_B200_F_RMSNORM) && reinterpret_cast<uintptr_t>(p.norm_w) % 16 != 0) return false;
+    return true;
+}
+
+template <int BITS, int NT, int RT, bool UNS, int EPI>
+static cudaError_t launch_fast_t(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+    auto kern = lowbit_gemv_mma_kernel<BITS, NT, RT, UNS, EPI>;
+    static thread_local int configured_dev = -1;
+    static thread_local size_t configured_smem = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev || configured_smem < smem) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured_dev = dev;
+        configured_smem = smem;
+    }
+    kern<<<grid, kGemvThreads, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <int BITS, int NT, bool UNS>
+static cudaError_t launch_fast_nt(const GemvParams& p, int epi, int grid, int rt, size_t smem, cudaStream_t st) {
+    if (epi == kEpiSwiGLU) return launch_fast_t<BITS, NT, 2, UNS, kEpiSwiGLU>(p, grid, smem, st);
+    if (rt == 2) return launch_fast_t<BITS, NT, 2, UNS, kEpiPlain>(p, grid, smem, st);
+    return launch_fast_t<BITS, NT, 1, UNS, kEpiPlain>(p, grid, smem, st);
+}
+
+template <int BITS, bool UNS>
+static cudaError_t launch_fast_bits(const GemvParams& p, int epi, int grid, int rt, size_t smem, cudaStream_t st) {
+    switch (gemv_nt(p.m)) {
+        case 1: return launch_fast_nt<BITS, 1, UNS>(p, epi, grid, rt, smem, st);
+        default: return launch_fast_nt<BITS, 2, UNS>(p, epi, grid, rt, smem, st);
+    }
+}
+
+int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int force_generic) {
+    if (bits < 2 || bits > 4) { set_error("bits must be 2, 3 or 4 (got %d)", bits); return VSPEC_B200_ERR_ARG; }
+    const bool swiglu = (p.flags & VSPEC_B200_F_SWIGLU) != 0;
+    if (swiglu && (p.n % 2 != 0)) { set_error("SwiGLU needs an even row count (n=%d)", p.n); return VSPEC_B200_ERR_ARG; }
+    p.kb_total = p.k / 128;
+    p.kb_per_group = (p.n_groups > 0 && p.k % p.n_groups == 0) ? (p.k / p.n_groups) / 128 : 1;
+    if (p.kb_per_group < 1) p.kb_per_group = 1;
+
+    const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
+    if (fast) {
+        const int half_rows = swiglu ? p.n / 2 : p.n;
+        const int tiles = (half_rows + 15) / 16;
+        int rt = 1;
+        if (swiglu) rt = 2;
+        else if (tiles >= 4 * device_sm_count() && tiles % 2 == 0) rt = 2;
+        const int grid = swiglu ? tiles : tiles / rt;
+        SmemPlan plan = smem_plan(p.m, p.kb_total, rt, kGemvWarps);
+        if (plan.total <= kGemvMaxSmem) {
+            cudaError_t e;
+            const int epi = swiglu ? kEpiSwiGLU : kEpiPlain;
+            if (unsigned_codes) {
+                if (bits == 4) e = launch_fast_bits<4, true>(p, epi, grid, rt, plan.total, st);
+                else if (bits == 3) e = launch_fast_bits<3, true>(p, epi, grid, rt, plan.total, st);
+                else e = launch_fast_bits<2, true>(p, epi, grid, rt, plan.total, st);
+            } else {
+                if (bits == 4) e = launch_fast_bits<4, false>(p, epi, grid, rt, plan.total, st);
+                else if (bits == 3) e = launch_fast_bits<3, false>(p, epi, grid, rt, plan.total, st);
+                else e = launch_fast_bits<2, false>(p, epi, grid, rt, plan.total, st);
+            }
+            if (e != cudaSuccess) return cuda_status(e, "lowbit_gemv_mma_kernel launch");
+            return VSPEC_B200_OK;
+        }
+    }
+    // generic path
+    if (swiglu) {
+        set_error("SwiGLU epilogue requires the fast path shape (k %% 128 == 0, groups of 128*i, n/2 %% 16 == 0, m <= %d)",
+                  kGemvMaxM);
+        return VSPEC_B200_ERR_UNSUPPORTED;
+    }
+    const int rows = p.n;
+    const int threads = 256;
+    const int blocks = (rows * 32 + threads - 1) / threads;
+    lowbit_gemv_generic_kernel<<<blocks, threads, 0, st>>>(p, bits, unsigned_codes, rows);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "lowbit_gemv_generic_kernel launch");
+    return VSPEC_B200_OK;
+}
+
+int unpack_codes_launch(const uint8_t* w, int n, int k, int bits, int unsigned_codes, int8_t* out, cudaStream_t st,
+                        int use_fast_decoder) {
+    const int rb = (int)row_bytes_for((size_t)k, bits);
+    if (use_fast_decoder) {
+        if (k % 32 != 0) { set_error("fast decoder needs k %% 32 == 0"); return VSPEC_B200_ERR_ARG; }
+        const size_t chunks = (size_t)n * (k / 32);
+        const int threads = 256;
+        const unsigned blocks = (unsigned)((chunks + threads - 1) / threads);
+        if (bits == 4) unsigned_codes ? unpack_codes_fast_kernel<4, true><<<blocks, threads, 0, st>>>(w, n, k, rb, out)
+                                      : unpack_codes_fast_kernel<4, false><<<blocks, threads, 0, st>>>(w, n, k, rb, out);
+        else if (bits == 3) unsigned_codes ? unpack_codes_fast_kernel<3, true><<<blocks, threads, 0, st>>>(w, n, k, rb, out)
+                                           : unpack_codes_fast_kernel<3, false><<<blocks, threads, 0, st>>>(w, n, k, rb, out);
+        else unsigned_codes ? unpack_codes_fast_kernel<2, true><<<blocks, threads, 0, st>>>(w, n, k, rb, out)
+                            : unpack_codes_fast_kernel<2, false><<<blocks, threads, 0, st>>>(w, n, k, rb, out);
+    } else {
+        const size_t total = (size_t)n * k;
+        const int threads = 256;
+        unpack_codes_generic_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
+            w, n, k, rb, bits, unsigned_codes, out);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "unpack_codes launch");
+    return VSPEC_B200_OK;
+}
+
+}  // namespace vb200

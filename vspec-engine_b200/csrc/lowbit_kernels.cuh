@@ -1,0 +1,38 @@
+// lowbit_kernels.cuh -- internal interface between the kernels and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace vb200 {
+
+struct GemvParams {
+    const float* x;          // [m][k] fp32 activations
+    const uint8_t* w;        // [n][row_bytes] packed codes
+    const void* s;           // [n][n_groups] fp32 or fp16
+    const void* zp;          // [n][n_groups] same dtype or nullptr
+    float zp_const;          // zero-point used when zp == nullptr
+    float* y;                // [m][n] (or [m][n/2] with SwiGLU)
+    const float* residual;   // [m][n] added when VSPEC_B200_F_RESIDUAL
+    const float* norm_w;     // [k] RMSNorm weight when VSPEC_B200_F_RMSNORM
+    float eps;
+    int m, n, k, n_groups;
+    int row_bytes;
+    int kb_total;            // k / 128 (fast path)
+    int kb_per_group;        // (k / n_groups) / 128 (fast path)
+    int flags;
+};
+
+constexpr int kEpiPlain = 0;
+constexpr int kEpiSwiGLU = 1;
+constexpr int kGemvMaxM = 8;
+constexpr size_t kGemvMaxSmem = 200 * 1024;
+
+#define EPI_HAS_RMSNORM(flags) (((flags) & VSPEC_B200_F_RMSNORM) != 0)
+
+int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int force_generic);
+int unpack_codes_launch(const uint8_t* w, int n, int k, int bits, int unsigned_codes, int8_t* out, cudaStream_t st,
+                        int use_fast_decoder);
+
+}  // namespace vb200
