@@ -178,37 +178,39 @@ def test_reference_named_device_launchers():
     x = rng.standard_normal((m, k)).astype(np.float32)
     dx = to_dev(x)
     dy = empty_dev((m, n), torch.float32)
+    keep = []   # device tensors must outlive the asynchronous launches
+
+    def dev(a):
+        keep.append(to_dev(a))
+        return keep[-1].data_ptr()
+
     # int4, group-wise with zp
     g = 2
     w, s, zp = make_lowbit(rng, n, k, 4, g)
-    V.lib.vspec_cuda_fused_linear_int4_device(dx.data_ptr(), to_dev(w).data_ptr(), to_dev(s).data_ptr(),
-                                              to_dev(zp).data_ptr(), dy.data_ptr(), m, n, k, g)
+    V.lib.vspec_cuda_fused_linear_int4_device(dx.data_ptr(), dev(w), dev(s), dev(zp), dy.data_ptr(), m, n, k, g)
     torch.cuda.synchronize()
     assert rel_err(dy.cpu().numpy(), O.lowbit_matmul(x, w, n, k, 4, s, zp, g)) <= RTOL_F32
     # int3 without stochastic rounding == per-row plain contraction
     w3, s3, _ = make_lowbit(rng, n, k, 3, 1, zp_mode="none")
-    V.lib.vspec_cuda_fused_linear_int3_device(dx.data_ptr(), to_dev(w3).data_ptr(), to_dev(s3).data_ptr(),
-                                              dy.data_ptr(), m, n, k, 0)
+    V.lib.vspec_cuda_fused_linear_int3_device(dx.data_ptr(), dev(w3), dev(s3), dy.data_ptr(), m, n, k, 0)
     torch.cuda.synchronize()
     assert rel_err(dy.cpu().numpy(), O.lowbit_matmul(x, w3, n, k, 3, s3, None, 1)) <= RTOL_F32
     # int2: unsigned codes, (q - 1.5) * s[row]
     w2, s2, _ = make_lowbit(rng, n, k, 2, 1, zp_mode="none")
-    V.lib.vspec_cuda_fused_linear_int2_device(dx.data_ptr(), to_dev(w2).data_ptr(), to_dev(s2).data_ptr(),
-                                              dy.data_ptr(), m, n, k)
+    V.lib.vspec_cuda_fused_linear_int2_device(dx.data_ptr(), dev(w2), dev(s2), dy.data_ptr(), m, n, k)
     torch.cuda.synchronize()
     ref2 = x.astype(np.float64) @ (((O.unpack_rows_np(w2, n, k, 2, unsigned=True) + 2).astype(np.float64) - 1.5)
                                    * s2.astype(np.float64)).T
     assert rel_err(dy.cpu().numpy(), ref2) <= RTOL_F32
     # dequant int4 -> f32 (bit-exact: one fp32 multiply per element)
     dwf = empty_dev((n, k), torch.float32)
-    V.lib.vspec_cuda_dequant_int4_to_f32_device(to_dev(w).data_ptr(), to_dev(s).data_ptr(), to_dev(zp).data_ptr(),
-                                                dwf.data_ptr(), n, k, g)
+    V.lib.vspec_cuda_dequant_int4_to_f32_device(dev(w), dev(s), dev(zp), dwf.data_ptr(), n, k, g)
     torch.cuda.synchronize()
     expect = ((O.unpack_rows(w, n, k, 4).astype(np.float32) - np.repeat(zp, k // g, axis=1))
               * np.repeat(s, k // g, axis=1))
     assert np.array_equal(dwf.cpu().numpy(), expect)
     # int3 -> int4 storage expansion: decoded codes identical
     d4 = empty_dev((n, (k + 1) // 2), torch.uint8)
-    V.lib.vspec_cuda_expand_int3_to_int4_device(to_dev(w3).data_ptr(), d4.data_ptr(), n, k)
+    V.lib.vspec_cuda_expand_int3_to_int4_device(dev(w3), d4.data_ptr(), n, k)
     torch.cuda.synchronize()
     assert np.array_equal(O.unpack_rows(d4.cpu().numpy(), n, k, 4), O.unpack_rows(w3, n, k, 3))

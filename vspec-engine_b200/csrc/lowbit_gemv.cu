@@ -134,7 +134,7 @@ __device__ __forceinline__ void unpack_chunk(const Chunk<BITS>& c, uint32_t h[16
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
             h[2 * w + 0] = hfma2_bits(lop3_and_or(R[w], 0x00070070u, kMagic), kMul0, kAdd0);
-            h[2 * w + 1] = hfma2_bits(lop3_and_or(R[w], 0x03800380u, kMagic), kMul1, kAdd1);
+            h[2 * w + 1] = hfma2_bits(lop3_and_or(R[w], 0x00380380u, kMagic), kMul1, kAdd1);
         }
     }
 }
@@ -194,7 +194,7 @@ __device__ __forceinline__ void unpack_mm(const Chunk<BITS>& c, const int mm, ui
         constexpr uint32_t kMul1 = f16x2_bits(1.0 / 128, 1.0 / 8);
         constexpr uint32_t kAdd1 = f16x2_bits(-12.0, -132.0);
         h0 = hfma2_bits(lop3_and_or(R, 0x00070070u, kMagic), kMul0, kAdd0);
-        h1 = hfma2_bits(lop3_and_or(R, 0x03800380u, kMagic), kMul1, kAdd1);
+        h1 = hfma2_bits(lop3_and_or(R, 0x00380380u, kMagic), kMul1, kAdd1);
     }
 }
 
