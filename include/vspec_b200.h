@@ -71,8 +71,19 @@ typedef struct VspecB200LinearArgs {
     size_t m, n, k, n_groups;
     int bits;                    /* 2, 3 or 4 */
     int flags;
+    void* d_workspace;           /* NULL = library-managed device scratch; else
+                                    >= vspec_b200_lowbit_linear_workspace_bytes()
+                                    bytes, zero-filled before first use (every
+                                    launch leaves it zero-filled again) */
+    size_t workspace_bytes;
 } VspecB200LinearArgs;
 
+/* Device scratch of the split-K merge (per-tile counters + fp32 partials).
+ * Calls sharing one workspace must be stream-ordered.  The library-managed
+ * workspace is allocated on the first call per device and grown when a larger
+ * shape arrives, so the first call of each shape must precede any stream
+ * capture. */
+size_t vspec_b200_lowbit_linear_workspace_bytes(size_t m, size_t n, size_t k, int flags);
 int vspec_b200_lowbit_linear(const VspecB200LinearArgs* args, void* stream);
 
 /* Same contraction through the any-shape path only (testing / odd shapes). */

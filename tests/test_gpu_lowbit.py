@@ -214,3 +214,43 @@ def test_reference_named_device_launchers():
     V.lib.vspec_cuda_expand_int3_to_int4_device(dev(w3), d4.data_ptr(), n, k)
     torch.cuda.synchronize()
     assert np.array_equal(O.unpack_rows(d4.cpu().numpy(), n, k, 4), O.unpack_rows(w3, n, k, 3))
+
+
+def test_split_merge_is_deterministic_and_self_cleaning():
+    """The split-K merge sums partials in a fixed order and leaves its counters at
+    zero: repeated launches give bit-identical outputs, with the library-managed
+    workspace and with a caller workspace."""
+    torch = torch_cuda()
+    rng = np.random.default_rng(99)
+    for bits, m, n, k, g in [(4, 1, 4096, 4096, 32), (3, 2, 1000, 2048, 16), (2, 8, 4096, 1024, 8)]:
+        w, s, zp = make_lowbit(rng, n, k, bits, g)
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        dx, dw, ds, dz = to_dev(x), to_dev(w), to_dev(s), to_dev(zp)
+        outs = []
+        ws_bytes = V.lib.vspec_b200_lowbit_linear_workspace_bytes(m, n, k, 0)
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+        for use_ws in (False, True, False, True):
+            dy = empty_dev((m, n), torch.float32)
+            V.lowbit_linear(dx.data_ptr(), dw.data_ptr(), ds.data_ptr(), dz.data_ptr(), dy.data_ptr(), m, n, k, g,
+                            bits, workspace=ws.data_ptr() if use_ws else None, workspace_bytes=ws_bytes)
+            torch.cuda.synchronize()
+            outs.append(dy.cpu().numpy())
+        for o in outs[1:]:
+            assert np.array_equal(o.view(np.uint32), outs[0].view(np.uint32))
+        counters = ws[: ((n + 15) // 16) * 4].view(torch.int32)
+        assert int(counters.abs().sum().item()) == 0
+        assert rel_err(outs[0], O.lowbit_matmul(x, w, n, k, bits, s, zp, g)) <= RTOL_F32
+
+
+def test_workspace_too_small_is_rejected():
+    torch = torch_cuda()
+    rng = np.random.default_rng(7)
+    n, k, g = 256, 1024, 8
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    dx, dw, ds, dz = to_dev(x), to_dev(w), to_dev(s), to_dev(zp)
+    dy = empty_dev((1, n), torch.float32)
+    ws = torch.zeros(16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(V.VspecB200Error, match="workspace too small"):
+        V.lowbit_linear(dx.data_ptr(), dw.data_ptr(), ds.data_ptr(), dz.data_ptr(), dy.data_ptr(), 1, n, k, g, 4,
+                        workspace=ws.data_ptr(), workspace_bytes=16)

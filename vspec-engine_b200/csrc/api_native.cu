@@ -110,12 +110,12 @@ static int linear_common(const VspecB200LinearArgs* a, void* stream, int force_g
             const size_t out_cols = (a->flags & VSPEC_B200_F_SWIGLU) ? (size_t)p.n / 2 : (size_t)p.n;
             q.y = p.y + (size_t)i0 * out_cols;
             if (p.residual) q.residual = p.residual + (size_t)i0 * p.n;
-            int rc = lowbit_gemv_launch(q, a->bits, uns, st, force_generic);
+            int rc = lowbit_gemv_launch(q, a->bits, uns, st, force_generic, a->d_workspace, a->workspace_bytes);
             if (rc != VSPEC_B200_OK) return rc;
         }
         return VSPEC_B200_OK;
     }
-    return lowbit_gemv_launch(p, a->bits, uns, st, force_generic);
+    return lowbit_gemv_launch(p, a->bits, uns, st, force_generic, a->d_workspace, a->workspace_bytes);
 }
 
 extern "C" int vspec_b200_lowbit_linear(const VspecB200LinearArgs* a, void* stream) {
@@ -124,6 +124,10 @@ extern "C" int vspec_b200_lowbit_linear(const VspecB200LinearArgs* a, void* stre
 
 extern "C" int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* a, void* stream) {
     return linear_common(a, stream, 1);
+}
+
+extern "C" size_t vspec_b200_lowbit_linear_workspace_bytes(size_t m, size_t n, size_t k, int flags) {
+    return gemv_workspace_bytes((int)m, (int)n, (int)k, (flags & VSPEC_B200_F_SWIGLU) != 0);
 }
 
 extern "C" int vspec_b200_unpack_codes(const uint8_t* d_w, size_t n, size_t k, int bits, int unsigned_codes,

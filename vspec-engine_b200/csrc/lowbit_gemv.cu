@@ -201,33 +201,42 @@ __device__ __forceinline__ void unpack_mm(const Chunk<BITS>& c, const int mm, ui
 // -------------------------------------------------------------------------
 // Shared-memory plan of the fast kernel.
 // -------------------------------------------------------------------------
-struct SmemPlan {
-    int lanes;        // lanes holding B columns per n-tile (8*min(8,2m)/2 ... = 4 * columns)
-    int nt;           // n8 tiles (2 columns per x row)
-    size_t frag_bytes, xs_bytes, red_bytes, total;
-};
+// Persistent split-K GEMV.
+//
+// Work unit = (16-row tile, 128-code k-block).  Units are numbered tile-major
+// and every warp of the (persistent) grid owns a contiguous run of them,
+// balanced to +-1 unit, so all SMs stream weights from the first to the last
+// cycle of the launch.  A warp keeps PIPE units of loads in flight across
+// tile boundaries.  When a warp finishes its part of a tile it publishes the
+// fp32 partial to scratch and bumps the tile's counter; the warp that brings
+// the counter to the tile's contributor count sums the partials in slot
+// (= k) order, applies the epilogue, writes y and resets the counter to zero,
+// so the next launch finds it clean.  No warp ever waits on another.
+// -------------------------------------------------------------------------
+constexpr int kGemvWarps = 8;
+constexpr int kGemvThreads = kGemvWarps * 32;
 
 __host__ __device__ __forceinline__ int gemv_nt(int m) { return (2 * m + 7) / 8; }
 __host__ __device__ __forceinline__ int gemv_lanes(int m) { return 4 * (2 * m < 8 ? 2 * m : 8); }
 
-static SmemPlan smem_plan(int m, int kb_total, int rt, int nwarps) {
-    SmemPlan p;
-    p.nt = gemv_nt(m);
-    p.lanes = gemv_lanes(m);
-    p.frag_bytes = (size_t)kb_total * 4 * p.nt * p.lanes * 16;
-    p.xs_bytes = (size_t)kb_total * m * sizeof(float);
-    p.red_bytes = (size_t)nwarps * rt * m * 16 * sizeof(float);
-    p.total = p.frag_bytes + p.xs_bytes + p.red_bytes + 2 * 16 * sizeof(float);
-    return p;
+static size_t gemv_smem_bytes(int m, int kbt) {
+    const int nt = gemv_nt(m);
+    return (size_t)kbt * 4 * nt * gemv_lanes(m) * 16   // B fragments
+           + (size_t)kbt * m * sizeof(float)             // per-(k-block,row) sums
+           + (size_t)kGemvWarps * 16 * sizeof(float)     // max-reduction area
+           + 32 * sizeof(float);                         // row scale + row norm
 }
 
-constexpr int kGemvWarps = 8;
-constexpr int kGemvThreads = kGemvWarps * 32;
+// warp that owns unit u when U units are split over W warps as
+// [floor(w*U/W), floor((w+1)*U/W))
+__device__ __forceinline__ int owner_of(long long u, long long U, long long W) {
+    return (int)(((u + 1) * W - 1) / U);
+}
 
-template <int BITS, int NT, int RT, bool UNSIGNED, int EPI>
+template <int BITS, int NT, bool UNSIGNED, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 2)
-lowbit_gemv_mma_kernel(const GemvParams p) {
-    constexpr int PIPE = (RT == 1) ? 4 : (NT == 1 ? 3 : 2);  // k-blocks in flight per warp
+lowbit_gemv_split_kernel(const GemvParams p) {
+    constexpr int PIPE = (NT == 1) ? 4 : 3;      // units in flight per warp
     constexpr int CHUNK_BYTES = 4 * BITS;        // 32 codes
     constexpr int KBLOCK_BYTES = 16 * BITS;      // 128 codes
 
@@ -237,162 +246,240 @@ lowbit_gemv_mma_kernel(const GemvParams p) {
     const int lanes = gemv_lanes(m);
     uint4* frag = reinterpret_cast<uint4*>(smem_raw);
     float* xs = reinterpret_cast<float*>(smem_raw + (size_t)kbt * 4 * NT * lanes * 16);
-    float* red = xs + (size_t)kbt * m;
-    float* row_scale = red + kGemvWarps * RT * m * 16;   // [16]: 2^-e per x row
-    float* row_norm = row_scale + 16;                      // [16]: RMSNorm inverse rms per row
+    float* maxbuf = xs + (size_t)kbt * m;          // [kGemvWarps][<=16]
+    float* row_scale = maxbuf + kGemvWarps * 16;   // [16]
+    float* row_norm = row_scale + 16;              // [16]
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int g = lane >> 2;
     const int c = lane & 3;
+    const long long U = (long long)p.tiles * kbt;
+    const long long W = p.total_warps;
+    const int gw = blockIdx.x * kGemvWarps + warp;
+    const bool active = gw < W;
+    const long long u0 = active ? ((long long)gw * U) / W : 0;
+    const long long u1 = active ? ((long long)(gw + 1) * U) / W : 0;
 
-    // Row bases of this CTA's tiles.
-    int tile_row0[RT];
-#pragma unroll
-    for (int tt = 0; tt < RT; ++tt) {
-        if (EPI == kEpiSwiGLU) tile_row0[tt] = blockIdx.x * 16 + tt * (p.n >> 1);
-        else tile_row0[tt] = (blockIdx.x * RT + tt) * 16;
-    }
+    // ---- weight stream: issue the first PIPE units before the prologue ----
+    Chunk<BITS> buf[PIPE][2];
+    float sz[PIPE][4];   // s(g), zp(g), s(g+8), zp(g+8)
 
-    // ---- issue the first weight loads before the activation prologue ----
-    Chunk<BITS> buf[PIPE][RT][2];
-    float sz[PIPE][RT][4];   // s(g), zp(g), s(g+8), zp(g+8)
-    const int my_kb = (kbt - warp + kGemvWarps - 1) / kGemvWarps;  // k-blocks of this warp
-
-    auto issue = [&](int stage_it, Chunk<BITS> (&b)[RT][2], float (&s)[RT][4]) {
-        const int kb = warp + stage_it * kGemvWarps;
+    auto issue = [&](long long u, Chunk<BITS> (&b)[2], float (&s)[4]) {
+        const int tile = (int)(u / kbt);
+        const int kb = (int)(u - (long long)tile * kbt);
         const int grp = kb / p.kb_per_group;
 #pragma unroll
-        for (int tt = 0; tt < RT; ++tt) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                int row = tile_row0[tt] + g + 8 * h;
-                row = row < p.n ? row : p.n - 1;
-                const uint8_t* src = p.w + (size_t)row * p.row_bytes + (size_t)kb * KBLOCK_BYTES + c * CHUNK_BYTES;
-                load_chunk<BITS>(b[tt][h], src);
-                const size_t sidx = (size_t)row * p.n_groups + grp;
-                float sv, zv;
-                if (p.flags & VSPEC_B200_F_SZ_F16) {
-                    sv = p.s ? __half2float(reinterpret_cast<const __half*>(p.s)[sidx]) : 1.0f;
-                    zv = p.zp ? __half2float(reinterpret_cast<const __half*>(p.zp)[sidx]) : p.zp_const;
-                } else {
-                    sv = p.s ? reinterpret_cast<const float*>(p.s)[sidx] : 1.0f;
-                    zv = p.zp ? reinterpret_cast<const float*>(p.zp)[sidx] : p.zp_const;
-                }
-                s[tt][2 * h] = sv;
-                s[tt][2 * h + 1] = zv;
+        for (int h = 0; h < 2; ++h) {
+            int row = tile * 16 + g + 8 * h;
+            row = row < p.n ? row : p.n - 1;
+            load_chunk<BITS>(b[h], p.w + (size_t)row * p.row_bytes + (size_t)kb * KBLOCK_BYTES + c * CHUNK_BYTES);
+            const size_t sidx = (size_t)row * p.n_groups + grp;
+            float sv, zv;
+            if (p.flags & VSPEC_B200_F_SZ_F16) {
+                sv = p.s ? __half2float(reinterpret_cast<const __half*>(p.s)[sidx]) : 1.0f;
+                zv = p.zp ? __half2float(reinterpret_cast<const __half*>(p.zp)[sidx]) : p.zp_const;
+            } else {
+                sv = p.s ? reinterpret_cast<const float*>(p.s)[sidx] : 1.0f;
+                zv = p.zp ? reinterpret_cast<const float*>(p.zp)[sidx] : p.zp_const;
             }
+            s[2 * h] = sv;
+            s[2 * h + 1] = zv;
         }
     };
-
 #pragma unroll
     for (int st = 0; st < PIPE; ++st)
-        if (st < my_kb) issue(st, buf[st], sz[st]);
+        if (u0 + st < u1) issue(u0 + st, buf[st], sz[st]);
 
-    // ---- activation prologue ----
+    // ---- activation prologue (once per CTA) ----
     const int K = p.k;
-    // (1) RMSNorm inverse rms per row (optional).
-    if (EPI_HAS_RMSNORM(p.flags)) {
+    const bool rms = EPI_HAS_RMSNORM(p.flags);
+    if (rms) {
         for (int r = warp; r < m; r += kGemvWarps) {
-            const float* xr = p.x + (size_t)r * K;
+            const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)r * K);
             float ss = 0.f;
-            for (int t = lane; t < K; t += 32) { float v = xr[t]; ss += v * v; }
+            for (int t = lane; t < K / 4; t += 32) {
+                const float4 v = xr[t];
+                ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+            }
             ss = warp_sum(ss);
             if (lane == 0) row_norm[r] = 1.0f / sqrtf(ss / (float)K + p.eps);
         }
         __syncthreads();
     }
-    // (2) per (k-block, row) sums and per-row max |x|.
+    auto xval4 = [&](int r, int t) -> float4 {   // x (or RMSNorm(x)) at t..t+3 of row r
+        float4 v = *reinterpret_cast<const float4*>(p.x + (size_t)r * K + t);
+        if (rms) {
+            const float nr = row_norm[r];
+            const float4 wn = *reinterpret_cast<const float4*>(p.norm_w + t);
+            v.x = v.x * nr * wn.x; v.y = v.y * nr * wn.y; v.z = v.z * nr * wn.z; v.w = v.w * nr * wn.w;
+        }
+        return v;
+    };
+    // (a) per-(k-block, row) sums and per-row max |x|
     {
-        float* maxbuf = red;  // reuse the reduction area: [kGemvWarps][m]
-        for (int r = 0; r < m; ++r) {
-            const float* xr = p.x + (size_t)r * K;
-            const float nr = EPI_HAS_RMSNORM(p.flags) ? row_norm[r] : 1.0f;
-            float mx = 0.f;
-            for (int kb = warp; kb < kbt; kb += kGemvWarps) {
-                const int t = kb * 128 + lane * 4;
-                float4 v = *reinterpret_cast<const float4*>(xr + t);
-                if (EPI_HAS_RMSNORM(p.flags)) {
-                    float4 wn = *reinterpret_cast<const float4*>(p.norm_w + t);
-                    v.x = v.x * nr * wn.x; v.y = v.y * nr * wn.y; v.z = v.z * nr * wn.z; v.w = v.w * nr * wn.w;
-                }
-                float sum = (v.x + v.y) + (v.z + v.w);
-                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-                sum = warp_sum(sum);
-                if (lane == 0) xs[kb * m + r] = sum;
+        float mx[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) mx[r] = 0.f;
+        for (int pr = warp; pr < kbt * m; pr += kGemvWarps) {
+            const int r = pr % m, kb = pr / m;
+            const float4 v = xval4(r, kb * 128 + lane * 4);
+            const float sum = warp_sum((v.x + v.y) + (v.z + v.w));
+            const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr)
+                if (rr == r) mx[rr] = fmaxf(mx[rr], a);
+            if (lane == 0) xs[kb * m + r] = sum;
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            if (r < m) {
+                const float v = warp_max(mx[r]);
+                if (lane == 0) maxbuf[warp * 16 + r] = v;
             }
-            mx = warp_max(mx);
-            if (lane == 0) maxbuf[warp * m + r] = mx;
         }
         __syncthreads();
         if (tid < m) {
-            float mx = 0.f;
-            for (int w = 0; w < kGemvWarps; ++w) mx = fmaxf(mx, maxbuf[w * m + tid]);
-            // Exact power-of-two rescale so that max|x| lands in [2^13, 2^14):
-            // fp16 hi never overflows and lo keeps full precision.
+            float v = 0.f;
+            for (int w = 0; w < kGemvWarps; ++w) v = fmaxf(v, maxbuf[w * 16 + tid]);
+            // exact power-of-two rescale: max |x| lands in [2^13, 2^14), so the
+            // fp16 hi part never overflows and the lo part stays normal
             int ex = 0;
-            if (mx > 0.f && isfinite(mx)) { (void)frexpf(mx, &ex); ex -= 14; }
+            if (v > 0.f && isfinite(v)) { (void)frexpf(v, &ex); ex -= 14; }
             row_scale[tid] = ldexpf(1.0f, -ex);
         }
         __syncthreads();
-        for (int i = tid; i < kbt * m; i += kGemvThreads) xs[i] *= row_scale[i % m];
     }
-    // (3) B fragments in fragment order: slot (kb, mp, nt, lane) = 16 bytes.
+    // (b) B fragments: for every (row, k-block, mp, c') the 4 fp16 pairs of MMA
+    // slot (kb, mp, lane) as hi and lo parts, in fragment order.
     {
-        const int slots = kbt * 4 * NT * lanes;
-        for (int z = tid; z < slots; z += kGemvThreads) {
-            const int ln = z % lanes;
-            const int nt = (z / lanes) % NT;
-            const int mp = (z / (lanes * NT)) & 3;
-            const int kb = z / (lanes * NT * 4);
-            const int gc = ln >> 2, cc = ln & 3;
-            const int col = 8 * nt + gc;
-            const int r = col >> 1;
-            uint32_t out[4] = {0u, 0u, 0u, 0u};
+        const int rows_pad = 4 * NT;
+        const int items = rows_pad * kbt * 16;
+        for (int it = tid; it < items; it += kGemvThreads) {
+            const int cc = it & 3;
+            const int mp = (it >> 2) & 3;
+            const int kb = (it >> 4) % kbt;
+            const int r = (it >> 4) / kbt;
+            uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = hi;
             if (r < m) {
-                const float* xr = p.x + (size_t)r * K;
-                const float nr = EPI_HAS_RMSNORM(p.flags) ? row_norm[r] : 1.0f;
+                // pair qq of this slot holds codes (lo_code(4mp)+qq, hi_code(4mp)+qq)
+                const int t = kb * 128 + 32 * cc;
                 const float sc = row_scale[r];
-                const int base = kb * 128 + 32 * cc;
+                const float4 a = xval4(r, t + lo_code<BITS>(4 * mp)), b = xval4(r, t + hi_code<BITS>(4 * mp));
+                const float va[4] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc};
+                const float vb[4] = {b.x * sc, b.y * sc, b.z * sc, b.w * sc};
+                uint32_t wh[4], wl[4];
 #pragma unroll
                 for (int qq = 0; qq < 4; ++qq) {
-                    const int q = 4 * mp + qq;
-                    const int t0 = base + lo_code<BITS>(q);
-                    const int t1 = base + hi_code<BITS>(q);
-                    float v0 = xr[t0], v1 = xr[t1];
-                    if (EPI_HAS_RMSNORM(p.flags)) { v0 = v0 * nr * p.norm_w[t0]; v1 = v1 * nr * p.norm_w[t1]; }
-                    v0 *= sc; v1 *= sc;
-                    __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-                    if (col & 1) {  // lo part: residual after the hi part
-                        h0 = __float2half_rn(v0 - __half2float(h0));
-                        h1 = __float2half_rn(v1 - __half2float(h1));
-                    }
-                    out[qq] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+                    const __half h0 = __float2half_rn(va[qq]), h1 = __float2half_rn(vb[qq]);
+                    const __half l0 = __float2half_rn(va[qq] - __half2float(h0));
+                    const __half l1 = __float2half_rn(vb[qq] - __half2float(h1));
+                    wh[qq] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+                    wl[qq] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
                 }
+                hi = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+                lo = make_uint4(wl[0], wl[1], wl[2], wl[3]);
             }
-            frag[z] = make_uint4(out[0], out[1], out[2], out[3]);
+            {
+                // columns 2r (hi) and 2r+1 (lo) of n-tile (2r)/8
+                const int col = 2 * r;
+                const int nt = col >> 3;
+                const int gh = col & 7;
+                const size_t base = ((size_t)(kb * 4 + mp) * NT + nt) * lanes;
+                if (4 * gh + cc < lanes) frag[base + 4 * gh + cc] = hi;
+                if (4 * (gh + 1) + cc < lanes) frag[base + 4 * (gh + 1) + cc] = lo;
+            }
         }
+        for (int i = tid; i < kbt * m; i += kGemvThreads) xs[i] *= row_scale[i % m];
     }
     __syncthreads();
+    if (!active) return;
 
-    // ---- main loop ----
-    float acc[RT][NT][2];
-#pragma unroll
-    for (int tt = 0; tt < RT; ++tt)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[tt][nt][0] = acc[tt][nt][1] = 0.f;
-
+    // ---- main stream ----
     const bool lane_has_b = lane < lanes;
     const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
+    int cur_tile = (int)(u0 / kbt);
+    const int half_tiles = p.tiles >> 1;
 
-    for (int base_it = 0; base_it < my_kb; base_it += PIPE) {
+    auto flush = [&](int tile) {
+        // contributors of this physical tile and this warp's slot
+        const int fw = owner_of((long long)tile * kbt, U, W);
+        const int lw = owner_of((long long)(tile + 1) * kbt - 1, U, W);
+        int L = tile, slot = gw - fw, total = lw - fw + 1, n_gate = total;
+        if (EPI == kEpiSwiGLU) {
+            const bool up = tile >= half_tiles;
+            L = up ? tile - half_tiles : tile;
+            const int gt = L, ut = L + half_tiles;
+            const int g_fw = owner_of((long long)gt * kbt, U, W);
+            const int g_n = owner_of((long long)(gt + 1) * kbt - 1, U, W) - g_fw + 1;
+            const int u_fw = owner_of((long long)ut * kbt, U, W);
+            const int u_n = owner_of((long long)(ut + 1) * kbt - 1, U, W) - u_fw + 1;
+            n_gate = g_n;
+            total = g_n + u_n;
+            slot = up ? g_n + (gw - u_fw) : (gw - g_fw);
+        }
+        float* part = p.scratch + ((size_t)L * p.max_slots + slot) * (16 * m);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int r = 4 * nt + c;
+            if (r < m) {
+                part[r * 16 + g] = acc[nt][0];
+                part[r * 16 + g + 8] = acc[nt][1];
+            }
+        }
+        __threadfence();
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(p.counters + L, 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == total - 1) {
+            __threadfence();
+            const float* base = p.scratch + (size_t)L * p.max_slots * (16 * m);
+            for (int z = lane; z < 16 * m; z += 32) {
+                const int r = z >> 4, i = z & 15;
+                const float inv = 1.0f / row_scale[r];
+                if (EPI == kEpiSwiGLU) {
+                    float gs = 0.f, us = 0.f;
+                    for (int s = 0; s < n_gate; ++s) gs += __ldcg(base + (size_t)s * 16 * m + z);
+                    for (int s = n_gate; s < total; ++s) us += __ldcg(base + (size_t)s * 16 * m + z);
+                    gs *= inv;
+                    us *= inv;
+                    const int orow = L * 16 + i;
+                    if (orow < (p.n >> 1)) p.y[(size_t)r * (p.n >> 1) + orow] = gs / (1.0f + expf(-gs)) * us;
+                } else {
+                    float sum = 0.f;
+                    for (int s = 0; s < total; ++s) sum += __ldcg(base + (size_t)s * 16 * m + z);
+                    sum *= inv;
+                    const int orow = L * 16 + i;
+                    if (orow < p.n) {
+                        const size_t o = (size_t)r * p.n + orow;
+                        if (p.flags & VSPEC_B200_F_RESIDUAL) sum += p.residual[o];
+                        p.y[o] = sum;
+                    }
+                }
+            }
+            if (lane == 0) p.counters[L] = 0;
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
+    };
+
+    for (long long base_u = u0; base_u < u1; base_u += PIPE) {
 #pragma unroll
         for (int st = 0; st < PIPE; ++st) {
-            const int it = base_it + st;
-            if (it < my_kb) {
-                const int kb = warp + it * kGemvWarps;
-                float d[RT][NT][4];
+            const long long u = base_u + st;
+            if (u < u1) {
+                const int tile = (int)(u / kbt);
+                const int kb = (int)(u - (long long)tile * kbt);
+                if (tile != cur_tile) {
+                    flush(cur_tile);
+                    cur_tile = tile;
+                }
+                float d[NT][4];
                 const uint4* fb = frag + (size_t)kb * 4 * NT * lanes;
 #pragma unroll
                 for (int mp = 0; mp < 4; ++mp) {
@@ -405,91 +492,34 @@ lowbit_gemv_mma_kernel(const GemvParams p) {
 #pragma unroll
                     for (int half = 0; half < 2; ++half) {
                         const int mm = 2 * mp + half;
+                        // A fragment: rows g / g+8, k-slots {2c,2c+1} and {2c+8,2c+9}
+                        uint32_t a[4];
+                        unpack_mm<BITS, UNSIGNED>(buf[st][0], mm, a[0], a[2]);
+                        unpack_mm<BITS, UNSIGNED>(buf[st][1], mm, a[1], a[3]);
 #pragma unroll
-                        for (int tt = 0; tt < RT; ++tt) {
-                            // A fragment: rows g / g+8, k-slots {2c,2c+1} and {2c+8,2c+9}
-                            uint32_t a[4];
-                            unpack_mm<BITS, UNSIGNED>(buf[st][tt][0], mm, a[0], a[2]);
-                            unpack_mm<BITS, UNSIGNED>(buf[st][tt][1], mm, a[1], a[3]);
-#pragma unroll
-                            for (int nt = 0; nt < NT; ++nt) {
-                                const uint32_t b0 = half ? bb[nt].z : bb[nt].x;
-                                const uint32_t b1 = half ? bb[nt].w : bb[nt].y;
-                                mma_16816_f16(d[tt][nt], a, b0, b1, mm == 0 ? zero4 : d[tt][nt]);
-                            }
+                        for (int nt = 0; nt < NT; ++nt) {
+                            const uint32_t b0 = half ? bb[nt].z : bb[nt].x;
+                            const uint32_t b1 = half ? bb[nt].w : bb[nt].y;
+                            mma_16816_f16(d[nt], a, b0, b1, mm == 0 ? zero4 : d[nt]);
                         }
                     }
                 }
-                float szc[RT][4];
-#pragma unroll
-                for (int tt = 0; tt < RT; ++tt)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) szc[tt][i] = sz[st][tt][i];
-                // refill this stage: the loads land while the next stages compute
-                if (it + PIPE < my_kb) issue(it + PIPE, buf[st], sz[st]);
-                // per-k-block scale / zero-point epilogue
+                const float s0 = sz[st][0], z0 = sz[st][1], s1 = sz[st][2], z1 = sz[st][3];
+                // refill this stage while the tensor cores drain
+                if (u + PIPE < u1) issue(u + PIPE, buf[st], sz[st]);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const int r = 4 * nt + c;
                     if (r < m) {
                         const float xsum = xs[kb * m + r];
-#pragma unroll
-                        for (int tt = 0; tt < RT; ++tt) {
-                            acc[tt][nt][0] = fmaf(szc[tt][0], (d[tt][nt][0] + d[tt][nt][1]) - szc[tt][1] * xsum, acc[tt][nt][0]);
-                            acc[tt][nt][1] = fmaf(szc[tt][2], (d[tt][nt][2] + d[tt][nt][3]) - szc[tt][3] * xsum, acc[tt][nt][1]);
-                        }
+                        acc[nt][0] = fmaf(s0, (d[nt][0] + d[nt][1]) - z0 * xsum, acc[nt][0]);
+                        acc[nt][1] = fmaf(s1, (d[nt][2] + d[nt][3]) - z1 * xsum, acc[nt][1]);
                     }
                 }
             }
         }
     }
-
-    // ---- cross-warp reduction (fixed order) and epilogue ----
-    __syncthreads();  // xs/frag no longer needed; red may overlap nothing else
-#pragma unroll
-    for (int tt = 0; tt < RT; ++tt)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int r = 4 * nt + c;
-            if (r < m) {
-                red[((warp * RT + tt) * m + r) * 16 + g] = acc[tt][nt][0];
-                red[((warp * RT + tt) * m + r) * 16 + g + 8] = acc[tt][nt][1];
-            }
-        }
-    __syncthreads();
-    if (EPI == kEpiSwiGLU) {
-        // rows [0, n/2) gate, [n/2, n) up; output row blockIdx.x*16 + i
-        for (int z = tid; z < m * 16; z += kGemvThreads) {
-            const int r = z >> 4, i = z & 15;
-            const int orow = blockIdx.x * 16 + i;
-            if (orow < (p.n >> 1)) {
-                float gsum = 0.f, usum = 0.f;
-                for (int w = 0; w < kGemvWarps; ++w) {
-                    gsum += red[((w * RT + 0) * m + r) * 16 + i];
-                    usum += red[((w * RT + 1) * m + r) * 16 + i];
-                }
-                const float inv = 1.0f / row_scale[r];
-                gsum *= inv; usum *= inv;
-                const float silu = gsum / (1.0f + expf(-gsum));
-                p.y[(size_t)r * (p.n >> 1) + orow] = silu * usum;
-            }
-        }
-    } else {
-        for (int z = tid; z < RT * m * 16; z += kGemvThreads) {
-            const int tt = z / (m * 16);
-            const int r = (z >> 4) % m;
-            const int i = z & 15;
-            const int orow = tile_row0[tt] + i;
-            if (orow < p.n) {
-                float sum = 0.f;
-                for (int w = 0; w < kGemvWarps; ++w) sum += red[((w * RT + tt) * m + r) * 16 + i];
-                sum *= 1.0f / row_scale[r];
-                const size_t o = (size_t)r * p.n + orow;
-                if (p.flags & VSPEC_B200_F_RESIDUAL) sum += p.residual[o];
-                p.y[o] = sum;
-            }
-        }
-    }
+    if (u1 > u0) flush(cur_tile);
 }
 
 // -------------------------------------------------------------------------
@@ -588,6 +618,9 @@ __global__ void unpack_codes_generic_kernel(const uint8_t* w, int n, int k, int 
 // -------------------------------------------------------------------------
 // Host-side dispatch
 // -------------------------------------------------------------------------
+// -------------------------------------------------------------------------
+// Host-side dispatch
+// -------------------------------------------------------------------------
 static bool fast_path_ok(const GemvParams& p, int bits) {
     if (p.m < 1 || p.m > kGemvMaxM) return false;
     if (p.k % 128 != 0) return false;
@@ -600,42 +633,100 @@ static bool fast_path_ok(const GemvParams& p, int bits) {
     if (a % need != 0) return false;
     if (reinterpret_cast<uintptr_t>(p.x) % 16 != 0) return false;
     if ((p.flags & VSPEC_B200_F_RMSNORM) && reinterpret_cast<uintptr_t>(p.norm_w) % 16 != 0) return false;
+    if (gemv_smem_bytes(p.m, p.k / 128) > kGemvMaxSmem) return false;
     return true;
 }
 
-template <int BITS, int NT, int RT, bool UNS, int EPI>
-static cudaError_t launch_fast_t(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
-    auto kern = lowbit_gemv_mma_kernel<BITS, NT, RT, UNS, EPI>;
-    static thread_local int configured_dev = -1;
-    static thread_local size_t configured_smem = 0;
+// Warps of the persistent grid and partial slots per tile for a launch.
+struct SplitPlan {
+    int tiles;          // physical 16-row tiles
+    int logical_tiles;  // tiles owning a counter (SwiGLU pairs gate+up tiles)
+    long long units;
+    int total_warps;
+    int max_slots;
+    int grid;
+    size_t scratch_floats;
+};
+
+static SplitPlan split_plan(int m, int n, int k, bool swiglu) {
+    SplitPlan sp;
+    sp.tiles = (n + 15) / 16;
+    sp.logical_tiles = swiglu ? sp.tiles / 2 : sp.tiles;
+    const int kbt = k / 128;
+    sp.units = (long long)sp.tiles * kbt;
+    const long long target = (long long)device_sm_count() * 2 * kGemvWarps;
+    sp.total_warps = (int)(sp.units < target ? sp.units : target);
+    const long long per = sp.units / sp.total_warps;  // >= 1
+    int per_tile = (int)((kbt + per - 1) / per) + 1;  // contributors of one physical tile
+    if (per_tile > sp.total_warps) per_tile = sp.total_warps;
+    sp.max_slots = swiglu ? 2 * per_tile : per_tile;
+    sp.grid = (sp.total_warps + kGemvWarps - 1) / kGemvWarps;
+    sp.scratch_floats = (size_t)sp.logical_tiles * sp.max_slots * 16 * m;
+    return sp;
+}
+
+size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu) {
+    if (m < 1 || n < 1 || k < 128) return 0;
+    SplitPlan sp = split_plan(m > kGemvMaxM ? kGemvMaxM : m, n, k, swiglu);
+    const size_t counters = ((size_t)sp.logical_tiles * sizeof(int) + 255) / 256 * 256;
+    return counters + sp.scratch_floats * sizeof(float);
+}
+
+// Library-managed workspace: one grow-only, zero-initialized buffer per device.
+struct GemvWs {
+    void* ptr;
+    size_t cap;
+};
+static GemvWs g_gemv_ws[64];
+
+static void* gemv_managed_ws(size_t bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    GemvWs& w = g_gemv_ws[dev];
+    if (w.cap < bytes) {
+        if (w.ptr) {
+            cudaDeviceSynchronize();
+            cudaFree(w.ptr);
+        }
+        w.ptr = nullptr;
+        w.cap = 0;
+        size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+        if (cudaMalloc(&w.ptr, want) != cudaSuccess) { w.ptr = nullptr; return nullptr; }
+        if (cudaMemset(w.ptr, 0, want) != cudaSuccess) { cudaFree(w.ptr); w.ptr = nullptr; return nullptr; }
+        if (cudaDeviceSynchronize() != cudaSuccess) { cudaFree(w.ptr); w.ptr = nullptr; return nullptr; }
+        w.cap = want;
+    }
+    return w.ptr;
+}
+
+template <int BITS, int NT, bool UNS, int EPI>
+static cudaError_t launch_split_t(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+    auto kern = lowbit_gemv_split_kernel<BITS, NT, UNS, EPI>;
+    static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (configured_dev != dev || configured_smem < smem) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (dev >= 0 && dev < 64 && (size_t)configured[dev] < smem) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem);
         if (e != cudaSuccess) return e;
-        configured_dev = dev;
-        configured_smem = smem;
+        configured[dev] = (int)kGemvMaxSmem;
     }
     kern<<<grid, kGemvThreads, smem, st>>>(p);
     return cudaGetLastError();
 }
 
-template <int BITS, int NT, bool UNS>
-static cudaError_t launch_fast_nt(const GemvParams& p, int epi, int grid, int rt, size_t smem, cudaStream_t st) {
-    if (epi == kEpiSwiGLU) return launch_fast_t<BITS, NT, 2, UNS, kEpiSwiGLU>(p, grid, smem, st);
-    if (rt == 2) return launch_fast_t<BITS, NT, 2, UNS, kEpiPlain>(p, grid, smem, st);
-    return launch_fast_t<BITS, NT, 1, UNS, kEpiPlain>(p, grid, smem, st);
-}
-
 template <int BITS, bool UNS>
-static cudaError_t launch_fast_bits(const GemvParams& p, int epi, int grid, int rt, size_t smem, cudaStream_t st) {
-    switch (gemv_nt(p.m)) {
-        case 1: return launch_fast_nt<BITS, 1, UNS>(p, epi, grid, rt, smem, st);
-        default: return launch_fast_nt<BITS, 2, UNS>(p, epi, grid, rt, smem, st);
+static cudaError_t launch_split_bits(const GemvParams& p, int epi, int grid, size_t smem, cudaStream_t st) {
+    const int nt = gemv_nt(p.m);
+    if (epi == kEpiSwiGLU) {
+        return nt == 1 ? launch_split_t<BITS, 1, UNS, kEpiSwiGLU>(p, grid, smem, st)
+                       : launch_split_t<BITS, 2, UNS, kEpiSwiGLU>(p, grid, smem, st);
     }
+    return nt == 1 ? launch_split_t<BITS, 1, UNS, kEpiPlain>(p, grid, smem, st)
+                   : launch_split_t<BITS, 2, UNS, kEpiPlain>(p, grid, smem, st);
 }
 
-int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int force_generic) {
+int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int force_generic,
+                       void* workspace, size_t workspace_bytes) {
     if (bits < 2 || bits > 4) { set_error("bits must be 2, 3 or 4 (got %d)", bits); return VSPEC_B200_ERR_ARG; }
     const bool swiglu = (p.flags & VSPEC_B200_F_SWIGLU) != 0;
     if (swiglu && (p.n % 2 != 0)) { set_error("SwiGLU needs an even row count (n=%d)", p.n); return VSPEC_B200_ERR_ARG; }
@@ -645,28 +736,38 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
 
     const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
     if (fast) {
-        const int half_rows = swiglu ? p.n / 2 : p.n;
-        const int tiles = (half_rows + 15) / 16;
-        int rt = 1;
-        if (swiglu) rt = 2;
-        else if (tiles >= 4 * device_sm_count() && tiles % 2 == 0) rt = 2;
-        const int grid = swiglu ? tiles : tiles / rt;
-        SmemPlan plan = smem_plan(p.m, p.kb_total, rt, kGemvWarps);
-        if (plan.total <= kGemvMaxSmem) {
-            cudaError_t e;
-            const int epi = swiglu ? kEpiSwiGLU : kEpiPlain;
-            if (unsigned_codes) {
-                if (bits == 4) e = launch_fast_bits<4, true>(p, epi, grid, rt, plan.total, st);
-                else if (bits == 3) e = launch_fast_bits<3, true>(p, epi, grid, rt, plan.total, st);
-                else e = launch_fast_bits<2, true>(p, epi, grid, rt, plan.total, st);
-            } else {
-                if (bits == 4) e = launch_fast_bits<4, false>(p, epi, grid, rt, plan.total, st);
-                else if (bits == 3) e = launch_fast_bits<3, false>(p, epi, grid, rt, plan.total, st);
-                else e = launch_fast_bits<2, false>(p, epi, grid, rt, plan.total, st);
+        SplitPlan sp = split_plan(p.m, p.n, p.k, swiglu);
+        const size_t need = gemv_workspace_bytes(p.m, p.n, p.k, swiglu);
+        void* ws = workspace;
+        if (ws) {
+            if (workspace_bytes < need) {
+                set_error("GEMV workspace too small (%zu < %zu)", workspace_bytes, need);
+                return VSPEC_B200_ERR_ARG;
             }
-            if (e != cudaSuccess) return cuda_status(e, "lowbit_gemv_mma_kernel launch");
-            return VSPEC_B200_OK;
+        } else {
+            ws = gemv_managed_ws(need);
+            if (!ws) { set_error("cannot allocate %zu bytes of GEMV workspace", need); return VSPEC_B200_ERR_NOMEM; }
         }
+        const size_t counters = ((size_t)sp.logical_tiles * sizeof(int) + 255) / 256 * 256;
+        p.counters = reinterpret_cast<int*>(ws);
+        p.scratch = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + counters);
+        p.tiles = sp.tiles;
+        p.total_warps = sp.total_warps;
+        p.max_slots = sp.max_slots;
+        const size_t smem = gemv_smem_bytes(p.m, p.kb_total);
+        const int epi = swiglu ? kEpiSwiGLU : kEpiPlain;
+        cudaError_t e;
+        if (unsigned_codes) {
+            if (bits == 4) e = launch_split_bits<4, true>(p, epi, sp.grid, smem, st);
+            else if (bits == 3) e = launch_split_bits<3, true>(p, epi, sp.grid, smem, st);
+            else e = launch_split_bits<2, true>(p, epi, sp.grid, smem, st);
+        } else {
+            if (bits == 4) e = launch_split_bits<4, false>(p, epi, sp.grid, smem, st);
+            else if (bits == 3) e = launch_split_bits<3, false>(p, epi, sp.grid, smem, st);
+            else e = launch_split_bits<2, false>(p, epi, sp.grid, smem, st);
+        }
+        if (e != cudaSuccess) return cuda_status(e, "lowbit_gemv_split_kernel launch");
+        return VSPEC_B200_OK;
     }
     // generic path
     if (swiglu) {

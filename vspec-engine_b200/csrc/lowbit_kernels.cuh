@@ -22,6 +22,12 @@ struct GemvParams {
     int kb_total;            // k / 128 (fast path)
     int kb_per_group;        // (k / n_groups) / 128 (fast path)
     int flags;
+    // persistent split-K plan (fast path)
+    int tiles;               // 16-row tiles
+    int total_warps;         // warps sharing the (tile, k-block) units
+    int max_slots;           // partial slots per counter
+    float* scratch;          // [counters][max_slots][16*m] fp32 partials
+    int* counters;           // [counters], zero between launches
 };
 
 constexpr int kEpiPlain = 0;
@@ -31,7 +37,9 @@ constexpr size_t kGemvMaxSmem = 200 * 1024;
 
 #define EPI_HAS_RMSNORM(flags) (((flags) & VSPEC_B200_F_RMSNORM) != 0)
 
-int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int force_generic);
+int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int force_generic,
+                       void* workspace, size_t workspace_bytes);
+size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu);
 int unpack_codes_launch(const uint8_t* w, int n, int k, int bits, int unsigned_codes, int8_t* out, cudaStream_t st,
                         int use_fast_decoder);
 

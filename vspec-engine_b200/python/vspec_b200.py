@@ -46,7 +46,7 @@ class LinearArgs(ctypes.Structure):
         ("d_x", c_void_p), ("d_w", c_void_p), ("d_scales", c_void_p), ("d_zero_points", c_void_p),
         ("zero_point_const", c_float), ("d_y", c_void_p), ("d_residual", c_void_p), ("d_norm_weight", c_void_p),
         ("norm_eps", c_float), ("m", c_size_t), ("n", c_size_t), ("k", c_size_t), ("n_groups", c_size_t),
-        ("bits", c_int), ("flags", c_int),
+        ("bits", c_int), ("flags", c_int), ("d_workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -96,6 +96,7 @@ _sigs = {
     "vspec_b200_version": ([], ctypes.c_char_p),
     "vspec_b200_lowbit_linear": ([POINTER(LinearArgs), c_void_p], c_int),
     "vspec_b200_lowbit_linear_generic": ([POINTER(LinearArgs), c_void_p], c_int),
+    "vspec_b200_lowbit_linear_workspace_bytes": ([c_size_t, c_size_t, c_size_t, c_int], c_size_t),
     "vspec_b200_unpack_codes": ([c_void_p, c_size_t, c_size_t, c_int, c_int, c_void_p, c_int, c_void_p], c_int),
     "vspec_b200_device_info": ([POINTER(c_int), POINTER(c_int), POINTER(c_int), POINTER(c_size_t)], c_int),
     "vspec_b200_dequant_f32": ([c_void_p, c_void_p, c_void_p, c_float, c_int, c_int, c_size_t, c_size_t, c_size_t,
@@ -187,8 +188,10 @@ def hptr(a: np.ndarray | None) -> int | None:
 
 def lowbit_linear(x: int, w: int, scales: int | None, zp: int | None, y: int, m: int, n: int, k: int, n_groups: int,
                   bits: int, flags: int = 0, zp_const: float = 0.0, residual: int | None = None,
-                  norm_weight: int | None = None, eps: float = 1e-6, stream: int = 0, generic: bool = False) -> None:
-    a = LinearArgs(x, w, scales, zp, zp_const, y, residual, norm_weight, eps, m, n, k, n_groups, bits, flags)
+                  norm_weight: int | None = None, eps: float = 1e-6, stream: int = 0, generic: bool = False,
+                  workspace: int | None = None, workspace_bytes: int = 0) -> None:
+    a = LinearArgs(x, w, scales, zp, zp_const, y, residual, norm_weight, eps, m, n, k, n_groups, bits, flags,
+                   workspace, workspace_bytes)
     fn = lib.vspec_b200_lowbit_linear_generic if generic else lib.vspec_b200_lowbit_linear
     check(fn(ctypes.byref(a), stream), "vspec_b200_lowbit_linear")
 
