@@ -78,11 +78,12 @@ typedef struct VspecB200LinearArgs {
     size_t workspace_bytes;
 } VspecB200LinearArgs;
 
-/* Device scratch of the split-K merge (per-tile counters + fp32 partials).
- * Calls sharing one workspace must be stream-ordered.  The library-managed
- * workspace is allocated on the first call per device and grown when a larger
- * shape arrives, so the first call of each shape must precede any stream
- * capture. */
+/* Device scratch of the split-K merge: a fixed 64 KiB region of per-tile
+ * counters (zero between launches) followed by fp32 partials.  Calls sharing
+ * one workspace must be stream-ordered; any sequence of shapes may share it.
+ * The library-managed workspace (d_workspace == NULL) is allocated per device
+ * and host thread on first use and grown when a larger shape arrives, so the
+ * first call of each shape must precede any stream capture. */
 size_t vspec_b200_lowbit_linear_workspace_bytes(size_t m, size_t n, size_t k, int flags);
 int vspec_b200_lowbit_linear(const VspecB200LinearArgs* args, void* stream);
 

@@ -16,7 +16,7 @@ struct Scratch {
     void* ptr;
     size_t cap;
 };
-static Scratch g_attn_scratch[64];
+static thread_local Scratch g_attn_scratch[64];
 
 static void* attn_scratch(size_t bytes) {
     int dev = 0;

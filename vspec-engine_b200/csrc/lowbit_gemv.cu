@@ -634,6 +634,7 @@ static bool fast_path_ok(const GemvParams& p, int bits) {
     if (reinterpret_cast<uintptr_t>(p.x) % 16 != 0) return false;
     if ((p.flags & VSPEC_B200_F_RMSNORM) && reinterpret_cast<uintptr_t>(p.norm_w) % 16 != 0) return false;
     if (gemv_smem_bytes(p.m, p.k / 128) > kGemvMaxSmem) return false;
+    if ((size_t)(p.n + 15) / 16 > 16384) return false;   // counter region of the workspace
     return true;
 }
 
@@ -665,19 +666,26 @@ static SplitPlan split_plan(int m, int n, int k, bool swiglu) {
     return sp;
 }
 
+// Workspace layout: a fixed region of kGemvCounterSlots int counters (zero
+// between launches: every merge resets the counter it used) followed by the
+// fp32 partials.  The counter region does not depend on the shape, so one
+// workspace serves any sequence of stream-ordered launches of any shape.
+constexpr size_t kGemvCounterSlots = 16384;
+constexpr size_t kGemvCounterBytes = kGemvCounterSlots * sizeof(int);
+
 size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu) {
     if (m < 1 || n < 1 || k < 128) return 0;
     SplitPlan sp = split_plan(m > kGemvMaxM ? kGemvMaxM : m, n, k, swiglu);
-    const size_t counters = ((size_t)sp.logical_tiles * sizeof(int) + 255) / 256 * 256;
-    return counters + sp.scratch_floats * sizeof(float);
+    return kGemvCounterBytes + sp.scratch_floats * sizeof(float);
 }
 
-// Library-managed workspace: one grow-only, zero-initialized buffer per device.
+// Library-managed workspace: one grow-only, zero-initialized buffer per device
+// and host thread (each host thread is expected to use one stream).
 struct GemvWs {
     void* ptr;
     size_t cap;
 };
-static GemvWs g_gemv_ws[64];
+static thread_local GemvWs g_gemv_ws[64];
 
 static void* gemv_managed_ws(size_t bytes) {
     int dev = 0;
@@ -748,9 +756,8 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
             ws = gemv_managed_ws(need);
             if (!ws) { set_error("cannot allocate %zu bytes of GEMV workspace", need); return VSPEC_B200_ERR_NOMEM; }
         }
-        const size_t counters = ((size_t)sp.logical_tiles * sizeof(int) + 255) / 256 * 256;
         p.counters = reinterpret_cast<int*>(ws);
-        p.scratch = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + counters);
+        p.scratch = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kGemvCounterBytes);
         p.tiles = sp.tiles;
         p.total_warps = sp.total_warps;
         p.max_slots = sp.max_slots;
