@@ -263,18 +263,21 @@ lowbit_gemv_split_kernel(const GemvParams p) {
     const long long u1 = active ? ((long long)(gw + 1) * U) / W : 0;
 
     // ---- weight stream: issue the first PIPE units before the prologue ----
+    // Units are walked with incremental (tile, k-block) cursors: no integer
+    // division on the streaming path.
     Chunk<BITS> buf[PIPE][2];
     float sz[PIPE][4];   // s(g), zp(g), s(g+8), zp(g+8)
+    int itile = (int)(u0 / kbt);
+    int ikb = (int)(u0 - (long long)itile * kbt);
+    const int grp_shift = p.kb_per_group_shift;   // -1: kb_per_group not a power of two
 
-    auto issue = [&](long long u, Chunk<BITS> (&b)[2], float (&s)[4]) {
-        const int tile = (int)(u / kbt);
-        const int kb = (int)(u - (long long)tile * kbt);
-        const int grp = kb / p.kb_per_group;
+    auto issue_next = [&](Chunk<BITS> (&b)[2], float (&s)[4]) {
+        const int grp = grp_shift >= 0 ? (ikb >> grp_shift) : ikb / p.kb_per_group;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            int row = tile * 16 + g + 8 * h;
+            int row = itile * 16 + g + 8 * h;
             row = row < p.n ? row : p.n - 1;
-            load_chunk<BITS>(b[h], p.w + (size_t)row * p.row_bytes + (size_t)kb * KBLOCK_BYTES + c * CHUNK_BYTES);
+            load_chunk<BITS>(b[h], p.w + (size_t)row * p.row_bytes + (size_t)ikb * KBLOCK_BYTES + c * CHUNK_BYTES);
             const size_t sidx = (size_t)row * p.n_groups + grp;
             float sv, zv;
             if (p.flags & VSPEC_B200_F_SZ_F16) {
@@ -287,10 +290,15 @@ lowbit_gemv_split_kernel(const GemvParams p) {
             s[2 * h] = sv;
             s[2 * h + 1] = zv;
         }
+        if (++ikb == kbt) {
+            ikb = 0;
+            ++itile;
+        }
     };
+    const int n_units = (int)(u1 - u0);
 #pragma unroll
     for (int st = 0; st < PIPE; ++st)
-        if (u0 + st < u1) issue(u0 + st, buf[st], sz[st]);
+        if (st < n_units) issue_next(buf[st], sz[st]);
 
     // ---- activation prologue (once per CTA) ----
     const int K = p.k;
@@ -468,17 +476,13 @@ lowbit_gemv_split_kernel(const GemvParams p) {
         for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
     };
 
-    for (long long base_u = u0; base_u < u1; base_u += PIPE) {
+    int ckb = (int)(u0 - (long long)cur_tile * kbt);
+    for (int base_i = 0; base_i < n_units; base_i += PIPE) {
 #pragma unroll
         for (int st = 0; st < PIPE; ++st) {
-            const long long u = base_u + st;
-            if (u < u1) {
-                const int tile = (int)(u / kbt);
-                const int kb = (int)(u - (long long)tile * kbt);
-                if (tile != cur_tile) {
-                    flush(cur_tile);
-                    cur_tile = tile;
-                }
+            const int i = base_i + st;
+            if (i < n_units) {
+                const int kb = ckb;
                 float d[NT][4];
                 const uint4* fb = frag + (size_t)kb * 4 * NT * lanes;
 #pragma unroll
@@ -506,7 +510,7 @@ lowbit_gemv_split_kernel(const GemvParams p) {
                 }
                 const float s0 = sz[st][0], z0 = sz[st][1], s1 = sz[st][2], z1 = sz[st][3];
                 // refill this stage while the tensor cores drain
-                if (u + PIPE < u1) issue(u + PIPE, buf[st], sz[st]);
+                if (i + PIPE < n_units) issue_next(buf[st], sz[st]);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const int r = 4 * nt + c;
@@ -516,10 +520,15 @@ lowbit_gemv_split_kernel(const GemvParams p) {
                         acc[nt][1] = fmaf(s1, (d[nt][2] + d[nt][3]) - z1 * xsum, acc[nt][1]);
                     }
                 }
+                // advance the consume cursor; publish a finished tile part
+                if (++ckb == kbt || i + 1 == n_units) {
+                    flush(cur_tile);
+                    ++cur_tile;
+                    ckb = 0;
+                }
             }
         }
     }
-    if (u1 > u0) flush(cur_tile);
 }
 
 // -------------------------------------------------------------------------
@@ -741,6 +750,9 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
     p.kb_total = p.k / 128;
     p.kb_per_group = (p.n_groups > 0 && p.k % p.n_groups == 0) ? (p.k / p.n_groups) / 128 : 1;
     if (p.kb_per_group < 1) p.kb_per_group = 1;
+    p.kb_per_group_shift = -1;
+    for (int sh = 0; sh < 31; ++sh)
+        if ((1 << sh) == p.kb_per_group) p.kb_per_group_shift = sh;
 
     const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
     if (fast) {

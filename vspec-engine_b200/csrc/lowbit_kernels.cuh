@@ -21,6 +21,7 @@ struct GemvParams {
     int row_bytes;
     int kb_total;            // k / 128 (fast path)
     int kb_per_group;        // (k / n_groups) / 128 (fast path)
+    int kb_per_group_shift;  // log2(kb_per_group), or -1 if not a power of two
     int flags;
     // persistent split-K plan (fast path)
     int tiles;               // 16-row tiles
