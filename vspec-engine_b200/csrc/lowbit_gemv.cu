@@ -26,6 +26,7 @@
 #include "lowbit_kernels.cuh"
 
 #include <stdio.h>
+#include <stdlib.h>
 
 namespace vb200 {
 
@@ -68,110 +69,40 @@ __device__ __forceinline__ void load_chunk(Chunk<BITS>& c, const uint8_t* p) {
 
 constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
 
-// Decode one 32-code chunk into 16 fp16 pairs of exact signed codes.
-template <int BITS, bool UNSIGNED>
-__device__ __forceinline__ void unpack_chunk(const Chunk<BITS>& c, uint32_t h[16]) {
-    if constexpr (BITS == 4) {
-        // signed(n) = (n ^ 8) - 8; unsigned-offset(u) = u - 8.
-        constexpr uint32_t kSub = f16x2_bits(1032.0, 1032.0);
-        constexpr uint32_t kMul = f16x2_bits(1.0 / 16, 1.0 / 16);
-        constexpr uint32_t kAdd = f16x2_bits(-72.0, -72.0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            uint32_t q = UNSIGNED ? c.w[i] : (c.w[i] ^ 0x88888888u);
-            h[4 * i + 0] = hsub2_bits(lop3_and_or(q, 0x000F000Fu, kMagic), kSub);
-            h[4 * i + 1] = hfma2_bits(lop3_and_or(q, 0x00F000F0u, kMagic), kMul, kAdd);
-            q >>= 8;
-            h[4 * i + 2] = hsub2_bits(lop3_and_or(q, 0x000F000Fu, kMagic), kSub);
-            h[4 * i + 3] = hfma2_bits(lop3_and_or(q, 0x00F000F0u, kMagic), kMul, kAdd);
-        }
-    } else if constexpr (BITS == 2) {
-        // signed(u) = (u ^ 2) - 2; unsigned-offset(u) = u - 2.
-        constexpr uint32_t kSub0 = f16x2_bits(1026.0, 1026.0);
-        constexpr uint32_t kMul1 = f16x2_bits(1.0 / 4, 1.0 / 4);
-        constexpr uint32_t kAdd1 = f16x2_bits(-258.0, -258.0);
-        constexpr uint32_t kMul2 = f16x2_bits(1.0 / 16, 1.0 / 16);
-        constexpr uint32_t kAdd2 = f16x2_bits(-66.0, -66.0);
-        constexpr uint32_t kMul3 = f16x2_bits(1.0 / 64, 1.0 / 64);
-        constexpr uint32_t kAdd3 = f16x2_bits(-18.0, -18.0);
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            uint32_t q = UNSIGNED ? c.w[i] : (c.w[i] ^ 0xAAAAAAAAu);
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int b = 8 * i + 4 * half;
-                h[b + 0] = hsub2_bits(lop3_and_or(q, 0x00030003u, kMagic), kSub0);
-                h[b + 1] = hfma2_bits(lop3_and_or(q, 0x000C000Cu, kMagic), kMul1, kAdd1);
-                h[b + 2] = hfma2_bits(lop3_and_or(q, 0x00300030u, kMagic), kMul2, kAdd2);
-                h[b + 3] = hfma2_bits(lop3_and_or(q, 0x00C000C0u, kMagic), kMul3, kAdd3);
-                q >>= 8;
-            }
-        }
-    } else {
-        // 32 three-bit codes in 96 bits; code j at bits [3j, 3j+3).
-        // signed(u) = (u ^ 4) - 4: flip every code's top bit, then subtract 4.
-        uint32_t w0 = c.w[0], w1 = c.w[1], w2 = c.w[2];
-        if (!UNSIGNED) {
-            w0 ^= 0x24924924u;
-            w1 ^= 0x49249249u;
-            w2 ^= 0x92492492u;
-        }
-        // Window R(j) = bits [3j-4, 3j+28) of the chunk: codes j, j+1 land at
-        // bits 4 and 7 (low half), codes j+4, j+5 at bits 16 and 19 (high half).
-        uint32_t R[8];
-        R[0] = w0 << 4;                 // j = 0
-        R[1] = w0 >> 2;                 // j = 2
-        R[2] = funnel_r(w0, w1, 20);    // j = 8
-        R[3] = funnel_r(w0, w1, 26);    // j = 10
-        R[4] = funnel_r(w1, w2, 12);    // j = 16
-        R[5] = funnel_r(w1, w2, 18);    // j = 18
-        R[6] = w2 >> 4;                 // j = 24
-        R[7] = w2 >> 10;                // j = 26
-        constexpr uint32_t kMul0 = f16x2_bits(1.0 / 16, 1.0);
-        constexpr uint32_t kAdd0 = f16x2_bits(-68.0, -1028.0);
-        constexpr uint32_t kMul1 = f16x2_bits(1.0 / 128, 1.0 / 8);
-        constexpr uint32_t kAdd1 = f16x2_bits(-12.0, -132.0);
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            h[2 * w + 0] = hfma2_bits(lop3_and_or(R[w], 0x00070070u, kMagic), kMul0, kAdd0);
-            h[2 * w + 1] = hfma2_bits(lop3_and_or(R[w], 0x00380380u, kMagic), kMul1, kAdd1);
-        }
-    }
+// Decoded fp16 pairs carry 1024 + mult * u, where u is the offset-encoded code
+// (u = code + 2^(bits-1), exact in fp16) and mult a power of two that depends
+// only on the code's position j inside its 32-code chunk.  The GEMV divides
+// the matching activation by mult and removes sum(x * (1024/mult + 2^(bits-1)))
+// per k-block, so no fp16 arithmetic is spent on decoding.
+template <int BITS>
+__host__ __device__ __forceinline__ float code_mult(int j) {
+    if (BITS == 4) return (j & 1) ? 16.0f : 1.0f;
+    if (BITS == 2) return (float)(1 << (2 * (j & 3)));
+    const int t = j & 7;   // BITS == 3
+    return t < 4 ? ((t & 1) ? 128.0f : 16.0f) : ((t & 1) ? 8.0f : 1.0f);
 }
 
-// Decode only fp16 pairs 2*mm and 2*mm+1 of a chunk (the A registers of MMA
-// number mm): the arithmetic of unpack_chunk, evaluated lazily so that only
-// four decoded registers per tile are live at a time.  mm is a constant
-// after loop unrolling, so every branch below folds away.
+// Pairs 2*mm and 2*mm+1 of a chunk (the A registers of MMA number mm) as raw
+// magic halves.  Two's-complement codes become offset codes by flipping every
+// field's top bit.  mm is a constant after loop unrolling.
 template <int BITS, bool UNSIGNED>
 __device__ __forceinline__ void unpack_mm(const Chunk<BITS>& c, const int mm, uint32_t& h0, uint32_t& h1) {
     if constexpr (BITS == 4) {
         uint32_t q = UNSIGNED ? c.w[mm >> 1] : (c.w[mm >> 1] ^ 0x88888888u);
         if (mm & 1) q >>= 8;
-        constexpr uint32_t kSub = f16x2_bits(1032.0, 1032.0);
-        constexpr uint32_t kMul = f16x2_bits(1.0 / 16, 1.0 / 16);
-        constexpr uint32_t kAdd = f16x2_bits(-72.0, -72.0);
-        h0 = hsub2_bits(lop3_and_or(q, 0x000F000Fu, kMagic), kSub);
-        h1 = hfma2_bits(lop3_and_or(q, 0x00F000F0u, kMagic), kMul, kAdd);
+        h0 = lop3_and_or(q, 0x000F000Fu, kMagic);    // nibbles 2(mm&1) and +4: mult 1
+        h1 = lop3_and_or(q, 0x00F000F0u, kMagic);    // nibbles 2(mm&1)+1 and +5: mult 16
     } else if constexpr (BITS == 2) {
         uint32_t q = UNSIGNED ? c.w[mm >> 2] : (c.w[mm >> 2] ^ 0xAAAAAAAAu);
         const int p0 = 2 * (mm & 3);  // pair index inside the word: 0, 2, 4, 6
         if (p0 >= 4) q >>= 8;
-        constexpr uint32_t kSub0 = f16x2_bits(1026.0, 1026.0);
-        constexpr uint32_t kMul1 = f16x2_bits(1.0 / 4, 1.0 / 4);
-        constexpr uint32_t kAdd1 = f16x2_bits(-258.0, -258.0);
-        constexpr uint32_t kMul2 = f16x2_bits(1.0 / 16, 1.0 / 16);
-        constexpr uint32_t kAdd2 = f16x2_bits(-66.0, -66.0);
-        constexpr uint32_t kMul3 = f16x2_bits(1.0 / 64, 1.0 / 64);
-        constexpr uint32_t kAdd3 = f16x2_bits(-18.0, -18.0);
-        if ((p0 & 3) == 0) {
-            h0 = hsub2_bits(lop3_and_or(q, 0x00030003u, kMagic), kSub0);
-            h1 = hfma2_bits(lop3_and_or(q, 0x000C000Cu, kMagic), kMul1, kAdd1);
-        } else {
-            h0 = hfma2_bits(lop3_and_or(q, 0x00300030u, kMagic), kMul2, kAdd2);
-            h1 = hfma2_bits(lop3_and_or(q, 0x00C000C0u, kMagic), kMul3, kAdd3);
-        }
+        const int j = p0 & 3;         // 0 or 2: field positions j and j+1
+        h0 = lop3_and_or(q, 0x00030003u << (2 * j), kMagic);
+        h1 = lop3_and_or(q, 0x00030003u << (2 * j + 2), kMagic);
     } else {
+        // 32 three-bit codes in 96 bits, code j at bits [3j, 3j+3).  Window
+        // R = bits [3J-4, 3J+28) puts codes J, J+1 at bits 4, 7 and codes
+        // J+4, J+5 at bits 16, 19, for J = 0,2,8,10,16,18,24,26.
         uint32_t w0 = c.w[0], w1 = c.w[1], w2 = c.w[2];
         if (!UNSIGNED) {
             w0 ^= 0x24924924u;
@@ -189,17 +120,11 @@ __device__ __forceinline__ void unpack_mm(const Chunk<BITS>& c, const int mm, ui
             case 6: R = w2 >> 4; break;
             default: R = w2 >> 10; break;
         }
-        constexpr uint32_t kMul0 = f16x2_bits(1.0 / 16, 1.0);
-        constexpr uint32_t kAdd0 = f16x2_bits(-68.0, -1028.0);
-        constexpr uint32_t kMul1 = f16x2_bits(1.0 / 128, 1.0 / 8);
-        constexpr uint32_t kAdd1 = f16x2_bits(-12.0, -132.0);
-        h0 = hfma2_bits(lop3_and_or(R, 0x00070070u, kMagic), kMul0, kAdd0);
-        h1 = hfma2_bits(lop3_and_or(R, 0x00380380u, kMagic), kMul1, kAdd1);
+        h0 = lop3_and_or(R, 0x00070070u, kMagic);    // codes J (mult 16), J+4 (mult 1)
+        h1 = lop3_and_or(R, 0x00380380u, kMagic);    // codes J+1 (mult 128), J+5 (mult 8)
     }
 }
 
-// -------------------------------------------------------------------------
-// Shared-memory plan of the fast kernel.
 // -------------------------------------------------------------------------
 // Persistent split-K GEMV.
 //
@@ -222,7 +147,7 @@ __host__ __device__ __forceinline__ int gemv_lanes(int m) { return 4 * (2 * m < 
 static size_t gemv_smem_bytes(int m, int kbt) {
     const int nt = gemv_nt(m);
     return (size_t)kbt * 4 * nt * gemv_lanes(m) * 16   // B fragments
-           + (size_t)kbt * m * sizeof(float)             // per-(k-block,row) sums
+           + 2 * (size_t)kbt * m * sizeof(float)         // per-(k-block,row) sums X and C
            + (size_t)kGemvWarps * 16 * sizeof(float)     // max-reduction area
            + 32 * sizeof(float);                         // row scale + row norm
 }
@@ -246,7 +171,8 @@ lowbit_gemv_split_kernel(const GemvParams p) {
     const int lanes = gemv_lanes(m);
     uint4* frag = reinterpret_cast<uint4*>(smem_raw);
     float* xs = reinterpret_cast<float*>(smem_raw + (size_t)kbt * 4 * NT * lanes * 16);
-    float* maxbuf = xs + (size_t)kbt * m;          // [kGemvWarps][<=16]
+    float* cs = xs + (size_t)kbt * m;              // [kbt][m] decode-offset sums
+    float* maxbuf = cs + (size_t)kbt * m;          // [kGemvWarps][<=16]
     float* row_scale = maxbuf + kGemvWarps * 16;   // [16]
     float* row_norm = row_scale + 16;              // [16]
 
@@ -301,6 +227,9 @@ lowbit_gemv_split_kernel(const GemvParams p) {
         if (st < n_units) issue_next(buf[st], sz[st]);
 
     // ---- activation prologue (once per CTA) ----
+    // Everything above touched only immutable weights; x may be the output of
+    // the previous kernel in the stream (programmatic dependent launch).
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
     const int K = p.k;
     const bool rms = EPI_HAS_RMSNORM(p.flags);
     if (rms) {
@@ -325,20 +254,40 @@ lowbit_gemv_split_kernel(const GemvParams p) {
         }
         return v;
     };
-    // (a) per-(k-block, row) sums and per-row max |x|
+    // (a) per-(k-block, row) sums X = sum x and W = sum x/mult(t), and per-row max |x|
     {
         float mx[8];
 #pragma unroll
         for (int r = 0; r < 8; ++r) mx[r] = 0.f;
-        for (int pr = warp; pr < kbt * m; pr += kGemvWarps) {
-            const int r = pr % m, kb = pr / m;
-            const float4 v = xval4(r, kb * 128 + lane * 4);
-            const float sum = warp_sum((v.x + v.y) + (v.z + v.w));
-            const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        const int pairs = kbt * m;
+        float mlt[4];
 #pragma unroll
-            for (int rr = 0; rr < 8; ++rr)
-                if (rr == r) mx[rr] = fmaxf(mx[rr], a);
-            if (lane == 0) xs[kb * m + r] = sum;
+        for (int e = 0; e < 4; ++e) mlt[e] = 1.0f / code_mult<BITS>((lane * 4 + e) & 31);
+        for (int pr0 = warp; pr0 < pairs; pr0 += 4 * kGemvWarps) {
+            float4 v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {   // four independent loads in flight
+                const int pr = pr0 + q * kGemvWarps;
+                v[q] = pr < pairs ? xval4(pr % m, (pr / m) * 128 + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int pr = pr0 + q * kGemvWarps;
+                if (pr < pairs) {
+                    const int r = pr % m, kb = pr / m;
+                    const float4 x4 = v[q];
+                    const float sx = warp_sum((x4.x + x4.y) + (x4.z + x4.w));
+                    const float sw = warp_sum((x4.x * mlt[0] + x4.y * mlt[1]) + (x4.z * mlt[2] + x4.w * mlt[3]));
+                    const float a = fmaxf(fmaxf(fabsf(x4.x), fabsf(x4.y)), fmaxf(fabsf(x4.z), fabsf(x4.w)));
+#pragma unroll
+                    for (int rr = 0; rr < 8; ++rr)
+                        if (rr == r) mx[rr] = fmaxf(mx[rr], a);
+                    if (lane == 0) {
+                        xs[kb * m + r] = sx;
+                        cs[kb * m + r] = sw;
+                    }
+                }
+            }
         }
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
@@ -374,9 +323,13 @@ lowbit_gemv_split_kernel(const GemvParams p) {
                 // pair qq of this slot holds codes (lo_code(4mp)+qq, hi_code(4mp)+qq)
                 const int t = kb * 128 + 32 * cc;
                 const float sc = row_scale[r];
-                const float4 a = xval4(r, t + lo_code<BITS>(4 * mp)), b = xval4(r, t + hi_code<BITS>(4 * mp));
-                const float va[4] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc};
-                const float vb[4] = {b.x * sc, b.y * sc, b.z * sc, b.w * sc};
+                const int jl = lo_code<BITS>(4 * mp), jh = hi_code<BITS>(4 * mp);
+                const float4 a = xval4(r, t + jl), b = xval4(r, t + jh);
+                // activation divided by the code's decode multiplier (exact: powers of two)
+                const float va[4] = {a.x * sc / code_mult<BITS>(jl), a.y * sc / code_mult<BITS>(jl + 1),
+                                     a.z * sc / code_mult<BITS>(jl + 2), a.w * sc / code_mult<BITS>(jl + 3)};
+                const float vb[4] = {b.x * sc / code_mult<BITS>(jh), b.y * sc / code_mult<BITS>(jh + 1),
+                                     b.z * sc / code_mult<BITS>(jh + 2), b.w * sc / code_mult<BITS>(jh + 3)};
                 uint32_t wh[4], wl[4];
 #pragma unroll
                 for (int qq = 0; qq < 4; ++qq) {
@@ -399,9 +352,18 @@ lowbit_gemv_split_kernel(const GemvParams p) {
                 if (4 * (gh + 1) + cc < lanes) frag[base + 4 * (gh + 1) + cc] = lo;
             }
         }
-        for (int i = tid; i < kbt * m; i += kGemvThreads) xs[i] *= row_scale[i % m];
+        // scaled sums: X and the decode offset C = 1024 * W + 2^(bits-1) * X
+        constexpr float kOff = (float)(1 << (BITS - 1));
+        for (int i = tid; i < kbt * m; i += kGemvThreads) {
+            const float sc = row_scale[i % m];
+            const float X = xs[i] * sc;
+            xs[i] = X;
+            cs[i] = fmaf(1024.0f, cs[i] * sc, kOff * X);
+        }
     }
     __syncthreads();
+    // the next kernel in the stream may start staging its weights now
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     if (!active) return;
 
     // ---- main stream ----
@@ -516,8 +478,9 @@ lowbit_gemv_split_kernel(const GemvParams p) {
                     const int r = 4 * nt + c;
                     if (r < m) {
                         const float xsum = xs[kb * m + r];
-                        acc[nt][0] = fmaf(s0, (d[nt][0] + d[nt][1]) - z0 * xsum, acc[nt][0]);
-                        acc[nt][1] = fmaf(s1, (d[nt][2] + d[nt][3]) - z1 * xsum, acc[nt][1]);
+                        const float coff = cs[kb * m + r];
+                        acc[nt][0] = fmaf(s0, (d[nt][0] + d[nt][1]) - fmaf(z0, xsum, coff), acc[nt][0]);
+                        acc[nt][1] = fmaf(s1, (d[nt][2] + d[nt][3]) - fmaf(z1, xsum, coff), acc[nt][1]);
                     }
                 }
                 // advance the consume cursor; publish a finished tile part
@@ -599,20 +562,25 @@ __global__ void unpack_codes_fast_kernel(const uint8_t* w, int n, int k, int row
     const size_t row = chunk / chunks_per_row, ci = chunk % chunks_per_row;
     Chunk<BITS> cbuf;
     const uint8_t* src = w + row * row_bytes + ci * (4 * BITS);
-    // byte-wise gather (no alignment assumption) into the chunk words
-    uint8_t tmp[4 * BITS];
+    uint8_t tmp[4 * BITS];   // byte-wise gather: no alignment assumption
     for (int i = 0; i < 4 * BITS; ++i) tmp[i] = src[i];
     for (int i = 0; i < BITS; ++i)
         cbuf.w[i] = (uint32_t)tmp[4 * i] | ((uint32_t)tmp[4 * i + 1] << 8) | ((uint32_t)tmp[4 * i + 2] << 16) |
                     ((uint32_t)tmp[4 * i + 3] << 24);
-    uint32_t h[16];
-    unpack_chunk<BITS, UNSIGNED>(cbuf, h);
     int8_t* o = out + row * (size_t)k + ci * 32;
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-        const __half2 v = *reinterpret_cast<const __half2*>(&h[q]);
-        o[lo_code<BITS>(q)] = (int8_t)__half2float(__low2half(v));
-        o[hi_code<BITS>(q)] = (int8_t)__half2float(__high2half(v));
+    for (int mm = 0; mm < 8; ++mm) {
+        uint32_t h[2];
+        unpack_mm<BITS, UNSIGNED>(cbuf, mm, h[0], h[1]);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int q = 2 * mm + e;
+            const __half2 v = *reinterpret_cast<const __half2*>(&h[e]);
+            const int jl = lo_code<BITS>(q), jh = hi_code<BITS>(q);
+            // decoded value = 1024 + mult * u, code = u - 2^(bits-1)
+            o[jl] = (int8_t)((int)((__half2float(__low2half(v)) - 1024.0f) / code_mult<BITS>(jl)) - (1 << (BITS - 1)));
+            o[jh] = (int8_t)((int)((__half2float(__high2half(v)) - 1024.0f) / code_mult<BITS>(jh)) - (1 << (BITS - 1)));
+        }
     }
 }
 
@@ -716,6 +684,16 @@ static void* gemv_managed_ws(size_t bytes) {
     return w.ptr;
 }
 
+// VSPEC_B200_PDL=0 disables programmatic dependent launch (A/B timing).
+static bool pdl_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_PDL");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
 template <int BITS, int NT, bool UNS, int EPI>
 static cudaError_t launch_split_t(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
     auto kern = lowbit_gemv_split_kernel<BITS, NT, UNS, EPI>;
@@ -727,8 +705,19 @@ static cudaError_t launch_split_t(const GemvParams& p, int grid, size_t smem, cu
         if (e != cudaSuccess) return e;
         configured[dev] = (int)kGemvMaxSmem;
     }
-    kern<<<grid, kGemvThreads, smem, st>>>(p);
-    return cudaGetLastError();
+    // Programmatic dependent launch: the kernel prefetches weights before
+    // griddepcontrol.wait, overlapping the previous kernel's tail.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <int BITS, bool UNS>
