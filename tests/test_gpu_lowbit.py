@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 
 
 def run_linear(x, w, s, zp, n, k, bits, n_groups, flags=0, zp_const=0.0, residual=None, norm_w=None, eps=1e-6,
-               generic=False, out_cols=None):
+               generic=False, out_cols=None, path=None):
     torch = torch_cuda()
     m = x.shape[0]
     dx, dw = to_dev(x), to_dev(w)
@@ -25,7 +25,7 @@ def run_linear(x, w, s, zp, n, k, bits, n_groups, flags=0, zp_const=0.0, residua
     V.lowbit_linear(dx.data_ptr(), dw.data_ptr(), ds.data_ptr() if ds is not None else None,
                     dzp.data_ptr() if dzp is not None else None, dy.data_ptr(), m, n, k, n_groups, bits, flags=flags,
                     zp_const=zp_const, residual=dres.data_ptr() if dres is not None else None,
-                    norm_weight=dnw.data_ptr() if dnw is not None else None, eps=eps, generic=generic)
+                    norm_weight=dnw.data_ptr() if dnw is not None else None, eps=eps, generic=generic, path=path)
     torch.cuda.synchronize()
     return dy.cpu().numpy()
 
@@ -254,3 +254,55 @@ def test_workspace_too_small_is_rejected():
     with pytest.raises(V.VspecB200Error, match="workspace too small"):
         V.lowbit_linear(dx.data_ptr(), dw.data_ptr(), ds.data_ptr(), dz.data_ptr(), dy.data_ptr(), 1, n, k, g, 4,
                         workspace=ws.data_ptr(), workspace_bytes=16)
+
+
+
+FAST_PATHS = [V.PATH_WARPMMA, V.PATH_TCGEN05]
+
+
+def test_tcgen05_path_smoke():
+    """One small launch of the TMA/TMEM/tcgen05 kernel first, on its own."""
+    rng = np.random.default_rng(1)
+    m, n, k, g = 1, 256, 1024, 8
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = run_linear(x, w, s, zp, n, k, 4, g, path=V.PATH_TCGEN05)
+    flag = __import__("ctypes").c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(__import__("ctypes").byref(flag)), "timeout flag")
+    assert flag.value == 0
+    assert rel_err(y, O.lowbit_matmul(x, w, n, k, 4, s, zp, g)) <= RTOL_F32
+
+
+@pytest.mark.parametrize("path", FAST_PATHS)
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("m,n,k,g", [(1, 4096, 4096, 32), (1, 1000, 2048, 16), (3, 384, 1024, 8), (4, 130, 512, 1),
+                                     (2, 12288, 4096, 32), (1, 200, 12288, 96)])
+def test_fast_paths_match_oracle(path, bits, m, n, k, g):
+    rng = np.random.default_rng(path * 100 + bits * 10 + m + n + k)
+    w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=(n % 2 == 0))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = run_linear(x, w, s, zp, n, k, bits, g, path=path)
+    ref = x.astype(np.float64) @ dequant_np(w, n, k, bits, s.astype(np.float32), zp.astype(np.float32), g).T
+    err = rel_err(y, ref)
+    print(f"path={path} bits={bits} m={m} n={n} k={k}: {err:.2e}")
+    assert err <= RTOL_F32
+
+
+@pytest.mark.parametrize("path", FAST_PATHS)
+def test_fast_paths_fused_epilogues(path):
+    rng = np.random.default_rng(70 + path)
+    m, k, g = 3, 1024, 8
+    n = 256
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    full = O.lowbit_matmul_f64(x, w, n, k, 4, s, zp, g)
+    y = run_linear(x, w, s, zp, n, k, 4, g, flags=V.F_RESIDUAL, residual=res, path=path)
+    assert rel_err(y, full + res) <= RTOL_F32
+    nw = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    xh = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6) * nw
+    y = run_linear(x, w, s, zp, n, k, 4, g, flags=V.F_RMSNORM, norm_w=nw, eps=1e-6, path=path)
+    assert rel_err(y, xh @ dequant_np(w, n, k, 4, s, zp, g).T) <= RTOL_F32
+    gate, up = full[:, : n // 2], full[:, n // 2:]
+    y = run_linear(x, w, s, zp, n, k, 4, g, flags=V.F_SWIGLU, out_cols=n // 2, path=path)
+    assert rel_err(y, gate / (1.0 + np.exp(-gate)) * up) <= RTOL_F32

@@ -69,7 +69,7 @@ extern "C" int vspec_b200_device_info(int* sm_count, int* cc_major, int* cc_mino
     return VSPEC_B200_OK;
 }
 
-static int linear_common(const VspecB200LinearArgs* a, void* stream, int force_generic) {
+static int linear_common(const VspecB200LinearArgs* a, void* stream, int path) {
     if (!a) { set_error("args is NULL"); return VSPEC_B200_ERR_ARG; }
     if (!a->d_x || !a->d_w || !a->d_y) { set_error("NULL x/w/y"); return VSPEC_B200_ERR_ARG; }
     if (a->m == 0 || a->n == 0 || a->k == 0) { set_error("zero dimension"); return VSPEC_B200_ERR_ARG; }
@@ -110,20 +110,30 @@ static int linear_common(const VspecB200LinearArgs* a, void* stream, int force_g
             const size_t out_cols = (a->flags & VSPEC_B200_F_SWIGLU) ? (size_t)p.n / 2 : (size_t)p.n;
             q.y = p.y + (size_t)i0 * out_cols;
             if (p.residual) q.residual = p.residual + (size_t)i0 * p.n;
-            int rc = lowbit_gemv_launch(q, a->bits, uns, st, force_generic, a->d_workspace, a->workspace_bytes);
+            int rc = lowbit_gemv_launch(q, a->bits, uns, st, path, a->d_workspace, a->workspace_bytes);
             if (rc != VSPEC_B200_OK) return rc;
         }
         return VSPEC_B200_OK;
     }
-    return lowbit_gemv_launch(p, a->bits, uns, st, force_generic, a->d_workspace, a->workspace_bytes);
+    return lowbit_gemv_launch(p, a->bits, uns, st, path, a->d_workspace, a->workspace_bytes);
 }
 
 extern "C" int vspec_b200_lowbit_linear(const VspecB200LinearArgs* a, void* stream) {
-    return linear_common(a, stream, 0);
+    return linear_common(a, stream, kPathAuto);
 }
 
 extern "C" int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* a, void* stream) {
-    return linear_common(a, stream, 1);
+    return linear_common(a, stream, kPathGeneric);
+}
+
+extern "C" int vspec_b200_lowbit_linear_path(const VspecB200LinearArgs* a, void* stream, int path) {
+    if (path < kPathAuto || path > kPathTensorCore) { set_error("unknown path %d", path); return VSPEC_B200_ERR_ARG; }
+    return linear_common(a, stream, path);
+}
+
+extern "C" int vspec_b200_gemv_timeout_flag(int* out_flag) {
+    if (!out_flag) { set_error("NULL out_flag"); return VSPEC_B200_ERR_ARG; }
+    return gemv_tc_read_and_clear_timeout(out_flag);
 }
 
 extern "C" size_t vspec_b200_lowbit_linear_workspace_bytes(size_t m, size_t n, size_t k, int flags) {

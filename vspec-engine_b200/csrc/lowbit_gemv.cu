@@ -23,107 +23,13 @@
 //         acc += s * (dot(x, code) - zp * sum(x over the block)).
 //   * Warps reduce through shared memory in a fixed order: deterministic.
 #include "common.cuh"
+#include "lowbit_decode.cuh"
 #include "lowbit_kernels.cuh"
 
 #include <stdio.h>
 #include <stdlib.h>
 
 namespace vb200 {
-
-// -------------------------------------------------------------------------
-// Code-order tables: fp16 pair q (0..15) of a decoded 32-code chunk holds
-// codes (lo_code(q), hi_code(q)).
-// -------------------------------------------------------------------------
-template <int BITS>
-__host__ __device__ __forceinline__ int lo_code(int q) {
-    if (BITS == 4) return 8 * (q >> 2) + (q & 3);
-    if (BITS == 2) return 16 * (q >> 3) + (q & 7);
-    // BITS == 3: window w = q/2 starts at code j(w) in {0,2,8,10,16,18,24,26}
-    const int w = q >> 1;
-    const int j = 8 * (w >> 1) + 2 * (w & 1);
-    return j + (q & 1);
-}
-template <int BITS>
-__host__ __device__ __forceinline__ int hi_code(int q) {
-    if (BITS == 4) return lo_code<4>(q) + 4;
-    if (BITS == 2) return lo_code<2>(q) + 8;
-    return lo_code<3>(q) + 4;
-}
-
-template <int BITS> struct Chunk { uint32_t w[BITS]; };  // 32 codes = 4*BITS bytes
-
-template <int BITS>
-__device__ __forceinline__ void load_chunk(Chunk<BITS>& c, const uint8_t* p) {
-    if constexpr (BITS == 4) {
-        uint4 v = ldg_stream_v4(p);
-        c.w[0] = v.x; c.w[1] = v.y; c.w[2] = v.z; c.w[3] = v.w;
-    } else if constexpr (BITS == 2) {
-        uint2 v = ldg_stream_v2(p);
-        c.w[0] = v.x; c.w[1] = v.y;
-    } else {
-        c.w[0] = ldg_stream_u32(p);
-        c.w[1] = ldg_stream_u32(p + 4);
-        c.w[2] = ldg_stream_u32(p + 8);
-    }
-}
-
-constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
-
-// Decoded fp16 pairs carry 1024 + mult * u, where u is the offset-encoded code
-// (u = code + 2^(bits-1), exact in fp16) and mult a power of two that depends
-// only on the code's position j inside its 32-code chunk.  The GEMV divides
-// the matching activation by mult and removes sum(x * (1024/mult + 2^(bits-1)))
-// per k-block, so no fp16 arithmetic is spent on decoding.
-template <int BITS>
-__host__ __device__ __forceinline__ float code_mult(int j) {
-    if (BITS == 4) return (j & 1) ? 16.0f : 1.0f;
-    if (BITS == 2) return (float)(1 << (2 * (j & 3)));
-    const int t = j & 7;   // BITS == 3
-    return t < 4 ? ((t & 1) ? 128.0f : 16.0f) : ((t & 1) ? 8.0f : 1.0f);
-}
-
-// Pairs 2*mm and 2*mm+1 of a chunk (the A registers of MMA number mm) as raw
-// magic halves.  Two's-complement codes become offset codes by flipping every
-// field's top bit.  mm is a constant after loop unrolling.
-template <int BITS, bool UNSIGNED>
-__device__ __forceinline__ void unpack_mm(const Chunk<BITS>& c, const int mm, uint32_t& h0, uint32_t& h1) {
-    if constexpr (BITS == 4) {
-        uint32_t q = UNSIGNED ? c.w[mm >> 1] : (c.w[mm >> 1] ^ 0x88888888u);
-        if (mm & 1) q >>= 8;
-        h0 = lop3_and_or(q, 0x000F000Fu, kMagic);    // nibbles 2(mm&1) and +4: mult 1
-        h1 = lop3_and_or(q, 0x00F000F0u, kMagic);    // nibbles 2(mm&1)+1 and +5: mult 16
-    } else if constexpr (BITS == 2) {
-        uint32_t q = UNSIGNED ? c.w[mm >> 2] : (c.w[mm >> 2] ^ 0xAAAAAAAAu);
-        const int p0 = 2 * (mm & 3);  // pair index inside the word: 0, 2, 4, 6
-        if (p0 >= 4) q >>= 8;
-        const int j = p0 & 3;         // 0 or 2: field positions j and j+1
-        h0 = lop3_and_or(q, 0x00030003u << (2 * j), kMagic);
-        h1 = lop3_and_or(q, 0x00030003u << (2 * j + 2), kMagic);
-    } else {
-        // 32 three-bit codes in 96 bits, code j at bits [3j, 3j+3).  Window
-        // R = bits [3J-4, 3J+28) puts codes J, J+1 at bits 4, 7 and codes
-        // J+4, J+5 at bits 16, 19, for J = 0,2,8,10,16,18,24,26.
-        uint32_t w0 = c.w[0], w1 = c.w[1], w2 = c.w[2];
-        if (!UNSIGNED) {
-            w0 ^= 0x24924924u;
-            w1 ^= 0x49249249u;
-            w2 ^= 0x92492492u;
-        }
-        uint32_t R;
-        switch (mm) {
-            case 0: R = w0 << 4; break;
-            case 1: R = w0 >> 2; break;
-            case 2: R = funnel_r(w0, w1, 20); break;
-            case 3: R = funnel_r(w0, w1, 26); break;
-            case 4: R = funnel_r(w1, w2, 12); break;
-            case 5: R = funnel_r(w1, w2, 18); break;
-            case 6: R = w2 >> 4; break;
-            default: R = w2 >> 10; break;
-        }
-        h0 = lop3_and_or(R, 0x00070070u, kMagic);    // codes J (mult 16), J+4 (mult 1)
-        h1 = lop3_and_or(R, 0x00380380u, kMagic);    // codes J+1 (mult 128), J+5 (mult 8)
-    }
-}
 
 // -------------------------------------------------------------------------
 // Persistent split-K GEMV.
@@ -652,8 +558,22 @@ constexpr size_t kGemvCounterBytes = kGemvCounterSlots * sizeof(int);
 
 size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu) {
     if (m < 1 || n < 1 || k < 128) return 0;
-    SplitPlan sp = split_plan(m > kGemvMaxM ? kGemvMaxM : m, n, k, swiglu);
-    return kGemvCounterBytes + sp.scratch_floats * sizeof(float);
+    const int mm = m > kGemvMaxM ? kGemvMaxM : m;
+    SplitPlan sp = split_plan(mm, n, k, swiglu);
+    size_t floats = sp.scratch_floats;
+    const size_t tc = gemv_tc_scratch_floats(mm, n, k, swiglu);
+    if (tc > floats) floats = tc;
+    return kGemvCounterBytes + floats * sizeof(float);
+}
+
+// VSPEC_B200_GEMV_TC=0 routes every shape to the warp-MMA kernel (A/B timing).
+static bool tc_path_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_GEMV_TC");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
 }
 
 // Library-managed workspace: one grow-only, zero-initialized buffer per device
@@ -731,8 +651,9 @@ static cudaError_t launch_split_bits(const GemvParams& p, int epi, int grid, siz
                    : launch_split_t<BITS, 2, UNS, kEpiPlain>(p, grid, smem, st);
 }
 
-int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int force_generic,
+int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int path,
                        void* workspace, size_t workspace_bytes) {
+    const int force_generic = path == kPathGeneric;
     if (bits < 2 || bits > 4) { set_error("bits must be 2, 3 or 4 (got %d)", bits); return VSPEC_B200_ERR_ARG; }
     const bool swiglu = (p.flags & VSPEC_B200_F_SWIGLU) != 0;
     if (swiglu && (p.n % 2 != 0)) { set_error("SwiGLU needs an even row count (n=%d)", p.n); return VSPEC_B200_ERR_ARG; }
@@ -744,6 +665,10 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
         if ((1 << sh) == p.kb_per_group) p.kb_per_group_shift = sh;
 
     const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
+    if (!fast && (path == kPathWarpMma || path == kPathTensorCore)) {
+        set_error("shape not supported by the requested fast path");
+        return VSPEC_B200_ERR_UNSUPPORTED;
+    }
     if (fast) {
         SplitPlan sp = split_plan(p.m, p.n, p.k, swiglu);
         const size_t need = gemv_workspace_bytes(p.m, p.n, p.k, swiglu);
@@ -759,6 +684,14 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
         }
         p.counters = reinterpret_cast<int*>(ws);
         p.scratch = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kGemvCounterBytes);
+        const bool tc_ok = gemv_tc_supported(p, bits);
+        if (path == kPathTensorCore && !tc_ok) {
+            set_error("shape not supported by the tcgen05 GEMV (m <= 4, groups of 128*i, smem)");
+            return VSPEC_B200_ERR_UNSUPPORTED;
+        }
+        if (tc_ok && (path == kPathTensorCore || (path == kPathAuto && tc_path_enabled()))) {
+            return gemv_tc_launch(p, bits, unsigned_codes, st, pdl_enabled());
+        }
         p.tiles = sp.tiles;
         p.total_warps = sp.total_warps;
         p.max_slots = sp.max_slots;

@@ -38,9 +38,18 @@ constexpr size_t kGemvMaxSmem = 200 * 1024;
 
 #define EPI_HAS_RMSNORM(flags) (((flags) & VSPEC_B200_F_RMSNORM) != 0)
 
-int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int force_generic,
+constexpr int kPathAuto = 0;
+constexpr int kPathGeneric = 1;
+constexpr int kPathWarpMma = 2;
+constexpr int kPathTensorCore = 3;
+int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int path,
                        void* workspace, size_t workspace_bytes);
 size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu);
+// tcgen05 / TMA path (lowbit_gemv_tc.cu)
+bool gemv_tc_supported(const GemvParams& p, int bits);
+int gemv_tc_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl);
+size_t gemv_tc_scratch_floats(int m, int n, int k, bool swiglu);
+int gemv_tc_read_and_clear_timeout(int* out);
 int unpack_codes_launch(const uint8_t* w, int n, int k, int bits, int unsigned_codes, int8_t* out, cudaStream_t st,
                         int use_fast_decoder);
 

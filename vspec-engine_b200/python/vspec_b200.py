@@ -26,6 +26,7 @@ F_RMSNORM = 0x8
 F_SWIGLU = 0x10
 KV_F32 = 0
 KV_F16 = 1
+PATH_AUTO, PATH_GENERIC, PATH_WARPMMA, PATH_TCGEN05 = 0, 1, 2, 3
 
 
 class VspecB200Error(RuntimeError):
@@ -96,7 +97,9 @@ _sigs = {
     "vspec_b200_version": ([], ctypes.c_char_p),
     "vspec_b200_lowbit_linear": ([POINTER(LinearArgs), c_void_p], c_int),
     "vspec_b200_lowbit_linear_generic": ([POINTER(LinearArgs), c_void_p], c_int),
+    "vspec_b200_lowbit_linear_path": ([POINTER(LinearArgs), c_void_p, c_int], c_int),
     "vspec_b200_lowbit_linear_workspace_bytes": ([c_size_t, c_size_t, c_size_t, c_int], c_size_t),
+    "vspec_b200_gemv_timeout_flag": ([POINTER(c_int)], c_int),
     "vspec_b200_unpack_codes": ([c_void_p, c_size_t, c_size_t, c_int, c_int, c_void_p, c_int, c_void_p], c_int),
     "vspec_b200_device_info": ([POINTER(c_int), POINTER(c_int), POINTER(c_int), POINTER(c_size_t)], c_int),
     "vspec_b200_dequant_f32": ([c_void_p, c_void_p, c_void_p, c_float, c_int, c_int, c_size_t, c_size_t, c_size_t,
@@ -189,11 +192,12 @@ def hptr(a: np.ndarray | None) -> int | None:
 def lowbit_linear(x: int, w: int, scales: int | None, zp: int | None, y: int, m: int, n: int, k: int, n_groups: int,
                   bits: int, flags: int = 0, zp_const: float = 0.0, residual: int | None = None,
                   norm_weight: int | None = None, eps: float = 1e-6, stream: int = 0, generic: bool = False,
-                  workspace: int | None = None, workspace_bytes: int = 0) -> None:
+                  workspace: int | None = None, workspace_bytes: int = 0, path: int | None = None) -> None:
     a = LinearArgs(x, w, scales, zp, zp_const, y, residual, norm_weight, eps, m, n, k, n_groups, bits, flags,
                    workspace, workspace_bytes)
-    fn = lib.vspec_b200_lowbit_linear_generic if generic else lib.vspec_b200_lowbit_linear
-    check(fn(ctypes.byref(a), stream), "vspec_b200_lowbit_linear")
+    if path is None:
+        path = PATH_GENERIC if generic else PATH_AUTO
+    check(lib.vspec_b200_lowbit_linear_path(ctypes.byref(a), stream, path), "vspec_b200_lowbit_linear")
 
 
 def unpack_codes(w: int, n: int, k: int, bits: int, out: int, unsigned: bool = False, fast: bool = True,
