@@ -102,4 +102,16 @@ __device__ __forceinline__ void unpack_mm(const Chunk<BITS>& c, const int mm, ui
     }
 }
 
+// Scale / zero-point element as raw bits (fp16 or fp32 storage), read through
+// the read-only path.  Converting only where the value is used keeps the load
+// latency off the critical path.
+__device__ __forceinline__ uint32_t load_sz_raw(const void* base, size_t idx, bool f16) {
+    if (!base) return 0u;
+    if (f16) return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(base) + idx);
+    return __ldg(reinterpret_cast<const unsigned int*>(base) + idx);
+}
+__device__ __forceinline__ float sz_to_float(uint32_t raw, bool f16) {
+    return f16 ? __half2float(__ushort_as_half((unsigned short)raw)) : __uint_as_float(raw);
+}
+
 }  // namespace vb200

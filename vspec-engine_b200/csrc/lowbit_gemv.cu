@@ -98,12 +98,13 @@ lowbit_gemv_split_kernel(const GemvParams p) {
     // Units are walked with incremental (tile, k-block) cursors: no integer
     // division on the streaming path.
     Chunk<BITS> buf[PIPE][2];
-    float sz[PIPE][4];   // s(g), zp(g), s(g+8), zp(g+8)
+    uint32_t sz[PIPE][4];   // raw bits of s(g), zp(g), s(g+8), zp(g+8)
+    const bool sz16 = (p.flags & VSPEC_B200_F_SZ_F16) != 0;
     int itile = (int)(u0 / kbt);
     int ikb = (int)(u0 - (long long)itile * kbt);
     const int grp_shift = p.kb_per_group_shift;   // -1: kb_per_group not a power of two
 
-    auto issue_next = [&](Chunk<BITS> (&b)[2], float (&s)[4]) {
+    auto issue_next = [&](Chunk<BITS> (&b)[2], uint32_t (&s)[4]) {
         const int grp = grp_shift >= 0 ? (ikb >> grp_shift) : ikb / p.kb_per_group;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -111,16 +112,8 @@ lowbit_gemv_split_kernel(const GemvParams p) {
             row = row < p.n ? row : p.n - 1;
             load_chunk<BITS>(b[h], p.w + (size_t)row * p.row_bytes + (size_t)ikb * KBLOCK_BYTES + c * CHUNK_BYTES);
             const size_t sidx = (size_t)row * p.n_groups + grp;
-            float sv, zv;
-            if (p.flags & VSPEC_B200_F_SZ_F16) {
-                sv = p.s ? __half2float(reinterpret_cast<const __half*>(p.s)[sidx]) : 1.0f;
-                zv = p.zp ? __half2float(reinterpret_cast<const __half*>(p.zp)[sidx]) : p.zp_const;
-            } else {
-                sv = p.s ? reinterpret_cast<const float*>(p.s)[sidx] : 1.0f;
-                zv = p.zp ? reinterpret_cast<const float*>(p.zp)[sidx] : p.zp_const;
-            }
-            s[2 * h] = sv;
-            s[2 * h + 1] = zv;
+            s[2 * h] = load_sz_raw(p.s, sidx, sz16);       // converted at use
+            s[2 * h + 1] = load_sz_raw(p.zp, sidx, sz16);
         }
         if (++ikb == kbt) {
             ikb = 0;
@@ -376,7 +369,10 @@ lowbit_gemv_split_kernel(const GemvParams p) {
                         }
                     }
                 }
-                const float s0 = sz[st][0], z0 = sz[st][1], s1 = sz[st][2], z1 = sz[st][3];
+                const float s0 = p.s ? sz_to_float(sz[st][0], sz16) : 1.0f;
+                const float s1 = p.s ? sz_to_float(sz[st][2], sz16) : 1.0f;
+                const float z0 = p.zp ? sz_to_float(sz[st][1], sz16) : p.zp_const;
+                const float z1 = p.zp ? sz_to_float(sz[st][3], sz16) : p.zp_const;
                 // refill this stage while the tensor cores drain
                 if (i + PIPE < n_units) issue_next(buf[st], sz[st]);
 #pragma unroll

@@ -267,7 +267,10 @@ lowbit_gemv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const GemvParams
         const int row = warp * 32 + lane;
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
         float acc[kTcMaxM] = {0.f, 0.f, 0.f, 0.f};
-        float e_s[NA], e_z[NA];
+        uint32_t e_s[NA], e_z[NA];
+        const bool sz16 = (p.flags & VSPEC_B200_F_SZ_F16) != 0;
+        const uint32_t one_bits = sz16 ? 0x3C00u : 0x3F800000u;
+        const uint32_t zc_bits = sz16 ? (uint32_t)__half_as_ushort(__float2half_rn(p.zp_const)) : __float_as_uint(p.zp_const);
         int e_kb[NA], e_tile[NA], e_last[NA];
         int c_tile = u0 / kbt, c_kb = u0 - c_tile * kbt;
         int flushes = 0;
@@ -350,11 +353,14 @@ lowbit_gemv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const GemvParams
                         tmem_ld_x8(tmem_base + lane_off + (uint32_t)(256 + 16 * a), d);
                         tmem_wait_ld();
                         const int kb = e_kb[a];
+                        const float sv = sz_to_float(p.s ? e_s[a] : one_bits, sz16);
+                        const float zv = p.zp ? sz_to_float(e_z[a], sz16) : p.zp_const;
+                        (void)zc_bits;
 #pragma unroll
                         for (int r = 0; r < kTcMaxM; ++r) {
                             if (r < m) {
                                 const float dd = d[2 * r] + d[2 * r + 1];
-                                acc[r] = fmaf(e_s[a], dd - fmaf(e_z[a], xs[kb * m + r], cs[kb * m + r]), acc[r]);
+                                acc[r] = fmaf(sv, dd - fmaf(zv, xs[kb * m + r], cs[kb * m + r]), acc[r]);
                             }
                         }
                         if (e_last[a]) flush(e_tile[a]);
@@ -381,14 +387,10 @@ lowbit_gemv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const GemvParams
                         int grow = c_tile * kTcRows + row;
                         grow = grow < p.n ? grow : p.n - 1;
                         const int grp = p.kb_per_group_shift >= 0 ? (c_kb >> p.kb_per_group_shift) : c_kb / p.kb_per_group;
+                        // raw bits only: the loads complete while later units decode
                         const size_t sidx = (size_t)grow * p.n_groups + grp;
-                        if (p.flags & VSPEC_B200_F_SZ_F16) {
-                            e_s[a] = p.s ? __half2float(reinterpret_cast<const __half*>(p.s)[sidx]) : 1.0f;
-                            e_z[a] = p.zp ? __half2float(reinterpret_cast<const __half*>(p.zp)[sidx]) : p.zp_const;
-                        } else {
-                            e_s[a] = p.s ? reinterpret_cast<const float*>(p.s)[sidx] : 1.0f;
-                            e_z[a] = p.zp ? reinterpret_cast<const float*>(p.zp)[sidx] : p.zp_const;
-                        }
+                        e_s[a] = load_sz_raw(p.s, sidx, sz16);
+                        e_z[a] = load_sz_raw(p.zp, sidx, sz16);
                         e_kb[a] = c_kb;
                         e_tile[a] = c_tile;
                         e_last[a] = (c_kb == kbt - 1) || (i == n_units - 1);
