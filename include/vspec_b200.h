@@ -87,24 +87,28 @@ typedef struct VspecB200LinearArgs {
 size_t vspec_b200_lowbit_linear_workspace_bytes(size_t m, size_t n, size_t k, int flags);
 int vspec_b200_lowbit_linear(const VspecB200LinearArgs* args, void* stream);
 
-/* Reads and clears the flag a tensor-core GEMV raises when one of its bounded
- * waits gave up (1 = seen since the last call; the launch then left y
- * incomplete and returned its resources). */
+/* Reads and clears the flag a TMA-fed GEMV (ring or tcgen05 kernel) raises
+ * when one of its bounded waits gave up (1 = seen since the last call; the
+ * launch then left y incomplete and returned its resources). */
 int vspec_b200_gemv_timeout_flag(int* out_flag);
 
 /* Same contraction through the any-shape path only (testing / odd shapes). */
 int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* args, void* stream);
 
 /* Same contraction through an explicit kernel family:
- *   VSPEC_B200_PATH_AUTO    the dispatcher's choice
+ *   VSPEC_B200_PATH_AUTO    the dispatcher's choice (ring, else warp-MMA,
+ *                           else generic)
  *   VSPEC_B200_PATH_GENERIC any shape, one warp per output row
- *   VSPEC_B200_PATH_WARPMMA persistent split-K warp-MMA kernel (m <= 8)
+ *   VSPEC_B200_PATH_WARPMMA persistent split-K warp-MMA kernel, weights
+ *                           streamed through registers (m <= 8)
  *   VSPEC_B200_PATH_TCGEN05 TMA + TMEM + tcgen05.mma kernel (m <= 4)
+ *   VSPEC_B200_PATH_RING    TMA shared-memory ring + warp-MMA decode (m <= 8)
  * A fast path that does not support the shape returns VSPEC_B200_ERR_UNSUPPORTED. */
 #define VSPEC_B200_PATH_AUTO 0
 #define VSPEC_B200_PATH_GENERIC 1
 #define VSPEC_B200_PATH_WARPMMA 2
 #define VSPEC_B200_PATH_TCGEN05 3
+#define VSPEC_B200_PATH_RING 4
 int vspec_b200_lowbit_linear_path(const VspecB200LinearArgs* args, void* stream, int path);
 
 /* Decode every code of a packed [n][k] matrix into int8 [n][k] (bit-exact

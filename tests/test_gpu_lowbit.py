@@ -257,7 +257,7 @@ def test_workspace_too_small_is_rejected():
 
 
 
-FAST_PATHS = [V.PATH_WARPMMA, V.PATH_TCGEN05]
+FAST_PATHS = [V.PATH_WARPMMA, V.PATH_TCGEN05, V.PATH_RING]
 
 
 def test_tcgen05_path_smoke():
@@ -273,11 +273,27 @@ def test_tcgen05_path_smoke():
     assert rel_err(y, O.lowbit_matmul(x, w, n, k, 4, s, zp, g)) <= RTOL_F32
 
 
+def test_ring_path_smoke():
+    """One small launch of the TMA-ring kernel on its own."""
+    rng = np.random.default_rng(2)
+    m, n, k, g = 1, 256, 1024, 8
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = run_linear(x, w, s, zp, n, k, 4, g, path=V.PATH_RING)
+    flag = __import__("ctypes").c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(__import__("ctypes").byref(flag)), "timeout flag")
+    assert flag.value == 0
+    assert rel_err(y, O.lowbit_matmul(x, w, n, k, 4, s, zp, g)) <= RTOL_F32
+
+
 @pytest.mark.parametrize("path", FAST_PATHS)
 @pytest.mark.parametrize("bits", [2, 3, 4])
 @pytest.mark.parametrize("m,n,k,g", [(1, 4096, 4096, 32), (1, 1000, 2048, 16), (3, 384, 1024, 8), (4, 130, 512, 1),
-                                     (2, 12288, 4096, 32), (1, 200, 12288, 96)])
+                                     (2, 12288, 4096, 32), (1, 200, 12288, 96), (8, 640, 1024, 8),
+                                     (6, 300, 2048, 16)])
 def test_fast_paths_match_oracle(path, bits, m, n, k, g):
+    if path == V.PATH_TCGEN05 and m > 4:
+        pytest.skip("the tcgen05 GEMV takes m <= 4")
     rng = np.random.default_rng(path * 100 + bits * 10 + m + n + k)
     w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=(n % 2 == 0))
     x = rng.standard_normal((m, k)).astype(np.float32)

@@ -127,13 +127,19 @@ extern "C" int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* a, vo
 }
 
 extern "C" int vspec_b200_lowbit_linear_path(const VspecB200LinearArgs* a, void* stream, int path) {
-    if (path < kPathAuto || path > kPathTensorCore) { set_error("unknown path %d", path); return VSPEC_B200_ERR_ARG; }
+    if (path < kPathAuto || path > kPathRing) { set_error("unknown path %d", path); return VSPEC_B200_ERR_ARG; }
     return linear_common(a, stream, path);
 }
 
 extern "C" int vspec_b200_gemv_timeout_flag(int* out_flag) {
     if (!out_flag) { set_error("NULL out_flag"); return VSPEC_B200_ERR_ARG; }
-    return gemv_tc_read_and_clear_timeout(out_flag);
+    int a = 0, b = 0;
+    int rc = gemv_tc_read_and_clear_timeout(&a);
+    if (rc != VSPEC_B200_OK) return rc;
+    rc = gemv_ring_read_and_clear_timeout(&b);
+    if (rc != VSPEC_B200_OK) return rc;
+    *out_flag = (a || b) ? 1 : 0;
+    return VSPEC_B200_OK;
 }
 
 extern "C" size_t vspec_b200_lowbit_linear_workspace_bytes(size_t m, size_t n, size_t k, int flags) {

@@ -104,6 +104,14 @@ __device__ __forceinline__ void mma_16816_f16(float d[4], const uint32_t a[4], u
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1),
           "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
 }
+// D += A * B with D in place.
+__device__ __forceinline__ void mma_16816_f16_acc(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

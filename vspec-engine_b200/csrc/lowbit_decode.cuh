@@ -59,6 +59,35 @@ __host__ __device__ __forceinline__ float code_mult(int j) {
     return t < 4 ? ((t & 1) ? 128.0f : 16.0f) : ((t & 1) ? 8.0f : 1.0f);
 }
 
+// Exact reciprocal of code_mult (powers of two), without a division.
+template <int BITS>
+__host__ __device__ __forceinline__ float code_inv_mult(int j) {
+    if (BITS == 4) return (j & 1) ? 0.0625f : 1.0f;
+    if (BITS == 2) {
+        const int e = j & 3;
+        return e == 0 ? 1.0f : (e == 1 ? 0.25f : (e == 2 ? 0.0625f : 0.015625f));
+    }
+    const int t = j & 7;   // BITS == 3
+    return t < 4 ? ((t & 1) ? 0.0078125f : 0.0625f) : ((t & 1) ? 0.125f : 1.0f);
+}
+
+// Inverse of (lo_code, hi_code): fp16 pair q (0..15) and half (0: low fp16,
+// 1: high fp16) that carry code j (0..31) of a 32-code chunk.
+template <int BITS>
+__host__ __device__ __forceinline__ void code_slot(int j, int& q, int& half) {
+    if (BITS == 4) {
+        half = (j >> 2) & 1;
+        q = 4 * (j >> 3) + (j & 3);
+    } else if (BITS == 2) {
+        half = (j >> 3) & 1;
+        q = 8 * (j >> 4) + (j & 7);
+    } else {
+        half = (j >> 2) & 1;
+        const int b = j - 4 * half;
+        q = 2 * (2 * (b >> 3) + ((b >> 1) & 1)) + (b & 1);
+    }
+}
+
 // Pairs 2*mm and 2*mm+1 of a chunk (the A registers of MMA number mm) as raw
 // magic halves.  Two's-complement codes become offset codes by flipping every
 // field's top bit.  mm is a constant after loop unrolling.

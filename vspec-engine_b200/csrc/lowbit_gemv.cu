@@ -559,14 +559,16 @@ size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu) {
     size_t floats = sp.scratch_floats;
     const size_t tc = gemv_tc_scratch_floats(mm, n, k, swiglu);
     if (tc > floats) floats = tc;
+    const size_t ring = gemv_ring_scratch_floats(mm, n, k, swiglu);
+    if (ring > floats) floats = ring;
     return kGemvCounterBytes + floats * sizeof(float);
 }
 
-// VSPEC_B200_GEMV_TC=0 routes every shape to the warp-MMA kernel (A/B timing).
-static bool tc_path_enabled() {
+// VSPEC_B200_GEMV_RING=0 makes the dispatcher skip the ring kernel (A/B timing).
+static bool ring_path_enabled() {
     static int v = -1;
     if (v < 0) {
-        const char* e = getenv("VSPEC_B200_GEMV_TC");
+        const char* e = getenv("VSPEC_B200_GEMV_RING");
         v = (e && e[0] == '0') ? 0 : 1;
     }
     return v == 1;
@@ -661,7 +663,7 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
         if ((1 << sh) == p.kb_per_group) p.kb_per_group_shift = sh;
 
     const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
-    if (!fast && (path == kPathWarpMma || path == kPathTensorCore)) {
+    if (!fast && (path == kPathWarpMma || path == kPathTensorCore || path == kPathRing)) {
         set_error("shape not supported by the requested fast path");
         return VSPEC_B200_ERR_UNSUPPORTED;
     }
@@ -680,13 +682,21 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
         }
         p.counters = reinterpret_cast<int*>(ws);
         p.scratch = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kGemvCounterBytes);
-        const bool tc_ok = gemv_tc_supported(p, bits);
-        if (path == kPathTensorCore && !tc_ok) {
-            set_error("shape not supported by the tcgen05 GEMV (m <= 4, groups of 128*i, smem)");
-            return VSPEC_B200_ERR_UNSUPPORTED;
-        }
-        if (tc_ok && (path == kPathTensorCore || (path == kPathAuto && tc_path_enabled()))) {
+        if (path == kPathTensorCore) {
+            if (!gemv_tc_supported(p, bits)) {
+                set_error("shape not supported by the tcgen05 GEMV (m <= 4, groups of 128*i, smem)");
+                return VSPEC_B200_ERR_UNSUPPORTED;
+            }
             return gemv_tc_launch(p, bits, unsigned_codes, st, pdl_enabled());
+        }
+        if (path == kPathRing || path == kPathAuto) {
+            const bool ring_ok = gemv_ring_supported(p, bits, kGemvCounterSlots);
+            if (path == kPathRing && !ring_ok) {
+                set_error("shape not supported by the ring GEMV (m <= 8, groups of 128*i, smem, n)");
+                return VSPEC_B200_ERR_UNSUPPORTED;
+            }
+            if (ring_ok && (path == kPathRing || ring_path_enabled()))
+                return gemv_ring_launch(p, bits, unsigned_codes, st, pdl_enabled());
         }
         p.tiles = sp.tiles;
         p.total_warps = sp.total_warps;

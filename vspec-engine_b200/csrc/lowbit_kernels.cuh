@@ -29,6 +29,7 @@ struct GemvParams {
     int max_slots;           // partial slots per counter
     float* scratch;          // [counters][max_slots][16*m] fp32 partials
     int* counters;           // [counters], zero between launches
+    int stages;              // tcgen05 path: weight ring depth
 };
 
 constexpr int kEpiPlain = 0;
@@ -42,6 +43,7 @@ constexpr int kPathAuto = 0;
 constexpr int kPathGeneric = 1;
 constexpr int kPathWarpMma = 2;
 constexpr int kPathTensorCore = 3;
+constexpr int kPathRing = 4;
 int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int path,
                        void* workspace, size_t workspace_bytes);
 size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu);
@@ -50,6 +52,11 @@ bool gemv_tc_supported(const GemvParams& p, int bits);
 int gemv_tc_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl);
 size_t gemv_tc_scratch_floats(int m, int n, int k, bool swiglu);
 int gemv_tc_read_and_clear_timeout(int* out);
+// TMA ring + warp-MMA path (lowbit_gemv_ring.cu)
+bool gemv_ring_supported(const GemvParams& p, int bits, size_t counter_slots);
+int gemv_ring_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl);
+size_t gemv_ring_scratch_floats(int m, int n, int k, bool swiglu);
+int gemv_ring_read_and_clear_timeout(int* out);
 int unpack_codes_launch(const uint8_t* w, int n, int k, int bits, int unsigned_codes, int8_t* out, cudaStream_t st,
                         int use_fast_decoder);
 

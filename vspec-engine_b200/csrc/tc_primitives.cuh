@@ -37,11 +37,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
+// Same test, but a thread whose phase is not complete sleeps in hardware
+// until the phase completes or about `hint_ns` nanoseconds pass, instead of
+// spending issue slots on polls.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
 // Polls until the phase with `parity` completed, `*abort` becomes non-zero,
 // or `limit` polls pass.  Returns true on completion.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t limit) {
     for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+    }
+    return false;
+}
+// Bounded wait that sleeps between checks: at most `limit` checks of at most
+// ~hint_ns each.  Returns true on completion.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t limit,
+                                                uint32_t hint_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
         if (*abort) return false;
     }
     return false;
