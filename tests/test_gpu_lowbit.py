@@ -308,7 +308,7 @@ def test_fast_paths_match_oracle(path, bits, m, n, k, g):
 def test_fast_paths_fused_epilogues(path):
     rng = np.random.default_rng(70 + path)
     m, k, g = 3, 1024, 8
-    n = 256
+    n = 512   # SwiGLU halves of 256 rows fill one tile of every fast path
     w, s, zp = make_lowbit(rng, n, k, 4, g)
     x = rng.standard_normal((m, k)).astype(np.float32)
     res = rng.standard_normal((m, n)).astype(np.float32)

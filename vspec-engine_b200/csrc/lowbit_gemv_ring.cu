@@ -8,13 +8,16 @@
 //     y[i][j] = sum_t x[i][t] * (code(j,t) - zp[j][g(t)]) * s[j][g(t)]
 //
 // Layout of the work:
-//   * unit = (128-row tile of W, 128-code k-block); one persistent CTA per SM
-//     owns a contiguous run of units in tile-major order (split-K across CTAs);
+//   * unit = (tile of W, 128-code k-block), a tile being 256 rows for m <= 4
+//     and 128 rows for m <= 8; persistent CTAs (two per SM when the shared
+//     memory plan allows) own contiguous runs of units in tile-major order
+//     (split-K across CTAs);
 //   * warp 8 (one thread) streams the units' weight tiles with 2-D TMA into a
 //     deep shared-memory ring (8-48 stages, 60-190 KB in flight per SM), so
 //     HBM sees many outstanding bulk requests without register staging;
-//   * warps 0-7 each own a 16-row slice of every tile.  A thread (g, c) reads
-//     its 32-code chunk c of rows g and g+8 from the ring, decodes it in
+//   * warps 0-7 each own a 32-row (m <= 4) or 16-row slice of every tile,
+//     i.e. one or two blocks of 16 rows.  A thread (g, c) reads its 32-code
+//     chunk c of rows g and g+8 of each block from the ring, decodes it in
 //     registers into fp16 pairs (magic-number LOP3, see lowbit_decode.cuh) --
 //     the A fragments of mma.sync m16n8k16 -- and multiplies them with the
 //     activation fragments (fp32 x split into fp16 hi + lo) staged once in
@@ -25,13 +28,13 @@
 //   * each k-block's fp32 partial is scaled on the fly:
 //         acc += s * inv_scale * (dot - (zp * X + C)),
 //     X and C being the block's scaled activation sums (decode offsets);
-//   * at the end of a tile part a warp publishes its 16-row partial and bumps
+//   * at the end of a tile part a warp publishes its slice's partial and bumps
 //     the slice's counter; the warp that completes the count sums the slots in
 //     CTA order (deterministic), applies the epilogue (residual, SwiGLU,
 //     RMSNorm row factor) and resets the counter.  No warp waits on another.
-// The CTA fits two per SM when the shape allows, so the next launch in the
-// stream (programmatic dependent launch) becomes resident early and fills its
-// own ring while this one drains.  Every wait is bounded.
+// Every CTA triggers programmatic dependent launch at its start, so the next
+// launch in the stream becomes resident as soon as resources free up and
+// stages its weights before it waits for this one.  Every wait is bounded.
 #include "common.cuh"
 #include "lowbit_decode.cuh"
 #include "lowbit_kernels.cuh"
@@ -43,7 +46,6 @@
 
 namespace vb200 {
 
-constexpr int kRingRows = 128;
 constexpr int kRingConsumerWarps = 8;
 constexpr int kRingThreads = (kRingConsumerWarps + 1) * 32;
 constexpr int kRingProducerWarp = kRingConsumerWarps;
@@ -52,17 +54,23 @@ constexpr uint32_t kRingWaitLimit = 1u << 16;   // checks of up to kRingSleepNs 
 constexpr uint32_t kRingSleepNs = 20000;
 constexpr uint32_t kRingSmemShared = 113u * 1024u;
 constexpr uint32_t kRingSmemMax = 227u * 1024u;
+constexpr uint32_t kRingMinSharedRing = 64u * 1024u;   // ring worth sharing an SM for
+constexpr uint32_t kRingMaxRing = 192u * 1024u;
 
 template <int BITS> struct RingCfg;
-template <> struct RingCfg<4> { static constexpr int kRowBytes = 64; static constexpr int kMaxStages = 24; };
-template <> struct RingCfg<3> { static constexpr int kRowBytes = 48; static constexpr int kMaxStages = 32; };
-template <> struct RingCfg<2> { static constexpr int kRowBytes = 32; static constexpr int kMaxStages = 48; };
+template <> struct RingCfg<4> { static constexpr int kRowBytes = 64; };
+template <> struct RingCfg<3> { static constexpr int kRowBytes = 48; };
+template <> struct RingCfg<2> { static constexpr int kRowBytes = 32; };
 
 // Set when a bounded wait of the ring GEMV gave up.
 __device__ int g_ring_timeout = 0;
 
 __host__ __device__ __forceinline__ int ring_nt(int m) { return (2 * m + 7) / 8; }
 __host__ __device__ __forceinline__ int ring_lanes(int m) { return 4 * (2 * m < 8 ? 2 * m : 8); }
+// 16-row blocks per consumer warp: two when one n-tile of activations (m <= 4)
+// leaves the registers for it, so per-unit costs are shared by 32 rows.
+__host__ __device__ constexpr int ring_row_blocks(int nt) { return nt == 1 ? 2 : 1; }
+__host__ __device__ inline int ring_tile_rows(int m) { return 16 * ring_row_blocks(ring_nt(m)) * kRingConsumerWarps; }
 
 struct RingSmem {
     uint32_t frag;        // offsets from the 1024-aligned base; the ring starts at 0
@@ -74,7 +82,7 @@ struct RingSmem {
 template <int BITS>
 __host__ __device__ inline RingSmem ring_smem_plan(int m, int kbt, int stages) {
     RingSmem s;
-    const uint32_t stage = kRingRows * RingCfg<BITS>::kRowBytes;
+    const uint32_t stage = (uint32_t)ring_tile_rows(m) * RingCfg<BITS>::kRowBytes;
     s.frag = (uint32_t)stages * stage;
     const uint32_t fbytes = (uint32_t)kbt * 4u * (uint32_t)ring_nt(m) * (uint32_t)ring_lanes(m) * 16u;
     s.xs = s.frag + fbytes;
@@ -112,8 +120,10 @@ template <int BITS, int NT, bool UNSIGNED, int EPI, bool SZ16>
 __global__ void __launch_bounds__(kRingThreads, 2)
 lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ GemvParams p) {
     constexpr int RB = RingCfg<BITS>::kRowBytes;
-    constexpr uint32_t STAGE_BYTES = kRingRows * RB;
-    constexpr int PD = kRingScalePipe;
+    constexpr int RBW = ring_row_blocks(NT);          // 16-row blocks per consumer warp
+    constexpr int TROWS = 16 * RBW * kRingConsumerWarps;
+    constexpr uint32_t STAGE_BYTES = TROWS * RB;
+    constexpr int PD = kRingScalePipe / RBW;
     const int NS = p.stages;
 
     extern __shared__ unsigned char smem_raw[];
@@ -161,7 +171,7 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
         tma_prefetch_desc(&wmap);
         for (; p_issued < n_units && p_issued < NS; ++p_issued) {
             mbar_arrive_expect_tx(&full[p_issued], STAGE_BYTES);
-            tma_load_2d(wring + p_issued * STAGE_BYTES, &wmap, p_kb * RB, p_tile * kRingRows, &full[p_issued]);
+            tma_load_2d(wring + p_issued * STAGE_BYTES, &wmap, p_kb * RB, p_tile * TROWS, &full[p_issued]);
             if (++p_kb == kbt) { p_kb = 0; ++p_tile; }
         }
     }
@@ -283,47 +293,57 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
 
     if (warp < kRingConsumerWarps) {
         // ======================= consumer warps ===============================
+        // Warp w owns rows [w*16*RBW, (w+1)*16*RBW) of every tile: RBW blocks
+        // of 16 rows, thread (g, c) rows g and g+8 of each block, chunk c.
         const int g = lane >> 2;
         const int c = lane & 3;
-        const int rr0 = warp * 16 + g;       // rows of this thread inside a tile
+        const int wrow = warp * 16 * RBW;
         const bool lane_has_b = lane < lanes;
         const bool has_s = p.s != nullptr, has_zp = p.zp != nullptr;
         constexpr int SZB = SZ16 ? 2 : 4;   // bytes per scale / zero-point element
         const int half_tiles = p.tiles >> 1;
-        float acc[NT][2];
+        float acc[RBW][NT][2];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
+        for (int j = 0; j < RBW; ++j)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) acc[j][nt][0] = acc[j][nt][1] = 0.f;
 
         // scale / zero-point prefetch, PD units ahead, as raw bits.  Byte
-        // offsets of this thread's two rows in the current tile are kept and
-        // only re-derived at tile boundaries.
-        uint32_t sz[PD][4];
+        // offsets of this thread's rows in the current tile are kept and only
+        // re-derived at tile boundaries.
+        uint32_t sz[PD][RBW][4];
         int s_tile = u0 / kbt, s_kb = u0 - s_tile * kbt;
         const unsigned char* sb = reinterpret_cast<const unsigned char*>(p.s);
         const unsigned char* zb = reinterpret_cast<const unsigned char*>(p.zp);
-        size_t srow0 = 0, srow1 = 0;
+        size_t srow[RBW][2];
         auto set_srows = [&]() {
-            int r0 = s_tile * kRingRows + rr0, r1 = r0 + 8;
-            r0 = r0 < p.n ? r0 : p.n - 1;
-            r1 = r1 < p.n ? r1 : p.n - 1;
-            srow0 = (size_t)r0 * p.n_groups * SZB;
-            srow1 = (size_t)r1 * p.n_groups * SZB;
+#pragma unroll
+            for (int j = 0; j < RBW; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    int r = s_tile * TROWS + wrow + 16 * j + g + 8 * h;
+                    r = r < p.n ? r : p.n - 1;
+                    srow[j][h] = (size_t)r * p.n_groups * SZB;
+                }
         };
         set_srows();
         auto ld_sz = [&](const unsigned char* b, size_t off) -> uint32_t {
             if constexpr (SZ16) return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(b + off));
             else return __ldg(reinterpret_cast<const unsigned int*>(b + off));
         };
-        auto issue_sz = [&](uint32_t (&d)[4]) {
+        auto issue_sz = [&](uint32_t (&d)[RBW][4]) {
             const int grp = p.kb_per_group_shift >= 0 ? (s_kb >> p.kb_per_group_shift) : s_kb / p.kb_per_group;
             const uint32_t go = (uint32_t)grp * SZB;
-            if (has_s) {
-                d[0] = ld_sz(sb, srow0 + go);
-                d[2] = ld_sz(sb, srow1 + go);
-            }
-            if (has_zp) {
-                d[1] = ld_sz(zb, srow0 + go);
-                d[3] = ld_sz(zb, srow1 + go);
+#pragma unroll
+            for (int j = 0; j < RBW; ++j) {
+                if (has_s) {
+                    d[j][0] = ld_sz(sb, srow[j][0] + go);
+                    d[j][2] = ld_sz(sb, srow[j][1] + go);
+                }
+                if (has_zp) {
+                    d[j][1] = ld_sz(zb, srow[j][0] + go);
+                    d[j][3] = ld_sz(zb, srow[j][1] + go);
+                }
             }
             if (++s_kb == kbt) {
                 s_kb = 0;
@@ -341,6 +361,7 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
         bool ok = true;
 
         auto flush = [&](int tile) {
+            constexpr int WR = 16 * RBW;   // rows of this warp's slice
             auto first_cta = [&](long long u) { return (int)(((u + 1) * C - 1) / U); };
             int L = tile;
             int slot = (int)blockIdx.x - first_cta((long long)tile * kbt);
@@ -358,16 +379,18 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                 total = g_n + u_n;
                 slot = up ? g_n + ((int)blockIdx.x - u_fw) : ((int)blockIdx.x - g_fw);
             }
-            const int ci = L * kRingConsumerWarps + warp;   // counter of this 16-row slice
-            float* part = p.scratch + ((size_t)ci * p.max_slots + slot) * (16 * m);
+            const int ci = L * kRingConsumerWarps + warp;   // counter of this warp's slice
+            float* part = p.scratch + ((size_t)ci * p.max_slots + slot) * (WR * m);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int r = 4 * nt + c;
-                if (r < m) {
-                    part[r * 16 + g] = acc[nt][0];
-                    part[r * 16 + g + 8] = acc[nt][1];
+            for (int j = 0; j < RBW; ++j)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int r = 4 * nt + c;
+                    if (r < m) {
+                        part[r * WR + 16 * j + g] = acc[j][nt][0];
+                        part[r * WR + 16 * j + g + 8] = acc[j][nt][1];
+                    }
                 }
-            }
             __threadfence();
             __syncwarp();
             int old = 0;
@@ -375,21 +398,21 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             old = __shfl_sync(0xffffffffu, old, 0);
             if (old == total - 1) {
                 __threadfence();
-                const float* sbase = p.scratch + (size_t)ci * p.max_slots * (16 * m);
-                for (int z = lane; z < 16 * m; z += 32) {
-                    const int r = z >> 4, i = z & 15;
+                const float* sbase = p.scratch + (size_t)ci * p.max_slots * (WR * m);
+                for (int z = lane; z < WR * m; z += 32) {
+                    const int r = z / WR, i = z - r * WR;
                     const float nr = rms ? row_norm[r] : 1.0f;
-                    const int orow = L * kRingRows + warp * 16 + i;
+                    const int orow = L * TROWS + wrow + i;
                     if (EPI == kEpiSwiGLU) {
                         float gs = 0.f, us = 0.f;
-                        for (int s = 0; s < n_gate; ++s) gs += __ldcg(sbase + (size_t)s * 16 * m + z);
-                        for (int s = n_gate; s < total; ++s) us += __ldcg(sbase + (size_t)s * 16 * m + z);
+                        for (int s = 0; s < n_gate; ++s) gs += __ldcg(sbase + (size_t)s * WR * m + z);
+                        for (int s = n_gate; s < total; ++s) us += __ldcg(sbase + (size_t)s * WR * m + z);
                         gs *= nr;
                         us *= nr;
                         if (orow < (p.n >> 1)) p.y[(size_t)r * (p.n >> 1) + orow] = gs / (1.0f + expf(-gs)) * us;
                     } else {
                         float sum = 0.f;
-                        for (int s = 0; s < total; ++s) sum += __ldcg(sbase + (size_t)s * 16 * m + z);
+                        for (int s = 0; s < total; ++s) sum += __ldcg(sbase + (size_t)s * WR * m + z);
                         sum *= nr;
                         if (orow < p.n) {
                             const size_t o = (size_t)r * p.n + orow;
@@ -401,7 +424,9 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                 if (lane == 0) p.counters[ci] = 0;
             }
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
+            for (int j = 0; j < RBW; ++j)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) acc[j][nt][0] = acc[j][nt][1] = 0.f;
         };
 
         for (int b0 = 0; ok && b0 < n_units; b0 += PD) {
@@ -413,16 +438,20 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                         ok = false;
                     } else {
                         const unsigned char* stg = wring + (size_t)ring * STAGE_BYTES;
-                        Chunk<BITS> ch0, ch1;
-                        lds_chunk<BITS>(ch0, stg + ring_chunk_offset<BITS>(rr0, c));
-                        lds_chunk<BITS>(ch1, stg + ring_chunk_offset<BITS>(rr0 + 8, c));
+                        Chunk<BITS> ch[RBW][2];
+#pragma unroll
+                        for (int j = 0; j < RBW; ++j) {
+                            lds_chunk<BITS>(ch[j][0], stg + ring_chunk_offset<BITS>(wrow + 16 * j + g, c));
+                            lds_chunk<BITS>(ch[j][1], stg + ring_chunk_offset<BITS>(wrow + 16 * j + g + 8, c));
+                        }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&empty[ring]);
                         if (++ring == NS) { ring = 0; ring_ph ^= 1u; }
 
                         const int kb = c_kb;
                         const uint4* fb = frag + (size_t)kb * 4 * NT * lanes;
-                        float d[2][NT][4];   // even / odd MMAs accumulate apart (shorter chains)
+                        // per row block, even / odd MMAs accumulate apart (shorter chains)
+                        float d[RBW][2][NT][4];
 #pragma unroll
                         for (int mp = 0; mp < 4; ++mp) {
                             uint4 bb[NT];
@@ -434,26 +463,33 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
 #pragma unroll
                             for (int hf = 0; hf < 2; ++hf) {
                                 const int mm = 2 * mp + hf;
-                                uint32_t a[4];
-                                unpack_mm<BITS, UNSIGNED>(ch0, mm, a[0], a[2]);
-                                unpack_mm<BITS, UNSIGNED>(ch1, mm, a[1], a[3]);
 #pragma unroll
-                                for (int nt = 0; nt < NT; ++nt) {
-                                    const uint32_t b0r = hf ? bb[nt].z : bb[nt].x;
-                                    const uint32_t b1r = hf ? bb[nt].w : bb[nt].y;
-                                    if (mp == 0) {
-                                        const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
-                                        mma_16816_f16(d[hf][nt], a, b0r, b1r, zero4);
-                                    } else {
-                                        mma_16816_f16_acc(d[hf][nt], a, b0r, b1r);
+                                for (int j = 0; j < RBW; ++j) {
+                                    uint32_t a[4];
+                                    unpack_mm<BITS, UNSIGNED>(ch[j][0], mm, a[0], a[2]);
+                                    unpack_mm<BITS, UNSIGNED>(ch[j][1], mm, a[1], a[3]);
+#pragma unroll
+                                    for (int nt = 0; nt < NT; ++nt) {
+                                        const uint32_t b0r = hf ? bb[nt].z : bb[nt].x;
+                                        const uint32_t b1r = hf ? bb[nt].w : bb[nt].y;
+                                        if (mp == 0) {
+                                            const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+                                            mma_16816_f16(d[j][hf][nt], a, b0r, b1r, zero4);
+                                        } else {
+                                            mma_16816_f16_acc(d[j][hf][nt], a, b0r, b1r);
+                                        }
                                     }
                                 }
                             }
                         }
-                        const float s0 = has_s ? sz_to_float(sz[st][0], SZ16) : 1.0f;
-                        const float s1 = has_s ? sz_to_float(sz[st][2], SZ16) : 1.0f;
-                        const float z0 = has_zp ? sz_to_float(sz[st][1], SZ16) : p.zp_const;
-                        const float z1 = has_zp ? sz_to_float(sz[st][3], SZ16) : p.zp_const;
+                        float sv[RBW][2], zv[RBW][2];
+#pragma unroll
+                        for (int j = 0; j < RBW; ++j) {
+                            sv[j][0] = has_s ? sz_to_float(sz[st][j][0], SZ16) : 1.0f;
+                            sv[j][1] = has_s ? sz_to_float(sz[st][j][2], SZ16) : 1.0f;
+                            zv[j][0] = has_zp ? sz_to_float(sz[st][j][1], SZ16) : p.zp_const;
+                            zv[j][1] = has_zp ? sz_to_float(sz[st][j][3], SZ16) : p.zp_const;
+                        }
                         if (i + PD < n_units) issue_sz(sz[st]);
 #pragma unroll
                         for (int nt = 0; nt < NT; ++nt) {
@@ -462,10 +498,13 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                                 const float xsum = xs[kb * m + r];
                                 const float coff = cs[kb * m + r];
                                 const float inv = isc[kb * m + r];
-                                const float e0 = (d[0][nt][0] + d[1][nt][0]) + (d[0][nt][1] + d[1][nt][1]);
-                                const float e1 = (d[0][nt][2] + d[1][nt][2]) + (d[0][nt][3] + d[1][nt][3]);
-                                acc[nt][0] = fmaf(s0 * inv, e0 - fmaf(z0, xsum, coff), acc[nt][0]);
-                                acc[nt][1] = fmaf(s1 * inv, e1 - fmaf(z1, xsum, coff), acc[nt][1]);
+#pragma unroll
+                                for (int j = 0; j < RBW; ++j) {
+                                    const float e0 = (d[j][0][nt][0] + d[j][1][nt][0]) + (d[j][0][nt][1] + d[j][1][nt][1]);
+                                    const float e1 = (d[j][0][nt][2] + d[j][1][nt][2]) + (d[j][0][nt][3] + d[j][1][nt][3]);
+                                    acc[j][nt][0] = fmaf(sv[j][0] * inv, e0 - fmaf(zv[j][0], xsum, coff), acc[j][nt][0]);
+                                    acc[j][nt][1] = fmaf(sv[j][1] * inv, e1 - fmaf(zv[j][1], xsum, coff), acc[j][nt][1]);
+                                }
                             }
                         }
                         if (++c_kb == kbt || i + 1 == n_units) {
@@ -494,7 +533,7 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                 break;
             }
             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_2d(wring + (size_t)s * STAGE_BYTES, &wmap, p_kb * RB, p_tile * kRingRows, &full[s]);
+            tma_load_2d(wring + (size_t)s * STAGE_BYTES, &wmap, p_kb * RB, p_tile * TROWS, &full[s]);
             if (++p_kb == kbt) { p_kb = 0; ++p_tile; }
             if (++s == NS) { s = 0; ph ^= 1u; }
         }
@@ -514,15 +553,17 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
 // the deepest ring one CTA can hold.  0 when not even 4 stages fit.
 template <int BITS>
 static int ring_pick_stages(int m, int kbt, size_t* smem_bytes) {
-    const uint32_t stage = kRingRows * RingCfg<BITS>::kRowBytes + 16u;
-    const uint32_t fixed = ring_smem_plan<BITS>(m, kbt, 0).total + 1024u;
+    const uint32_t sbytes = (uint32_t)ring_tile_rows(m) * RingCfg<BITS>::kRowBytes;
+    const uint32_t stage = sbytes + 16u;   // ring bytes + 2 barriers
+    const uint32_t fixed = ring_smem_plan<BITS>(m, kbt, 0).total + 1024u;   // + base alignment
+    const int max_ns = (int)(kRingMaxRing / sbytes);
     int ns = fixed < kRingSmemShared ? (int)((kRingSmemShared - fixed) / stage) : 0;
-    if (ns > RingCfg<BITS>::kMaxStages) ns = RingCfg<BITS>::kMaxStages;
-    if (ns < 8) {
+    if (ns > max_ns) ns = max_ns;
+    if ((uint32_t)ns * sbytes < kRingMinSharedRing) {
         ns = fixed < kRingSmemMax ? (int)((kRingSmemMax - fixed) / stage) : 0;
-        if (ns > RingCfg<BITS>::kMaxStages) ns = RingCfg<BITS>::kMaxStages;
+        if (ns > max_ns) ns = max_ns;
     }
-    if (ns < 4) return 0;
+    if (ns < 3) return 0;
     *smem_bytes = ring_smem_plan<BITS>(m, kbt, ns).total + 1024u;
     return ns;
 }
@@ -555,7 +596,8 @@ static RingPlan ring_plan(int m, int n, int k, int bits, bool swiglu) {
     RingPlan rp;
     memset(&rp, 0, sizeof(rp));
     const int kbt = k / 128;
-    rp.tiles = (n + kRingRows - 1) / kRingRows;
+    const int trows = ring_tile_rows(m);
+    rp.tiles = (n + trows - 1) / trows;
     const long long U = (long long)rp.tiles * kbt;
     rp.stages = ring_stages_for(bits, m, kbt, &rp.smem);
     // two CTAs per SM only when the shared-memory plan lets them co-reside
@@ -568,7 +610,7 @@ static RingPlan ring_plan(int m, int n, int k, int bits, bool swiglu) {
     if (per_tile > rp.grid) per_tile = rp.grid;
     rp.max_slots = swiglu ? 2 * per_tile : per_tile;
     const int logical = swiglu ? rp.tiles / 2 : rp.tiles;
-    rp.scratch_floats = (size_t)logical * kRingConsumerWarps * rp.max_slots * 16 * m;
+    rp.scratch_floats = (size_t)logical * kRingConsumerWarps * rp.max_slots * (trows / kRingConsumerWarps) * m;
     return rp;
 }
 
@@ -579,8 +621,9 @@ bool gemv_ring_supported(const GemvParams& p, int bits, size_t counter_slots) {
     if ((size_t)p.row_bytes % 16 != 0) return false;   // TMA global stride
     if ((p.flags & VSPEC_B200_F_RMSNORM) && reinterpret_cast<uintptr_t>(p.norm_w) % 16 != 0) return false;
     const bool swiglu = (p.flags & VSPEC_B200_F_SWIGLU) != 0;
-    if (swiglu && ((p.n / 2) % kRingRows != 0)) return false;
-    const int tiles = (p.n + kRingRows - 1) / kRingRows;
+    const int trows = ring_tile_rows(p.m);
+    if (swiglu && ((p.n / 2) % trows != 0)) return false;
+    const int tiles = (p.n + trows - 1) / trows;
     const int logical = swiglu ? tiles / 2 : tiles;
     if ((size_t)logical * kRingConsumerWarps > counter_slots) return false;
     size_t smem = 0;
@@ -667,7 +710,7 @@ int gemv_ring_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st
     const CUtensorMapSwizzle swz = bits == 4 ? CU_TENSOR_MAP_SWIZZLE_64B
                                  : (bits == 2 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE);
     const int box = bits == 4 ? RingCfg<4>::kRowBytes : (bits == 3 ? RingCfg<3>::kRowBytes : RingCfg<2>::kRowBytes);
-    const int rc = make_row_tile_map(&map, p.w, p.n, p.row_bytes, box, kRingRows, swz);
+    const int rc = make_row_tile_map(&map, p.w, p.n, p.row_bytes, box, ring_tile_rows(p.m), swz);
     if (rc != VSPEC_B200_OK) return rc;
     p.tiles = rp.tiles;
     p.max_slots = rp.max_slots;
