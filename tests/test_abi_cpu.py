@@ -114,3 +114,36 @@ def test_reference_bridges_fail_closed_on_bad_input():
     stats = [ctypes.c_uint64() for _ in range(6)]
     assert V.lib.vspec_cuda_int4_cached_stats_bridge(*[ctypes.byref(s) for s in stats]) == 1
     assert stats[2].value >= 1   # the failed cached call counted as a miss
+
+
+def test_reference_python_bridge_binds_library(tmp_path):
+    """The reference's unmodified ctypes bridge (Vspec-chat/python/vspec_cuda_bridge.py)
+    loads <root>/build/vspec_cuda_bridge.dll with root = parents[2] of the module
+    (vspec_cuda_bridge.py:9-31).  A symlink to this library there must satisfy
+    every unconditional binding at import and every optional hasattr probe on the
+    path (the ANF hybrid bridge is not part of it)."""
+    import shutil
+    import subprocess
+    import sys
+    ref = os.environ.get("VSPEC_REFERENCE", "/root/reference")
+    src = os.path.join(ref, "Vspec-chat", "python", "vspec_cuda_bridge.py")
+    if not os.path.exists(src):
+        pytest.skip("reference tree not present")
+    pkg = tmp_path / "vspec" / "Vspec-chat" / "python"
+    pkg.mkdir(parents=True)
+    (tmp_path / "vspec" / "build").mkdir()
+    shutil.copy(src, pkg / "vspec_cuda_bridge.py")
+    os.symlink(V.LIB_PATH, tmp_path / "vspec" / "build" / "vspec_cuda_bridge.dll")
+    names = ["_HAS_FUSED_INT4", "_HAS_FUSED_INT3", "_HAS_INT4_REGISTERED", "_HAS_INT4_REGISTERED_MANY",
+             "_HAS_INT4_CACHED_STATS", "_HAS_GEMM_DISPATCH", "_HAS_FUSED_ATTN", "_HAS_FLASH_ATTN",
+             "_HAS_DEVICE_CAP", "_HAS_INT4_TENSORCORE", "_HAS_FUSED_HYBRID"]
+    code = ("import vspec_cuda_bridge as b; print(b._lib is not None, "
+            + ", ".join(f"b.{n}" for n in names) + ")")
+    env = dict(os.environ, PYTHONPATH=str(pkg))
+    out = subprocess.run([sys.executable, "-c", code], cwd=str(tmp_path), env=env, capture_output=True,
+                         text=True, timeout=120)
+    assert out.returncode == 0, out.stderr[-2000:]
+    got = dict(zip(["loaded"] + names, out.stdout.split()))
+    assert got.pop("loaded") == "True"
+    assert got.pop("_HAS_FUSED_HYBRID") == "False"
+    assert all(v == "True" for v in got.values()), got
