@@ -92,6 +92,20 @@ int vspec_b200_lowbit_linear(const VspecB200LinearArgs* args, void* stream);
  * launch then left y incomplete and returned its resources). */
 int vspec_b200_gemv_timeout_flag(int* out_flag);
 
+/* Same contraction with scratch the library never allocates: a static 16 MiB
+ * device array per device (no counterpart in the reference).  For callers that
+ * cannot allow a device allocation inside the call: a runtime whose arena/pool
+ * allocator owns the device memory, or a decode loop that must not stall on
+ * the synchronising cudaFree/cudaMalloc of a growing library workspace.
+ * args->d_workspace must be NULL and workspace_bytes 0; shapes whose
+ * vspec_b200_lowbit_linear_workspace_bytes() exceeds 16 MiB return
+ * VSPEC_B200_ERR_ARG.  The first call on a device (that device current) looks
+ * up the array with cudaGetSymbolAddress: make it before any stream capture.
+ * The array's 64 KiB counter region is zero at module load and every launch
+ * leaves it zero.  One array per device: overlapping calls on a device (other
+ * streams, threads, concurrent graph replays) race; order them on one stream. */
+int vspec_b200_lowbit_linear_static(const VspecB200LinearArgs* args, void* stream);
+
 /* Same contraction through the any-shape path only (testing / odd shapes). */
 int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* args, void* stream);
 
