@@ -253,6 +253,71 @@ def time_e2e_bridge(torch, V, copies: int, steps: int, warmup: int, world: int):
     return ms, bytes_per_call, k * 4, n * 4
 
 
+ATTN_B, ATTN_HQ, ATTN_HKV, ATTN_D, ATTN_PT = 32, 32, 8, 128, 16
+
+
+def make_config3(torch, seed: int = 3):
+    """B=32, Hq=32, Hkv=8, d=128, ctx ~U[512,8192], 16-token
+    pages of fp16 K/V ~N(0,1), page table = seeded permutation of the shared pool."""
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(512, 8193, size=ATTN_B).astype(np.int32)
+    need = (ctx + ATTN_PT - 1) // ATTN_PT
+    total = int(need.sum())
+    perm = rng.permutation(total).astype(np.int32)
+    table = np.zeros((ATTN_B, int(need.max())), dtype=np.int32)
+    off = 0
+    for b, nb in enumerate(need):
+        table[b, :nb] = perm[off:off + nb]
+        off += nb
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    shape = (total, ATTN_PT, ATTN_HKV, ATTN_D)
+    kp = torch.randn(shape, device="cuda", dtype=torch.float16, generator=g)
+    vp = torch.randn(shape, device="cuda", dtype=torch.float16, generator=g)
+    q = torch.randn((ATTN_B, ATTN_HQ, ATTN_D), device="cuda", dtype=torch.float32, generator=g)
+    return ctx, table, total, kp, vp, q
+
+
+def time_attention(torch, V, steps: int, warmup: int, world: int):
+    """Paged GQA decode attention over config 3 (K+V ~570 MB per step, >> L2)."""
+    ctx, table, total, kp, vp, q = make_config3(torch)
+    dt = torch.from_numpy(table).cuda()
+    dc = torch.from_numpy(ctx).cuda()
+    out = torch.empty((ATTN_B, ATTN_HQ, ATTN_D), device="cuda", dtype=torch.float32)
+    stream = torch.cuda.Stream()
+    scale = 1.0 / float(np.sqrt(ATTN_D))
+
+    def call(st):
+        V.paged_attention(q.data_ptr(), kp.data_ptr(), vp.data_ptr(), dt.data_ptr(), dc.data_ptr(), out.data_ptr(),
+                          ATTN_B, ATTN_HQ, ATTN_HKV, ATTN_D, ATTN_PT, table.shape[1], total, int(ctx.max()), scale,
+                          V.KV_F16, stream=st)
+
+    with torch.cuda.stream(stream):
+        call(stream.cuda_stream)          # library scratch set up before capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        call(stream.cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    del graph
+    kv_bytes = int(ctx.astype(np.int64).sum()) * ATTN_HKV * ATTN_D * 2 * 2
+    other = q.numel() * 4 + out.numel() * 4 + table.size * 4 + ctx.size * 4
+    return ms, kv_bytes, other
+
+
 # ------------------------------------------------------------------ CPU legs
 def cpu_oracle_sample(seconds: float = 10.0) -> dict:
     """The oracle restatement (group-wise int4, one thread) on a bounded sample
@@ -357,6 +422,8 @@ def main() -> None:
 
     ms4, clocks = time_gemv_graph(torch, V, 4, args.copies, args.steps, args.warmup, world, sampler)
     ms3, _ = time_gemv_graph(torch, V, 3, args.copies, args.steps, args.warmup, world)
+    attn_steps = max(3, args.steps // 5)
+    attn_ms, attn_kv, attn_other = time_attention(torch, V, attn_steps, args.warmup, world)
     e2e_steps = max(3, args.steps // 5)
     e2e_ms, e2e_bytes_call, h2d_call, d2h_call = time_e2e_bridge(torch, V, args.copies, e2e_steps, 2, world)
 
@@ -396,9 +463,15 @@ def main() -> None:
         "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d_call * args.copies,
                 "d2h_bytes_per_step": d2h_call * args.copies,
                 "api": "vspec_cuda_fused_linear_int4_cached_bridge (host x / host y per call, fp32 s+zp)"},
+        "attention": {"value": round(world * attn_steps * (attn_kv + attn_other) / (attn_ms * 1e-3) / 1e9, 2),
+                      "unit": "GB/s", "ms_per_step": round(attn_ms / attn_steps, 4),
+                      "frac": round((attn_kv + attn_other) / (attn_ms * 1e-3 / attn_steps) / 1e9 / peak, 4),
+                      "kv_bytes_per_step": attn_kv,
+                      "config": "config 3: B=32 Hq=32 Hkv=8 d=128, ctx ~U[512,8192] (seeded), 16-token fp16 pages, "
+                                "page table = seeded permutation of the pool, one step = one decode-attention call"},
         "cpu_baseline": cpu,
         "clocks": clocks,
-        "gpu_launches": launches * 2,
+        "gpu_launches": launches * 2 + attn_steps * 2,
     }
     print(json.dumps(line))
 

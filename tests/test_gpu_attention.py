@@ -179,3 +179,43 @@ def test_reference_host_attention_entry_points():
     refh = O.paged_attention(qh.reshape(1, h, d), kc, vc, np.zeros((1, 1), np.int32), np.array([t], np.int32), h, h,
                              d, t, 1.0 / np.sqrt(d), f64=True).reshape(-1)
     assert rel_err(outh, refh) <= RTOL_F32
+
+
+def test_config3_full_size_sampled_sequences():
+    """BASELINE config 3 at full size (B=32, Hq=32, Hkv=8, d=128, ctx ~U[512,8192],
+    16-token fp16 pages, page table = seeded permutation of the shared pool):
+    every output is finite, and the shortest, the longest and one more sequence
+    match the f64 oracle (run on just those sequences' pages)."""
+    torch = torch_cuda()
+    rng = np.random.default_rng(33)
+    b, hq, hkv, d, pt = 32, 32, 8, 128, 16
+    ctx = rng.integers(512, 8193, size=b).astype(np.int32)
+    need = (ctx + pt - 1) // pt
+    total = int(need.sum())
+    perm = rng.permutation(total).astype(np.int32)
+    table = np.zeros((b, int(need.max())), dtype=np.int32)
+    off = 0
+    for i, nb in enumerate(need):
+        table[i, :nb] = perm[off:off + nb]
+        off += nb
+    g = torch.Generator(device="cuda")
+    g.manual_seed(33)
+    kp = torch.randn((total, pt, hkv, d), device="cuda", dtype=torch.float16, generator=g)
+    vp = torch.randn((total, pt, hkv, d), device="cuda", dtype=torch.float16, generator=g)
+    q = rng.standard_normal((b, hq, d)).astype(np.float32)
+    dq, dt, dc = to_dev(q), to_dev(table), to_dev(ctx)
+    out = empty_dev((b, hq, d), torch.float32)
+    out.fill_(float("nan"))
+    scale = 1.0 / np.sqrt(d)
+    V.paged_attention(dq.data_ptr(), kp.data_ptr(), vp.data_ptr(), dt.data_ptr(), dc.data_ptr(), out.data_ptr(), b,
+                      hq, hkv, d, pt, table.shape[1], total, int(ctx.max()), scale, V.KV_F16)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    for i in sorted({int(np.argmin(ctx)), int(np.argmax(ctx)), 7}):
+        pages = torch.from_numpy(table[i, :need[i]].astype(np.int64)).cuda()
+        ks = kp[pages].float().cpu().numpy()
+        vs = vp[pages].float().cpu().numpy()
+        small = np.arange(need[i], dtype=np.int32)[None, :]
+        ref = O.paged_attention(q[i:i + 1], ks, vs, small, ctx[i:i + 1], hq, hkv, d, pt, scale, f64=True)
+        assert rel_err(got[i], ref[0]) <= RTOL_F32, (i, int(ctx[i]))

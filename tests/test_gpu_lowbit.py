@@ -322,3 +322,18 @@ def test_fast_paths_fused_epilogues(path):
     gate, up = full[:, : n // 2], full[:, n // 2:]
     y = run_linear(x, w, s, zp, n, k, 4, g, flags=V.F_SWIGLU, out_cols=n // 2, path=path)
     assert rel_err(y, gate / (1.0 + np.exp(-gate)) * up) <= RTOL_F32
+
+
+def test_large_n_beyond_tile_counters():
+    """More output tiles than split-K counters (the fixed 16384-slot region):
+    automatic dispatch stays correct (the any-shape kernel runs) and the
+    explicit warp-MMA path refuses the shape instead of overrunning them."""
+    rng = np.random.default_rng(77)
+    m, n, k, g, bits = 5, 270000, 128, 1, 4
+    w, s, zp = make_lowbit(rng, n, k, bits, g)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = run_linear(x, w, s, zp, n, k, bits, g)
+    ref = x.astype(np.float64) @ dequant_np(w, n, k, bits, s, zp, g).T
+    assert rel_err(y, ref) <= RTOL_F32
+    with pytest.raises(V.VspecB200Error, match="not supported"):
+        run_linear(x, w, s, zp, n, k, bits, g, path=V.PATH_WARPMMA)

@@ -683,7 +683,7 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
         p.counters = reinterpret_cast<int*>(ws);
         p.scratch = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kGemvCounterBytes);
         if (path == kPathTensorCore) {
-            if (!gemv_tc_supported(p, bits)) {
+            if (!gemv_tc_supported(p, bits, kGemvCounterSlots)) {
                 set_error("shape not supported by the tcgen05 GEMV (m <= 4, groups of 128*i, smem)");
                 return VSPEC_B200_ERR_UNSUPPORTED;
             }

@@ -562,8 +562,11 @@ static int tc_stages_for(int bits, int m, int kbt, size_t* smem_bytes) {
     return tc_pick_stages<2>(m, kbt, smem_bytes);
 }
 
-bool gemv_tc_supported(const GemvParams& p, int bits) {
+bool gemv_tc_supported(const GemvParams& p, int bits, size_t counter_slots) {
     if (p.m < 1 || p.m > kTcMaxM) return false;
+    const int tiles = (p.n + kTcRows - 1) / kTcRows;
+    const int logical = (p.flags & VSPEC_B200_F_SWIGLU) ? tiles / 2 : tiles;
+    if ((size_t)logical > counter_slots) return false;
     if (p.k % 128 != 0 || p.n_groups < 1 || p.k % p.n_groups != 0 || (p.k / p.n_groups) % 128 != 0) return false;
     if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || reinterpret_cast<uintptr_t>(p.x) % 16 != 0) return false;
     if ((p.flags & VSPEC_B200_F_RMSNORM) && reinterpret_cast<uintptr_t>(p.norm_w) % 16 != 0) return false;

@@ -48,7 +48,7 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
                        void* workspace, size_t workspace_bytes);
 size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu);
 // tcgen05 / TMA path (lowbit_gemv_tc.cu)
-bool gemv_tc_supported(const GemvParams& p, int bits);
+bool gemv_tc_supported(const GemvParams& p, int bits, size_t counter_slots);
 int gemv_tc_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl);
 size_t gemv_tc_scratch_floats(int m, int n, int k, bool swiglu);
 int gemv_tc_read_and_clear_timeout(int* out);
