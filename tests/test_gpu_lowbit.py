@@ -5,7 +5,7 @@ import pytest
 
 import oracle as O
 import vspec_b200 as V
-from gpu_util import RTOL_F32, dequant_np, empty_dev, make_lowbit, rel_err, to_dev, torch_cuda
+from gpu_util import RTOL_BF16, RTOL_F32, dequant_np, empty_dev, make_lowbit, rel_err, to_dev, torch_cuda
 
 pytestmark = pytest.mark.gpu
 
@@ -337,3 +337,55 @@ def test_large_n_beyond_tile_counters():
     assert rel_err(y, ref) <= RTOL_F32
     with pytest.raises(V.VspecB200Error, match="not supported"):
         run_linear(x, w, s, zp, n, k, bits, g, path=V.PATH_WARPMMA)
+
+
+# ---------------------------------------------------------------- tcgen05 GEMM (m > 8)
+def test_gemm_tcgen05_smoke():
+    """One small launch of the tcgen05 GEMM on its own (fp16 operands, tolerance RTOL_BF16)."""
+    rng = np.random.default_rng(5)
+    m, n, k, g = 16, 128, 128, 1
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = run_linear(x, w, s, zp, n, k, 4, g, path=V.PATH_TCGEN05)
+    flag = __import__("ctypes").c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(__import__("ctypes").byref(flag)), "timeout flag")
+    assert flag.value == 0
+    ref = x.astype(np.float64) @ dequant_np(w, n, k, 4, s, zp, g).T
+    err = rel_err(y, ref)
+    print(f"gemm smoke err {err:.3e}")
+    assert err <= RTOL_BF16
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("m,n,k,g", [(16, 256, 512, 4), (64, 1024, 2048, 16), (130, 384, 1024, 8),
+                                     (512, 4096, 4096, 32)])
+def test_gemm_tcgen05_matches_oracle(bits, m, n, k, g):
+    rng = np.random.default_rng(900 + bits * 10 + m)
+    w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=(m == 64))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = run_linear(x, w, s, zp, n, k, bits, g)
+    ref = x.astype(np.float64) @ dequant_np(w, n, k, bits, s.astype(np.float32), zp.astype(np.float32), g).T
+    err = rel_err(y, ref)
+    print(f"gemm bits={bits} m={m} n={n} k={k}: {err:.3e}")
+    assert err <= RTOL_BF16
+
+
+def test_gemm_tcgen05_unsigned_and_fused_epilogues():
+    rng = np.random.default_rng(919)
+    m, n, k, g = 48, 512, 1024, 8
+    w, s, _ = make_lowbit(rng, n, k, 4, g, sz_f16=True, zp_mode="none")
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    deq = dequant_np(w, n, k, 4, s.astype(np.float32), None, g, unsigned=True, zp_const=8.0)
+    full = x.astype(np.float64) @ deq.T
+    y = run_linear(x, w, s, None, n, k, 4, g, flags=V.F_UNSIGNED, zp_const=8.0)
+    assert rel_err(y, full) <= RTOL_BF16
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    y = run_linear(x, w, s, None, n, k, 4, g, flags=V.F_UNSIGNED | V.F_RESIDUAL, zp_const=8.0, residual=res)
+    assert rel_err(y, full + res) <= RTOL_BF16
+    nw = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    xh = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6) * nw
+    y = run_linear(x, w, s, None, n, k, 4, g, flags=V.F_UNSIGNED | V.F_RMSNORM, zp_const=8.0, norm_w=nw, eps=1e-6)
+    assert rel_err(y, xh @ deq.T) <= RTOL_BF16
+    gate, up = full[:, : n // 2], full[:, n // 2:]
+    y = run_linear(x, w, s, None, n, k, 4, g, flags=V.F_UNSIGNED | V.F_SWIGLU, zp_const=8.0, out_cols=n // 2)
+    assert rel_err(y, gate / (1.0 + np.exp(-gate)) * up) <= RTOL_BF16

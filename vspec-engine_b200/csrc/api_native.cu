@@ -100,21 +100,6 @@ static int linear_common(const VspecB200LinearArgs* a, void* stream, int path) {
     p.flags = a->flags;
     const int uns = (a->flags & VSPEC_B200_F_UNSIGNED) ? 1 : 0;
     cudaStream_t st = (cudaStream_t)stream;
-    if (p.m > kGemvMaxM) {
-        // Row-blocks of at most kGemvMaxM activations (the tcgen05 GEMM takes
-        // over large m where it applies; this keeps every m correct).
-        for (int i0 = 0; i0 < p.m; i0 += kGemvMaxM) {
-            GemvParams q = p;
-            q.m = (p.m - i0) < kGemvMaxM ? (p.m - i0) : kGemvMaxM;
-            q.x = p.x + (size_t)i0 * p.k;
-            const size_t out_cols = (a->flags & VSPEC_B200_F_SWIGLU) ? (size_t)p.n / 2 : (size_t)p.n;
-            q.y = p.y + (size_t)i0 * out_cols;
-            if (p.residual) q.residual = p.residual + (size_t)i0 * p.n;
-            int rc = lowbit_gemv_launch(q, a->bits, uns, st, path, a->d_workspace, a->workspace_bytes);
-            if (rc != VSPEC_B200_OK) return rc;
-        }
-        return VSPEC_B200_OK;
-    }
     return lowbit_gemv_launch(p, a->bits, uns, st, path, a->d_workspace, a->workspace_bytes);
 }
 
@@ -133,12 +118,14 @@ extern "C" int vspec_b200_lowbit_linear_path(const VspecB200LinearArgs* a, void*
 
 extern "C" int vspec_b200_gemv_timeout_flag(int* out_flag) {
     if (!out_flag) { set_error("NULL out_flag"); return VSPEC_B200_ERR_ARG; }
-    int a = 0, b = 0;
+    int a = 0, b = 0, c = 0;
     int rc = gemv_tc_read_and_clear_timeout(&a);
     if (rc != VSPEC_B200_OK) return rc;
     rc = gemv_ring_read_and_clear_timeout(&b);
     if (rc != VSPEC_B200_OK) return rc;
-    *out_flag = (a || b) ? 1 : 0;
+    rc = gemm_tc_read_and_clear_timeout(&c);
+    if (rc != VSPEC_B200_OK) return rc;
+    *out_flag = (a || b || c) ? 1 : 0;
     return VSPEC_B200_OK;
 }
 

@@ -12,7 +12,7 @@ namespace vb200 {
 // codes (lo_code(q), hi_code(q)).
 // -------------------------------------------------------------------------
 template <int BITS>
-__host__ __device__ __forceinline__ int lo_code(int q) {
+__host__ __device__ constexpr int lo_code(int q) {
     if (BITS == 4) return 8 * (q >> 2) + (q & 3);
     if (BITS == 2) return 16 * (q >> 3) + (q & 7);
     // BITS == 3: window w = q/2 starts at code j(w) in {0,2,8,10,16,18,24,26}
@@ -21,7 +21,7 @@ __host__ __device__ __forceinline__ int lo_code(int q) {
     return j + (q & 1);
 }
 template <int BITS>
-__host__ __device__ __forceinline__ int hi_code(int q) {
+__host__ __device__ constexpr int hi_code(int q) {
     if (BITS == 4) return lo_code<4>(q) + 4;
     if (BITS == 2) return lo_code<2>(q) + 8;
     return lo_code<3>(q) + 4;
@@ -52,7 +52,7 @@ constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
 // the matching activation by mult and removes sum(x * (1024/mult + 2^(bits-1)))
 // per k-block, so no fp16 arithmetic is spent on decoding.
 template <int BITS>
-__host__ __device__ __forceinline__ float code_mult(int j) {
+__host__ __device__ constexpr float code_mult(int j) {
     if (BITS == 4) return (j & 1) ? 16.0f : 1.0f;
     if (BITS == 2) return (float)(1 << (2 * (j & 3)));
     const int t = j & 7;   // BITS == 3

@@ -561,7 +561,22 @@ size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu) {
     if (tc > floats) floats = tc;
     const size_t ring = gemv_ring_scratch_floats(mm, n, k, swiglu);
     if (ring > floats) floats = ring;
-    return kGemvCounterBytes + floats * sizeof(float);
+    size_t bytes = kGemvCounterBytes + floats * sizeof(float);
+    if (m > kGemvMaxM) {
+        const size_t gemm = kGemvCounterBytes + gemm_tc_workspace_bytes(m, n, k, swiglu);
+        if (gemm > bytes) bytes = gemm;
+    }
+    return bytes;
+}
+
+// VSPEC_B200_GEMM=0 makes the dispatcher run m > 8 as row blocks of the GEMV.
+static bool gemm_path_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_GEMM");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
 }
 
 // VSPEC_B200_GEMV_RING=0 makes the dispatcher skip the ring kernel (A/B timing).
@@ -661,6 +676,42 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
     p.kb_per_group_shift = -1;
     for (int sh = 0; sh < 31; ++sh)
         if ((1 << sh) == p.kb_per_group) p.kb_per_group_shift = sh;
+
+    if (p.m > kGemvMaxM) {
+        // large m: the tcgen05 GEMM where it applies, else row blocks of the GEMV
+        if (!force_generic && (path == kPathTensorCore || (path == kPathAuto && gemm_path_enabled())) &&
+            gemm_tc_supported(p, bits, kGemvCounterSlots)) {
+            const size_t need = kGemvCounterBytes + gemm_tc_workspace_bytes(p.m, p.n, p.k, swiglu);
+            void* ws = workspace;
+            if (ws) {
+                if (workspace_bytes < need) {
+                    set_error("GEMM workspace too small (%zu < %zu)", workspace_bytes, need);
+                    return VSPEC_B200_ERR_ARG;
+                }
+            } else {
+                ws = gemv_managed_ws(need);
+                if (!ws) { set_error("cannot allocate %zu bytes of GEMM workspace", need); return VSPEC_B200_ERR_NOMEM; }
+            }
+            p.counters = reinterpret_cast<int*>(ws);
+            return gemm_tc_launch(p, bits, unsigned_codes, st, reinterpret_cast<char*>(ws) + kGemvCounterBytes);
+        }
+        if (path == kPathTensorCore) {
+            set_error("shape not supported by the tcgen05 GEMM (k %% 128 == 0, groups of 128*i, n/2 %% 128 == 0 "
+                      "with SwiGLU)");
+            return VSPEC_B200_ERR_UNSUPPORTED;
+        }
+        const size_t out_cols = swiglu ? (size_t)p.n / 2 : (size_t)p.n;
+        for (int i0 = 0; i0 < p.m; i0 += kGemvMaxM) {
+            GemvParams q = p;
+            q.m = (p.m - i0) < kGemvMaxM ? (p.m - i0) : kGemvMaxM;
+            q.x = p.x + (size_t)i0 * p.k;
+            q.y = p.y + (size_t)i0 * out_cols;
+            if (p.residual) q.residual = p.residual + (size_t)i0 * p.n;
+            const int rc = lowbit_gemv_launch(q, bits, unsigned_codes, st, path, workspace, workspace_bytes);
+            if (rc != VSPEC_B200_OK) return rc;
+        }
+        return VSPEC_B200_OK;
+    }
 
     const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
     if (!fast && (path == kPathWarpMma || path == kPathTensorCore || path == kPathRing)) {

@@ -57,6 +57,11 @@ bool gemv_ring_supported(const GemvParams& p, int bits, size_t counter_slots);
 int gemv_ring_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl);
 size_t gemv_ring_scratch_floats(int m, int n, int k, bool swiglu);
 int gemv_ring_read_and_clear_timeout(int* out);
+// tcgen05 GEMM for m > kGemvMaxM (lowbit_gemm_tc.cu)
+bool gemm_tc_supported(const GemvParams& p, int bits, size_t counter_slots);
+size_t gemm_tc_workspace_bytes(int m, int n, int k, bool swiglu);
+int gemm_tc_launch(const GemvParams& p, int bits, int unsigned_codes, cudaStream_t st, void* work);
+int gemm_tc_read_and_clear_timeout(int* out);
 int unpack_codes_launch(const uint8_t* w, int n, int k, int bits, int unsigned_codes, int8_t* out, cudaStream_t st,
                         int use_fast_decoder);
 

@@ -115,7 +115,32 @@ __device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, float (&v)[8]) {
                  : "memory");
 }
 
+// 32 lanes x 16 consecutive columns.
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, float (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7]),
+                   "=f"(v[8]), "=f"(v[9]), "=f"(v[10]), "=f"(v[11]), "=f"(v[12]), "=f"(v[13]), "=f"(v[14]), "=f"(v[15])
+                 : "r"(taddr)
+                 : "memory");
+}
+
 // ---------------------------------------------------------------- MMA
+// Shared-memory descriptor of a K-major operand tile written by TMA with
+// 128-byte swizzle: rows of 128 bytes (64 fp16), 8-row groups 1024 bytes
+// apart (stride byte offset), leading byte offset unused (encoded as 16 B),
+// descriptor version 1, layout type 2 (SWIZZLE_128B) in bits [61,64).  The
+// tile must start on a 1024-byte boundary; the K-th 16-element step inside a
+// 64-element row is addressed by adding 32*step bytes to the start address.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;                 // LBO = 16 B (ignored for swizzled K-major)
+    d |= (uint64_t)(1024u >> 4) << 32;       // SBO = 1024 B
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
 // Shared-memory matrix descriptor (sm_100 UMMA format): start >> 4 in bits
 // [0,14), leading byte offset >> 4 in [16,30), stride byte offset >> 4 in
 // [32,46), descriptor version 1 in [46,48), layout type (0 = no swizzle) in [61,64).
