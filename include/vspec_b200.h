@@ -217,6 +217,68 @@ int vspec_b200_debug_fail_alloc_after(int n);
 /* Device properties used by the dispatch (filled on first use). */
 int vspec_b200_device_info(int* sm_count, int* cc_major, int* cc_minor, size_t* smem_per_block_optin);
 
+/* ------------------------------------------------------------------------
+ * Decode-step kernels (no reference counterpart as kernels: the reference
+ * runs this glue in numpy, Vspec-chat/python/runtime_inference.py:1297-1311,
+ * 554-567).  Device pointers, async on `stream`.
+ * ------------------------------------------------------------------------ */
+/* x[b][:] = fp16 table[tok[b]][:] widened to fp32. */
+int vspec_b200_decode_embed(const void* d_table_f16, const int32_t* d_tok, int batch, int hidden, float* d_x,
+                            void* stream);
+/* qkv [batch][(hq + 2 hkv) * head_dim] -> per-head RMSNorm of q and k (weights
+ * [head_dim]), half-split rotary at position pos[b] (inv_freq = theta^(-i/(d/2))),
+ * q to d_q_out [batch][hq][head_dim]; k and v appended as fp16 at slot
+ * pos % page_tokens of page page_table[b][pos / page_tokens] ([P][page_tokens]
+ * [hkv][head_dim] pools); ctx_len[b] = pos[b] + 1. */
+int vspec_b200_decode_qk_rope_append(const float* d_qkv, const float* d_q_norm, const float* d_k_norm,
+                                     const int32_t* d_pos, int batch, int hq, int hkv, int head_dim, float eps,
+                                     float theta, float* d_q_out, void* d_k_pages, void* d_v_pages,
+                                     const int32_t* d_page_table, int max_pages, int page_tokens, int32_t* d_ctx_len,
+                                     void* stream);
+/* Next token per sequence: the prompt's token at pos+1 while the prompt lasts,
+ * else the argmax of the logits cleaned like _stabilize_logits (NaN -> 0,
+ * clip to +-clip; ties -> lowest index); recorded at out_tokens[b][pos+1];
+ * pos[b] += 1. */
+int vspec_b200_decode_next_token(const float* d_logits, int batch, int vocab, float clip, const int32_t* d_prompt,
+                                 const int32_t* d_prompt_len, int max_prompt, int32_t* d_pos, int32_t* d_tok,
+                                 int32_t* d_out_tokens, int max_steps, void* stream);
+/* Seeded fill: kind 0 uniform bytes, 1 fp16 uniform in [lo, hi), 2 fp32 constant lo. */
+int vspec_b200_random_fill(void* d_dst, size_t count, int kind, uint64_t seed, float lo, float hi, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Qwen3-shape low-bit decode loop, random-init weights.
+ * Host C driving the kernels above, the low-bit linears (RMSNorm / SwiGLU /
+ * residual fused) and the paged attention; one decode step = one CUDA graph.
+ * Linear weights: packed `bits`-bit codes (unsigned reading, mid-range
+ * zero-point), fp16 group scales (group 128) -- the engine's int4 layout.
+ * ------------------------------------------------------------------------ */
+typedef struct VspecB200QwenConfig {
+    int num_layers, hidden, num_heads, num_kv_heads, head_dim, intermediate, vocab;
+    int bits;          /* 4, 3 or 2 */
+    int group;         /* codes per scale group along k (multiple of 128) */
+    float rms_eps, rope_theta, logit_clip;
+    int page_tokens;
+} VspecB200QwenConfig;
+
+int vspec_b200_qwen_create(const VspecB200QwenConfig* cfg, uint64_t seed, int max_batch, int max_ctx,
+                           void** out_model);
+void vspec_b200_qwen_destroy(void* model);
+/* Prompt prefill (one decode step per prompt token) and greedy generation for
+ * `batch` sequences.  h_prompts [batch][prompt_len]; h_tokens_out
+ * [batch][prompt_len + gen_tokens] receives the prompt followed by the
+ * generated tokens.  *out_gen_ms (optional) = device time of the steps that
+ * produced the gen_tokens tokens.  h_logits_out (optional) receives the
+ * logits of every step, [steps][batch][vocab] with steps = prompt_len +
+ * gen_tokens - 1. */
+int vspec_b200_qwen_generate(void* model, int batch, const int32_t* h_prompts, int prompt_len, int gen_tokens,
+                             int32_t* h_tokens_out, float* out_gen_ms, float* h_logits_out);
+/* Device tensors of the model, for checking against a host oracle:
+ * kind 0 embedding fp16 [vocab][hidden]; per layer 1/2 qkv codes/scales,
+ * 3/4 o-proj, 5/6 gate+up (gate rows first), 7/8 down; 9/10 lm_head
+ * codes/scales.  Norm weights are all ones.  Returns the byte size, copies
+ * it to h_dst when h_dst is not NULL (0 on error). */
+size_t vspec_b200_qwen_tensor(void* model, int kind, int layer, void* h_dst);
+
 #ifdef __cplusplus
 }
 #endif

@@ -337,3 +337,170 @@ void oracle_int3_blocknorm_f32(const float* a, size_t m, size_t k, const uint8_t
         }
     }
 }
+
+/* ------------------------------------------------------------------------
+ * fp16 rounding (round to nearest, ties to even; subnormals and overflow to
+ * infinity handled), used where the engine stores fp16.
+ * ------------------------------------------------------------------------ */
+uint16_t oracle_float_to_half(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+    const uint32_t absx = x & 0x7FFFFFFFu;
+    if (absx >= 0x7F800000u) return (uint16_t)(sign | (absx > 0x7F800000u ? 0x7E00u : 0x7C00u));
+    const int e = (int)(absx >> 23) - 127;
+    if (e > 15) return (uint16_t)(sign | 0x7C00u);
+    if (e >= -14) {
+        /* normal: keep 10 mantissa bits, round the 13 dropped bits */
+        uint32_t mant = absx & 0x7FFFFFu;
+        uint32_t h = ((uint32_t)(e + 15) << 10) | (mant >> 13);
+        const uint32_t rem = mant & 0x1FFFu;
+        if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h += 1u;   /* may carry into the exponent: fine */
+        return (uint16_t)(sign | h);
+    }
+    if (e < -25) return sign;
+    /* subnormal: value = mant_full * 2^(e-23), in units of 2^-24 */
+    const uint32_t mant_full = (absx & 0x7FFFFFu) | 0x800000u;
+    const int shift = -e - 14 + 13;   /* 14..24 */
+    uint32_t h = mant_full >> shift;
+    const uint32_t rem = mant_full & ((1u << shift) - 1u);
+    const uint32_t halfway = 1u << (shift - 1);
+    if (rem > halfway || (rem == halfway && (h & 1u))) h += 1u;
+    return (uint16_t)(sign | h);
+}
+
+/* ------------------------------------------------------------------------
+ * Qwen3-shape decode (test oracle; see oracle.h for the reference lines).
+ * ------------------------------------------------------------------------ */
+static void oq_rmsnorm(const float* x, int n, float eps, float* out) {
+    double ss = 0.0;
+    for (int i = 0; i < n; ++i) ss += (double)x[i] * (double)x[i];
+    const float inv = (float)(1.0 / sqrt(ss / (double)n + (double)eps));
+    for (int i = 0; i < n; ++i) out[i] = x[i] * inv;   /* weight = 1 */
+}
+
+/* y[n] = sum_t x[t] * (u(n,t) - 2^(bits-1)) * s[n][t / group], double accumulate */
+static void oq_linear(const float* x, int k, const uint8_t* w, const uint16_t* s, int n, int bits, int group, float* y) {
+    const size_t rb = oracle_row_bytes((size_t)k, bits);
+    const int groups = k / group;
+    const int off = 1 << (bits - 1);
+    for (int j = 0; j < n; ++j) {
+        const uint8_t* row = w + (size_t)j * rb;
+        double acc = 0.0;
+        for (int g = 0; g < groups; ++g) {
+            const double sc = (double)oracle_half_to_float(s[(size_t)j * groups + g]);
+            double part = 0.0;
+            for (int t = g * group; t < (g + 1) * group; ++t) {
+                /* unsigned field: the two's-complement reading plus 2^(bits-1), mod 2^bits */
+                const int code = oracle_get_code(row, (size_t)t, bits);
+                const int u = (code + (1 << bits)) & ((1 << bits) - 1);
+                part += (double)x[t] * (double)(u - off);
+            }
+            acc += part * sc;
+        }
+        y[j] = (float)acc;
+    }
+}
+
+int oracle_qwen_generate(const OracleQwen* q, const int32_t* prompt, int prompt_len, int gen, int32_t* tokens_out,
+                         float* logits_out) {
+    const int H = q->hidden, hq = q->heads, hkv = q->kv_heads, d = q->head_dim, I = q->inter, V = q->vocab;
+    const int qdim = hq * d, qkvn = qdim + 2 * hkv * d;
+    const int total = prompt_len + gen;
+    const int steps = total - 1;
+    float* x = (float*)malloc(sizeof(float) * H);
+    float* xn = (float*)malloc(sizeof(float) * (H > I ? H : I));
+    float* qkv = (float*)malloc(sizeof(float) * qkvn);
+    float* att = (float*)malloc(sizeof(float) * qdim);
+    float* tmp = (float*)malloc(sizeof(float) * (H > 2 * I ? H : 2 * I));
+    float* hbuf = (float*)malloc(sizeof(float) * I);
+    float* logits = (float*)malloc(sizeof(float) * V);
+    float* scores = (float*)malloc(sizeof(float) * total);
+    /* fp16 K/V cache [layers][total][hkv][d] */
+    uint16_t* kc = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)q->layers * total * hkv * d);
+    uint16_t* vc = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)q->layers * total * hkv * d);
+    if (!x || !xn || !qkv || !att || !tmp || !hbuf || !logits || !scores || !kc || !vc) return -1;
+    for (int i = 0; i < prompt_len; ++i) tokens_out[i] = prompt[i];
+    int tok = prompt[0];
+    const int half = d / 2;
+    for (int pos = 0; pos < steps; ++pos) {
+        for (int i = 0; i < H; ++i) x[i] = oracle_half_to_float(q->emb[(size_t)tok * H + i]);
+        for (int l = 0; l < q->layers; ++l) {
+            const uint8_t* const* W = q->w + (size_t)l * 4;
+            const uint16_t* const* S = q->s + (size_t)l * 4;
+            oq_rmsnorm(x, H, q->eps, xn);
+            oq_linear(xn, H, W[0], S[0], qkvn, q->bits, q->group, qkv);
+            /* per-head RMSNorm of q and k, rotary, cache k and v as fp16 */
+            for (int h = 0; h < hq + hkv; ++h) {
+                float* v = qkv + (size_t)h * d;
+                float nv[256];
+                oq_rmsnorm(v, d, q->eps, nv);
+                for (int t = 0; t < d; ++t) {
+                    const int i = t < half ? t : t - half;
+                    const float inv_freq = 1.0f / powf(q->theta, (float)i / (float)half);
+                    const float ang = (float)pos * inv_freq;
+                    const float cs = cosf(ang), sn = sinf(ang);
+                    v[t] = t < half ? nv[t] * cs - nv[t + half] * sn : nv[t - half] * sn + nv[t] * cs;
+                }
+                if (h >= hq) {
+                    uint16_t* dst = kc + (((size_t)l * total + pos) * hkv + (h - hq)) * d;
+                    for (int t = 0; t < d; ++t) dst[t] = oracle_float_to_half(v[t]);
+                }
+            }
+            for (int h = 0; h < hkv; ++h) {
+                const float* v = qkv + (size_t)(hq + hkv + h) * d;
+                uint16_t* dst = vc + (((size_t)l * total + pos) * hkv + h) * d;
+                for (int t = 0; t < d; ++t) dst[t] = oracle_float_to_half(v[t]);
+            }
+            /* GQA attention over positions 0..pos (flash_stub math) */
+            const int group = hq / hkv;
+            const float scale = 1.0f / sqrtf((float)d);
+            for (int h = 0; h < hq; ++h) {
+                const int kh = h / group;
+                const float* qh = qkv + (size_t)h * d;
+                float mx = -INFINITY;
+                for (int t = 0; t <= pos; ++t) {
+                    const uint16_t* kr = kc + (((size_t)l * total + t) * hkv + kh) * d;
+                    double dot = 0.0;
+                    for (int e = 0; e < d; ++e) dot += (double)qh[e] * (double)oracle_half_to_float(kr[e]);
+                    scores[t] = (float)dot * scale;
+                    if (scores[t] > mx) mx = scores[t];
+                }
+                double sum = 0.0;
+                for (int t = 0; t <= pos; ++t) { scores[t] = expf(scores[t] - mx); sum += scores[t]; }
+                for (int e = 0; e < d; ++e) {
+                    double o = 0.0;
+                    for (int t = 0; t <= pos; ++t)
+                        o += (double)scores[t] * (double)oracle_half_to_float(vc[(((size_t)l * total + t) * hkv + kh) * d + e]);
+                    att[(size_t)h * d + e] = (float)(o / sum);
+                }
+            }
+            oq_linear(att, qdim, W[1], S[1], H, q->bits, q->group, tmp);
+            for (int i = 0; i < H; ++i) x[i] += tmp[i];
+            oq_rmsnorm(x, H, q->eps, xn);
+            oq_linear(xn, H, W[2], S[2], 2 * I, q->bits, q->group, tmp);
+            for (int i = 0; i < I; ++i) {
+                const float g = tmp[i], u = tmp[I + i];
+                hbuf[i] = g / (1.0f + expf(-g)) * u;
+            }
+            oq_linear(hbuf, I, W[3], S[3], H, q->bits, q->group, tmp);
+            for (int i = 0; i < H; ++i) x[i] += tmp[i];
+        }
+        oq_rmsnorm(x, H, q->eps, xn);
+        oq_linear(xn, H, q->w_lm, q->s_lm, V, q->bits, q->group, logits);
+        if (logits_out) memcpy(logits_out + (size_t)pos * V, logits, sizeof(float) * V);
+        int best = 0;
+        float bv = -INFINITY;
+        for (int j = 0; j < V; ++j) {
+            float v = logits[j];
+            if (v != v) v = 0.f;
+            v = v > q->clip ? q->clip : (v < -q->clip ? -q->clip : v);
+            if (v > bv) { bv = v; best = j; }
+        }
+        const int nxt = (pos + 1 < prompt_len) ? prompt[pos + 1] : best;
+        tokens_out[pos + 1] = nxt;
+        tok = nxt;
+    }
+    free(x); free(xn); free(qkv); free(att); free(tmp); free(hbuf); free(logits); free(scores); free(kc); free(vc);
+    return 0;
+}

@@ -49,6 +49,48 @@ for _n, (_a, _r) in _o.items():
     _f.argtypes = _a
     _f.restype = _r
 
+
+class OracleQwenC(ctypes.Structure):
+    _fields_ = [("layers", ctypes.c_int), ("hidden", ctypes.c_int), ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("inter", ctypes.c_int), ("vocab", ctypes.c_int), ("bits", ctypes.c_int),
+                ("group", ctypes.c_int), ("eps", ctypes.c_float), ("theta", ctypes.c_float), ("clip", ctypes.c_float),
+                ("emb", c_void_p), ("w", c_void_p), ("s", c_void_p), ("w_lm", c_void_p), ("s_lm", c_void_p)]
+
+
+ORACLE.oracle_qwen_generate.argtypes = [ctypes.POINTER(OracleQwenC), c_void_p, ctypes.c_int, ctypes.c_int, c_void_p,
+                                        c_void_p]
+ORACLE.oracle_qwen_generate.restype = ctypes.c_int
+ORACLE.oracle_float_to_half.argtypes = [c_float]
+ORACLE.oracle_float_to_half.restype = ctypes.c_uint16
+
+
+def qwen_generate(cfg: dict, tensors: dict, prompt, gen: int):
+    """Greedy decode of one sequence with the C restatement (oracle_qwen_generate).
+    tensors: 'emb' (fp16 bits), per layer 'w{l}_{i}' / 's{l}_{i}' (i = 0 qkv, 1 o,
+    2 gate+up, 3 down), 'w_lm', 's_lm' as numpy arrays.  Returns (tokens, logits)."""
+    L = cfg["num_layers"]
+    keep = []
+
+    def ptr(a):
+        a = np.ascontiguousarray(a)
+        keep.append(a)
+        return a.ctypes.data
+    wp = (c_void_p * (4 * L))(*[ptr(tensors[f"w{l}_{i}"]) for l in range(L) for i in range(4)])
+    sp = (c_void_p * (4 * L))(*[ptr(tensors[f"s{l}_{i}"]) for l in range(L) for i in range(4)])
+    q = OracleQwenC(L, cfg["hidden"], cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"], cfg["intermediate"],
+                    cfg["vocab"], cfg["bits"], cfg["group"], cfg["rms_eps"], cfg["rope_theta"], cfg["logit_clip"],
+                    ptr(tensors["emb"]), ctypes.cast(wp, c_void_p), ctypes.cast(sp, c_void_p), ptr(tensors["w_lm"]),
+                    ptr(tensors["s_lm"]))
+    prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+    total = prompt.size + gen
+    toks = np.zeros(total, dtype=np.int32)
+    logits = np.zeros((total - 1, cfg["vocab"]), dtype=np.float32)
+    rc = ORACLE.oracle_qwen_generate(ctypes.byref(q), prompt.ctypes.data, prompt.size, gen, toks.ctypes.data,
+                                     logits.ctypes.data)
+    if rc != 0:
+        raise RuntimeError("oracle_qwen_generate failed")
+    return toks, logits
+
 if REF is not None:
     _r = {
         "vspec_quant_packed_bytes": ([c_size_t, ctypes.c_uint8], c_size_t),

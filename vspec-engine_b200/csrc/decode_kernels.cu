@@ -1,0 +1,204 @@
+// decode_kernels.cu -- the small per-token kernels of a Qwen3-shape decode step
+// (everything between the low-bit linears and the paged attention):
+//   * token embedding lookup;
+//   * per-head q/k RMSNorm + half-split rotary embedding + append of k and v
+//     (fp16) into the paged KV pools, and the context length update
+//     (Vspec-chat/python/runtime_inference.py:1297-1311: q/k RMSNorm, then
+//      q1*cos - q2*sin, q1*sin + q2*cos on the two halves, inv_freq =
+//      theta^(-i/(d/2)), runtime_inference.py:4227);
+//   * greedy next token: logits cleaned like _stabilize_logits
+//     (runtime_inference.py:554-567: NaN -> 0, +-inf -> +-clip, clip to
+//     +-clip; the entropy/margin steps never change the argmax), argmax with
+//     the lowest index on ties, or the next prompt token while the prompt lasts;
+//   * seeded random initialisation of packed weights, scales and fp16
+//     tensors (random-init model of the benchmark; no checkpoint exists).
+// Positions live in device memory so a captured decode step replays as is.
+#include "common.cuh"
+
+#include <stdint.h>
+
+#include "vspec_b200.h"
+
+namespace vb200 {
+
+__global__ void embed_kernel(const __half* __restrict__ table, const int32_t* __restrict__ tok, int hidden,
+                             float* __restrict__ x) {
+    const int b = blockIdx.y;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < hidden) x[(size_t)b * hidden + t] = __half2float(table[(size_t)tok[b] * hidden + t]);
+}
+
+// One block per (head, sequence): heads [0, hq) are query heads, [hq, hq+hkv)
+// key heads, [hq+hkv, hq+2hkv) value heads.  blockDim.x = head_dim (<= 256).
+__global__ void qk_norm_rope_append_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
+                                           const float* __restrict__ k_norm, const int32_t* __restrict__ pos,
+                                           int hq, int hkv, int d, float eps, float theta, float* __restrict__ q_out,
+                                           __half* __restrict__ k_pages, __half* __restrict__ v_pages,
+                                           const int32_t* __restrict__ page_table, int max_pages, int page_tokens,
+                                           int32_t* __restrict__ ctx_len) {
+    __shared__ float vals[256];
+    __shared__ float red[8];
+    const int h = blockIdx.x;
+    const int b = blockIdx.y;
+    const int t = threadIdx.x;
+    const int row = (hq + 2 * hkv) * d;
+    const float v = qkv[(size_t)b * row + (size_t)h * d + t];
+    const int p = pos[b];
+    const int page = page_table[(size_t)b * max_pages + p / page_tokens];
+    const int slot = p % page_tokens;
+    if (h >= hq + hkv) {
+        // value head: straight into the page
+        const int kvh = h - hq - hkv;
+        v_pages[(((size_t)page * page_tokens + slot) * hkv + kvh) * d + t] = __float2half_rn(v);
+        return;
+    }
+    // RMSNorm over the head
+    float ss = warp_sum(v * v);
+    if ((t & 31) == 0) red[t >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
+    for (int w = 0; w < (d + 31) / 32; ++w) ss += red[w];
+    const bool is_q = h < hq;
+    const float nw = is_q ? q_norm[t] : k_norm[t];
+    const float y = v / sqrtf(ss / (float)d + eps) * nw;
+    vals[t] = y;
+    __syncthreads();
+    // rotary, half split
+    const int half = d / 2;
+    const int i = t < half ? t : t - half;
+    const float inv_freq = 1.0f / powf(theta, (float)i / (float)half);
+    float sn, cs;
+    sincosf((float)p * inv_freq, &sn, &cs);
+    const float r = t < half ? vals[t] * cs - vals[t + half] * sn : vals[t - half] * sn + vals[t] * cs;
+    if (is_q) {
+        q_out[((size_t)b * hq + h) * d + t] = r;
+    } else {
+        const int kvh = h - hq;
+        k_pages[(((size_t)page * page_tokens + slot) * hkv + kvh) * d + t] = __float2half_rn(r);
+        if (kvh == 0 && t == 0) ctx_len[b] = p + 1;
+    }
+}
+
+// One block per sequence: next token (prompt or greedy argmax), position + 1.
+__global__ void __launch_bounds__(1024) next_token_kernel(const float* __restrict__ logits, int vocab, float clip,
+                                                          const int32_t* __restrict__ prompt, const int32_t* __restrict__ prompt_len,
+                                                          int max_prompt, int32_t* __restrict__ pos, int32_t* __restrict__ tok,
+                                                          int32_t* __restrict__ out_tokens, int max_steps) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const int b = blockIdx.x;
+    const float* lg = logits + (size_t)b * vocab;
+    float best = -INFINITY;
+    int besti = 0x7fffffff;
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+        float v = lg[j];
+        if (isnan(v)) v = 0.f;
+        v = fminf(fmaxf(v, -clip), clip);
+        if (v > best) { best = v; besti = j; }   // j ascends per thread: first index kept
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti, off);
+        if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = best; bi[threadIdx.x >> 5] = besti; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (bv[w] > best || (bv[w] == best && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
+        const int p = pos[b];
+        const int nxt = (p + 1 < prompt_len[b]) ? prompt[(size_t)b * max_prompt + p + 1] : besti;
+        tok[b] = nxt;
+        if (p + 1 < max_steps) out_tokens[(size_t)b * max_steps + p + 1] = nxt;
+        pos[b] = p + 1;
+    }
+}
+
+// splitmix64 of (seed, index): the random-init stream of every tensor.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void rand_bytes_kernel(uint8_t* __restrict__ out, size_t n, uint64_t seed) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = (uint8_t)(mix64(seed ^ mix64(i)) >> 32);
+}
+
+// uniform in [lo, hi)
+__global__ void rand_half_kernel(__half* __restrict__ out, size_t n, uint64_t seed, float lo, float hi) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float u = (float)(mix64(seed ^ mix64(i)) >> 40) * (1.0f / 16777216.0f);
+        out[i] = __float2half_rn(lo + (hi - lo) * u);
+    }
+}
+
+__global__ void fill_f32_kernel(float* __restrict__ out, size_t n, float v) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = v;
+}
+
+static int grid_for(size_t n) {
+    size_t g = (n + 255) / 256;
+    return (int)(g < 65535 ? (g > 0 ? g : 1) : 65535);
+}
+
+}  // namespace vb200
+
+using namespace vb200;
+
+extern "C" int vspec_b200_decode_embed(const void* d_table_f16, const int32_t* d_tok, int batch, int hidden,
+                                       float* d_x, void* stream) {
+    if (!d_table_f16 || !d_tok || !d_x || batch <= 0 || hidden <= 0) { set_error("bad embed arguments"); return VSPEC_B200_ERR_ARG; }
+    embed_kernel<<<dim3((hidden + 255) / 256, batch), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const __half*>(d_table_f16), d_tok, hidden, d_x);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "embed_kernel launch");
+}
+
+extern "C" int vspec_b200_decode_qk_rope_append(const float* d_qkv, const float* d_q_norm, const float* d_k_norm,
+                                                const int32_t* d_pos, int batch, int hq, int hkv, int head_dim,
+                                                float eps, float theta, float* d_q_out, void* d_k_pages,
+                                                void* d_v_pages, const int32_t* d_page_table, int max_pages,
+                                                int page_tokens, int32_t* d_ctx_len, void* stream) {
+    if (!d_qkv || !d_q_norm || !d_k_norm || !d_pos || !d_q_out || !d_k_pages || !d_v_pages || !d_page_table ||
+        !d_ctx_len || batch <= 0 || hq <= 0 || hkv <= 0 || hq % hkv != 0 || head_dim <= 0 || head_dim > 256 ||
+        head_dim % 64 != 0 || page_tokens <= 0 || max_pages <= 0) {
+        set_error("bad qk/rope/append arguments");
+        return VSPEC_B200_ERR_ARG;
+    }
+    qk_norm_rope_append_kernel<<<dim3(hq + 2 * hkv, batch), head_dim, 0, (cudaStream_t)stream>>>(
+        d_qkv, d_q_norm, d_k_norm, d_pos, hq, hkv, head_dim, eps, theta, d_q_out,
+        reinterpret_cast<__half*>(d_k_pages), reinterpret_cast<__half*>(d_v_pages), d_page_table, max_pages,
+        page_tokens, d_ctx_len);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "qk_norm_rope_append_kernel launch");
+}
+
+extern "C" int vspec_b200_decode_next_token(const float* d_logits, int batch, int vocab, float clip,
+                                            const int32_t* d_prompt, const int32_t* d_prompt_len, int max_prompt,
+                                            int32_t* d_pos, int32_t* d_tok, int32_t* d_out_tokens, int max_steps,
+                                            void* stream) {
+    if (!d_logits || !d_prompt || !d_prompt_len || !d_pos || !d_tok || !d_out_tokens || batch <= 0 || vocab <= 0) {
+        set_error("bad next-token arguments");
+        return VSPEC_B200_ERR_ARG;
+    }
+    next_token_kernel<<<batch, 1024, 0, (cudaStream_t)stream>>>(d_logits, vocab, clip, d_prompt, d_prompt_len,
+                                                                max_prompt, d_pos, d_tok, d_out_tokens, max_steps);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "next_token_kernel launch");
+}
+
+extern "C" int vspec_b200_random_fill(void* d_dst, size_t count, int kind, uint64_t seed, float lo, float hi,
+                                      void* stream) {
+    if (!d_dst || count == 0) { set_error("bad random_fill arguments"); return VSPEC_B200_ERR_ARG; }
+    cudaStream_t st = (cudaStream_t)stream;
+    if (kind == 0) rand_bytes_kernel<<<grid_for(count), 256, 0, st>>>(reinterpret_cast<uint8_t*>(d_dst), count, seed);
+    else if (kind == 1) rand_half_kernel<<<grid_for(count), 256, 0, st>>>(reinterpret_cast<__half*>(d_dst), count, seed, lo, hi);
+    else if (kind == 2) fill_f32_kernel<<<grid_for(count), 256, 0, st>>>(reinterpret_cast<float*>(d_dst), count, lo);
+    else { set_error("unknown random_fill kind %d", kind); return VSPEC_B200_ERR_ARG; }
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "random_fill launch");
+}

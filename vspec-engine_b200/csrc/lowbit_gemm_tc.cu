@@ -239,7 +239,6 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
 
     // Work items it = (tile, ks), tile-major: tile = it / splits, K range
     // [ks, ks + 1) * kb_per_split; CTA b takes items b, b + G, ...
-    const int kbt = p.kb_total;
     int it_cur = blockIdx.x;
     auto next_item = [&](int& cur, int& tile, int& kb0, int& kb1, int& ks) -> bool {
         if (cur >= p.items) return false;

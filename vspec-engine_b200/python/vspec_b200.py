@@ -33,6 +33,17 @@ class VspecB200Error(RuntimeError):
     pass
 
 
+class QwenConfig(ctypes.Structure):
+    _fields_ = [("num_layers", c_int), ("hidden", c_int), ("num_heads", c_int), ("num_kv_heads", c_int),
+                ("head_dim", c_int), ("intermediate", c_int), ("vocab", c_int), ("bits", c_int), ("group", c_int),
+                ("rms_eps", c_float), ("rope_theta", c_float), ("logit_clip", c_float), ("page_tokens", c_int)]
+
+
+# BASELINE config 4 (Qwen3-8B shape, W4 group 128)
+QWEN3_8B = dict(num_layers=36, hidden=4096, num_heads=32, num_kv_heads=8, head_dim=128, intermediate=12288,
+                vocab=151936, bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16)
+
+
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(f"libvspec_b200.so not built: {LIB_PATH} (run __graft_entry__.build())")
@@ -118,6 +129,19 @@ _sigs = {
     "vspec_b200_silu_f32": ([c_void_p, c_size_t, c_void_p], c_int),
     "vspec_b200_mul_f32": ([c_void_p, c_void_p, c_size_t, c_void_p], c_int),
     "vspec_b200_debug_fail_alloc_after": ([c_int], c_int),
+    "vspec_b200_lowbit_linear_static": ([POINTER(LinearArgs), c_void_p], c_int),
+    "vspec_b200_decode_embed": ([c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p], c_int),
+    "vspec_b200_decode_qk_rope_append": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float,
+                                          c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
+                                          c_void_p], c_int),
+    "vspec_b200_decode_next_token": ([c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                                      c_void_p, c_int, c_void_p], c_int),
+    "vspec_b200_random_fill": ([c_void_p, c_size_t, c_int, c_uint64, c_float, c_float, c_void_p], c_int),
+    "vspec_b200_qwen_create": ([POINTER(QwenConfig), c_uint64, c_int, c_int, POINTER(c_void_p)], c_int),
+    "vspec_b200_qwen_destroy": ([c_void_p], None),
+    "vspec_b200_qwen_generate": ([c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, POINTER(c_float), c_void_p],
+                                 c_int),
+    "vspec_b200_qwen_tensor": ([c_void_p, c_int, c_int, c_void_p], c_size_t),
     # reference-named (compat) exports
     "vspec_cuda_fused_available": ([], c_int),
     "vspec_cuda_backend_available": ([], c_int),
@@ -218,3 +242,46 @@ def page_fault_flag() -> int:
     v = c_int(0)
     check(lib.vspec_b200_paged_attention_page_fault(ctypes.byref(v)), "page_fault")
     return v.value
+
+
+class QwenModel:
+    """Random-init Qwen3-shape low-bit decoder on the device (vspec_b200_qwen_*)."""
+
+    def __init__(self, cfg: dict, seed: int, max_batch: int, max_ctx: int):
+        self.cfg = dict(cfg)
+        self._c = QwenConfig(**self.cfg)
+        h = c_void_p()
+        check(lib.vspec_b200_qwen_create(ctypes.byref(self._c), seed, max_batch, max_ctx, ctypes.byref(h)),
+              "vspec_b200_qwen_create")
+        self.handle = h
+
+    def close(self) -> None:
+        if self.handle:
+            lib.vspec_b200_qwen_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def generate(self, prompts: np.ndarray, gen: int, want_logits: bool = False):
+        prompts = np.ascontiguousarray(prompts, dtype=np.int32)
+        b, plen = prompts.shape
+        toks = np.zeros((b, plen + gen), dtype=np.int32)
+        ms = c_float(0.0)
+        logits = np.zeros((plen + gen - 1, b, self.cfg["vocab"]), dtype=np.float32) if want_logits else None
+        check(lib.vspec_b200_qwen_generate(self.handle, b, prompts.ctypes.data, plen, gen, toks.ctypes.data,
+                                           ctypes.byref(ms), logits.ctypes.data if logits is not None else None),
+              "vspec_b200_qwen_generate")
+        return toks, ms.value, logits
+
+    def tensor(self, kind: int, layer: int = 0) -> np.ndarray:
+        nbytes = lib.vspec_b200_qwen_tensor(self.handle, kind, layer, None)
+        if nbytes == 0:
+            raise VspecB200Error(f"no tensor kind={kind} layer={layer}")
+        out = np.empty(nbytes, dtype=np.uint8)
+        if lib.vspec_b200_qwen_tensor(self.handle, kind, layer, out.ctypes.data) != nbytes:
+            raise VspecB200Error("tensor download failed")
+        return out
