@@ -318,6 +318,67 @@ def time_attention(torch, V, steps: int, warmup: int, world: int):
     return ms, kv_bytes, other
 
 
+DEC_PROMPT, DEC_GEN, DEC_BATCH = 512, 256, 64
+
+
+def decode_bytes_per_step(cfg: dict, batch: int, ctx: int) -> int:
+    """HBM bytes one decode step must read: every packed weight and fp16 scale
+    once, plus each sequence's fp16 K/V at context ctx."""
+    H, I, L, V = cfg["hidden"], cfg["intermediate"], cfg["num_layers"], cfg["vocab"]
+    qd = cfg["num_heads"] * cfg["head_dim"]
+    kvd = cfg["num_kv_heads"] * cfg["head_dim"]
+    mats = [(qd + 2 * kvd, H), (H, qd), (2 * I, H), (H, I)]
+    per_layer = sum(n * (k * cfg["bits"] // 8) + n * (k // cfg["group"]) * 2 for n, k in mats)
+    lm = V * (H * cfg["bits"] // 8) + V * (H // cfg["group"]) * 2
+    kv = batch * ctx * L * kvd * 2 * 2
+    return L * per_layer + lm + kv
+
+
+def time_decode(torch, V, world: int, rank: int, peak: float):
+    """Qwen3-8B shape, W4 group 128, random-init, prompts of
+    512 random ids, 256 greedy tokens; batch 1 (every rank its own sequence) and
+    batch 64 sharded over the ranks.  tok/s over the generation phase (device
+    time, max over ranks)."""
+    cfg = V.QWEN3_8B
+    shard = DEC_BATCH // world
+    rng = np.random.default_rng(4 + rank)
+    prompts = rng.integers(0, cfg["vocab"], size=(shard, DEC_PROMPT)).astype(np.int32)
+    model = V.QwenModel(cfg, seed=1234, max_batch=shard, max_ctx=DEC_PROMPT + DEC_GEN)
+    try:
+        barrier(world)
+        _, ms1, _ = model.generate(prompts[:1], DEC_GEN)
+        ms1 = max_over_ranks(ms1, world)
+        barrier(world)
+        _, ms64, _ = model.generate(prompts, DEC_GEN)
+        ms64 = max_over_ranks(ms64, world)
+    finally:
+        model.close()
+    ctx_mid = DEC_PROMPT + DEC_GEN // 2
+    b1_bytes = decode_bytes_per_step(cfg, 1, ctx_mid)
+    b64_bytes = decode_bytes_per_step(cfg, shard, ctx_mid)
+    step1_s = ms1 * 1e-3 / DEC_GEN
+    step64_s = ms64 * 1e-3 / DEC_GEN
+    return {
+        "metric": "Qwen3-8B-shape W4 decode tok/s",
+        "b1": {"value": round(world * DEC_GEN / (ms1 * 1e-3), 2), "unit": "tok/s", "ms_per_token": round(ms1 / DEC_GEN, 4),
+               "parallelism": f"{world} independent sequence(s), one per GPU",
+               "roofline": {"bound": "hbm", "bytes_per_step": b1_bytes,
+                            "achieved": round(b1_bytes / step1_s / 1e9, 1), "peak": peak, "unit": "GB/s",
+                            "frac": round(b1_bytes / step1_s / 1e9 / peak, 4)}},
+        "b64": {"value": round(DEC_BATCH * DEC_GEN / (ms64 * 1e-3), 2), "unit": "tok/s",
+                "ms_per_step": round(ms64 / DEC_GEN, 4), "parallelism": f"batch 64 sharded dp{world} ({shard} per GPU)",
+                "scaling": "strong",
+                "roofline": {"bound": "hbm", "bytes_per_step_per_gpu": b64_bytes,
+                             "achieved": round(b64_bytes / step64_s / 1e9, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(b64_bytes / step64_s / 1e9 / peak, 4)}},
+        "config": "config 4: 36 layers, hidden 4096, 32/8 heads x 128, q/k RMSNorm, SwiGLU 12288, vocab 151936, "
+                  "eps 1e-6, RoPE theta 1e6, W4 group 128 (fp16 scales, mid-range zero-point), random-init; "
+                  f"prompt {DEC_PROMPT} seeded random ids (prefilled by decode steps), {DEC_GEN} greedy tokens; "
+                  "fp16 paged KV, 16-token pages; one CUDA graph per step",
+        "data": "synthetic (seeded random weights and token ids)",
+    }
+
+
 # ------------------------------------------------------------------ CPU legs
 def cpu_oracle_sample(seconds: float = 10.0) -> dict:
     """The oracle restatement (group-wise int4, one thread) on a bounded sample
@@ -406,6 +467,7 @@ def main() -> None:
     ap.add_argument("--copies", type=int, default=24)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -424,6 +486,7 @@ def main() -> None:
     ms3, _ = time_gemv_graph(torch, V, 3, args.copies, args.steps, args.warmup, world)
     attn_steps = max(3, args.steps // 5)
     attn_ms, attn_kv, attn_other = time_attention(torch, V, attn_steps, args.warmup, world)
+    decode = None if args.no_decode else time_decode(torch, V, world, rank, peak)
     e2e_steps = max(3, args.steps // 5)
     e2e_ms, e2e_bytes_call, h2d_call, d2h_call = time_e2e_bridge(torch, V, args.copies, e2e_steps, 2, world)
 
@@ -438,6 +501,12 @@ def main() -> None:
     cpu = None
     if rank == 0 and not args.no_cpu:
         cpu = cpu_oracle_sample(args.cpu_seconds)
+    if decode is not None and cpu is not None:
+        b1_bytes = decode["b1"]["roofline"]["bytes_per_step"]
+        decode["cpu_baseline"] = {
+            "value": round(cpu["value"] * 1e9 / b1_bytes, 5), "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
+            "sample": "extrapolated: batch-1 decode bytes per token / the oracle's measured single-thread group-wise "
+                      "W4 GEMV rate (the linears are >98 % of a decode step's bytes)"}
     if world > 1:
         import torch.distributed as dist
         barrier(world)
@@ -469,6 +538,7 @@ def main() -> None:
                       "kv_bytes_per_step": attn_kv,
                       "config": "config 3: B=32 Hq=32 Hkv=8 d=128, ctx ~U[512,8192] (seeded), 16-token fp16 pages, "
                                 "page table = seeded permutation of the pool, one step = one decode-attention call"},
+        "decode": decode,
         "cpu_baseline": cpu,
         "clocks": clocks,
         "gpu_launches": launches * 2 + attn_steps * 2,
