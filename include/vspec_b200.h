@@ -238,10 +238,11 @@ int vspec_b200_decode_qk_rope_append(const float* d_qkv, const float* d_q_norm, 
 /* Next token per sequence: the prompt's token at pos+1 while the prompt lasts,
  * else the argmax of the logits cleaned like _stabilize_logits (NaN -> 0,
  * clip to +-clip; ties -> lowest index); recorded at out_tokens[b][pos+1];
- * pos[b] += 1. */
+ * pos[b] += 1.  d_state: 12 bytes per sequence (8-byte aligned), zero before
+ * the first call; every call leaves it zero. */
 int vspec_b200_decode_next_token(const float* d_logits, int batch, int vocab, float clip, const int32_t* d_prompt,
                                  const int32_t* d_prompt_len, int max_prompt, int32_t* d_pos, int32_t* d_tok,
-                                 int32_t* d_out_tokens, int max_steps, void* stream);
+                                 int32_t* d_out_tokens, int max_steps, void* d_state, void* stream);
 /* Seeded fill: kind 0 uniform bytes, 1 fp16 uniform in [lo, hi), 2 fp32 constant lo. */
 int vspec_b200_random_fill(void* d_dst, size_t count, int kind, uint64_t seed, float lo, float hi, void* stream);
 

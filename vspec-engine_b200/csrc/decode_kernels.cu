@@ -79,38 +79,57 @@ __global__ void qk_norm_rope_append_kernel(const float* __restrict__ qkv, const 
     }
 }
 
-// One block per sequence: next token (prompt or greedy argmax), position + 1.
-__global__ void __launch_bounds__(1024) next_token_kernel(const float* __restrict__ logits, int vocab, float clip,
-                                                          const int32_t* __restrict__ prompt, const int32_t* __restrict__ prompt_len,
-                                                          int max_prompt, int32_t* __restrict__ pos, int32_t* __restrict__ tok,
-                                                          int32_t* __restrict__ out_tokens, int max_steps) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    const int b = blockIdx.x;
+// Next token (prompt or greedy argmax), position + 1.  Grid (blocks, batch):
+// every block folds its share of the vocabulary into one 64-bit key per
+// sequence -- cleaned value in the high word (order-preserving bits), lowest
+// index winning ties in the low word -- with atomicMax; the last block of a
+// sequence to finish reads and resets the key and its counter and moves the
+// sequence on.  state: [batch] keys then [batch] counters, zero between calls.
+__device__ __forceinline__ uint32_t ordered_bits(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(256) next_token_kernel(const float* __restrict__ logits, int vocab, float clip,
+                                                         const int32_t* __restrict__ prompt, const int32_t* __restrict__ prompt_len,
+                                                         int max_prompt, int32_t* __restrict__ pos, int32_t* __restrict__ tok,
+                                                         int32_t* __restrict__ out_tokens, int max_steps,
+                                                         unsigned long long* __restrict__ keys, unsigned int* __restrict__ counts) {
+    __shared__ unsigned long long red[8];
+    const int b = blockIdx.y;
     const float* lg = logits + (size_t)b * vocab;
-    float best = -INFINITY;
-    int besti = 0x7fffffff;
-    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+    const int chunk = (vocab + gridDim.x - 1) / gridDim.x;
+    const int j0 = blockIdx.x * chunk;
+    const int j1 = min(vocab, j0 + chunk);
+    unsigned long long best = 0ull;
+    for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
         float v = lg[j];
         if (isnan(v)) v = 0.f;
         v = fminf(fmaxf(v, -clip), clip);
-        if (v > best) { best = v; besti = j; }   // j ascends per thread: first index kept
+        const unsigned long long key = ((unsigned long long)ordered_bits(v) << 32) | (0xFFFFFFFFu - (uint32_t)j);
+        best = key > best ? key : best;
     }
     for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, besti, off);
-        if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+        best = o > best ? o : best;
     }
-    if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = best; bi[threadIdx.x >> 5] = besti; }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-            if (bv[w] > best || (bv[w] == best && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
-        const int p = pos[b];
-        const int nxt = (p + 1 < prompt_len[b]) ? prompt[(size_t)b * max_prompt + p + 1] : besti;
-        tok[b] = nxt;
-        if (p + 1 < max_steps) out_tokens[(size_t)b * max_steps + p + 1] = nxt;
-        pos[b] = p + 1;
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+        atomicMax(&keys[b], best);
+        __threadfence();
+        if (atomicAdd(&counts[b], 1u) == gridDim.x - 1) {
+            __threadfence();
+            const unsigned long long key = atomicExch(&keys[b], 0ull);
+            counts[b] = 0u;
+            const int arg = (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+            const int p = pos[b];
+            const int nxt = (p + 1 < prompt_len[b]) ? prompt[(size_t)b * max_prompt + p + 1] : arg;
+            tok[b] = nxt;
+            if (p + 1 < max_steps) out_tokens[(size_t)b * max_steps + p + 1] = nxt;
+            pos[b] = p + 1;
+        }
     }
 }
 
@@ -180,13 +199,19 @@ extern "C" int vspec_b200_decode_qk_rope_append(const float* d_qkv, const float*
 extern "C" int vspec_b200_decode_next_token(const float* d_logits, int batch, int vocab, float clip,
                                             const int32_t* d_prompt, const int32_t* d_prompt_len, int max_prompt,
                                             int32_t* d_pos, int32_t* d_tok, int32_t* d_out_tokens, int max_steps,
-                                            void* stream) {
-    if (!d_logits || !d_prompt || !d_prompt_len || !d_pos || !d_tok || !d_out_tokens || batch <= 0 || vocab <= 0) {
+                                            void* d_state, void* stream) {
+    if (!d_logits || !d_prompt || !d_prompt_len || !d_pos || !d_tok || !d_out_tokens || !d_state || batch <= 0 ||
+        vocab <= 0) {
         set_error("bad next-token arguments");
         return VSPEC_B200_ERR_ARG;
     }
-    next_token_kernel<<<batch, 1024, 0, (cudaStream_t)stream>>>(d_logits, vocab, clip, d_prompt, d_prompt_len,
-                                                                max_prompt, d_pos, d_tok, d_out_tokens, max_steps);
+    if (reinterpret_cast<uintptr_t>(d_state) % 8 != 0) { set_error("next-token state must be 8-byte aligned"); return VSPEC_B200_ERR_ARG; }
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(d_state);
+    unsigned int* counts = reinterpret_cast<unsigned int*>(keys + batch);
+    int blocks = (vocab + 2047) / 2048;   // ~8 values per thread
+    blocks = blocks < 1 ? 1 : (blocks > 256 ? 256 : blocks);
+    next_token_kernel<<<dim3(blocks, batch), 256, 0, (cudaStream_t)stream>>>(
+        d_logits, vocab, clip, d_prompt, d_prompt_len, max_prompt, d_pos, d_tok, d_out_tokens, max_steps, keys, counts);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "next_token_kernel launch");
 }

@@ -114,33 +114,42 @@ __host__ __device__ __forceinline__ int gm_src_code(int p) {
 // ---------------------------------------------------------------------------
 // Pre-pass: x (fp32, optional RMSNorm) -> fp16 rows in decoder order.
 // ---------------------------------------------------------------------------
+constexpr int kGmPrepThreads = 512;
+
 template <int BITS>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kGmPrepThreads)
 gemm_prep_x_kernel(const float* __restrict__ x, const float* __restrict__ norm_w, float eps, int rms, int k,
                    __half* __restrict__ xh, float* __restrict__ xinv) {
-    __shared__ float red[2][8];
+    __shared__ float red[2][kGmPrepThreads / 32];
     const int row = blockIdx.x;
     const float* xr = x + (size_t)row * k;
-    float ss = 0.f;
-    if (rms) {
-        for (int t = threadIdx.x; t < k; t += blockDim.x) ss += xr[t] * xr[t];
-        ss = warp_sum(ss);
-        if ((threadIdx.x & 31) == 0) red[0][threadIdx.x >> 5] = ss;
-        __syncthreads();
-        ss = 0.f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) ss += red[0][w];
+    const float4* xr4 = reinterpret_cast<const float4*>(xr);
+    const float4* nw4 = reinterpret_cast<const float4*>(norm_w);
+    const int k4 = k / 4;
+    constexpr int NWARP = kGmPrepThreads / 32;
+    // pass 1: sum of squares (RMSNorm) and max |x * norm_w| (the latter is
+    // rescaled by the row factor afterwards: both are positive scalings)
+    float ss = 0.f, mx = 0.f;
+    for (int t = threadIdx.x; t < k4; t += kGmPrepThreads) {
+        const float4 v = xr4[t];
+        ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+        float4 u = v;
+        if (rms) {
+            const float4 w = nw4[t];
+            u.x *= w.x; u.y *= w.y; u.z *= w.z; u.w *= w.w;
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))));
     }
-    const float nr = rms ? 1.0f / sqrtf(ss / (float)k + eps) : 1.0f;
-    float mx = 0.f;
-    for (int t = threadIdx.x; t < k; t += blockDim.x) {
-        const float v = rms ? xr[t] * nr * norm_w[t] : xr[t];
-        mx = fmaxf(mx, fabsf(v));
-    }
+    ss = warp_sum(ss);
     mx = warp_max(mx);
-    if ((threadIdx.x & 31) == 0) red[1][threadIdx.x >> 5] = mx;
+    if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = ss; red[1][threadIdx.x >> 5] = mx; }
     __syncthreads();
+    ss = 0.f;
     mx = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[1][w]);
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) { ss += red[0][w]; mx = fmaxf(mx, red[1][w]); }
+    const float nr = rms ? 1.0f / sqrtf(ss / (float)k + eps) : 1.0f;
+    mx *= nr;
     // sc = 2^(14 - floor(log2 max)): max lands in [2^14, 2^15), below fp16 max
     int sbits = 127;
     if (mx > 0.f && isfinite(mx)) {
@@ -148,12 +157,25 @@ gemm_prep_x_kernel(const float* __restrict__ x, const float* __restrict__ norm_w
         sbits = sbits < 1 ? 1 : (sbits > 253 ? 253 : sbits);
     }
     const float sc = __uint_as_float((uint32_t)sbits << 23);
+    const float f = rms ? nr * sc : sc;
     if (threadIdx.x == 0) xinv[row] = __uint_as_float((uint32_t)(254 - sbits) << 23);
-    __half* out = xh + (size_t)row * k;
-    for (int p = threadIdx.x; p < k; p += blockDim.x) {
-        const int t = (p & ~127) + gm_src_code<BITS>(p & 127);
-        const float v = rms ? xr[t] * nr * norm_w[t] : xr[t];
-        out[p] = __float2half_rn(v * sc);
+    // pass 2: eight consecutive output positions per thread (one 16-byte
+    // store), gathered from the same 128-code block of x
+    uint4* out = reinterpret_cast<uint4*>(xh + (size_t)row * k);
+    for (int i = threadIdx.x; i < k / 8; i += kGmPrepThreads) {
+        const int p0 = 8 * i;
+        const int blk = p0 & ~127;
+        uint32_t h2[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int ta = blk + gm_src_code<BITS>((p0 + 2 * e) & 127);
+            const int tb = blk + gm_src_code<BITS>((p0 + 2 * e + 1) & 127);
+            float va = xr[ta] * f, vb = xr[tb] * f;
+            if (rms) { va *= norm_w[ta]; vb *= norm_w[tb]; }
+            const __half2 hp = __floats2half2_rn(va, vb);
+            h2[e] = *reinterpret_cast<const uint32_t*>(&hp);
+        }
+        out[i] = make_uint4(h2[0], h2[1], h2[2], h2[3]);
     }
 }
 
@@ -594,6 +616,8 @@ bool gemm_tc_supported(const GemvParams& p, int bits, size_t counter_slots) {
     if (p.m <= kGemvMaxM) return false;
     if (p.k % 128 != 0 || p.n_groups < 1 || p.k % p.n_groups != 0 || (p.k / p.n_groups) % 128 != 0) return false;
     if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || (size_t)p.row_bytes % 16 != 0) return false;
+    if (reinterpret_cast<uintptr_t>(p.x) % 16 != 0) return false;   // vectorised pre-pass
+    if ((p.flags & VSPEC_B200_F_RMSNORM) && reinterpret_cast<uintptr_t>(p.norm_w) % 16 != 0) return false;
     const bool swiglu = (p.flags & VSPEC_B200_F_SWIGLU) != 0;
     if (swiglu && (p.n % 2 != 0 || (p.n / 2) % kGmRows != 0)) return false;
     GemmPlan gp;
@@ -664,9 +688,9 @@ int gemm_tc_launch(const GemvParams& p, int bits, int unsigned_codes, cudaStream
     float* xinv = reinterpret_cast<float*>(wb + plan.xh_bytes);
     float* part = reinterpret_cast<float*>(wb + plan.xh_bytes + plan.xinv_bytes);
     const int rms = (p.flags & VSPEC_B200_F_RMSNORM) ? 1 : 0;
-    if (bits == 4) gemm_prep_x_kernel<4><<<p.m, 256, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
-    else if (bits == 3) gemm_prep_x_kernel<3><<<p.m, 256, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
-    else gemm_prep_x_kernel<2><<<p.m, 256, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
+    if (bits == 4) gemm_prep_x_kernel<4><<<p.m, kGmPrepThreads, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
+    else if (bits == 3) gemm_prep_x_kernel<3><<<p.m, kGmPrepThreads, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
+    else gemm_prep_x_kernel<2><<<p.m, kGmPrepThreads, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "gemm_prep_x_kernel launch");
 

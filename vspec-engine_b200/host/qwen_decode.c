@@ -42,6 +42,7 @@ typedef struct QwenModel {
     float* ones;            /* norm weights (all ones), max(hidden, intermediate, head_dim) */
     float *x, *qkv, *q, *attn, *h, *logits;
     int32_t *tok, *pos, *ctx_len, *page_table, *prompt, *prompt_len, *out_tokens;
+    void* nt_state;         /* next-token reduction state, zero between steps */
     int max_prompt, max_steps;
     cudaStream_t stream;
     cudaGraphExec_t exec;
@@ -137,7 +138,8 @@ static int enqueue_step(QwenModel* m, int batch) {
     rc = linear(m, m->x, m->w_lm, m->s_lm, m->logits, batch, c->vocab, c->hidden, VSPEC_B200_F_RMSNORM, NULL, m->ones);
     if (rc != VSPEC_B200_OK) return rc;
     return vspec_b200_decode_next_token(m->logits, batch, c->vocab, c->logit_clip, m->prompt, m->prompt_len,
-                                        m->max_prompt, m->pos, m->tok, m->out_tokens, m->max_steps, m->stream);
+                                        m->max_prompt, m->pos, m->tok, m->out_tokens, m->max_steps, m->nt_state,
+                                        m->stream);
 }
 
 void vspec_b200_qwen_destroy(void* model) {
@@ -157,7 +159,7 @@ void vspec_b200_qwen_destroy(void* model) {
     cudaFree(m->emb); cudaFree(m->w_lm); cudaFree(m->s_lm); cudaFree(m->ones);
     cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->q); cudaFree(m->attn); cudaFree(m->h); cudaFree(m->logits);
     cudaFree(m->tok); cudaFree(m->pos); cudaFree(m->ctx_len); cudaFree(m->page_table);
-    cudaFree(m->prompt); cudaFree(m->prompt_len); cudaFree(m->out_tokens);
+    cudaFree(m->prompt); cudaFree(m->prompt_len); cudaFree(m->out_tokens); cudaFree(m->nt_state);
     if (m->stream) cudaStreamDestroy(m->stream);
     free(m);
 }
@@ -214,7 +216,8 @@ int vspec_b200_qwen_create(const VspecB200QwenConfig* cfg, uint64_t seed, int ma
          alloc_dev((void**)&m->tok, B * 4) && alloc_dev((void**)&m->pos, B * 4) && alloc_dev((void**)&m->ctx_len, B * 4) &&
          alloc_dev((void**)&m->page_table, B * m->pages_per_seq * 4) &&
          alloc_dev((void**)&m->prompt, B * m->max_prompt * 4) && alloc_dev((void**)&m->prompt_len, B * 4) &&
-         alloc_dev((void**)&m->out_tokens, B * m->max_steps * 4);
+         alloc_dev((void**)&m->out_tokens, B * m->max_steps * 4) && alloc_dev(&m->nt_state, B * 16) &&
+         cuda_ok(cudaMemsetAsync(m->nt_state, 0, B * 16, m->stream));
     if (ok) {
         /* page table: a seeded permutation of the pool (pages of one sequence
          * scattered over the pool, as a paged cache hands them out) */

@@ -135,7 +135,7 @@ _sigs = {
                                           c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                           c_void_p], c_int),
     "vspec_b200_decode_next_token": ([c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
-                                      c_void_p, c_int, c_void_p], c_int),
+                                      c_void_p, c_int, c_void_p, c_void_p], c_int),
     "vspec_b200_random_fill": ([c_void_p, c_size_t, c_int, c_uint64, c_float, c_float, c_void_p], c_int),
     "vspec_b200_qwen_create": ([POINTER(QwenConfig), c_uint64, c_int, c_int, POINTER(c_void_p)], c_int),
     "vspec_b200_qwen_destroy": ([c_void_p], None),
