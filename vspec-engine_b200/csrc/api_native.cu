@@ -1,6 +1,8 @@
 // api_native.cu -- extern "C" entry points of include/vspec_b200.h (GEMV part,
 // error state, device info).
 #include "common.cuh"
+
+#include <stdlib.h>
 #include "lowbit_kernels.cuh"
 
 #include <stdarg.h>
@@ -44,6 +46,15 @@ static const DevInfo* dev_info() {
         d.valid = 1;
     }
     return &d;
+}
+
+bool pdl_allowed() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_PDL");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
 }
 
 int device_sm_count() {

@@ -75,6 +75,8 @@ __device__ __forceinline__ size_t token_row(const int32_t* table, int t, int pt,
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kAttnThreads)
 paged_attn_f16_mma_kernel(const AttnParams p) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int D = 128;
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / p.head_groups;
@@ -291,6 +293,8 @@ template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __h
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads)
 paged_attn_simt_kernel(const AttnParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int D = p.d;
     const int group = p.hq / p.hkv;
@@ -358,6 +362,8 @@ paged_attn_simt_kernel(const AttnParams p) {
 
 // Merge of the context splits (exp2 domain), fixed order over splits.
 __global__ void paged_attn_combine_kernel(const AttnParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int h = blockIdx.x, b = blockIdx.y;
     const int ctx = p.ctx_len[b];
     const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
@@ -424,20 +430,19 @@ int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st) {
     const int group = p.hq / p.hkv;
     const bool mma = kv_dtype == kKvF16 && p.d == 128 && p.page_tokens > 0;
     const dim3 block(kAttnThreads);
+    p.head_groups = mma ? (group + 3) / 4 : 1;
+    const dim3 grid(p.max_splits, p.hkv * p.head_groups, p.batch);
+    cudaError_t e;
     if (mma) {
-        p.head_groups = (group + 3) / 4;
-        dim3 grid(p.max_splits, p.hkv * p.head_groups, p.batch);
-        paged_attn_f16_mma_kernel<<<grid, block, 0, st>>>(p);
+        e = launch_pdl(paged_attn_f16_mma_kernel, grid, block, 0, st, p);
     } else {
         p.head_groups = 1;
-        dim3 grid(p.max_splits, p.hq, p.batch);
-        if (kv_dtype == kKvF16) paged_attn_simt_kernel<__half><<<grid, block, 0, st>>>(p);
-        else paged_attn_simt_kernel<float><<<grid, block, 0, st>>>(p);
+        const dim3 sgrid(p.max_splits, p.hq, p.batch);
+        if (kv_dtype == kKvF16) e = launch_pdl(paged_attn_simt_kernel<__half>, sgrid, block, 0, st, p);
+        else e = launch_pdl(paged_attn_simt_kernel<float>, sgrid, block, 0, st, p);
     }
-    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "paged attention launch");
-    paged_attn_combine_kernel<<<dim3(p.hq, p.batch), 128, 0, st>>>(p);
-    e = cudaGetLastError();
+    e = launch_pdl(paged_attn_combine_kernel, dim3(p.hq, p.batch), dim3(128), 0, st, p);
     if (e != cudaSuccess) return cuda_status(e, "paged attention combine launch");
     return VSPEC_B200_OK;
 }

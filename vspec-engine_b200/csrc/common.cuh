@@ -150,4 +150,29 @@ __host__ __device__ __forceinline__ size_t group_of(size_t t, size_t k, size_t n
 
 int device_sm_count();
 
+// Programmatic dependent launch (VSPEC_B200_PDL=0 turns it off).  A kernel
+// launched with launch_pdl() may start while its predecessor in the stream is
+// still running, so it must call pdl_wait() before it reads or writes any
+// global memory the predecessors touch; pdl_trigger() lets the next launch
+// in the stream start early in turn.
+bool pdl_allowed();
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_allowed() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace vb200

@@ -23,6 +23,8 @@ namespace vb200 {
 
 __global__ void embed_kernel(const __half* __restrict__ table, const int32_t* __restrict__ tok, int hidden,
                              float* __restrict__ x) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.y;
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t < hidden) x[(size_t)b * hidden + t] = __half2float(table[(size_t)tok[b] * hidden + t]);
@@ -38,6 +40,8 @@ __global__ void qk_norm_rope_append_kernel(const float* __restrict__ qkv, const 
                                            int32_t* __restrict__ ctx_len) {
     __shared__ float vals[256];
     __shared__ float red[8];
+    pdl_wait();
+    pdl_trigger();
     const int h = blockIdx.x;
     const int b = blockIdx.y;
     const int t = threadIdx.x;
@@ -96,6 +100,8 @@ __global__ void __launch_bounds__(256) next_token_kernel(const float* __restrict
                                                          int32_t* __restrict__ out_tokens, int max_steps,
                                                          unsigned long long* __restrict__ keys, unsigned int* __restrict__ counts) {
     __shared__ unsigned long long red[8];
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.y;
     const float* lg = logits + (size_t)b * vocab;
     const int chunk = (vocab + gridDim.x - 1) / gridDim.x;
@@ -171,9 +177,9 @@ using namespace vb200;
 extern "C" int vspec_b200_decode_embed(const void* d_table_f16, const int32_t* d_tok, int batch, int hidden,
                                        float* d_x, void* stream) {
     if (!d_table_f16 || !d_tok || !d_x || batch <= 0 || hidden <= 0) { set_error("bad embed arguments"); return VSPEC_B200_ERR_ARG; }
-    embed_kernel<<<dim3((hidden + 255) / 256, batch), 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const __half*>(d_table_f16), d_tok, hidden, d_x);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(embed_kernel, dim3((hidden + 255) / 256, batch), dim3(256), 0,
+                                     (cudaStream_t)stream, reinterpret_cast<const __half*>(d_table_f16), d_tok, hidden,
+                                     d_x);
     return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "embed_kernel launch");
 }
 
@@ -188,11 +194,11 @@ extern "C" int vspec_b200_decode_qk_rope_append(const float* d_qkv, const float*
         set_error("bad qk/rope/append arguments");
         return VSPEC_B200_ERR_ARG;
     }
-    qk_norm_rope_append_kernel<<<dim3(hq + 2 * hkv, batch), head_dim, 0, (cudaStream_t)stream>>>(
-        d_qkv, d_q_norm, d_k_norm, d_pos, hq, hkv, head_dim, eps, theta, d_q_out,
-        reinterpret_cast<__half*>(d_k_pages), reinterpret_cast<__half*>(d_v_pages), d_page_table, max_pages,
-        page_tokens, d_ctx_len);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(qk_norm_rope_append_kernel, dim3(hq + 2 * hkv, batch), dim3(head_dim), 0,
+                                     (cudaStream_t)stream, d_qkv, d_q_norm, d_k_norm, d_pos, hq, hkv, head_dim, eps,
+                                     theta, d_q_out, reinterpret_cast<__half*>(d_k_pages),
+                                     reinterpret_cast<__half*>(d_v_pages), d_page_table, max_pages, page_tokens,
+                                     d_ctx_len);
     return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "qk_norm_rope_append_kernel launch");
 }
 
@@ -210,9 +216,9 @@ extern "C" int vspec_b200_decode_next_token(const float* d_logits, int batch, in
     unsigned int* counts = reinterpret_cast<unsigned int*>(keys + batch);
     int blocks = (vocab + 2047) / 2048;   // ~8 values per thread
     blocks = blocks < 1 ? 1 : (blocks > 256 ? 256 : blocks);
-    next_token_kernel<<<dim3(blocks, batch), 256, 0, (cudaStream_t)stream>>>(
-        d_logits, vocab, clip, d_prompt, d_prompt_len, max_prompt, d_pos, d_tok, d_out_tokens, max_steps, keys, counts);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(next_token_kernel, dim3(blocks, batch), dim3(256), 0, (cudaStream_t)stream,
+                                     d_logits, vocab, clip, d_prompt, d_prompt_len, max_prompt, d_pos, d_tok,
+                                     d_out_tokens, max_steps, keys, counts);
     return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "next_token_kernel launch");
 }
 

@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(kGmPrepThreads)
 gemm_prep_x_kernel(const float* __restrict__ x, const float* __restrict__ norm_w, float eps, int rms, int k,
                    __half* __restrict__ xh, float* __restrict__ xinv) {
     __shared__ float red[2][kGmPrepThreads / 32];
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x;
     const float* xr = x + (size_t)row * k;
     const float4* xr4 = reinterpret_cast<const float4*>(xr);
@@ -234,6 +236,9 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int G = gridDim.x;
+    // activations come from the pre-pass just before this launch
+    pdl_wait();
+    pdl_trigger();
 
     if (tid == 0) {
         for (int i = 0; i < NSW; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 128); }
@@ -660,6 +665,8 @@ static cudaError_t launch_gemm_t(const CUtensorMap& wm, const CUtensorMap& xm, c
         if (e != cudaSuccess) return e;
         configured[dev] = 1;
     }
+    // plain stream order: letting the next launch become resident early
+    // measured slower for this 1-CTA-per-SM kernel
     kern<<<grid, kGmThreads, smem, st>>>(wm, xm, gp);
     return cudaGetLastError();
 }
