@@ -245,6 +245,11 @@ int vspec_b200_decode_next_token(const float* d_logits, int batch, int vocab, fl
                                  int32_t* d_out_tokens, int max_steps, void* d_state, void* stream);
 /* Seeded fill: kind 0 uniform bytes, 1 fp16 uniform in [lo, hi), 2 fp32 constant lo. */
 int vspec_b200_random_fill(void* d_dst, size_t count, int kind, uint64_t seed, float lo, float hi, void* stream);
+/* Same streams (kinds 0 and 1) for a rows x cols block of a [*][global_cols]
+ * tensor starting at (row0, col0), stored with row stride dst_stride: a shard
+ * receives exactly the values the whole tensor has there. */
+int vspec_b200_random_fill_block(void* d_dst, size_t rows, size_t cols, size_t dst_stride, int kind, uint64_t seed,
+                                 size_t global_cols, size_t row0, size_t col0, float lo, float hi, void* stream);
 
 /* ------------------------------------------------------------------------
  * Qwen3-shape low-bit decode loop, random-init weights.
@@ -255,14 +260,29 @@ int vspec_b200_random_fill(void* d_dst, size_t count, int kind, uint64_t seed, f
  * ------------------------------------------------------------------------ */
 typedef struct VspecB200QwenConfig {
     int num_layers, hidden, num_heads, num_kv_heads, head_dim, intermediate, vocab;
-    int bits;          /* 4, 3 or 2 */
+    int bits;          /* attention projections and lm_head: 4, 3 or 2 */
     int group;         /* codes per scale group along k (multiple of 128) */
     float rms_eps, rope_theta, logit_clip;
     int page_tokens;
+    int bits_mlp;      /* gate/up and down projections; 0 = same as bits */
 } VspecB200QwenConfig;
 
 int vspec_b200_qwen_create(const VspecB200QwenConfig* cfg, uint64_t seed, int max_batch, int max_ctx,
                            void** out_model);
+/* The 128-byte NCCL unique id a tensor-parallel group shares: rank 0 makes it
+ * and hands the same bytes to every rank. */
+int vspec_b200_nccl_unique_id(void* out_id128);
+/* Tensor-parallel shard (rank tp_rank of tp_size, one GPU each, the device
+ * current when called; every rank calls it, it returns once all joined).
+ * Column-parallel q/k/v heads and gate/up rows, row-parallel o-proj and down
+ * projections followed by an NCCL all-reduce over NVLink; embedding and
+ * lm_head replicated, so every rank produces the same tokens.  Each rank holds
+ * exactly its slice of the same random-init weights as the unsharded model.
+ * Requires num_heads, num_kv_heads and intermediate divisible by tp_size, and
+ * the row-parallel slices (num_heads*head_dim/tp, intermediate/tp) to be whole
+ * scale groups. */
+int vspec_b200_qwen_create_tp(const VspecB200QwenConfig* cfg, uint64_t seed, int max_batch, int max_ctx, int tp_size,
+                              int tp_rank, const void* nccl_id128, void** out_model);
 void vspec_b200_qwen_destroy(void* model);
 /* Prompt prefill (one decode step per prompt token) and greedy generation for
  * `batch` sequences.  h_prompts [batch][prompt_len]; h_tokens_out
@@ -273,7 +293,7 @@ void vspec_b200_qwen_destroy(void* model);
  * gen_tokens - 1. */
 int vspec_b200_qwen_generate(void* model, int batch, const int32_t* h_prompts, int prompt_len, int gen_tokens,
                              int32_t* h_tokens_out, float* out_gen_ms, float* h_logits_out);
-/* Device tensors of the model, for checking against a host oracle:
+/* Device tensors of the model (this rank's shard), for checking against a host oracle:
  * kind 0 embedding fp16 [vocab][hidden]; per layer 1/2 qkv codes/scales,
  * 3/4 o-proj, 5/6 gate+up (gate rows first), 7/8 down; 9/10 lm_head
  * codes/scales.  Norm weights are all ones.  Returns the byte size, copies

@@ -406,6 +406,7 @@ int oracle_qwen_generate(const OracleQwen* q, const int32_t* prompt, int prompt_
                          float* logits_out) {
     const int H = q->hidden, hq = q->heads, hkv = q->kv_heads, d = q->head_dim, I = q->inter, V = q->vocab;
     const int qdim = hq * d, qkvn = qdim + 2 * hkv * d;
+    const int bm = q->bits_mlp ? q->bits_mlp : q->bits;
     const int total = prompt_len + gen;
     const int steps = total - 1;
     float* x = (float*)malloc(sizeof(float) * H);
@@ -478,12 +479,12 @@ int oracle_qwen_generate(const OracleQwen* q, const int32_t* prompt, int prompt_
             oq_linear(att, qdim, W[1], S[1], H, q->bits, q->group, tmp);
             for (int i = 0; i < H; ++i) x[i] += tmp[i];
             oq_rmsnorm(x, H, q->eps, xn);
-            oq_linear(xn, H, W[2], S[2], 2 * I, q->bits, q->group, tmp);
+            oq_linear(xn, H, W[2], S[2], 2 * I, bm, q->group, tmp);
             for (int i = 0; i < I; ++i) {
                 const float g = tmp[i], u = tmp[I + i];
                 hbuf[i] = g / (1.0f + expf(-g)) * u;
             }
-            oq_linear(hbuf, I, W[3], S[3], H, q->bits, q->group, tmp);
+            oq_linear(hbuf, I, W[3], S[3], H, bm, q->group, tmp);
             for (int i = 0; i < H; ++i) x[i] += tmp[i];
         }
         oq_rmsnorm(x, H, q->eps, xn);

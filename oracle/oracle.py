@@ -54,7 +54,8 @@ class OracleQwenC(ctypes.Structure):
     _fields_ = [("layers", ctypes.c_int), ("hidden", ctypes.c_int), ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int),
                 ("head_dim", ctypes.c_int), ("inter", ctypes.c_int), ("vocab", ctypes.c_int), ("bits", ctypes.c_int),
                 ("group", ctypes.c_int), ("eps", ctypes.c_float), ("theta", ctypes.c_float), ("clip", ctypes.c_float),
-                ("emb", c_void_p), ("w", c_void_p), ("s", c_void_p), ("w_lm", c_void_p), ("s_lm", c_void_p)]
+                ("emb", c_void_p), ("w", c_void_p), ("s", c_void_p), ("w_lm", c_void_p), ("s_lm", c_void_p),
+                ("bits_mlp", ctypes.c_int)]
 
 
 ORACLE.oracle_qwen_generate.argtypes = [ctypes.POINTER(OracleQwenC), c_void_p, ctypes.c_int, ctypes.c_int, c_void_p,
@@ -80,7 +81,7 @@ def qwen_generate(cfg: dict, tensors: dict, prompt, gen: int):
     q = OracleQwenC(L, cfg["hidden"], cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"], cfg["intermediate"],
                     cfg["vocab"], cfg["bits"], cfg["group"], cfg["rms_eps"], cfg["rope_theta"], cfg["logit_clip"],
                     ptr(tensors["emb"]), ctypes.cast(wp, c_void_p), ctypes.cast(sp, c_void_p), ptr(tensors["w_lm"]),
-                    ptr(tensors["s_lm"]))
+                    ptr(tensors["s_lm"]), cfg.get("bits_mlp", 0) or 0)
     prompt = np.ascontiguousarray(prompt, dtype=np.int32)
     total = prompt.size + gen
     toks = np.zeros(total, dtype=np.int32)

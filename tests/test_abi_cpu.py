@@ -147,3 +147,39 @@ def test_reference_python_bridge_binds_library(tmp_path):
     assert got.pop("loaded") == "True"
     assert got.pop("_HAS_FUSED_HYBRID") == "False"
     assert all(v == "True" for v in got.values()), got
+
+
+def test_tensor_parallel_create_rejects_bad_shards_on_host():
+    """Shard checks run before any CUDA call: heads, kv heads and intermediate
+    must divide by tp_size, the row-parallel slices must be whole scale
+    groups, rank must be in range and a group of more than one needs an id."""
+    base = dict(num_layers=2, hidden=256, num_heads=4, num_kv_heads=2, head_dim=64, intermediate=512, vocab=1000,
+                bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16, bits_mlp=3)
+    nid = ctypes.create_string_buffer(128)
+    h = ctypes.c_void_p()
+    cases = [
+        (dict(base), 3, 0, nid),                       # 4 heads over 3 ranks
+        (dict(base, num_kv_heads=1, num_heads=2), 2, 0, nid),
+        (dict(base), 4, 0, nid),                       # q slice 64 columns: not a whole group
+        (dict(base, intermediate=384), 2, 0, nid),     # 192-column down slice
+        (dict(base), 2, 2, nid),                       # rank out of range
+        (dict(base), 2, 0, None),                      # no id
+        (dict(base, bits_mlp=5), 1, 0, None),
+    ]
+    for cfg, tp, rank, idbuf in cases:
+        c = V.QwenConfig(**cfg)
+        rc = V.lib.vspec_b200_qwen_create_tp(ctypes.byref(c), 1, 4, 64, tp, rank, idbuf, ctypes.byref(h))
+        assert rc == 1, (cfg, tp, rank)
+        assert not h.value
+
+
+def test_nccl_unique_id_and_later_torch_import():
+    """The tensor-parallel group id comes from the NCCL that PyTorch also
+    loads, so importing torch afterwards in the same process still works."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, sys.argv[1]); import vspec_b200 as V; i = V.nccl_unique_id(); "
+            "assert len(i) == 128 and any(i); import torch; print('ok')")
+    r = subprocess.run([sys.executable, "-c", code, os.path.dirname(V.__file__)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]

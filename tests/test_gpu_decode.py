@@ -16,7 +16,7 @@ from gpu_util import RTOL_BF16, RTOL_F32, rel_err, torch_cuda
 pytestmark = pytest.mark.gpu
 
 SMALL = dict(num_layers=2, hidden=256, num_heads=4, num_kv_heads=2, head_dim=64, intermediate=512, vocab=1000,
-             bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16)
+             bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16, bits_mlp=0)
 
 
 def _tensors(model, cfg):
@@ -33,11 +33,13 @@ def _clean_argmax(lg, clip):
     return int(np.argmax(np.clip(v, -clip, clip)))
 
 
-@pytest.mark.parametrize("batch,bits", [(1, 4), (3, 4), (2, 3), (12, 4)])
-def test_decode_loop_matches_oracle(batch, bits):
+@pytest.mark.parametrize("batch,bits,bits_mlp", [(1, 4, 0), (3, 4, 0), (2, 3, 0), (12, 4, 0), (2, 4, 3), (12, 4, 3)])
+def test_decode_loop_matches_oracle(batch, bits, bits_mlp):
+    """bits_mlp 3 with bits 4 is config 5's mixed precision (W4 attention and
+    lm_head, W3 gate/up and down)."""
     torch_cuda()
-    cfg = dict(SMALL, bits=bits)
-    rng = np.random.default_rng(40 + batch + bits)
+    cfg = dict(SMALL, bits=bits, bits_mlp=bits_mlp)
+    rng = np.random.default_rng(40 + batch + bits + 10 * bits_mlp)
     plen, gen = 5, 7
     model = V.QwenModel(cfg, seed=7 + bits, max_batch=batch, max_ctx=64)
     try:

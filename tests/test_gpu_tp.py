@@ -1,0 +1,173 @@
+"""Tensor-parallel decode (BASELINE config 5 structure: column-parallel q/k/v
+and gate/up, row-parallel o-proj and down with an NCCL all-reduce) on two
+GPUs, one process per rank, against the unsharded model of the same seed.
+
+* Every rank's weight shard is, byte for byte, its slice of the unsharded
+  model's packed codes and fp16 scales (bit-exact).
+* Fed the unsharded model's token sequence (teacher forcing), the sharded
+  model's logits match the unsharded ones within the decode tolerance: the
+  all-reduce changes only the fp32 summation order.
+* Both ranks produce the same tokens and bit-identical logits, and each
+  greedy token is the argmax of the rank's own logits.
+The unsharded model is pinned to the C oracle by test_gpu_decode."""
+from __future__ import annotations
+
+import multiprocessing as mp
+import os
+import queue
+
+import numpy as np
+import pytest
+
+from gpu_util import RTOL_BF16, RTOL_F32, rel_err, torch_cuda
+from test_gpu_decode import SMALL, _clean_argmax
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+JOIN_S = 300
+
+
+def _download(model, cfg):
+    t = {"w_lm": model.tensor(9), "s_lm": model.tensor(10)}
+    for l in range(cfg["num_layers"]):
+        for kind in range(1, 9):
+            t[(l, kind)] = model.tensor(kind, l)
+    return t
+
+
+def _rank_main(rank, nccl_id, cfg, seed, max_batch, forced, prompts, gen, barrier, out_q):
+    """One rank of the group: build the shard, wait until every rank has one,
+    then run the same two generations on all ranks."""
+    try:
+        import torch
+        torch.cuda.set_device(rank)
+        import vspec_b200 as V
+        model = V.QwenModel(cfg, seed=seed, max_batch=max_batch, max_ctx=64, tp_size=WORLD, tp_rank=rank,
+                            nccl_id=nccl_id)
+        try:
+            # no rank enters a collective unless every rank built its shard
+            barrier.wait(timeout=120)
+            _, _, lf = model.generate(forced, 1, want_logits=True)
+            toks, _, lg = model.generate(prompts, gen, want_logits=True)
+            shards = _download(model, cfg)
+        finally:
+            model.close()
+        out_q.put((rank, None, lf, toks, lg, shards))
+    except Exception as e:  # reported to the parent, which fails the test
+        try:
+            barrier.abort()
+        except Exception:
+            pass
+        out_q.put((rank, repr(e), None, None, None, None))
+
+
+def _row_bytes(k, bits):
+    return (k * bits + 7) // 8
+
+
+def _expected_shard(full, cfg, rank):
+    """Slices of the unsharded tensors that rank `rank` must hold."""
+    T, g = WORLD, cfg["group"]
+    ba = cfg["bits"]
+    bm = cfg["bits_mlp"] or ba
+    H, d, I = cfg["hidden"], cfg["head_dim"], cfg["intermediate"]
+    gq, gkv = cfg["num_heads"] * d, cfg["num_kv_heads"] * d
+    qd, kvl, il = gq // T, gkv // T, I // T
+    exp = {}
+    for l in range(cfg["num_layers"]):
+        for kind, bits, n, k in ((1, ba, gq + 2 * gkv, H), (5, bm, 2 * I, H)):
+            w = full[(l, kind)].reshape(n, _row_bytes(k, bits))
+            s = full[(l, kind + 1)].reshape(n, 2 * (k // g))
+            if kind == 1:
+                rows = np.r_[rank * qd:(rank + 1) * qd, gq + rank * kvl:gq + (rank + 1) * kvl,
+                             gq + gkv + rank * kvl:gq + gkv + (rank + 1) * kvl]
+            else:
+                rows = np.r_[rank * il:(rank + 1) * il, I + rank * il:I + (rank + 1) * il]
+            exp[(l, kind)], exp[(l, kind + 1)] = w[rows].ravel(), s[rows].ravel()
+        for kind, bits, kg, kl in ((3, ba, gq, qd), (7, bm, I, il)):
+            w = full[(l, kind)].reshape(H, _row_bytes(kg, bits))
+            s = full[(l, kind + 1)].reshape(H, 2 * (kg // g))
+            b0 = _row_bytes(rank * kl, bits)
+            exp[(l, kind)] = w[:, b0:b0 + _row_bytes(kl, bits)].ravel()
+            exp[(l, kind + 1)] = s[:, 2 * (rank * kl // g):2 * ((rank + 1) * kl // g)].ravel()
+    exp["w_lm"], exp["s_lm"] = full["w_lm"], full["s_lm"]
+    return exp
+
+
+@pytest.mark.parametrize("batch,bits_mlp", [(3, 3), (12, 0)])
+def test_tensor_parallel_matches_unsharded(batch, bits_mlp):
+    torch = torch_cuda()
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import vspec_b200 as V
+    cfg = dict(SMALL, bits_mlp=bits_mlp)
+    seed = 21 + bits_mlp
+    rng = np.random.default_rng(60 + batch)
+    plen, gen = 5, 7
+    prompts = rng.integers(0, cfg["vocab"], size=(batch, plen)).astype(np.int32)
+    ref = V.QwenModel(cfg, seed=seed, max_batch=batch, max_ctx=64)
+    try:
+        forced, _, _ = ref.generate(prompts, gen, want_logits=False)
+        _, _, ref_logits = ref.generate(forced, 1, want_logits=True)
+        full = _download(ref, cfg)
+    finally:
+        ref.close()
+
+    nccl_id = V.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    barrier, out_q = ctx.Barrier(WORLD), ctx.Queue()
+    env_old = os.environ.get("NCCL_NVLS_ENABLE")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    procs = [ctx.Process(target=_rank_main, args=(r, nccl_id, cfg, seed, batch, forced, prompts, gen, barrier, out_q))
+             for r in range(WORLD)]
+    try:
+        for p in procs:
+            p.start()
+        results = {}
+        for _ in range(WORLD):
+            try:
+                r = out_q.get(timeout=JOIN_S)
+            except queue.Empty:
+                break
+            results[r[0]] = r
+        for p in procs:
+            p.join(timeout=60)
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
+        if env_old is None:
+            os.environ.pop("NCCL_NVLS_ENABLE", None)
+        else:
+            os.environ["NCCL_NVLS_ENABLE"] = env_old
+    assert sorted(results) == list(range(WORLD)), f"ranks reported: {sorted(results)}"
+    for r in range(WORLD):
+        assert results[r][1] is None, f"rank {r}: {results[r][1]}"
+
+    for r in range(WORLD):
+        exp = _expected_shard(full, cfg, r)
+        got = results[r][5]
+        for key, want in exp.items():
+            assert np.array_equal(got[key], want), (r, key)
+
+    # teacher-forced logits against the unsharded model; above m = 8 the
+    # tcgen05 GEMM rounds each rank's activation slice to fp16 with its own
+    # row scale, so the median step is held to the tensor-core tolerance there
+    med_tol = RTOL_BF16 / 2 if batch > 8 else RTOL_F32
+    steps = forced.shape[1] - 1
+    for r in range(WORLD):
+        lf = results[r][2]
+        for b in range(batch):
+            errs = [rel_err(lf[s, b], ref_logits[s, b]) for s in range(steps)]
+            assert max(errs) <= RTOL_BF16, (r, b, errs)
+            assert float(np.median(errs)) <= med_tol, (r, b, errs)
+    # ranks agree exactly; greedy tokens are each rank's own argmax
+    t0, l0 = results[0][3], results[0][4]
+    for r in range(1, WORLD):
+        assert np.array_equal(results[r][3], t0) and np.array_equal(results[r][4], l0)
+    assert np.array_equal(t0[:, :plen], prompts)
+    for b in range(batch):
+        for s in range(plen - 1, plen + gen - 1):
+            assert t0[b, s + 1] == _clean_argmax(l0[s, b], cfg["logit_clip"])

@@ -160,6 +160,24 @@ __global__ void rand_half_kernel(__half* __restrict__ out, size_t n, uint64_t se
     }
 }
 
+// Rows x cols block of a larger tensor: element (j, t) of the block is element
+// (row0 + j, col0 + t) of a [*][global_cols] tensor, whose random stream it
+// takes, so a shard of a tensor holds exactly the values of the whole.
+__global__ void rand_block_kernel(void* __restrict__ out, int kind, size_t rows, size_t cols, size_t dst_stride,
+                                  uint64_t seed, size_t global_cols, size_t row0, size_t col0, float lo, float hi) {
+    const size_t n = rows * cols;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t j = i / cols, t = i - j * cols;
+        const uint64_t h = mix64(seed ^ mix64((row0 + j) * global_cols + col0 + t));
+        if (kind == 0) {
+            reinterpret_cast<uint8_t*>(out)[j * dst_stride + t] = (uint8_t)(h >> 32);
+        } else {
+            const float u = (float)(h >> 40) * (1.0f / 16777216.0f);
+            reinterpret_cast<__half*>(out)[j * dst_stride + t] = __float2half_rn(lo + (hi - lo) * u);
+        }
+    }
+}
+
 __global__ void fill_f32_kernel(float* __restrict__ out, size_t n, float v) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         out[i] = v;
@@ -232,4 +250,17 @@ extern "C" int vspec_b200_random_fill(void* d_dst, size_t count, int kind, uint6
     else { set_error("unknown random_fill kind %d", kind); return VSPEC_B200_ERR_ARG; }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "random_fill launch");
+}
+
+extern "C" int vspec_b200_random_fill_block(void* d_dst, size_t rows, size_t cols, size_t dst_stride, int kind,
+                                            uint64_t seed, size_t global_cols, size_t row0, size_t col0, float lo,
+                                            float hi, void* stream) {
+    if (!d_dst || rows == 0 || cols == 0 || dst_stride < cols || (kind != 0 && kind != 1) || col0 + cols > global_cols) {
+        set_error("bad random_fill_block arguments");
+        return VSPEC_B200_ERR_ARG;
+    }
+    rand_block_kernel<<<grid_for(rows * cols), 256, 0, (cudaStream_t)stream>>>(d_dst, kind, rows, cols, dst_stride,
+                                                                               seed, global_cols, row0, col0, lo, hi);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "random_fill_block launch");
 }

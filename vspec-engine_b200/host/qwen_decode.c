@@ -1,6 +1,7 @@
 /* qwen_decode.c -- Qwen3-shape low-bit decode loop on the B200 kernels
- * (the reference's GenericTransformerRuntime._forward_token,
- * Vspec-chat/python/runtime_inference.py:1245-1500, Qwen profile).
+ * (BASELINE configs 4 and 5; the reference's GenericTransformerRuntime
+ * ._forward_token, Vspec-chat/python/runtime_inference.py:1245-1500, Qwen
+ * profile).
  *
  * One decode step for a batch of sequences, all on one stream:
  *   x = embed(tok)
@@ -15,13 +16,26 @@
  * captured once as a CUDA graph and replayed for every position (prompt
  * prefill and generation alike); the host only waits at the end.
  * The residual stabilisation of the reference is the identity for this
- * profile (residual_clamp_alpha = 0, runtime_inference.py:162-171). */
+ * profile (residual_clamp_alpha = 0, runtime_inference.py:162-171).
+ *
+ * Tensor parallelism (tp > 1, one GPU per rank): each rank keeps its slice of
+ * the query/key/value heads and of the gate/up rows (column parallel) and the
+ * matching input columns of the o-proj and down projections (row parallel);
+ * the partial products of those two are summed by an in-place NCCL
+ * all-reduce, rank 0 alone adding the residual.  Embedding and lm_head are
+ * replicated, so every rank computes the same logits and tokens.
+ * NCCL is resolved at run time, when the first tensor-parallel model is made
+ * (an NCCL already loaded into the process is reused, VSPEC_B200_NCCL_LIB
+ * names another), so single-GPU users never load it. */
+#include <dlfcn.h>
 #include <math.h>
+#include <pthread.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
 #include <cuda_runtime_api.h>
+#include <nccl.h>
 
 #include "vspec_b200.h"
 
@@ -33,13 +47,16 @@ typedef struct QwenLayer {
 
 typedef struct QwenModel {
     VspecB200QwenConfig cfg;
+    int bits_attn, bits_mlp;
+    int tp, rank;
+    ncclComm_t comm;
     int max_batch, max_ctx, pages_per_seq, num_pages;
-    int qkv_n, q_dim;
+    int hq, hkv, q_dim, qkv_n, inter;   /* this rank's heads, q width, qkv rows, intermediate slice */
     void* emb;              /* fp16 [vocab][hidden] */
     QwenLayer* layers;
     uint8_t* w_lm;
     void* s_lm;
-    float* ones;            /* norm weights (all ones), max(hidden, intermediate, head_dim) */
+    float* ones;            /* norm weights (all ones), max(hidden, intermediate slice, head_dim) */
     float *x, *qkv, *q, *attn, *h, *logits;
     int32_t *tok, *pos, *ctx_len, *page_table, *prompt, *prompt_len, *out_tokens;
     void* nt_state;         /* next-token reduction state, zero between steps */
@@ -51,6 +68,40 @@ typedef struct QwenModel {
 
 static size_t row_bytes(int k, int bits) { return ((size_t)k * (size_t)bits + 7) / 8; }
 
+/* The NCCL entry points the decode loop uses. */
+typedef struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*);
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*comm_destroy)(ncclComm_t);
+} NcclApi;
+
+static NcclApi g_nccl;
+static int g_nccl_ok;
+static pthread_once_t g_nccl_once = PTHREAD_ONCE_INIT;
+
+static void nccl_load(void) {
+    const char* name = getenv("VSPEC_B200_NCCL_LIB");
+    void* h = NULL;
+    if (name && *name) {
+        h = dlopen(name, RTLD_NOW | RTLD_GLOBAL);
+    } else {
+        h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    }
+    if (!h) return;
+    *(void**)&g_nccl.get_unique_id = dlsym(h, "ncclGetUniqueId");
+    *(void**)&g_nccl.comm_init_rank = dlsym(h, "ncclCommInitRank");
+    *(void**)&g_nccl.all_reduce = dlsym(h, "ncclAllReduce");
+    *(void**)&g_nccl.comm_destroy = dlsym(h, "ncclCommDestroy");
+    g_nccl_ok = g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.all_reduce && g_nccl.comm_destroy;
+}
+
+static const NcclApi* nccl_api(void) {
+    pthread_once(&g_nccl_once, nccl_load);
+    return g_nccl_ok ? &g_nccl : NULL;
+}
+
 static int cuda_ok(cudaError_t e) { return e == cudaSuccess; }
 
 static int alloc_dev(void** p, size_t bytes) {
@@ -59,20 +110,34 @@ static int alloc_dev(void** p, size_t bytes) {
     return cuda_ok(cudaMalloc(p, bytes));
 }
 
+static int alloc_linear(QwenModel* m, uint8_t** w, void** s, int n, int k, int bits) {
+    return alloc_dev((void**)w, (size_t)n * row_bytes(k, bits)) &&
+           alloc_dev(s, (size_t)n * (size_t)(k / m->cfg.group) * 2);
+}
+
 /* Random-init linear: codes uniform, fp16 scales ~U(0.003, 0.006), which with
- * the mid-range zero-point gives weights of std ~0.02. */
-static int init_linear(QwenModel* m, uint8_t** w, void** s, int n, int k, uint64_t seed) {
-    const int bits = m->cfg.bits;
-    const size_t wb = (size_t)n * row_bytes(k, bits);
-    const size_t ns = (size_t)n * (size_t)(k / m->cfg.group);
-    if (!alloc_dev((void**)w, wb) || !alloc_dev(s, ns * 2)) return 0;
-    if (vspec_b200_random_fill(*w, wb, 0, seed, 0.f, 0.f, m->stream) != VSPEC_B200_OK) return 0;
-    if (vspec_b200_random_fill(*s, ns, 1, seed ^ 0x5ca1eull, 0.003f, 0.006f, m->stream) != VSPEC_B200_OK) return 0;
-    return 1;
+ * the mid-range zero-point gives weights of std ~0.02.  Writes rows
+ * [row0, row0 + rows) of the whole [*][k_global] tensor, restricted to input
+ * columns [k0, k0 + k_local), at local row `lrow` of a [*][k_local] shard.
+ * Every element takes the random stream of its place in the whole tensor
+ * (byte index row * row_bytes(k_global) + byte, scale index row * groups +
+ * group), so shards hold exactly the unsharded model's values.  k0 is a whole
+ * number of scale groups, so the sliced LSB-first bitstream starts on a byte. */
+static int fill_rows(QwenModel* m, uint8_t* w, void* s, int bits, int lrow, int rows, int row0, int k_local,
+                     int k_global, int k0, uint64_t seed) {
+    const int g = m->cfg.group;
+    const size_t lrb = row_bytes(k_local, bits), grb = row_bytes(k_global, bits);
+    const size_t lg = (size_t)(k_local / g), gg = (size_t)(k_global / g);
+    if (vspec_b200_random_fill_block(w + (size_t)lrow * lrb, (size_t)rows, lrb, lrb, 0, seed, grb, (size_t)row0,
+                                     row_bytes(k0, bits), 0.f, 0.f, m->stream) != VSPEC_B200_OK)
+        return 0;
+    return vspec_b200_random_fill_block((uint8_t*)s + (size_t)lrow * lg * 2, (size_t)rows, lg, lg, 1,
+                                        seed ^ 0x5ca1eull, gg, (size_t)row0, (size_t)(k0 / g), 0.003f, 0.006f,
+                                        m->stream) == VSPEC_B200_OK;
 }
 
 static int linear(QwenModel* m, const float* x, const uint8_t* w, const void* s, float* y, int batch, int n, int k,
-                  int flags, const float* residual, const float* norm_w) {
+                  int bits, int flags, const float* residual, const float* norm_w) {
     VspecB200LinearArgs a;
     memset(&a, 0, sizeof(a));
     a.d_x = x;
@@ -88,23 +153,36 @@ static int linear(QwenModel* m, const float* x, const uint8_t* w, const void* s,
     a.n = (size_t)n;
     a.k = (size_t)k;
     a.n_groups = (size_t)(k / m->cfg.group);
-    a.bits = m->cfg.bits;
+    a.bits = bits;
     a.flags = flags | VSPEC_B200_F_SZ_F16 | VSPEC_B200_F_UNSIGNED;
     return vspec_b200_lowbit_linear(&a, m->stream);
+}
+
+/* x = sum over the ranks of the row-parallel partials, in place. */
+static int allreduce_x(QwenModel* m, int batch) {
+    if (m->tp == 1) return VSPEC_B200_OK;
+    if (nccl_api()->all_reduce(m->x, m->x, (size_t)batch * (size_t)m->cfg.hidden, ncclFloat, ncclSum, m->comm,
+                               m->stream) != ncclSuccess)
+        return VSPEC_B200_ERR_CUDA;
+    return VSPEC_B200_OK;
 }
 
 /* One decode step (enqueue only). */
 static int enqueue_step(QwenModel* m, int batch) {
     const VspecB200QwenConfig* c = &m->cfg;
+    /* rank 0 adds the residual to its row-parallel partial, the others write theirs */
+    const int res_flag = m->rank == 0 ? VSPEC_B200_F_RESIDUAL : 0;
+    const float* res = m->rank == 0 ? m->x : NULL;
     int rc = vspec_b200_decode_embed(m->emb, m->tok, batch, c->hidden, m->x, m->stream);
     if (rc != VSPEC_B200_OK) return rc;
     for (int l = 0; l < c->num_layers; ++l) {
         QwenLayer* L = &m->layers[l];
-        rc = linear(m, m->x, L->w_qkv, L->s_qkv, m->qkv, batch, m->qkv_n, c->hidden, VSPEC_B200_F_RMSNORM, NULL, m->ones);
+        rc = linear(m, m->x, L->w_qkv, L->s_qkv, m->qkv, batch, m->qkv_n, c->hidden, m->bits_attn,
+                    VSPEC_B200_F_RMSNORM, NULL, m->ones);
         if (rc != VSPEC_B200_OK) return rc;
-        rc = vspec_b200_decode_qk_rope_append(m->qkv, m->ones, m->ones, m->pos, batch, c->num_heads, c->num_kv_heads,
-                                              c->head_dim, c->rms_eps, c->rope_theta, m->q, L->k_pages, L->v_pages,
-                                              m->page_table, m->pages_per_seq, c->page_tokens, m->ctx_len, m->stream);
+        rc = vspec_b200_decode_qk_rope_append(m->qkv, m->ones, m->ones, m->pos, batch, m->hq, m->hkv, c->head_dim,
+                                              c->rms_eps, c->rope_theta, m->q, L->k_pages, L->v_pages, m->page_table,
+                                              m->pages_per_seq, c->page_tokens, m->ctx_len, m->stream);
         if (rc != VSPEC_B200_OK) return rc;
         VspecB200PagedAttnArgs pa;
         memset(&pa, 0, sizeof(pa));
@@ -115,8 +193,8 @@ static int enqueue_step(QwenModel* m, int batch) {
         pa.d_ctx_len = m->ctx_len;
         pa.d_out = m->attn;
         pa.batch = (size_t)batch;
-        pa.num_q_heads = (size_t)c->num_heads;
-        pa.num_kv_heads = (size_t)c->num_kv_heads;
+        pa.num_q_heads = (size_t)m->hq;
+        pa.num_kv_heads = (size_t)m->hkv;
         pa.head_dim = (size_t)c->head_dim;
         pa.page_tokens = (size_t)c->page_tokens;
         pa.max_pages_per_seq = (size_t)m->pages_per_seq;
@@ -126,16 +204,18 @@ static int enqueue_step(QwenModel* m, int batch) {
         pa.kv_dtype = VSPEC_B200_KV_F16;
         rc = vspec_b200_paged_attention(&pa, m->stream);
         if (rc != VSPEC_B200_OK) return rc;
-        rc = linear(m, m->attn, L->w_o, L->s_o, m->x, batch, c->hidden, m->q_dim, VSPEC_B200_F_RESIDUAL, m->x, NULL);
+        rc = linear(m, m->attn, L->w_o, L->s_o, m->x, batch, c->hidden, m->q_dim, m->bits_attn, res_flag, res, NULL);
+        if (rc == VSPEC_B200_OK) rc = allreduce_x(m, batch);
         if (rc != VSPEC_B200_OK) return rc;
-        rc = linear(m, m->x, L->w_gu, L->s_gu, m->h, batch, 2 * c->intermediate, c->hidden,
+        rc = linear(m, m->x, L->w_gu, L->s_gu, m->h, batch, 2 * m->inter, c->hidden, m->bits_mlp,
                     VSPEC_B200_F_RMSNORM | VSPEC_B200_F_SWIGLU, NULL, m->ones);
         if (rc != VSPEC_B200_OK) return rc;
-        rc = linear(m, m->h, L->w_down, L->s_down, m->x, batch, c->hidden, c->intermediate, VSPEC_B200_F_RESIDUAL, m->x,
-                    NULL);
+        rc = linear(m, m->h, L->w_down, L->s_down, m->x, batch, c->hidden, m->inter, m->bits_mlp, res_flag, res, NULL);
+        if (rc == VSPEC_B200_OK) rc = allreduce_x(m, batch);
         if (rc != VSPEC_B200_OK) return rc;
     }
-    rc = linear(m, m->x, m->w_lm, m->s_lm, m->logits, batch, c->vocab, c->hidden, VSPEC_B200_F_RMSNORM, NULL, m->ones);
+    rc = linear(m, m->x, m->w_lm, m->s_lm, m->logits, batch, c->vocab, c->hidden, m->bits_attn, VSPEC_B200_F_RMSNORM,
+                NULL, m->ones);
     if (rc != VSPEC_B200_OK) return rc;
     return vspec_b200_decode_next_token(m->logits, batch, c->vocab, c->logit_clip, m->prompt, m->prompt_len,
                                         m->max_prompt, m->pos, m->tok, m->out_tokens, m->max_steps, m->nt_state,
@@ -146,7 +226,9 @@ void vspec_b200_qwen_destroy(void* model) {
     QwenModel* m = (QwenModel*)model;
     if (!m) return;
     if (m->stream) cudaStreamSynchronize(m->stream);
+    /* the captured step holds NCCL calls: release it before the communicator */
     if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->comm) nccl_api()->comm_destroy(m->comm);
     if (m->layers) {
         for (int l = 0; l < m->cfg.num_layers; ++l) {
             QwenLayer* L = &m->layers[l];
@@ -164,39 +246,87 @@ void vspec_b200_qwen_destroy(void* model) {
     free(m);
 }
 
-int vspec_b200_qwen_create(const VspecB200QwenConfig* cfg, uint64_t seed, int max_batch, int max_ctx,
-                           void** out_model) {
-    if (!cfg || !out_model || max_batch <= 0 || max_ctx <= 0) return VSPEC_B200_ERR_ARG;
+int vspec_b200_nccl_unique_id(void* out_id128) {
+    if (!out_id128) return VSPEC_B200_ERR_ARG;
+    const NcclApi* nc = nccl_api();
+    if (!nc) return VSPEC_B200_ERR_UNSUPPORTED;
+    ncclUniqueId id;
+    if (nc->get_unique_id(&id) != ncclSuccess) return VSPEC_B200_ERR_CUDA;
+    memset(out_id128, 0, 128);
+    memcpy(out_id128, &id, sizeof(id) < 128 ? sizeof(id) : 128);
+    return VSPEC_B200_OK;
+}
+
+int vspec_b200_qwen_create_tp(const VspecB200QwenConfig* cfg, uint64_t seed, int max_batch, int max_ctx, int tp_size,
+                              int tp_rank, const void* nccl_id128, void** out_model) {
+    if (!cfg || !out_model || max_batch <= 0 || max_ctx <= 0 || tp_size <= 0 || tp_rank < 0 || tp_rank >= tp_size ||
+        (tp_size > 1 && !nccl_id128))
+        return VSPEC_B200_ERR_ARG;
     *out_model = NULL;
     const VspecB200QwenConfig* c = cfg;
+    const int T = tp_size, r = tp_rank;
+    const int bits_mlp = c->bits_mlp ? c->bits_mlp : c->bits;
     if (c->num_layers <= 0 || c->hidden <= 0 || c->num_heads <= 0 || c->num_kv_heads <= 0 ||
         c->num_heads % c->num_kv_heads != 0 || c->head_dim <= 0 || c->head_dim % 64 != 0 || c->head_dim > 256 ||
         c->intermediate <= 0 || c->vocab <= 0 || c->group <= 0 || c->group % 128 != 0 || c->hidden % c->group != 0 ||
-        c->intermediate % c->group != 0 || (c->num_heads * c->head_dim) % c->group != 0 ||
-        (c->bits != 2 && c->bits != 3 && c->bits != 4) || c->page_tokens <= 0)
+        (c->bits != 2 && c->bits != 3 && c->bits != 4) || (bits_mlp != 2 && bits_mlp != 3 && bits_mlp != 4) ||
+        c->page_tokens <= 0 || c->num_heads % T != 0 || c->num_kv_heads % T != 0 || c->intermediate % T != 0 ||
+        ((c->num_heads / T) * c->head_dim) % c->group != 0 || (c->intermediate / T) % c->group != 0)
         return VSPEC_B200_ERR_ARG;
+    if (T > 1 && !nccl_api()) return VSPEC_B200_ERR_UNSUPPORTED;
     QwenModel* m = (QwenModel*)calloc(1, sizeof(QwenModel));
     if (!m) return VSPEC_B200_ERR_NOMEM;
     m->cfg = *cfg;
+    m->bits_attn = c->bits;
+    m->bits_mlp = bits_mlp;
+    m->tp = T;
+    m->rank = r;
     m->max_batch = max_batch;
     m->max_ctx = max_ctx;
     m->pages_per_seq = (max_ctx + c->page_tokens - 1) / c->page_tokens;
     m->num_pages = m->pages_per_seq * max_batch;
-    m->q_dim = c->num_heads * c->head_dim;
-    m->qkv_n = m->q_dim + 2 * c->num_kv_heads * c->head_dim;
+    m->hq = c->num_heads / T;
+    m->hkv = c->num_kv_heads / T;
+    m->q_dim = m->hq * c->head_dim;
+    m->qkv_n = m->q_dim + 2 * m->hkv * c->head_dim;
+    m->inter = c->intermediate / T;
     m->max_prompt = max_ctx;
     m->max_steps = max_ctx;
     int ok = cuda_ok(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    if (ok && T > 1) {
+        const NcclApi* nc = nccl_api();
+        ncclUniqueId id;
+        memcpy(&id, nccl_id128, sizeof(id) < 128 ? sizeof(id) : 128);
+        ok = nc != NULL && nc->comm_init_rank(&m->comm, T, id, r) == ncclSuccess;
+        if (!ok) m->comm = NULL;
+    }
     m->layers = (QwenLayer*)calloc((size_t)c->num_layers, sizeof(QwenLayer));
     ok = ok && m->layers != NULL;
-    const size_t page_elems = (size_t)m->num_pages * c->page_tokens * c->num_kv_heads * c->head_dim;
+    const int gq = c->num_heads * c->head_dim, gkv = c->num_kv_heads * c->head_dim;   /* unsharded widths */
+    const int lkv = m->hkv * c->head_dim;
+    const int ba = m->bits_attn, bm = m->bits_mlp;
+    const size_t page_elems = (size_t)m->num_pages * c->page_tokens * m->hkv * c->head_dim;
     for (int l = 0; ok && l < c->num_layers; ++l) {
         QwenLayer* L = &m->layers[l];
         const uint64_t ls = seed * 1000003ull + (uint64_t)l * 16ull;
-        ok = init_linear(m, &L->w_qkv, &L->s_qkv, m->qkv_n, c->hidden, ls + 1) &&
-             init_linear(m, &L->w_o, &L->s_o, c->hidden, m->q_dim, ls + 2) &&
-             init_linear(m, &L->w_gu, &L->s_gu, 2 * c->intermediate, c->hidden, ls + 3) &&
-             init_linear(m, &L->w_down, &L->s_down, c->hidden, c->intermediate, ls + 4) &&
+        /* qkv: this rank's q, k and v head rows of the whole [q | k | v] */
+        ok = alloc_linear(m, &L->w_qkv, &L->s_qkv, m->qkv_n, c->hidden, ba) &&
+             fill_rows(m, L->w_qkv, L->s_qkv, ba, 0, m->q_dim, r * m->q_dim, c->hidden, c->hidden, 0, ls + 1) &&
+             fill_rows(m, L->w_qkv, L->s_qkv, ba, m->q_dim, lkv, gq + r * lkv, c->hidden, c->hidden, 0, ls + 1) &&
+             fill_rows(m, L->w_qkv, L->s_qkv, ba, m->q_dim + lkv, lkv, gq + gkv + r * lkv, c->hidden, c->hidden, 0,
+                       ls + 1) &&
+             /* o-proj: every row, this rank's input columns */
+             alloc_linear(m, &L->w_o, &L->s_o, c->hidden, m->q_dim, ba) &&
+             fill_rows(m, L->w_o, L->s_o, ba, 0, c->hidden, 0, m->q_dim, gq, r * m->q_dim, ls + 2) &&
+             /* gate rows then up rows of this rank's intermediate slice */
+             alloc_linear(m, &L->w_gu, &L->s_gu, 2 * m->inter, c->hidden, bm) &&
+             fill_rows(m, L->w_gu, L->s_gu, bm, 0, m->inter, r * m->inter, c->hidden, c->hidden, 0, ls + 3) &&
+             fill_rows(m, L->w_gu, L->s_gu, bm, m->inter, m->inter, c->intermediate + r * m->inter, c->hidden,
+                       c->hidden, 0, ls + 3) &&
+             /* down: every row, this rank's input columns */
+             alloc_linear(m, &L->w_down, &L->s_down, c->hidden, m->inter, bm) &&
+             fill_rows(m, L->w_down, L->s_down, bm, 0, c->hidden, 0, m->inter, c->intermediate, r * m->inter,
+                       ls + 4) &&
              alloc_dev(&L->k_pages, page_elems * 2) && alloc_dev(&L->v_pages, page_elems * 2) &&
              cuda_ok(cudaMemsetAsync(L->k_pages, 0, page_elems * 2, m->stream)) &&
              cuda_ok(cudaMemsetAsync(L->v_pages, 0, page_elems * 2, m->stream));
@@ -204,15 +334,16 @@ int vspec_b200_qwen_create(const VspecB200QwenConfig* cfg, uint64_t seed, int ma
     const size_t emb_elems = (size_t)c->vocab * c->hidden;
     ok = ok && alloc_dev(&m->emb, emb_elems * 2) &&
          vspec_b200_random_fill(m->emb, emb_elems, 1, seed * 7919ull + 11ull, -0.05f, 0.05f, m->stream) == VSPEC_B200_OK;
-    ok = ok && init_linear(m, &m->w_lm, &m->s_lm, c->vocab, c->hidden, seed * 7919ull + 13ull);
-    int ones_n = c->hidden > c->intermediate ? c->hidden : c->intermediate;
+    ok = ok && alloc_linear(m, &m->w_lm, &m->s_lm, c->vocab, c->hidden, ba) &&
+         fill_rows(m, m->w_lm, m->s_lm, ba, 0, c->vocab, 0, c->hidden, c->hidden, 0, seed * 7919ull + 13ull);
+    int ones_n = c->hidden > m->inter ? c->hidden : m->inter;
     if (c->head_dim > ones_n) ones_n = c->head_dim;
     ok = ok && alloc_dev((void**)&m->ones, (size_t)ones_n * 4) &&
          vspec_b200_random_fill(m->ones, (size_t)ones_n, 2, 0, 1.0f, 0.f, m->stream) == VSPEC_B200_OK;
     const size_t B = (size_t)max_batch;
     ok = ok && alloc_dev((void**)&m->x, B * c->hidden * 4) && alloc_dev((void**)&m->qkv, B * m->qkv_n * 4) &&
          alloc_dev((void**)&m->q, B * m->q_dim * 4) && alloc_dev((void**)&m->attn, B * m->q_dim * 4) &&
-         alloc_dev((void**)&m->h, B * c->intermediate * 4) && alloc_dev((void**)&m->logits, B * c->vocab * 4) &&
+         alloc_dev((void**)&m->h, B * m->inter * 4) && alloc_dev((void**)&m->logits, B * c->vocab * 4) &&
          alloc_dev((void**)&m->tok, B * 4) && alloc_dev((void**)&m->pos, B * 4) && alloc_dev((void**)&m->ctx_len, B * 4) &&
          alloc_dev((void**)&m->page_table, B * m->pages_per_seq * 4) &&
          alloc_dev((void**)&m->prompt, B * m->max_prompt * 4) && alloc_dev((void**)&m->prompt_len, B * 4) &&
@@ -243,6 +374,11 @@ int vspec_b200_qwen_create(const VspecB200QwenConfig* cfg, uint64_t seed, int ma
     }
     *out_model = m;
     return VSPEC_B200_OK;
+}
+
+int vspec_b200_qwen_create(const VspecB200QwenConfig* cfg, uint64_t seed, int max_batch, int max_ctx,
+                           void** out_model) {
+    return vspec_b200_qwen_create_tp(cfg, seed, max_batch, max_ctx, 1, 0, NULL, out_model);
 }
 
 int vspec_b200_qwen_generate(void* model, int batch, const int32_t* h_prompts, int prompt_len, int gen_tokens,
@@ -335,20 +471,21 @@ size_t vspec_b200_qwen_tensor(void* model, int kind, int layer, void* h_dst) {
     const void* src = NULL;
     size_t bytes = 0;
     const int g = c->group;
+    const int ba = m->bits_attn, bm = m->bits_mlp;
     if (kind == 0) { src = m->emb; bytes = (size_t)c->vocab * c->hidden * 2; }
-    else if (kind == 9) { src = m->w_lm; bytes = (size_t)c->vocab * row_bytes(c->hidden, c->bits); }
+    else if (kind == 9) { src = m->w_lm; bytes = (size_t)c->vocab * row_bytes(c->hidden, ba); }
     else if (kind == 10) { src = m->s_lm; bytes = (size_t)c->vocab * (c->hidden / g) * 2; }
     else if (kind >= 1 && kind <= 8 && layer >= 0 && layer < c->num_layers) {
         const QwenLayer* L = &m->layers[layer];
         switch (kind) {
-            case 1: src = L->w_qkv; bytes = (size_t)m->qkv_n * row_bytes(c->hidden, c->bits); break;
+            case 1: src = L->w_qkv; bytes = (size_t)m->qkv_n * row_bytes(c->hidden, ba); break;
             case 2: src = L->s_qkv; bytes = (size_t)m->qkv_n * (c->hidden / g) * 2; break;
-            case 3: src = L->w_o; bytes = (size_t)c->hidden * row_bytes(m->q_dim, c->bits); break;
+            case 3: src = L->w_o; bytes = (size_t)c->hidden * row_bytes(m->q_dim, ba); break;
             case 4: src = L->s_o; bytes = (size_t)c->hidden * (m->q_dim / g) * 2; break;
-            case 5: src = L->w_gu; bytes = (size_t)2 * c->intermediate * row_bytes(c->hidden, c->bits); break;
-            case 6: src = L->s_gu; bytes = (size_t)2 * c->intermediate * (c->hidden / g) * 2; break;
-            case 7: src = L->w_down; bytes = (size_t)c->hidden * row_bytes(c->intermediate, c->bits); break;
-            default: src = L->s_down; bytes = (size_t)c->hidden * (c->intermediate / g) * 2; break;
+            case 5: src = L->w_gu; bytes = (size_t)2 * m->inter * row_bytes(c->hidden, bm); break;
+            case 6: src = L->s_gu; bytes = (size_t)2 * m->inter * (c->hidden / g) * 2; break;
+            case 7: src = L->w_down; bytes = (size_t)c->hidden * row_bytes(m->inter, bm); break;
+            default: src = L->s_down; bytes = (size_t)c->hidden * (m->inter / g) * 2; break;
         }
     }
     if (!src) return 0;

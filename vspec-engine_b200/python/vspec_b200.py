@@ -36,12 +36,19 @@ class VspecB200Error(RuntimeError):
 class QwenConfig(ctypes.Structure):
     _fields_ = [("num_layers", c_int), ("hidden", c_int), ("num_heads", c_int), ("num_kv_heads", c_int),
                 ("head_dim", c_int), ("intermediate", c_int), ("vocab", c_int), ("bits", c_int), ("group", c_int),
-                ("rms_eps", c_float), ("rope_theta", c_float), ("logit_clip", c_float), ("page_tokens", c_int)]
+                ("rms_eps", c_float), ("rope_theta", c_float), ("logit_clip", c_float), ("page_tokens", c_int),
+                ("bits_mlp", c_int)]
 
 
 # BASELINE config 4 (Qwen3-8B shape, W4 group 128)
 QWEN3_8B = dict(num_layers=36, hidden=4096, num_heads=32, num_kv_heads=8, head_dim=128, intermediate=12288,
-                vocab=151936, bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16)
+                vocab=151936, bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16,
+                bits_mlp=0)
+
+# BASELINE config 5 (Qwen3-32B shape; attention projections and lm_head W4, MLP W3, group 128)
+QWEN3_32B = dict(num_layers=64, hidden=5120, num_heads=64, num_kv_heads=8, head_dim=128, intermediate=25600,
+                 vocab=151936, bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16,
+                 bits_mlp=3)
 
 
 def _load() -> ctypes.CDLL:
@@ -137,7 +144,12 @@ _sigs = {
     "vspec_b200_decode_next_token": ([c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                       c_void_p, c_int, c_void_p, c_void_p], c_int),
     "vspec_b200_random_fill": ([c_void_p, c_size_t, c_int, c_uint64, c_float, c_float, c_void_p], c_int),
+    "vspec_b200_random_fill_block": ([c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_uint64, c_size_t, c_size_t,
+                                      c_size_t, c_float, c_float, c_void_p], c_int),
     "vspec_b200_qwen_create": ([POINTER(QwenConfig), c_uint64, c_int, c_int, POINTER(c_void_p)], c_int),
+    "vspec_b200_nccl_unique_id": ([c_void_p], c_int),
+    "vspec_b200_qwen_create_tp": ([POINTER(QwenConfig), c_uint64, c_int, c_int, c_int, c_int, c_void_p,
+                                   POINTER(c_void_p)], c_int),
     "vspec_b200_qwen_destroy": ([c_void_p], None),
     "vspec_b200_qwen_generate": ([c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, POINTER(c_float), c_void_p],
                                  c_int),
@@ -244,15 +256,55 @@ def page_fault_flag() -> int:
     return v.value
 
 
-class QwenModel:
-    """Random-init Qwen3-shape low-bit decoder on the device (vspec_b200_qwen_*)."""
+def _prefer_wheel_nccl() -> None:
+    """Point the library at the NCCL of the `nvidia-nccl` wheel when one is
+    installed (the copy PyTorch loads), so that a process which later imports
+    torch does not meet an older system NCCL already loaded under the same
+    soname.  An explicit VSPEC_B200_NCCL_LIB is kept."""
+    if os.environ.get("VSPEC_B200_NCCL_LIB"):
+        return
+    import importlib.util
+    try:
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        spec = None
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        cand = os.path.join(base, "lib", "libnccl.so.2")
+        if os.path.exists(cand):
+            os.environ["VSPEC_B200_NCCL_LIB"] = cand
+            return
 
-    def __init__(self, cfg: dict, seed: int, max_batch: int, max_ctx: int):
+
+def nccl_unique_id() -> bytes:
+    """128-byte NCCL unique id for a tensor-parallel group (made by one rank, shared with all)."""
+    _prefer_wheel_nccl()
+    buf = ctypes.create_string_buffer(128)
+    check(lib.vspec_b200_nccl_unique_id(buf), "vspec_b200_nccl_unique_id")
+    return buf.raw
+
+
+class QwenModel:
+    """Random-init Qwen3-shape low-bit decoder on the device (vspec_b200_qwen_*).
+    With tp_size > 1 this is one rank's shard of a tensor-parallel group (the
+    current CUDA device; every rank constructs it with the same nccl_id)."""
+
+    def __init__(self, cfg: dict, seed: int, max_batch: int, max_ctx: int, tp_size: int = 1, tp_rank: int = 0,
+                 nccl_id: bytes | None = None):
         self.cfg = dict(cfg)
+        self.cfg.setdefault("bits_mlp", 0)
         self._c = QwenConfig(**self.cfg)
         h = c_void_p()
-        check(lib.vspec_b200_qwen_create(ctypes.byref(self._c), seed, max_batch, max_ctx, ctypes.byref(h)),
-              "vspec_b200_qwen_create")
+        if tp_size == 1:
+            check(lib.vspec_b200_qwen_create(ctypes.byref(self._c), seed, max_batch, max_ctx, ctypes.byref(h)),
+                  "vspec_b200_qwen_create")
+        else:
+            if nccl_id is None or len(nccl_id) != 128:
+                raise ValueError("tensor-parallel shard needs the group's 128-byte nccl_id")
+            _prefer_wheel_nccl()
+            idbuf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+            check(lib.vspec_b200_qwen_create_tp(ctypes.byref(self._c), seed, max_batch, max_ctx, tp_size, tp_rank,
+                                                idbuf, ctypes.byref(h)), "vspec_b200_qwen_create_tp")
+        self.tp_size, self.tp_rank = tp_size, tp_rank
         self.handle = h
 
     def close(self) -> None:
