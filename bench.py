@@ -56,6 +56,14 @@ def load_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def load_peak_table() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
 def load_traffic() -> float | None:
     """DRAM bytes per W4 GEMV launch from the committed ncu summary (one capture)."""
     try:
@@ -379,6 +387,74 @@ def time_decode(torch, V, world: int, rank: int, peak: float):
     }
 
 
+TP_PROMPT, TP_GEN, TP_BATCH = 1024, 128, 256
+
+
+def tp_step_work(cfg: dict, batch: int, ctx: int, tp: int) -> dict:
+    """Per-GPU algorithmic work of one config-5 decode step at tensor-parallel
+    degree tp: tensor-core FLOPs of the linears (sharded) and the replicated
+    lm_head, HBM bytes of this rank's packed weights, scales and K/V, and the
+    bytes each all-reduce sums (2 per layer, [batch, hidden] fp32)."""
+    H, I, L, V = cfg["hidden"], cfg["intermediate"], cfg["num_layers"], cfg["vocab"]
+    qd = cfg["num_heads"] * cfg["head_dim"]
+    kvd = cfg["num_kv_heads"] * cfg["head_dim"]
+    ba, bm, g = cfg["bits"], cfg["bits_mlp"] or cfg["bits"], cfg["group"]
+    attn = [(qd + 2 * kvd, H), (H, qd)]
+    mlp = [(2 * I, H), (H, I)]
+    p_attn = sum(n * k for n, k in attn)
+    p_mlp = sum(n * k for n, k in mlp)
+    p_lm = V * H
+    flops = 2 * batch * (L * (p_attn + p_mlp) / tp + p_lm)
+    wbytes = (L * (p_attn * ba / 8 + p_mlp * bm / 8 + (p_attn + p_mlp) / g * 2) / tp + p_lm * ba / 8 + p_lm / g * 2)
+    kv = batch * ctx * L * (kvd // tp) * 2 * 2
+    return {"flops": flops, "hbm_bytes": wbytes + kv, "allreduce_bytes": 2 * L * batch * H * 4 if tp > 1 else 0}
+
+
+def time_decode_tp(torch, V, world: int, rank: int, peaks: dict):
+    """Qwen3-32B shape, attention projections and lm_head
+    W4, MLP W3, group 128, random-init; batch 256 sequences of 1024 seeded
+    random prompt ids (prefilled by decode steps) + 128 greedy tokens,
+    tensor-parallel over all ranks (NCCL all-reduce after o-proj and down).
+    tok/s over the generation phase (device time, max over ranks)."""
+    import torch.distributed as dist
+    cfg = V.QWEN3_32B
+    nid = [V.nccl_unique_id() if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(nid, src=0)
+    rng = np.random.default_rng(5)
+    prompts = rng.integers(0, cfg["vocab"], size=(TP_BATCH, TP_PROMPT)).astype(np.int32)
+    model = V.QwenModel(cfg, seed=4321, max_batch=TP_BATCH, max_ctx=TP_PROMPT + TP_GEN, tp_size=world, tp_rank=rank,
+                        nccl_id=nid[0] if world > 1 else None)
+    try:
+        barrier(world)
+        toks, ms, _ = model.generate(prompts, TP_GEN)
+        ms = max_over_ranks(ms, world)
+    finally:
+        model.close()
+    step_s = ms * 1e-3 / TP_GEN
+    work = tp_step_work(cfg, TP_BATCH, TP_PROMPT + TP_GEN // 2, world)
+    tflops = work["flops"] / step_s / 1e12
+    gbs = work["hbm_bytes"] / step_s / 1e9
+    return {
+        "metric": "Qwen3-32B-shape W4/W3 tensor-parallel decode tok/s",
+        "value": round(TP_BATCH * TP_GEN / (ms * 1e-3), 2), "unit": "tok/s", "ms_per_step": round(ms / TP_GEN, 4),
+        "parallelism": f"tp{world} (NCCL all-reduce after o-proj and down, fp32 [256, 5120])",
+        "scaling": "strong",
+        "roofline": {"bound": "tensor", "flops_per_step_per_gpu": work["flops"], "achieved": round(tflops, 1),
+                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": round(tflops / peaks["bf16_tflops_sustained"], 4),
+                     "peak_source": "measured bf16_tflops_sustained (fp16 operands, same tensor rate)",
+                     "hbm_bytes_per_step_per_gpu": round(work["hbm_bytes"]), "hbm_achieved_gbs": round(gbs, 1),
+                     "allreduce_bytes_per_step": work["allreduce_bytes"]},
+        "tokens_checksum": int(np.asarray(toks, dtype=np.int64).sum() % 1000003),
+        "config": "config 5: 64 layers, hidden 5120, 64/8 heads x 128, q/k RMSNorm, SwiGLU 25600, vocab 151936, "
+                  "attention + lm_head W4, MLP W3, group 128 (fp16 scales, mid-range zero-point), random-init; "
+                  f"batch {TP_BATCH}, prompt {TP_PROMPT} seeded random ids (prefilled by decode steps), {TP_GEN} "
+                  "greedy tokens; fp16 paged KV, 16-token pages; one CUDA graph per step",
+        "data": "synthetic (seeded random weights and token ids)",
+    }
+
+
 # ------------------------------------------------------------------ CPU legs
 def cpu_oracle_sample(seconds: float = 10.0) -> dict:
     """The oracle restatement (group-wise int4, one thread) on a bounded sample
@@ -468,6 +544,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="skip the config-5 tensor-parallel decode (N >= 2)")
+    ap.add_argument("--tp1", action="store_true", help="also run config 5 on one GPU (tp1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -487,6 +565,9 @@ def main() -> None:
     attn_steps = max(3, args.steps // 5)
     attn_ms, attn_kv, attn_other = time_attention(torch, V, attn_steps, args.warmup, world)
     decode = None if args.no_decode else time_decode(torch, V, world, rank, peak)
+    tp = None
+    if not args.no_tp and (world > 1 or args.tp1):
+        tp = time_decode_tp(torch, V, world, rank, load_peak_table())
     e2e_steps = max(3, args.steps // 5)
     e2e_ms, e2e_bytes_call, h2d_call, d2h_call = time_e2e_bridge(torch, V, args.copies, e2e_steps, 2, world)
 
@@ -539,6 +620,8 @@ def main() -> None:
                       "config": "config 3: B=32 Hq=32 Hkv=8 d=128, ctx ~U[512,8192] (seeded), 16-token fp16 pages, "
                                 "page table = seeded permutation of the pool, one step = one decode-attention call"},
         "decode": decode,
+        "decode_tp": tp if tp is not None else {
+            "skipped": "config 5 is tensor-parallel over 2/4/8 GPUs; runs with --gpus >= 2 (or --tp1)"},
         "cpu_baseline": cpu,
         "clocks": clocks,
         "gpu_launches": launches * 2 + attn_steps * 2,

@@ -399,20 +399,33 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             if (old == total - 1) {
                 __threadfence();
                 const float* sbase = p.scratch + (size_t)ci * p.max_slots * (WR * m);
+                // Sum of slots [s0, s1) in slot order; the loads of a batch of
+                // eight are issued together, so the merge costs one L2 round
+                // trip per eight partials instead of one per partial.
+                auto slot_sum = [&](int s0, int s1, int z) {
+                    float sum = 0.f;
+                    for (int sb0 = s0; sb0 < s1; sb0 += 8) {
+                        float v[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            v[q] = sb0 + q < s1 ? __ldcg(sbase + (size_t)(sb0 + q) * WR * m + z) : 0.f;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            if (sb0 + q < s1) sum += v[q];
+                    }
+                    return sum;
+                };
                 for (int z = lane; z < WR * m; z += 32) {
                     const int r = z / WR, i = z - r * WR;
                     const float nr = rms ? row_norm[r] : 1.0f;
                     const int orow = L * TROWS + wrow + i;
                     if (EPI == kEpiSwiGLU) {
-                        float gs = 0.f, us = 0.f;
-                        for (int s = 0; s < n_gate; ++s) gs += __ldcg(sbase + (size_t)s * WR * m + z);
-                        for (int s = n_gate; s < total; ++s) us += __ldcg(sbase + (size_t)s * WR * m + z);
+                        float gs = slot_sum(0, n_gate, z), us = slot_sum(n_gate, total, z);
                         gs *= nr;
                         us *= nr;
                         if (orow < (p.n >> 1)) p.y[(size_t)r * (p.n >> 1) + orow] = gs / (1.0f + expf(-gs)) * us;
                     } else {
-                        float sum = 0.f;
-                        for (int s = 0; s < total; ++s) sum += __ldcg(sbase + (size_t)s * WR * m + z);
+                        float sum = slot_sum(0, total, z);
                         sum *= nr;
                         if (orow < p.n) {
                             const size_t o = (size_t)r * p.n + orow;
