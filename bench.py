@@ -597,7 +597,7 @@ def main() -> None:
     line = {
         "metric": METRIC, "value": round(gbs4, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms4 / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes -> f16 pairs, fp32 accumulate",
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes x int8 activation parts, exact int32 block dots, fp32 accumulate",
         "data": "synthetic (seeded uniform codes, fp16 scales ~U(0.005,0.02), x ~N(0,1))",
         "config": {"workload": "config 2 (BASELINE.json configs[1]) M=1 points: W4 and W3 GEMV, K=4096, N=12288, "
                                "group 128, fp16 scales, zero-point mid-range",

@@ -131,6 +131,86 @@ __device__ __forceinline__ void unpack_mm(const Chunk<BITS>& c, const int mm, ui
     }
 }
 
+// -------------------------------------------------------------------------
+// Integer-MMA decode (mma.sync m16n8k32, A unsigned 8-bit, B signed 8-bit).
+// A 32-code chunk of one row feeds four k32 MMAs; MMA q takes two registers
+// of four byte lanes each (register r = 0 goes to a0/a1, r = 1 to a2/a3).  A
+// byte carries an offset code v in [0, 2^bits) times a power of two 2^shift
+// that depends only on the MMA's class, so a register is one mask of the
+// packed word (one LOP3, no shifts for int4 and int2).  MMAs of one class
+// accumulate into their own int32 registers, which are shifted back exactly.
+// -------------------------------------------------------------------------
+template <int BITS> struct I8Cfg;
+// int4: byte i of word j holds codes 8j+2i (low nibble, class 0) and 8j+2i+1
+// (high nibble x16, class 1); MMA q = 2*class + pair, pair p -> words 2p, 2p+1.
+template <> struct I8Cfg<4> { static constexpr int kClasses = 2; };
+// int2: byte i of word j holds codes 16j+4i+s at bits 2s (class s, x4^s);
+// MMA q = s, register r = word j.
+template <> struct I8Cfg<2> { static constexpr int kClasses = 4; };
+// int3: each 24-bit group k (codes 8k..8k+7) is spread so byte i holds code
+// 8k+2i at bits 0-2 (class 0) and 8k+2i+1 at bits 3-5 (class 1, x8); MMA
+// q = 2*class + pair, pair p -> groups 2p, 2p+1.
+template <> struct I8Cfg<3> { static constexpr int kClasses = 2; };
+
+template <int BITS>
+__host__ __device__ constexpr int i8_class(int q) { return BITS == 2 ? q : (q >> 1); }
+template <int BITS>
+__host__ __device__ constexpr int i8_class_shift(int cls) { return BITS == 4 ? 4 * cls : (BITS == 3 ? 3 * cls : 2 * cls); }
+
+// Code t (0..31) of a chunk -> MMA q, register r, byte i.
+template <int BITS>
+__host__ __device__ inline void i8_code_place(int t, int& q, int& r, int& i) {
+    if (BITS == 2) {
+        q = t & 3;
+        r = t >> 4;
+        i = (t & 15) >> 2;
+    } else {
+        const int j = t >> 3;
+        i = (t & 7) >> 1;
+        q = 2 * (t & 1) + (j >> 1);
+        r = j & 1;
+    }
+}
+
+// A chunk prepared for masking: offset codes (two's-complement fields with
+// their top bit flipped, or the raw fields in the unsigned reading), and for
+// int3 the four spread 24-bit groups.
+template <int BITS> struct I8Words { uint32_t v[BITS == 2 ? 2 : 4]; };
+
+template <int BITS, bool UNSIGNED>
+__device__ __forceinline__ void i8_prepare(const Chunk<BITS>& c, I8Words<BITS>& o) {
+    if constexpr (BITS == 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o.v[j] = UNSIGNED ? c.w[j] : (c.w[j] ^ 0x88888888u);
+    } else if constexpr (BITS == 2) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) o.v[j] = UNSIGNED ? c.w[j] : (c.w[j] ^ 0xAAAAAAAAu);
+    } else {
+        uint32_t w0 = c.w[0], w1 = c.w[1], w2 = c.w[2];
+        if (!UNSIGNED) {
+            w0 ^= 0x24924924u;
+            w1 ^= 0x49249249u;
+            w2 ^= 0x92492492u;
+        }
+        const uint32_t g[4] = {w0, funnel_r(w0, w1, 24), funnel_r(w1, w2, 16), w2 >> 8};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            // codes 4..7 of the group move up 4 bits (to 16..27), then codes
+            // 2, 3 and 6, 7 up 2 more: code 2i at byte i bits 0-2, 2i+1 at 3-5
+            const uint32_t a = (g[k] & 0x0000FFFFu) | ((g[k] << 4) & 0xFFFF0000u);
+            o.v[k] = (a & 0x00FF00FFu) | ((a << 2) & 0xFF00FF00u);
+        }
+    }
+}
+
+// Register r of MMA q.
+template <int BITS>
+__device__ __forceinline__ uint32_t i8_reg(const I8Words<BITS>& o, int q, int r) {
+    if constexpr (BITS == 4) return o.v[2 * (q & 1) + r] & ((q >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu);
+    else if constexpr (BITS == 2) return o.v[r] & (0x03030303u << (2 * q));
+    else return o.v[2 * (q & 1) + r] & ((q >> 1) ? 0x38383838u : 0x07070707u);
+}
+
 // Scale / zero-point element as raw bits (fp16 or fp32 storage), read through
 // the read-only path.  Converting only where the value is used keeps the load
 // latency off the critical path.

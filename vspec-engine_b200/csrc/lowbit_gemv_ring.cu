@@ -17,11 +17,14 @@
 //     HBM sees many outstanding bulk requests without register staging;
 //   * warps 0-7 each own a 32-row (m <= 4) or 16-row slice of every tile,
 //     i.e. one or two blocks of 16 rows.  A thread (g, c) reads its 32-code
-//     chunk c of rows g and g+8 of each block from the ring, decodes it in
-//     registers into fp16 pairs (magic-number LOP3, see lowbit_decode.cuh) --
-//     the A fragments of mma.sync m16n8k16 -- and multiplies them with the
-//     activation fragments (fp32 x split into fp16 hi + lo) staged once in
-//     shared memory.  Warp-level MMA sustains ~128 codes/cycle/SM here, well
+//     chunk c of rows g and g+8 of each block from the ring and decodes it in
+//     registers into MMA A fragments, multiplied with activation fragments
+//     staged once in shared memory.  Default (IMMA): one mask per register
+//     gives offset codes as bytes for mma.sync m16n8k32 u8 x s8, against x
+//     quantised per k-block to 14-bit integers split into int8 hi/lo columns,
+//     so block dot products are exact int32.  Otherwise: fp16 pairs from a
+//     magic-number LOP3 for m16n8k16 against x split into fp16 hi + lo (see
+//     lowbit_decode.cuh).  Warp-level MMA sustains ~128 codes/cycle/SM here, well
 //     above what HBM delivers; small-N tcgen05.mma does not (it costs ~95
 //     cycles per 128x16 A tile whatever N is), so the tensor-memory path is
 //     kept for large M only;
@@ -79,12 +82,14 @@ struct RingSmem {
     uint32_t total;
 };
 
+// Activation fragments per k-block: fp16 path 4 MMA steps x NT x lanes x 16 B;
+// integer path NT x lanes x 32 B (four k32 MMAs x two registers).
 template <int BITS>
-__host__ __device__ inline RingSmem ring_smem_plan(int m, int kbt, int stages) {
+__host__ __device__ inline RingSmem ring_smem_plan(int m, int kbt, int stages, bool imma) {
     RingSmem s;
     const uint32_t stage = (uint32_t)ring_tile_rows(m) * RingCfg<BITS>::kRowBytes;
     s.frag = (uint32_t)stages * stage;
-    const uint32_t fbytes = (uint32_t)kbt * 4u * (uint32_t)ring_nt(m) * (uint32_t)ring_lanes(m) * 16u;
+    const uint32_t fbytes = (uint32_t)kbt * (uint32_t)ring_nt(m) * (uint32_t)ring_lanes(m) * (imma ? 32u : 64u);
     s.xs = s.frag + fbytes;
     s.cs = s.xs + (uint32_t)(kbt * m) * 4u;
     s.is = s.cs + (uint32_t)(kbt * m) * 4u;
@@ -116,7 +121,7 @@ __device__ __forceinline__ void lds_chunk(Chunk<BITS>& ch, const unsigned char* 
     }
 }
 
-template <int BITS, int NT, bool UNSIGNED, int EPI, bool SZ16>
+template <int BITS, int NT, bool UNSIGNED, int EPI, bool SZ16, bool IMMA>
 __global__ void __launch_bounds__(kRingThreads, 2)
 lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ GemvParams p) {
     constexpr int RB = RingCfg<BITS>::kRowBytes;
@@ -132,7 +137,7 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
     const int m = p.m;
     const int kbt = p.kb_total;
     const int lanes = ring_lanes(m);
-    const RingSmem plan = ring_smem_plan<BITS>(m, kbt, NS);
+    const RingSmem plan = ring_smem_plan<BITS>(m, kbt, NS, IMMA);
     unsigned char* wring = base;
     const uint4* frag = reinterpret_cast<const uint4*>(base + plan.frag);
     float* xs = reinterpret_cast<float*>(base + plan.xs);
@@ -192,7 +197,99 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             if (lane == 0) row_norm[r] = 1.0f / sqrtf(ss / (float)K + p.eps);
         }
     }
-    {
+    if constexpr (IMMA) {
+        // Per (k-block, row) of the k-blocks this CTA touches: an exact
+        // power-of-two scale sc (block max |x| * sc in [2^13, 2^14)), the
+        // integer activations q = rint(x * sc) in [-2^14, 2^14] split as
+        // q = 256 * xh + xl (xh in [-64, 64], xl in [-128, 127]) into the int8
+        // B columns 2r (xh) and 2r + 1 (xl), and X = sum q.  Integer MMAs
+        // then give sum q * v exactly; the epilogue removes the offset
+        // (2^(bits-1) + zp) * X and multiplies by s / sc.
+        const int kb_first = n_units >= kbt ? 0 : u0 % kbt;
+        const int kb_count = n_units >= kbt ? kbt : n_units;
+        constexpr float kOff = (float)(1 << (BITS - 1));
+        int boff[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int t = 4 * lane + e;   // code of the k-block this lane holds
+            int q, r, i;
+            i8_code_place<BITS>(t & 31, q, r, i);
+            boff[e] = (t >> 5) * 32 + q * 8 + r * 4 + i;   // + B lane 4n' of the column, x 32
+        }
+        unsigned char* fbase = base + plan.frag;
+        constexpr int NW = kRingThreads / 32;
+        constexpr int QB = 4;
+        const int npairs = kb_count * m;
+        for (int pr0 = warp; pr0 < npairs; pr0 += QB * NW) {
+            float4 v[QB];
+            int kbq[QB], rq[QB];
+#pragma unroll
+            for (int q = 0; q < QB; ++q) {
+                const int pr = pr0 + q * NW;
+                rq[q] = pr % m;
+                int kb = kb_first + pr / m;
+                kbq[q] = kb >= kbt ? kb - kbt : kb;
+                v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (pr < npairs) {
+                    const int t = kbq[q] * 128 + lane * 4;
+                    v[q] = *reinterpret_cast<const float4*>(p.x + (size_t)rq[q] * K + t);
+                    if (rms) {
+                        const float4 wn = *reinterpret_cast<const float4*>(p.norm_w + t);
+                        v[q].x *= wn.x; v[q].y *= wn.y; v[q].z *= wn.z; v[q].w *= wn.w;
+                    }
+                }
+            }
+            float amax[QB];
+#pragma unroll
+            for (int q = 0; q < QB; ++q)
+                amax[q] = fmaxf(fmaxf(fabsf(v[q].x), fabsf(v[q].y)), fmaxf(fabsf(v[q].z), fabsf(v[q].w)));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int q = 0; q < QB; ++q) amax[q] = fmaxf(amax[q], __shfl_xor_sync(0xffffffffu, amax[q], off));
+            int qv[QB][4], xsum[QB];
+            float sc[QB];
+#pragma unroll
+            for (int q = 0; q < QB; ++q) {
+                int sbits = 127;   // sc = 2^(13 - floor(log2 amax)) from the exponent bits
+                if (amax[q] > 0.f && isfinite(amax[q])) {
+                    sbits = 267 - (int)((__float_as_uint(amax[q]) >> 23) & 0xFFu);
+                    sbits = sbits < 1 ? 1 : (sbits > 253 ? 253 : sbits);
+                }
+                sc[q] = __uint_as_float((uint32_t)sbits << 23);
+                qv[q][0] = __float2int_rn(v[q].x * sc[q]);
+                qv[q][1] = __float2int_rn(v[q].y * sc[q]);
+                qv[q][2] = __float2int_rn(v[q].z * sc[q]);
+                qv[q][3] = __float2int_rn(v[q].w * sc[q]);
+                xsum[q] = (qv[q][0] + qv[q][1]) + (qv[q][2] + qv[q][3]);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int q = 0; q < QB; ++q) xsum[q] += __shfl_xor_sync(0xffffffffu, xsum[q], off);
+#pragma unroll
+            for (int q = 0; q < QB; ++q) {
+                if (pr0 + q * NW < npairs) {
+                    const int kb = kbq[q], r = rq[q];
+                    if (lane == 0) {
+                        const float X = (float)xsum[q];
+                        xs[kb * m + r] = X;
+                        cs[kb * m + r] = kOff * X;
+                        isc[kb * m + r] = 1.0f / sc[q];   // power of two: exact
+                    }
+                    const int n = 2 * r;   // xh column; xl is n + 1, four B lanes on
+                    unsigned char* fb = fbase + ((size_t)(kb * NT + (n >> 3)) * lanes + 4 * (n & 7)) * 32;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int xh = (qv[q][e] + 128) >> 8;
+                        const int xl = qv[q][e] - (xh << 8);
+                        fb[boff[e]] = (unsigned char)(signed char)xh;
+                        fb[boff[e] + 128] = (unsigned char)(signed char)xl;
+                    }
+                }
+            }
+        }
+    } else {
         // Per (k-block, row) of the k-blocks this CTA touches: an exact
         // power-of-two scale (block max |x| lands in [2^13, 2^14)), the scaled
         // sums and the B fragments.  Lane l holds codes 4l..4l+3 of the block;
@@ -462,6 +559,65 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                         if (++ring == NS) { ring = 0; ring_ph ^= 1u; }
 
                         const int kb = c_kb;
+                        // e[j][nt][h]: the block's dot product for rows g (h=0) and g+8
+                        // of row block j, activation row 4*nt + c, before scaling
+                        float e[RBW][NT][2];
+                        if constexpr (IMMA) {
+                            constexpr int NC = I8Cfg<BITS>::kClasses;
+                            const uint4* fb = frag + (size_t)kb * NT * lanes * 2;
+                            uint4 bb[NT][2];
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt) {
+                                bb[nt][0] = bb[nt][1] = make_uint4(0u, 0u, 0u, 0u);
+                                if (lane_has_b) {
+                                    bb[nt][0] = fb[(nt * lanes + lane) * 2];
+                                    bb[nt][1] = fb[(nt * lanes + lane) * 2 + 1];
+                                }
+                            }
+                            I8Words<BITS> wv[RBW][2];
+#pragma unroll
+                            for (int j = 0; j < RBW; ++j) {
+                                i8_prepare<BITS, UNSIGNED>(ch[j][0], wv[j][0]);
+                                i8_prepare<BITS, UNSIGNED>(ch[j][1], wv[j][1]);
+                            }
+                            int D[RBW][NC][NT][4];
+#pragma unroll
+                            for (int j = 0; j < RBW; ++j)
+#pragma unroll
+                                for (int cl = 0; cl < NC; ++cl)
+#pragma unroll
+                                    for (int nt = 0; nt < NT; ++nt)
+                                        D[j][cl][nt][0] = D[j][cl][nt][1] = D[j][cl][nt][2] = D[j][cl][nt][3] = 0;
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                                for (int j = 0; j < RBW; ++j) {
+                                    const uint32_t a[4] = {i8_reg<BITS>(wv[j][0], q, 0), i8_reg<BITS>(wv[j][1], q, 0),
+                                                           i8_reg<BITS>(wv[j][0], q, 1), i8_reg<BITS>(wv[j][1], q, 1)};
+#pragma unroll
+                                    for (int nt = 0; nt < NT; ++nt) {
+                                        const uint4& b = bb[nt][q >> 1];
+                                        imma_16832_u8s8(D[j][i8_class<BITS>(q)][nt], a, (q & 1) ? b.z : b.x,
+                                                        (q & 1) ? b.w : b.y);
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int j = 0; j < RBW; ++j)
+#pragma unroll
+                                for (int nt = 0; nt < NT; ++nt) {
+                                    int cmb[4];
+#pragma unroll
+                                    for (int k4 = 0; k4 < 4; ++k4) {
+                                        int v = D[j][0][nt][k4];
+#pragma unroll
+                                        for (int cl = 1; cl < NC; ++cl) v += D[j][cl][nt][k4] >> i8_class_shift<BITS>(cl);
+                                        cmb[k4] = v;
+                                    }
+                                    e[j][nt][0] = (float)(cmb[0] * 256 + cmb[1]);   // xh * 256 + xl parts
+                                    e[j][nt][1] = (float)(cmb[2] * 256 + cmb[3]);
+                                }
+                        } else {
                         const uint4* fb = frag + (size_t)kb * 4 * NT * lanes;
                         // per row block, even / odd MMAs accumulate apart (shorter chains)
                         float d[RBW][2][NT][4];
@@ -495,6 +651,14 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                                 }
                             }
                         }
+#pragma unroll
+                        for (int j = 0; j < RBW; ++j)
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt) {
+                                e[j][nt][0] = (d[j][0][nt][0] + d[j][1][nt][0]) + (d[j][0][nt][1] + d[j][1][nt][1]);
+                                e[j][nt][1] = (d[j][0][nt][2] + d[j][1][nt][2]) + (d[j][0][nt][3] + d[j][1][nt][3]);
+                            }
+                        }
                         float sv[RBW][2], zv[RBW][2];
 #pragma unroll
                         for (int j = 0; j < RBW; ++j) {
@@ -513,10 +677,8 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                                 const float inv = isc[kb * m + r];
 #pragma unroll
                                 for (int j = 0; j < RBW; ++j) {
-                                    const float e0 = (d[j][0][nt][0] + d[j][1][nt][0]) + (d[j][0][nt][1] + d[j][1][nt][1]);
-                                    const float e1 = (d[j][0][nt][2] + d[j][1][nt][2]) + (d[j][0][nt][3] + d[j][1][nt][3]);
-                                    acc[j][nt][0] = fmaf(sv[j][0] * inv, e0 - fmaf(zv[j][0], xsum, coff), acc[j][nt][0]);
-                                    acc[j][nt][1] = fmaf(sv[j][1] * inv, e1 - fmaf(zv[j][1], xsum, coff), acc[j][nt][1]);
+                                    acc[j][nt][0] = fmaf(sv[j][0] * inv, e[j][nt][0] - fmaf(zv[j][0], xsum, coff), acc[j][nt][0]);
+                                    acc[j][nt][1] = fmaf(sv[j][1] * inv, e[j][nt][1] - fmaf(zv[j][1], xsum, coff), acc[j][nt][1]);
                                 }
                             }
                         }
@@ -565,10 +727,10 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
 // CTAs share an SM, or, when the activation fragments are too large for that,
 // the deepest ring one CTA can hold.  0 when not even 4 stages fit.
 template <int BITS>
-static int ring_pick_stages(int m, int kbt, size_t* smem_bytes) {
+static int ring_pick_stages(int m, int kbt, size_t* smem_bytes, bool imma) {
     const uint32_t sbytes = (uint32_t)ring_tile_rows(m) * RingCfg<BITS>::kRowBytes;
     const uint32_t stage = sbytes + 16u;   // ring bytes + 2 barriers
-    const uint32_t fixed = ring_smem_plan<BITS>(m, kbt, 0).total + 1024u;   // + base alignment
+    const uint32_t fixed = ring_smem_plan<BITS>(m, kbt, 0, imma).total + 1024u;   // + base alignment
     const int max_ns = (int)(kRingMaxRing / sbytes);
     int ns = fixed < kRingSmemShared ? (int)((kRingSmemShared - fixed) / stage) : 0;
     if (ns > max_ns) ns = max_ns;
@@ -577,14 +739,25 @@ static int ring_pick_stages(int m, int kbt, size_t* smem_bytes) {
         if (ns > max_ns) ns = max_ns;
     }
     if (ns < 3) return 0;
-    *smem_bytes = ring_smem_plan<BITS>(m, kbt, ns).total + 1024u;
+    *smem_bytes = ring_smem_plan<BITS>(m, kbt, ns, imma).total + 1024u;
     return ns;
 }
 
-static int ring_stages_for(int bits, int m, int kbt, size_t* smem) {
-    if (bits == 4) return ring_pick_stages<4>(m, kbt, smem);
-    if (bits == 3) return ring_pick_stages<3>(m, kbt, smem);
-    return ring_pick_stages<2>(m, kbt, smem);
+static int ring_stages_for(int bits, int m, int kbt, size_t* smem, bool imma) {
+    if (bits == 4) return ring_pick_stages<4>(m, kbt, smem, imma);
+    if (bits == 3) return ring_pick_stages<3>(m, kbt, smem, imma);
+    return ring_pick_stages<2>(m, kbt, smem, imma);
+}
+
+// Integer-MMA decode (VSPEC_B200_GEMV_IMMA, default on; "0" selects the
+// fp16-pair decode with hi/lo fp16 activations).
+static bool ring_imma() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_GEMV_IMMA");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
 }
 
 // Persistent CTAs per SM (VSPEC_B200_RING_CTAS_PER_SM, 1 or 2; default 2:
@@ -605,14 +778,14 @@ struct RingPlan {
     size_t scratch_floats;
 };
 
-static RingPlan ring_plan(int m, int n, int k, int bits, bool swiglu) {
+static RingPlan ring_plan(int m, int n, int k, int bits, bool swiglu, bool imma) {
     RingPlan rp;
     memset(&rp, 0, sizeof(rp));
     const int kbt = k / 128;
     const int trows = ring_tile_rows(m);
     rp.tiles = (n + trows - 1) / trows;
     const long long U = (long long)rp.tiles * kbt;
-    rp.stages = ring_stages_for(bits, m, kbt, &rp.smem);
+    rp.stages = ring_stages_for(bits, m, kbt, &rp.smem, imma);
     // two CTAs per SM only when the shared-memory plan lets them co-reside
     const int per_sm = rp.smem <= kRingSmemShared ? ring_ctas_per_sm() : 1;
     const int ctas = device_sm_count() * per_sm;
@@ -640,15 +813,17 @@ bool gemv_ring_supported(const GemvParams& p, int bits, size_t counter_slots) {
     const int logical = swiglu ? tiles / 2 : tiles;
     if ((size_t)logical * kRingConsumerWarps > counter_slots) return false;
     size_t smem = 0;
-    return ring_stages_for(bits, p.m, p.k / 128, &smem) > 0;
+    return ring_stages_for(bits, p.m, p.k / 128, &smem, ring_imma()) > 0;
 }
 
 size_t gemv_ring_scratch_floats(int m, int n, int k, bool swiglu) {
     if (k < 128) return 0;
     size_t most = 0;
     for (int bits = 2; bits <= 4; ++bits) {
-        const size_t f = ring_plan(m, n, k, bits, swiglu).scratch_floats;
-        if (f > most) most = f;
+        for (int im = 0; im < 2; ++im) {
+            const size_t f = ring_plan(m, n, k, bits, swiglu, im != 0).scratch_floats;
+            if (f > most) most = f;
+        }
     }
     return most;
 }
@@ -663,10 +838,10 @@ int gemv_ring_read_and_clear_timeout(int* out) {
     return VSPEC_B200_OK;
 }
 
-template <int BITS, int NT, bool UNS, int EPI, bool SZ16>
+template <int BITS, int NT, bool UNS, int EPI, bool SZ16, bool IMMA>
 static cudaError_t launch_ring_k(const CUtensorMap& map, const GemvParams& p, int grid, size_t smem, cudaStream_t st,
                                  bool pdl) {
-    auto kern = lowbit_gemv_ring_kernel<BITS, NT, UNS, EPI, SZ16>;
+    auto kern = lowbit_gemv_ring_kernel<BITS, NT, UNS, EPI, SZ16, IMMA>;
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -694,8 +869,13 @@ static cudaError_t launch_ring_k(const CUtensorMap& map, const GemvParams& p, in
 template <int BITS, int NT, bool UNS, int EPI>
 static cudaError_t launch_ring_t(const CUtensorMap& map, const GemvParams& p, int grid, size_t smem, cudaStream_t st,
                                  bool pdl) {
-    if (p.flags & VSPEC_B200_F_SZ_F16) return launch_ring_k<BITS, NT, UNS, EPI, true>(map, p, grid, smem, st, pdl);
-    return launch_ring_k<BITS, NT, UNS, EPI, false>(map, p, grid, smem, st, pdl);
+    const bool sz16 = (p.flags & VSPEC_B200_F_SZ_F16) != 0;
+    if (ring_imma()) {
+        if (sz16) return launch_ring_k<BITS, NT, UNS, EPI, true, true>(map, p, grid, smem, st, pdl);
+        return launch_ring_k<BITS, NT, UNS, EPI, false, true>(map, p, grid, smem, st, pdl);
+    }
+    if (sz16) return launch_ring_k<BITS, NT, UNS, EPI, true, false>(map, p, grid, smem, st, pdl);
+    return launch_ring_k<BITS, NT, UNS, EPI, false, false>(map, p, grid, smem, st, pdl);
 }
 
 template <int BITS, int NT>
@@ -717,7 +897,7 @@ static cudaError_t launch_ring_bits(const CUtensorMap& map, const GemvParams& p,
 // p must carry kb_total / kb_per_group(_shift), counters and scratch.
 int gemv_ring_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl) {
     const bool swiglu = (p.flags & VSPEC_B200_F_SWIGLU) != 0;
-    const RingPlan rp = ring_plan(p.m, p.n, p.k, bits, swiglu);
+    const RingPlan rp = ring_plan(p.m, p.n, p.k, bits, swiglu, ring_imma());
     if (rp.stages <= 0 || rp.grid <= 0) { set_error("shape too large for the ring GEMV"); return VSPEC_B200_ERR_UNSUPPORTED; }
     CUtensorMap map;
     const CUtensorMapSwizzle swz = bits == 4 ? CU_TENSOR_MAP_SWIZZLE_64B
