@@ -181,6 +181,67 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
         }
     }
 
+    // ---- consumer state and the first scale / zero-point loads: model
+    // data like the weights, so they are requested before the dependency
+    // wait and arrive while the activation prologue runs ----
+    // Warp w owns rows [w*16*RBW, (w+1)*16*RBW) of every tile: RBW blocks
+    // of 16 rows, thread (g, c) rows g and g+8 of each block, chunk c.
+    const int g = lane >> 2;
+    const int c = lane & 3;
+    const int wrow = warp * 16 * RBW;
+    const bool lane_has_b = lane < lanes;
+    const bool has_s = p.s != nullptr, has_zp = p.zp != nullptr;
+    constexpr int SZB = SZ16 ? 2 : 4;   // bytes per scale / zero-point element
+    const int half_tiles = p.tiles >> 1;
+    // scale / zero-point prefetch, PD units ahead, as raw bits.  Byte
+    // offsets of this thread's rows in the current tile are kept and only
+    // re-derived at tile boundaries.
+    uint32_t sz[PD][RBW][4];
+    int s_tile = u0 / kbt, s_kb = u0 - s_tile * kbt;
+    const unsigned char* sb = reinterpret_cast<const unsigned char*>(p.s);
+    const unsigned char* zb = reinterpret_cast<const unsigned char*>(p.zp);
+    size_t srow[RBW][2];
+    auto set_srows = [&]() {
+#pragma unroll
+        for (int j = 0; j < RBW; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                int r = s_tile * TROWS + wrow + 16 * j + g + 8 * h;
+                r = r < p.n ? r : p.n - 1;
+                srow[j][h] = (size_t)r * p.n_groups * SZB;
+            }
+    };
+    set_srows();
+    auto ld_sz = [&](const unsigned char* b, size_t off) -> uint32_t {
+        if constexpr (SZ16) return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(b + off));
+        else return __ldg(reinterpret_cast<const unsigned int*>(b + off));
+    };
+    auto issue_sz = [&](uint32_t (&d)[RBW][4]) {
+        const int grp = p.kb_per_group_shift >= 0 ? (s_kb >> p.kb_per_group_shift) : s_kb / p.kb_per_group;
+        const uint32_t go = (uint32_t)grp * SZB;
+#pragma unroll
+        for (int j = 0; j < RBW; ++j) {
+            if (has_s) {
+                d[j][0] = ld_sz(sb, srow[j][0] + go);
+                d[j][2] = ld_sz(sb, srow[j][1] + go);
+            }
+            if (has_zp) {
+                d[j][1] = ld_sz(zb, srow[j][0] + go);
+                d[j][3] = ld_sz(zb, srow[j][1] + go);
+            }
+        }
+        if (++s_kb == kbt) {
+            s_kb = 0;
+            ++s_tile;
+            set_srows();
+        }
+    };
+    if (warp < kRingConsumerWarps) {
+#pragma unroll
+        for (int st = 0; st < PD; ++st)
+            if (st < n_units) issue_sz(sz[st]);
+    }
+
     // ---- activation prologue (x may be the previous kernel's output) ----
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     const int K = p.k;
@@ -243,10 +304,10 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
 #pragma unroll
             for (int q = 0; q < QB; ++q)
                 amax[q] = fmaxf(fmaxf(fabsf(v[q].x), fabsf(v[q].y)), fmaxf(fabsf(v[q].z), fabsf(v[q].w)));
+            // |x| bit patterns order like the values: one warp max each
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-                for (int q = 0; q < QB; ++q) amax[q] = fmaxf(amax[q], __shfl_xor_sync(0xffffffffu, amax[q], off));
+            for (int q = 0; q < QB; ++q)
+                amax[q] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax[q])));
             int qv[QB][4], xsum[QB];
             float sc[QB];
 #pragma unroll
@@ -264,9 +325,7 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                 xsum[q] = (qv[q][0] + qv[q][1]) + (qv[q][2] + qv[q][3]);
             }
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-                for (int q = 0; q < QB; ++q) xsum[q] += __shfl_xor_sync(0xffffffffu, xsum[q], off);
+            for (int q = 0; q < QB; ++q) xsum[q] = __reduce_add_sync(0xffffffffu, xsum[q]);
 #pragma unroll
             for (int q = 0; q < QB; ++q) {
                 if (pr0 + q * NW < npairs) {
@@ -392,65 +451,12 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
         // ======================= consumer warps ===============================
         // Warp w owns rows [w*16*RBW, (w+1)*16*RBW) of every tile: RBW blocks
         // of 16 rows, thread (g, c) rows g and g+8 of each block, chunk c.
-        const int g = lane >> 2;
-        const int c = lane & 3;
-        const int wrow = warp * 16 * RBW;
-        const bool lane_has_b = lane < lanes;
-        const bool has_s = p.s != nullptr, has_zp = p.zp != nullptr;
-        constexpr int SZB = SZ16 ? 2 : 4;   // bytes per scale / zero-point element
-        const int half_tiles = p.tiles >> 1;
         float acc[RBW][NT][2];
 #pragma unroll
         for (int j = 0; j < RBW; ++j)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) acc[j][nt][0] = acc[j][nt][1] = 0.f;
 
-        // scale / zero-point prefetch, PD units ahead, as raw bits.  Byte
-        // offsets of this thread's rows in the current tile are kept and only
-        // re-derived at tile boundaries.
-        uint32_t sz[PD][RBW][4];
-        int s_tile = u0 / kbt, s_kb = u0 - s_tile * kbt;
-        const unsigned char* sb = reinterpret_cast<const unsigned char*>(p.s);
-        const unsigned char* zb = reinterpret_cast<const unsigned char*>(p.zp);
-        size_t srow[RBW][2];
-        auto set_srows = [&]() {
-#pragma unroll
-            for (int j = 0; j < RBW; ++j)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    int r = s_tile * TROWS + wrow + 16 * j + g + 8 * h;
-                    r = r < p.n ? r : p.n - 1;
-                    srow[j][h] = (size_t)r * p.n_groups * SZB;
-                }
-        };
-        set_srows();
-        auto ld_sz = [&](const unsigned char* b, size_t off) -> uint32_t {
-            if constexpr (SZ16) return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(b + off));
-            else return __ldg(reinterpret_cast<const unsigned int*>(b + off));
-        };
-        auto issue_sz = [&](uint32_t (&d)[RBW][4]) {
-            const int grp = p.kb_per_group_shift >= 0 ? (s_kb >> p.kb_per_group_shift) : s_kb / p.kb_per_group;
-            const uint32_t go = (uint32_t)grp * SZB;
-#pragma unroll
-            for (int j = 0; j < RBW; ++j) {
-                if (has_s) {
-                    d[j][0] = ld_sz(sb, srow[j][0] + go);
-                    d[j][2] = ld_sz(sb, srow[j][1] + go);
-                }
-                if (has_zp) {
-                    d[j][1] = ld_sz(zb, srow[j][0] + go);
-                    d[j][3] = ld_sz(zb, srow[j][1] + go);
-                }
-            }
-            if (++s_kb == kbt) {
-                s_kb = 0;
-                ++s_tile;
-                set_srows();
-            }
-        };
-#pragma unroll
-        for (int st = 0; st < PD; ++st)
-            if (st < n_units) issue_sz(sz[st]);
 
         int c_tile = u0 / kbt, c_kb = u0 - c_tile * kbt;
         int ring = 0;
@@ -488,13 +494,19 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                         part[r * WR + 16 * j + g + 8] = acc[j][nt][1];
                     }
                 }
-            __threadfence();
+            // message passing: the warp's stores, then (lane 0) a release
+            // fence and the counter bump; the warp that completes the count
+            // acquires before it reads the other slots
             __syncwarp();
             int old = 0;
-            if (lane == 0) old = atomicAdd(p.counters + ci, 1);
+            if (lane == 0) {
+                asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+                old = atomicAdd(p.counters + ci, 1);
+                if (old == total - 1) asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+            }
             old = __shfl_sync(0xffffffffu, old, 0);
             if (old == total - 1) {
-                __threadfence();
+                __syncwarp();
                 const float* sbase = p.scratch + (size_t)ci * p.max_slots * (WR * m);
                 // Sum of slots [s0, s1) in slot order; the loads of a batch of
                 // eight are issued together, so the merge costs one L2 round
