@@ -153,8 +153,13 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
     const int lane = tid & 31;
     const long long U = (long long)p.tiles * kbt;
     const long long C = gridDim.x;
-    const int u0 = (int)(((long long)blockIdx.x * U) / C);
-    const int u1 = (int)(((long long)(blockIdx.x + 1) * U) / C);
+    // units [u0, u1) of this CTA: a contiguous run in tile-major order, or
+    // (tile_parts P > 0) part blockIdx % P of tile blockIdx / P
+    const int TP = p.tile_parts;
+    const int tp_tile = TP > 0 ? (int)blockIdx.x / TP : 0;
+    const int tp_part = TP > 0 ? (int)blockIdx.x - tp_tile * TP : 0;
+    const int u0 = TP > 0 ? tp_tile * kbt + (tp_part * kbt) / TP : (int)(((long long)blockIdx.x * U) / C);
+    const int u1 = TP > 0 ? tp_tile * kbt + ((tp_part + 1) * kbt) / TP : (int)(((long long)(blockIdx.x + 1) * U) / C);
     const int n_units = u1 - u0;
 
     if (tid == 0) {
@@ -467,9 +472,21 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             constexpr int WR = 16 * RBW;   // rows of this warp's slice
             auto first_cta = [&](long long u) { return (int)(((u + 1) * C - 1) / U); };
             int L = tile;
-            int slot = (int)blockIdx.x - first_cta((long long)tile * kbt);
-            int total = first_cta((long long)(tile + 1) * kbt - 1) - first_cta((long long)tile * kbt) + 1;
-            int n_gate = total;
+            int slot, total, n_gate;
+            if (TP > 0) {
+                // one tile per CTA: slot = part; SwiGLU gate parts first, then up parts
+                slot = tp_part;
+                total = n_gate = TP;
+                if (EPI == kEpiSwiGLU) {
+                    const bool up = tile >= half_tiles;
+                    L = up ? tile - half_tiles : tile;
+                    slot += up ? TP : 0;
+                    total = 2 * TP;
+                }
+            } else {
+            slot = (int)blockIdx.x - first_cta((long long)tile * kbt);
+            total = first_cta((long long)(tile + 1) * kbt - 1) - first_cta((long long)tile * kbt) + 1;
+            n_gate = total;
             if (EPI == kEpiSwiGLU) {
                 const bool up = tile >= half_tiles;
                 L = up ? tile - half_tiles : tile;
@@ -481,6 +498,7 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                 n_gate = g_n;
                 total = g_n + u_n;
                 slot = up ? g_n + ((int)blockIdx.x - u_fw) : ((int)blockIdx.x - g_fw);
+            }
             }
             const int ci = L * kRingConsumerWarps + warp;   // counter of this warp's slice
             float* part = p.scratch + ((size_t)ci * p.max_slots + slot) * (WR * m);
@@ -785,7 +803,7 @@ static int ring_ctas_per_sm() {
 }
 
 struct RingPlan {
-    int tiles, grid, max_slots, stages;
+    int tiles, grid, max_slots, stages, tile_parts;
     size_t smem;
     size_t scratch_floats;
 };
@@ -806,6 +824,20 @@ static RingPlan ring_plan(int m, int n, int k, int bits, bool swiglu, bool imma)
     const long long per = U / rp.grid;
     int per_tile = (int)((kbt + per - 1) / per) + 1;
     if (per_tile > rp.grid) per_tile = rp.grid;
+    // Fewer tiles than CTA slots: split every tile's k-blocks over P CTAs
+    // instead, when that costs no more units on the busiest CTA.  No CTA then
+    // crosses a tile boundary, so none pays a mid-run merge.
+    if (rp.tiles <= ctas) {
+        int P = ctas / rp.tiles;
+        if (P > kbt) P = kbt;
+        const long long tp_max = (kbt + P - 1) / P;
+        const long long ct_max = (U + ctas - 1) / ctas;
+        if (tp_max <= ct_max) {
+            rp.tile_parts = P;
+            rp.grid = rp.tiles * P;
+            per_tile = P;
+        }
+    }
     rp.max_slots = swiglu ? 2 * per_tile : per_tile;
     const int logical = swiglu ? rp.tiles / 2 : rp.tiles;
     rp.scratch_floats = (size_t)logical * kRingConsumerWarps * rp.max_slots * (trows / kRingConsumerWarps) * m;
@@ -921,6 +953,7 @@ int gemv_ring_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st
     p.max_slots = rp.max_slots;
     p.total_warps = rp.grid;
     p.stages = rp.stages;
+    p.tile_parts = rp.tile_parts;
     cudaError_t e;
     const bool uns = unsigned_codes != 0;
     if (bits == 4) e = launch_ring_bits<4>(map, p, uns, swiglu, rp.grid, rp.smem, st, pdl);

@@ -30,6 +30,7 @@ struct GemvParams {
     float* scratch;          // [counters][max_slots][16*m] fp32 partials
     int* counters;           // [counters], zero between launches
     int stages;              // tcgen05 path: weight ring depth
+    int tile_parts;          // ring path: 0 = contiguous unit runs, P = each tile's k-blocks split over P CTAs
 };
 
 constexpr int kEpiPlain = 0;
