@@ -324,6 +324,29 @@ def test_fast_paths_fused_epilogues(path):
     assert rel_err(y, gate / (1.0 + np.exp(-gate)) * up) <= RTOL_F32
 
 
+@pytest.mark.parametrize("m,n", [(1, 12288), (4, 9984), (7, 12288)])
+def test_ring_cluster_merge_epilogues(m, n):
+    """Shapes whose tiles split over 2..8 CTAs per tile take the cluster
+    (distributed shared memory) split-K merge: residual and RMSNorm epilogues
+    against the oracle, and the result bit-identical to a second launch."""
+    rng = np.random.default_rng(90 + m)
+    k, g, bits = 4096, 32, 4
+    w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=True, zp_mode="none")
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    nw = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    xh = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6) * nw
+    deq = dequant_np(w, n, k, bits, s, None, g, unsigned=True)
+    y = run_linear(x, w, s, None, n, k, bits, g, flags=V.F_RESIDUAL | V.F_UNSIGNED | V.F_SZ_F16, residual=res,
+                   path=V.PATH_RING)
+    assert rel_err(y, x.astype(np.float64) @ deq.T + res) <= RTOL_F32
+    f = V.F_RMSNORM | V.F_UNSIGNED | V.F_SZ_F16
+    y1 = run_linear(x, w, s, None, n, k, bits, g, flags=f, norm_w=nw, eps=1e-6, path=V.PATH_RING)
+    y2 = run_linear(x, w, s, None, n, k, bits, g, flags=f, norm_w=nw, eps=1e-6, path=V.PATH_RING)
+    assert rel_err(y1, xh @ deq.T) <= RTOL_F32
+    assert np.array_equal(y1, y2)
+
+
 def test_large_n_beyond_tile_counters():
     """More output tiles than split-K counters (the fixed 16384-slot region):
     automatic dispatch stays correct (the any-shape kernel runs) and the

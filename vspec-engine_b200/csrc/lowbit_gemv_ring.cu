@@ -11,7 +11,9 @@
 //   * unit = (tile of W, 128-code k-block), a tile being 256 rows for m <= 4
 //     and 128 rows for m <= 8; persistent CTAs (two per SM when the shared
 //     memory plan allows) own contiguous runs of units in tile-major order
-//     (split-K across CTAs);
+//     (split-K across CTAs), or, when the tiles are fewer than the CTA
+//     slots, each tile's k-blocks are split evenly over P CTAs so that no
+//     CTA crosses a tile boundary;
 //   * warp 8 (one thread) streams the units' weight tiles with 2-D TMA into a
 //     deep shared-memory ring (8-48 stages, 60-190 KB in flight per SM), so
 //     HBM sees many outstanding bulk requests without register staging;
@@ -35,6 +37,10 @@
 //     the slice's counter; the warp that completes the count sums the slots in
 //     CTA order (deterministic), applies the epilogue (residual, SwiGLU,
 //     RMSNorm row factor) and resets the counter.  No warp waits on another.
+//     When the P parts of a tile can run as one thread-block cluster (all
+//     clusters resident in one wave), the partials stay in shared memory and
+//     the cluster sums them through distributed shared memory after a
+//     cluster barrier instead, in part order.
 // Every CTA triggers programmatic dependent launch at its start, so the next
 // launch in the stream becomes resident as soon as resources free up and
 // stages its weights before it waits for this one.  Every wait is bounded.
@@ -78,6 +84,7 @@ __host__ __device__ inline int ring_tile_rows(int m) { return 16 * ring_row_bloc
 struct RingSmem {
     uint32_t frag;        // offsets from the 1024-aligned base; the ring starts at 0
     uint32_t xs, cs, is;  // per (k-block, row): scaled sum, decode offset, inverse scale
+    uint32_t cpart;       // this CTA's tile partial for the cluster merge
     uint32_t misc;
     uint32_t total;
 };
@@ -93,7 +100,8 @@ __host__ __device__ inline RingSmem ring_smem_plan(int m, int kbt, int stages, b
     s.xs = s.frag + fbytes;
     s.cs = s.xs + (uint32_t)(kbt * m) * 4u;
     s.is = s.cs + (uint32_t)(kbt * m) * 4u;
-    s.misc = (s.is + (uint32_t)(kbt * m) * 4u + 15u) & ~15u;
+    s.cpart = (s.is + (uint32_t)(kbt * m) * 4u + 15u) & ~15u;   // cluster merge: [warp][row][slice row] fp32
+    s.misc = s.cpart + (uint32_t)ring_tile_rows(m) * (uint32_t)m * 4u;
     s.total = s.misc + 8u * 2u * (uint32_t)stages + 64u;   // full/empty barriers, abort flag, row norms
     return s;
 }
@@ -143,6 +151,7 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
     float* xs = reinterpret_cast<float*>(base + plan.xs);
     float* cs = reinterpret_cast<float*>(base + plan.cs);
     float* isc = reinterpret_cast<float*>(base + plan.is);
+    float* cpart = reinterpret_cast<float*>(base + plan.cpart);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + plan.misc);
     uint64_t* empty = full + NS;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NS);
@@ -470,6 +479,26 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
 
         auto flush = [&](int tile) {
             constexpr int WR = 16 * RBW;   // rows of this warp's slice
+            if (p.cluster_merge) {
+                // the tile's parts are one cluster: keep the partial in shared
+                // memory; the cluster reduces it after the barrier below
+                float* cp = cpart + warp * (WR * m);
+#pragma unroll
+                for (int j = 0; j < RBW; ++j)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const int r = 4 * nt + c;
+                        if (r < m) {
+                            cp[r * WR + 16 * j + g] = acc[j][nt][0];
+                            cp[r * WR + 16 * j + g + 8] = acc[j][nt][1];
+                        }
+                    }
+#pragma unroll
+                for (int j = 0; j < RBW; ++j)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) acc[j][nt][0] = acc[j][nt][1] = 0.f;
+                return;
+            }
             auto first_cta = [&](long long u) { return (int)(((u + 1) * C - 1) / U); };
             int L = tile;
             int slot, total, n_gate;
@@ -747,6 +776,34 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
         for (int i = first; i < p_issued; ++i)
             (void)mbar_wait_sleep(&full[i % NS], (uint32_t)((i / NS) & 1), abort_flag, kRingWaitLimit, kRingSleepNs);
     }
+
+    if (p.cluster_merge) {
+        // Cluster merge (plain epilogue, one tile per cluster of TP CTAs): after
+        // the barrier every CTA sums a share of the tile's outputs over the
+        // parts' shared-memory partials in part order (deterministic), applies
+        // the epilogue and writes y; the second barrier keeps every CTA's
+        // shared memory alive until all reads are done.
+        constexpr int WR = 16 * RBW;
+        __syncwarp();
+        cluster_sync_all();
+        const int rank = (int)cluster_cta_rank();
+        const int outs = TROWS * m;
+        const uint32_t cp_addr = smem_u32(cpart);
+        for (int o = rank * kRingThreads + tid; o < outs; o += TP * kRingThreads) {
+            const int r = o / TROWS, i = o - r * TROWS;
+            const uint32_t off = (uint32_t)(((i / WR) * m + r) * WR + (i % WR)) * 4u;
+            float sum = 0.f;
+            for (int j = 0; j < TP; ++j) sum += ld_dsmem_f32(cp_addr + off, (uint32_t)j);
+            const int orow = tp_tile * TROWS + i;
+            if (rms) sum *= row_norm[r];
+            if (orow < p.n) {
+                const size_t o2 = (size_t)r * p.n + orow;
+                if (p.flags & VSPEC_B200_F_RESIDUAL) sum += p.residual[o2];
+                p.y[o2] = sum;
+            }
+        }
+        cluster_sync_all();
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -803,7 +860,7 @@ static int ring_ctas_per_sm() {
 }
 
 struct RingPlan {
-    int tiles, grid, max_slots, stages, tile_parts;
+    int tiles, grid, max_slots, stages, tile_parts, cluster;
     size_t smem;
     size_t scratch_floats;
 };
@@ -882,8 +939,19 @@ int gemv_ring_read_and_clear_timeout(int* out) {
     return VSPEC_B200_OK;
 }
 
+// Cluster merge (VSPEC_B200_RING_CLUSTER, default on; "0" keeps the
+// global-memory merge for every shape).
+static bool ring_cluster_allowed() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_RING_CLUSTER");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
+}
+
 template <int BITS, int NT, bool UNS, int EPI, bool SZ16, bool IMMA>
-static cudaError_t launch_ring_k(const CUtensorMap& map, const GemvParams& p, int grid, size_t smem, cudaStream_t st,
+static cudaError_t launch_ring_k(const CUtensorMap& map, GemvParams p, int grid, size_t smem, cudaStream_t st,
                                  bool pdl) {
     auto kern = lowbit_gemv_ring_kernel<BITS, NT, UNS, EPI, SZ16, IMMA>;
     static int configured[64] = {0};
@@ -902,11 +970,72 @@ static cudaError_t launch_ring_k(const CUtensorMap& map, const GemvParams& p, in
     cfg.blockDim = dim3(kRingThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (p.cluster_merge) {
+        // every cluster of the grid must be resident at once (one wave): the
+        // largest cluster size P' <= P (and <= 8) whose clusters all fit
+        // takes the tile's parts; otherwise the global-memory merge.  The
+        // occupancy answer is cached per (device, cluster size, smem) and
+        // taken before any capture by the first, eager launch of a shape.
+        struct Ent { int dev, P, smem, active; };
+        static Ent cache[64];
+        static int n_cache = 0;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int tiles = grid / p.tile_parts;
+        // a smaller cluster puts more units on the busiest CTA: accept none
+        // for m = 1, at most one more for larger m (whose merge moves more)
+        const int kbt_ = p.kb_total;
+        const int units0 = (kbt_ + p.tile_parts - 1) / p.tile_parts;
+        const int extra_ok = p.m >= 2 ? 1 : 0;
+        int chosen = 0;
+        for (int P = p.tile_parts < 8 ? p.tile_parts : 8; P >= 2 && !chosen; --P) {
+            if ((kbt_ + P - 1) / P - units0 > extra_ok) break;
+            int active = -1;
+            for (int i = 0; i < n_cache; ++i)
+                if (cache[i].dev == dev && cache[i].P == P && cache[i].smem == (int)smem) active = cache[i].active;
+            if (active < 0) {
+                cudaLaunchAttribute ca;
+                ca.id = cudaLaunchAttributeClusterDimension;
+                ca.val.clusterDim.x = (unsigned)P;
+                ca.val.clusterDim.y = 1;
+                ca.val.clusterDim.z = 1;
+                cfg.gridDim = dim3(tiles * P);
+                cfg.attrs = &ca;
+                cfg.numAttrs = 1;
+                int nclusters = 0;
+                if (cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg) != cudaSuccess) {
+                    (void)cudaGetLastError();
+                    nclusters = 0;
+                }
+                active = nclusters;
+                if (n_cache < 64) cache[n_cache++] = Ent{dev, P, (int)smem, active};
+            }
+            if (active >= tiles) chosen = P;
+        }
+        if (chosen) {
+            p.tile_parts = chosen;
+            grid = tiles * chosen;
+            cfg.gridDim = dim3(grid);
+        } else {
+            p.cluster_merge = 0;
+        }
+    }
+    if (p.cluster_merge) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)p.tile_parts;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, kern, map, p);
 }
 
@@ -954,6 +1083,7 @@ int gemv_ring_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st
     p.total_warps = rp.grid;
     p.stages = rp.stages;
     p.tile_parts = rp.tile_parts;
+    p.cluster_merge = (rp.tile_parts >= 2 && rp.tile_parts <= 8 && !swiglu && ring_cluster_allowed()) ? 1 : 0;
     cudaError_t e;
     const bool uns = unsigned_codes != 0;
     if (bits == 4) e = launch_ring_bits<4>(map, p, uns, swiglu, rp.grid, rp.smem, st, pdl);

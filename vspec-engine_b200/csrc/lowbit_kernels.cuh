@@ -31,6 +31,7 @@ struct GemvParams {
     int* counters;           // [counters], zero between launches
     int stages;              // tcgen05 path: weight ring depth
     int tile_parts;          // ring path: 0 = contiguous unit runs, P = each tile's k-blocks split over P CTAs
+    int cluster_merge;       // ring path: the P parts of a tile are one cluster, merged through DSMEM
 };
 
 constexpr int kEpiPlain = 0;

@@ -176,6 +176,26 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  ::"r"(smem_u32(bar)) : "memory");
 }
 
+// ---------------------------------------------------------------- clusters
+// Full cluster barrier: every thread of every CTA of the cluster; release /
+// acquire order shared-memory writes before it with reads after it.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_cta_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+// fp32 at shared address `addr` of this CTA, read from CTA `rank` of the cluster.
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr, uint32_t rank) {
+    uint32_t ra;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(ra) : "r"(addr), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
 }
