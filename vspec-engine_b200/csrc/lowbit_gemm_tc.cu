@@ -24,7 +24,8 @@
 //     TMEM; tcgen05.commit recycles the A and B stages;
 //   * warps 0-3 then read the accumulator (tcgen05.ld), undo the activation
 //     scale and apply residual / SwiGLU; a tile split along K is published as
-//     fp32 partials that its last contributor sums in K order (deterministic).
+//     fp32 partials that gemm_merge_kernel, launched right after over the
+//     whole GPU, sums in K order (deterministic).
 // Numerics: fp16 operands (dequantised weight rounded once to fp16, x to
 // fp16 after the exact row scale), fp32 accumulation: the tensor-core
 // tolerance 2e-2 applies, observed errors are ~1e-3.
@@ -35,6 +36,7 @@
 #include "tc_primitives.cuh"
 #include "tma_map.cuh"
 
+#include <stdlib.h>
 #include <string.h>
 
 namespace vb200 {
@@ -47,6 +49,7 @@ constexpr uint32_t kGmTmemCols = 512;
 constexpr uint32_t kGmWaitLimit = 1u << 16;    // checks of up to kGmSleepNs each
 constexpr uint32_t kGmSleepNs = 20000;
 constexpr uint32_t kGmSmemMax = 227u * 1024u;
+constexpr int kGmScalePipe = 4;                // k-blocks of scale loads in flight per decode thread
 
 // Set when a bounded wait of the GEMM gave up.
 __device__ int g_gemm_timeout = 0;
@@ -60,7 +63,6 @@ struct GemmParams {
     const float* residual;
     const float* xinv;       // [m] inverse row scales of the fp16 activations
     float* scratch;          // [tiles][splits] fp32 partials of tiles split along K
-    int* counters;           // per-tile contributor counters (zero between launches)
     int m, n, k, n_groups;
     int row_bytes, kb_total, kb_per_group, kb_per_group_shift;
     int flags;
@@ -185,7 +187,7 @@ gemm_prep_x_kernel(const float* __restrict__ x, const float* __restrict__ norm_w
 // GEMM kernel
 // ---------------------------------------------------------------------------
 struct GmSmem {
-    uint32_t b_ring, w_ring, misc, total;
+    uint32_t b_ring, w_ring, misc, xsc, total;
 };
 
 template <int BITS>
@@ -195,8 +197,9 @@ __host__ __device__ inline GmSmem gm_smem_plan(int bn, int nw, int nsw, int nsb)
     s.w_ring = (uint32_t)nsb * (uint32_t)bn * 256u;
     s.misc = s.w_ring + (uint32_t)nsw * kGmRows * GmCfg<BITS>::kRowBytes * (uint32_t)nw;
     s.misc = (s.misc + 15u) & ~15u;
-    // barriers: w full/empty, b full/empty, a full/empty (<= 4 groups), d full/empty, 2 flush, drain; slot + flags
-    s.total = s.misc + 8u * (2u * nsw + 2u * nsb + 8u + 2u + 2u + 1u) + 64u;
+    // barriers: w full/empty, b full/empty, a full/empty (<= 4 groups), d full/empty, drain; slot + flags
+    s.xsc = s.misc + ((8u * (2u * nsw + 2u * nsb + 8u + 2u + 1u) + 64u + 15u) & ~15u);
+    s.total = s.xsc + 256u * 4u;   // + one tile's inverse activation scales (BN <= 256)
     return s;
 }
 
@@ -226,11 +229,10 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
     uint64_t* a_empty = a_full + AS;      // [AS]
     uint64_t* d_full = a_empty + AS;
     uint64_t* d_empty = d_full + 1;
-    uint64_t* fl_bar = d_empty + 1;       // [2]
-    uint64_t* drain_bar = fl_bar + 2;
+    uint64_t* drain_bar = d_empty + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    volatile int* merge_flag = abort_flag + 1;
+    float* xsc_smem = reinterpret_cast<float*>(base + plan.xsc);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -246,8 +248,6 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
         for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], 128); mbar_init(&a_empty[i], 1); }
         mbar_init(d_full, 1);
         mbar_init(d_empty, 128);
-        mbar_init(&fl_bar[0], 128);
-        mbar_init(&fl_bar[1], 1);
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         mbar_fence_init();
@@ -372,33 +372,57 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
         uint32_t pw = 0;
         long long u = 0;
         int n_items = 0;
-        uint32_t flushes = 0;
         bool ok = true;
-        auto ld_sz = [&](const void* b, size_t idx) -> float {
-            return sz16 ? __half2float(__ldg(reinterpret_cast<const __half*>(b) + idx))
-                        : __ldg(reinterpret_cast<const float*>(b) + idx);
+        // Group scale / zero-point of this thread's row (and its up row) as raw
+        // bits, kGmScalePipe k-blocks ahead along this CTA's item sequence, so
+        // no decode waits on their load latency.
+        auto ld_raw = [&](const void* b, size_t idx) -> uint32_t {
+            return sz16 ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(b) + idx)
+                        : __ldg(reinterpret_cast<const unsigned int*>(b) + idx);
         };
+        auto raw_to_f = [&](uint32_t v) -> float {
+            return sz16 ? __half2float(__ushort_as_half((unsigned short)v)) : __uint_as_float(v);
+        };
+        uint32_t szq[kGmScalePipe][NW][2];
+        int pf_cur = it_cur, pf_tile = 0, pf_kb = 0, pf_kb1 = 0, pf_ks = 0;
+        auto pf_issue = [&](uint32_t (&d)[NW][2]) {
+            if (pf_kb >= pf_kb1 && !next_item(pf_cur, pf_tile, pf_kb, pf_kb1, pf_ks)) return;
+            const int pwt = pf_tile % p.wtiles, pkb = pf_kb++;
+            const int grp = p.kb_per_group_shift >= 0 ? (pkb >> p.kb_per_group_shift) : pkb / p.kb_per_group;
+#pragma unroll
+            for (int h = 0; h < NW; ++h) {
+                int grow = (h ? p.half_n : 0) + pwt * kGmRows + row;
+                grow = grow < p.n ? grow : p.n - 1;
+                const size_t idx = (size_t)grow * p.n_groups + grp;
+                d[h][0] = has_s ? ld_raw(p.s, idx) : 0u;
+                d[h][1] = has_zp ? ld_raw(p.zp, idx) : 0u;
+            }
+        };
+#pragma unroll
+        for (int i = 0; i < kGmScalePipe; ++i) pf_issue(szq[i]);
         int cur = it_cur;
         int tile, kb0, kb1, ks;
         for (; ok && next_item(cur, tile, kb0, kb1, ks); ++n_items) {
             const int wt = tile % p.wtiles, tt = tile / p.wtiles;
             for (int kb = kb0; kb < kb1; ++kb, ++u) {
                 const int g = (int)(u % AS);
-                // group scale / zero-point of this row (and its up row), as fp16 pairs
-                const int grp = p.kb_per_group_shift >= 0 ? (kb >> p.kb_per_group_shift) : kb / p.kb_per_group;
+                // this k-block's scale / zero-point as fp16 pairs; then shift the
+                // queue and request the one kGmScalePipe k-blocks ahead
                 uint32_t s2[NW], nz2[NW];
 #pragma unroll
                 for (int h = 0; h < NW; ++h) {
-                    int grow = (h ? p.half_n : 0) + wt * kGmRows + row;
-                    grow = grow < p.n ? grow : p.n - 1;
-                    const size_t idx = (size_t)grow * p.n_groups + grp;
-                    const float sv = has_s ? ld_sz(p.s, idx) : 1.0f;
-                    const float zv = has_zp ? ld_sz(p.zp, idx) : p.zp_const;
+                    const float sv = has_s ? raw_to_f(szq[0][h][0]) : 1.0f;
+                    const float zv = has_zp ? raw_to_f(szq[0][h][1]) : p.zp_const;
                     const __half2 sh = __float2half2_rn(sv);
                     const __half2 nzh = __float2half2_rn(-zv * sv);
                     s2[h] = *reinterpret_cast<const uint32_t*>(&sh);
                     nz2[h] = *reinterpret_cast<const uint32_t*>(&nzh);
                 }
+#pragma unroll
+                for (int i = 0; i + 1 < kGmScalePipe; ++i)
+#pragma unroll
+                    for (int h = 0; h < NW; ++h) { szq[i][h][0] = szq[i + 1][h][0]; szq[i][h][1] = szq[i + 1][h][1]; }
+                pf_issue(szq[kGmScalePipe - 1]);
                 if (!mbar_wait_sleep(&w_full[sw], pw, abort_flag, kGmWaitLimit, kGmSleepNs)) { ok = false; break; }
                 uint32_t words[NW][4 * BITS];
                 const unsigned char* wst = wring + (size_t)sw * W_TILE * NW;
@@ -452,35 +476,59 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
             const int out_n = SWIGLU ? p.half_n : p.n;
             const int col = wt * kGmRows + row;           // output column of this thread
             if (p.splits == 1) {
-                // the whole tile: finish it directly
+                // the whole tile: finish it directly.  The tile's inverse
+                // activation scales are staged once in shared memory and the
+                // residuals of the next 16 tokens are requested while these are
+                // stored, so no chunk waits a full load round trip.
+                for (int t = row; t < BN; t += kGmRows) {
+                    const int tok = tt * BN + t;
+                    xsc_smem[t] = tok < p.m ? p.xinv[tok] : 0.f;
+                }
+                named_bar_sync(1, kGmRows);
+                const bool add_res = !SWIGLU && (p.flags & VSPEC_B200_F_RESIDUAL) && col < out_n;
+                float rv[16];
+                auto load_res = [&](int j0) {
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int tok = tt * BN + j0 + jj;
+                        rv[jj] = (add_res && tok < p.m) ? p.residual[(size_t)tok * out_n + col] : 0.f;
+                    }
+                };
+                load_res(0);
                 for (int j0 = 0; j0 < BN; j0 += 16) {
                     float dv[NW][16];
 #pragma unroll
                     for (int h = 0; h < NW; ++h) tmem_ld_x16(tmem_base + lane_off + d_col0 + (uint32_t)(h * BN + j0), dv[h]);
+                    float rc[16];
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) rc[jj] = rv[jj];
+                    if (j0 + 16 < BN) load_res(j0 + 16);
                     tmem_wait_ld();
 #pragma unroll
                     for (int jj = 0; jj < 16; ++jj) {
                         const int tok = tt * BN + j0 + jj;
                         if (tok < p.m && col < out_n) {
-                            const float xi = p.xinv[tok];
+                            const float xi = xsc_smem[j0 + jj];
                             float v = dv[0][jj] * xi;
                             if (SWIGLU) {
                                 const float up = dv[NW - 1][jj] * xi;
                                 v = v / (1.0f + expf(-v)) * up;
                             }
-                            const size_t o = (size_t)tok * out_n + col;
-                            if (!SWIGLU && (p.flags & VSPEC_B200_F_RESIDUAL)) v += p.residual[o];
-                            p.y[o] = v;
+                            if (add_res) v += rc[jj];
+                            p.y[(size_t)tok * out_n + col] = v;
                         }
                     }
                 }
+                named_bar_sync(1, kGmRows);   // the staged scales are reused by the next item
                 tc_fence_before();
                 mbar_arrive(d_empty);
             } else {
-                // split along K: publish this item's partial in slot ks; the tile's
-                // last contributor sums the slots in order and finishes the tile
-                const size_t part_floats = (size_t)NW * BN * kGmRows;
-                float* part = p.scratch + ((size_t)tile * p.splits + ks) * part_floats;
+                // split along K: publish this item's fp32 partial in slot ks,
+                // [tile][split][h][token quad][row] float4s (coalesced: a warp
+                // writes 32 consecutive rows); gemm_merge_kernel sums the
+                // slots in K order and finishes the tile
+                float4* part4 = reinterpret_cast<float4*>(p.scratch) +
+                                ((size_t)tile * p.splits + ks) * (size_t)NW * (size_t)(BN / 4) * kGmRows;
                 for (int j0 = 0; j0 < BN; j0 += 16) {
                     float dv[NW][16];
 #pragma unroll
@@ -489,58 +537,12 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
 #pragma unroll
                     for (int h = 0; h < NW; ++h)
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) part[((size_t)h * BN + j0 + jj) * kGmRows + row] = dv[h][jj];
+                        for (int q = 0; q < 4; ++q)
+                            part4[((size_t)h * (BN / 4) + (j0 >> 2) + q) * kGmRows + row] =
+                                make_float4(dv[h][4 * q], dv[h][4 * q + 1], dv[h][4 * q + 2], dv[h][4 * q + 3]);
                 }
                 tc_fence_before();
                 mbar_arrive(d_empty);
-                __threadfence();
-                const uint32_t ph = flushes & 1u;
-                ++flushes;
-                mbar_arrive(&fl_bar[0]);
-                if (tid == 0) {
-                    if (mbar_wait_sleep(&fl_bar[0], ph, abort_flag, kGmWaitLimit, kGmSleepNs)) {
-                        const int old = atomicAdd(p.counters + tile, 1);
-                        *merge_flag = (old == p.splits - 1) ? 1 : 0;
-                    } else {
-                        *merge_flag = 0;
-                    }
-                    __threadfence_block();
-                    mbar_arrive(&fl_bar[1]);
-                }
-                if (!mbar_wait_sleep(&fl_bar[1], ph, abort_flag, kGmWaitLimit, kGmSleepNs)) { ok = false; break; }
-                if (*merge_flag) {
-                    __threadfence();
-                    for (int j0 = 0; j0 < BN; j0 += 16) {
-                        float acc[NW][16];
-#pragma unroll
-                        for (int h = 0; h < NW; ++h)
-#pragma unroll
-                            for (int jj = 0; jj < 16; ++jj) acc[h][jj] = 0.f;
-                        for (int sl = 0; sl < p.splits; ++sl) {
-                            const float* src = p.scratch + ((size_t)tile * p.splits + sl) * part_floats;
-#pragma unroll
-                            for (int h = 0; h < NW; ++h)
-#pragma unroll
-                                for (int jj = 0; jj < 16; ++jj)
-                                    acc[h][jj] += __ldcg(src + ((size_t)h * BN + j0 + jj) * kGmRows + row);
-                        }
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int tok = tt * BN + j0 + jj;
-                            if (tok >= p.m || col >= out_n) continue;
-                            const float xi = p.xinv[tok];
-                            float v = acc[0][jj] * xi;
-                            if (SWIGLU) {
-                                const float up = acc[NW - 1][jj] * xi;
-                                v = v / (1.0f + expf(-v)) * up;
-                            }
-                            const size_t o = (size_t)tok * out_n + col;
-                            if (!SWIGLU && (p.flags & VSPEC_B200_F_RESIDUAL)) v += p.residual[o];
-                            p.y[o] = v;
-                        }
-                    }
-                    if (tid == 0) p.counters[tile] = 0;
-                }
             }
         }
         if (!ok) { *abort_flag = 1; atomicOr(&g_gemm_timeout, 1); }
@@ -551,6 +553,71 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
     if (warp == kGmMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_base, kGmTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Split-K merge: one thread per (tile, token quad, weight row) sums the K
+// slots' fp32 partials in slot order (deterministic), undoes the activation
+// row scale and applies SwiGLU / residual.  Runs over the whole GPU right
+// after the GEMM (programmatic dependent launch), so no CTA of the GEMM sums
+// a tile alone.
+// ---------------------------------------------------------------------------
+template <bool SWIGLU>
+__global__ void __launch_bounds__(256) gemm_merge_kernel(const GemmParams p) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int NW = SWIGLU ? 2 : 1;
+    const int q4 = p.bn / 4;
+    const long long per_tile = (long long)q4 * kGmRows;   // float4 slots of one (split, h)
+    const long long total = (long long)p.wtiles * p.ttiles * per_tile;
+    const int out_n = SWIGLU ? p.half_n : p.n;
+    const float4* part = reinterpret_cast<const float4*>(p.scratch);
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const int tile = (int)(idx / per_tile);
+        const int rem = (int)(idx - (long long)tile * per_tile);
+        const int jq = rem / kGmRows, row = rem - jq * kGmRows;
+        const int wt = tile % p.wtiles, tt = tile / p.wtiles;
+        const float4* src = part + (size_t)tile * p.splits * NW * per_tile + (size_t)jq * kGmRows + row;
+        float4 acc[NW];
+#pragma unroll
+        for (int h = 0; h < NW; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < p.splits; s0 += 4) {
+            float4 v[4][NW];
+#pragma unroll
+            for (int sl = 0; sl < 4; ++sl)
+#pragma unroll
+                for (int h = 0; h < NW; ++h)
+                    v[sl][h] = s0 + sl < p.splits ? __ldcg(src + ((size_t)(s0 + sl) * NW + h) * per_tile)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int sl = 0; sl < 4; ++sl)
+                if (s0 + sl < p.splits)
+#pragma unroll
+                    for (int h = 0; h < NW; ++h) {
+                        acc[h].x += v[sl][h].x; acc[h].y += v[sl][h].y;
+                        acc[h].z += v[sl][h].z; acc[h].w += v[sl][h].w;
+                    }
+        }
+        const int col = wt * kGmRows + row;
+        if (col >= out_n) continue;
+        const float g4[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
+        const float u4[4] = {acc[NW - 1].x, acc[NW - 1].y, acc[NW - 1].z, acc[NW - 1].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int tok = tt * p.bn + 4 * jq + e;
+            if (tok >= p.m) break;
+            const float xi = p.xinv[tok];
+            float v = g4[e] * xi;
+            if (SWIGLU) {
+                const float up = u4[e] * xi;
+                v = v / (1.0f + expf(-v)) * up;
+            }
+            const size_t o = (size_t)tok * out_n + col;
+            if (!SWIGLU && (p.flags & VSPEC_B200_F_RESIDUAL)) v += p.residual[o];
+            p.y[o] = v;
+        }
     }
 }
 
@@ -587,18 +654,24 @@ static bool gemm_plan(int m, int n, int k, int bits, bool swiglu, GemmPlan* gp) 
     const int tiles = gp->wtiles * gp->ttiles;
     const int sms = device_sm_count();
     // K split with the shortest makespan, in k-block times: rounds of items per
-    // CTA x (k-blocks of an item + publishing its fp32 partial), plus the merge
-    // that ends a split tile; moving a 128 x BN fp32 partial costs about BN/32
-    // k-blocks
+    // CTA x (k-blocks of an item + ~3 for its epilogue, which drains the TMEM
+    // accumulator before the next item's MMAs start), plus the merge kernel: ~3 k-blocks of launch and latency and the partial
+    // bytes (items x NW x BN x 128 fp32, mostly L2-resident), ~20000 such
+    // per-token columns per k-block time (calibrated on B200 at M = 64 and 256)
     int splits = 1;
-    long long best = -1;
-    const int pcost = (bn + 31) / 32;
+    double best = -1.0;
     for (int d = 1; d <= kbt; ++d) {
         if (kbt % d != 0 || (d > 1 && kbt / d < 2)) continue;
         const long long items = (long long)tiles * d;
         const long long rounds = (items + sms - 1) / sms;
-        const long long cost = rounds * (kbt / d + (d > 1 ? pcost : 0)) + (d > 1 ? pcost * d / 2 + 2 : 0);
-        if (best < 0 || cost < best) { best = cost; splits = d; }
+        double cost = (double)rounds * (kbt / d + 3);
+        if (d > 1) cost += 3.0 + (double)items * nw * bn / 20000.0;
+        if (best < 0.0 || cost < best) { best = cost; splits = d; }
+    }
+    // tuning override: VSPEC_B200_GEMM_SPLITS=d (a divisor of the k-blocks)
+    if (const char* e = getenv("VSPEC_B200_GEMM_SPLITS")) {
+        const int d = atoi(e);
+        if (d >= 1 && d <= kbt && kbt % d == 0) splits = d;
     }
     gp->splits = splits;
     gp->kb_per_split = kbt / splits;
@@ -627,7 +700,7 @@ bool gemm_tc_supported(const GemvParams& p, int bits, size_t counter_slots) {
     if (swiglu && (p.n % 2 != 0 || (p.n / 2) % kGmRows != 0)) return false;
     GemmPlan gp;
     if (!gemm_plan(p.m, p.n, p.k, bits, swiglu, &gp)) return false;
-    if (gp.splits > 1 && (size_t)gp.wtiles * gp.ttiles > counter_slots) return false;
+    (void)counter_slots;   // split tiles merge in gemm_merge_kernel: no counters
     return true;
 }
 
@@ -714,7 +787,7 @@ int gemm_tc_launch(const GemvParams& p, int bits, int unsigned_codes, cudaStream
     GemmParams gp;
     memset(&gp, 0, sizeof(gp));
     gp.w = p.w; gp.s = p.s; gp.zp = p.zp; gp.zp_const = p.zp_const;
-    gp.y = p.y; gp.residual = p.residual; gp.xinv = xinv; gp.scratch = part; gp.counters = p.counters;
+    gp.y = p.y; gp.residual = p.residual; gp.xinv = xinv; gp.scratch = part;
     gp.m = p.m; gp.n = p.n; gp.k = p.k; gp.n_groups = p.n_groups;
     gp.row_bytes = p.row_bytes; gp.kb_total = p.kb_total; gp.kb_per_group = p.kb_per_group;
     gp.kb_per_group_shift = p.kb_per_group_shift; gp.flags = p.flags;
@@ -726,6 +799,15 @@ int gemm_tc_launch(const GemvParams& p, int bits, int unsigned_codes, cudaStream
     else if (bits == 3) e = launch_gemm_bits<3>(wm, xm, gp, uns, swiglu, plan.grid, plan.smem, st);
     else e = launch_gemm_bits<2>(wm, xm, gp, uns, swiglu, plan.grid, plan.smem, st);
     if (e != cudaSuccess) return cuda_status(e, "lowbit_gemm_tc_kernel launch");
+    if (plan.splits > 1) {
+        const long long work = (long long)plan.wtiles * plan.ttiles * (plan.bn / 4) * kGmRows;
+        long long blocks = (work + 255) / 256;
+        const long long cap = (long long)device_sm_count() * 8;
+        if (blocks > cap) blocks = cap;
+        e = swiglu ? launch_pdl(gemm_merge_kernel<true>, dim3((unsigned)blocks), dim3(256), 0, st, gp)
+                   : launch_pdl(gemm_merge_kernel<false>, dim3((unsigned)blocks), dim3(256), 0, st, gp);
+        if (e != cudaSuccess) return cuda_status(e, "gemm_merge_kernel launch");
+    }
     return VSPEC_B200_OK;
 }
 
