@@ -74,7 +74,8 @@ def test_long_context_splits_and_uneven_lengths():
 
 
 @pytest.mark.parametrize("hq,hkv,d,dtype", [(8, 8, 128, np.float16), (64, 8, 128, np.float16), (16, 2, 128, np.float16),
-                                             (8, 2, 64, np.float32), (4, 4, 96, np.float16), (32, 8, 128, np.float32)])
+                                             (8, 2, 64, np.float32), (4, 4, 96, np.float16), (32, 8, 128, np.float32),
+                                             (48, 8, 128, np.float16), (32, 2, 128, np.float16), (12, 2, 128, np.float16)])
 def test_head_layouts_and_dtypes(hq, hkv, d, dtype):
     rng = np.random.default_rng(hq * 3 + hkv + d)
     b, pt = 4, 16

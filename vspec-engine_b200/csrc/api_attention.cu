@@ -101,7 +101,7 @@ using namespace vb200;
 extern "C" size_t vspec_b200_paged_attention_workspace_bytes(size_t batch, size_t hq, size_t hkv, size_t d,
                                                              size_t max_ctx) {
     if (batch == 0 || hq == 0 || hkv == 0 || d == 0) return 0;
-    const int split = attn_choose_split((int)batch, (int)hkv, (int)(max_ctx ? max_ctx : 1), device_sm_count());
+    const int split = attn_choose_split((int)batch, (int)hq, (int)hkv, (int)(max_ctx ? max_ctx : 1), 0, device_sm_count());
     const int max_splits = (int)((max_ctx + split - 1) / split);
     return attn_workspace_bytes((int)batch, (int)hq, (int)d, max_splits > 0 ? max_splits : 1);
 }
@@ -139,7 +139,7 @@ extern "C" int vspec_b200_paged_attention(const VspecB200PagedAttnArgs* a, void*
     p.page_tokens = (int)a->page_tokens;
     p.max_pages = (int)a->max_pages_per_seq;
     p.num_pages = (int)a->num_pages;
-    p.split_tokens = attn_choose_split(p.batch, p.hkv, (int)max_ctx, device_sm_count());
+    p.split_tokens = attn_choose_split(p.batch, p.hq, p.hkv, (int)max_ctx, p.page_tokens, device_sm_count());
     p.max_splits = (int)((max_ctx + p.split_tokens - 1) / p.split_tokens);
     if (p.max_splits < 1) p.max_splits = 1;
     const size_t need = attn_workspace_bytes(p.batch, p.hq, p.d, p.max_splits);

@@ -9,17 +9,19 @@
 // every page but the last one is full.
 //
 // fp16 pages, d = 128 (the decode product path): warp-level tensor-core MMA.
-//   QK^T: A = 16 tokens x 16 dims of K straight from the page rows (thread
-//         (g,c) streams 64 contiguous bytes per token row), B = 8 columns =
-//         4 query heads x {hi, lo} fp16 parts of q -> fp32-accurate scores.
-//   PV:   A = V^T (pairs of token rows merged with PRMT), B = p as {hi, lo}
-//         fp16 parts (p pre-scaled by 2^14 so no part underflows).
+//   K and V page rows stream through a per-warp cp.async shared-memory ring.
+//   QK^T: A = 16 tokens x 16 dims of K (ldmatrix), B = one or two 8-column
+//         tiles of 4 query heads x {hi, lo} fp16 parts of q -> fp32-accurate
+//         scores; a CTA serves up to 8 heads of one KV head.
+//   PV:   A = V^T (ldmatrix.trans), B = p as {hi, lo} fp16 parts (p
+//         pre-scaled by 2^14 so no part underflows).
 //   Online softmax per warp in fp32; warps merge in shared memory; splits of
 //   the context merge in a second kernel (fixed order: deterministic).
 // fp32 pages or other head sizes: a plain fp32 SIMT kernel with the same
 // split/merge structure.
 #include "common.cuh"
 #include "attention_kernels.cuh"
+#include "tc_primitives.cuh"
 
 #include <math.h>
 #include <string.h>
@@ -32,25 +34,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegBig = -1.0e30f;
 constexpr float kPScale = 16384.0f;  // 2^14: keeps p's fp16 hi/lo parts normal
 
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm volatile("prmt.b32 %0, %1, %2, %3;\n" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
-
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
-}
-
-__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t u4_word(const uint4& v, int w) {
-    return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
 }
 
 // Set when a page table entry lies outside [0, num_pages): the access is
@@ -69,15 +54,56 @@ __device__ __forceinline__ size_t token_row(const int32_t* table, int t, int pt,
     return ((size_t)page * pt + (size_t)(t % pt)) * (size_t)hkv * d + (size_t)kvh * d;
 }
 
+// Page ids of a CTA's context piece, staged once in shared memory (checked
+// and redirected like token_row), so the K/V loads of a tile do not wait on a
+// page-table load first.
+constexpr int kAttnMaxStagedPages = 512;
+
+__device__ __forceinline__ size_t staged_row(const int* sm_pages, int t, int first_page, int pt, int hkv, int d,
+                                             int kvh) {
+    const int page = sm_pages[t / pt - first_page];
+    return ((size_t)page * pt + (size_t)(t % pt)) * (size_t)hkv * d + (size_t)kvh * d;
+}
+
 // ---------------------------------------------------------------------------
-// Tensor-core kernel: fp16 pages, d = 128, up to 4 query heads per CTA.
-// grid = (splits, Hkv * head_groups, B)
+// Tensor-core kernel: fp16 pages, d = 128, up to 4*NT query heads per CTA
+// (NT column tiles of 4 heads x {hi, lo}); every K/V row a CTA streams serves
+// all its heads, so a GQA group of up to 8 reads each page row once.
+// Each warp owns the 16-token tiles warp, warp + 4, ... of the CTA's context
+// piece and streams their K and V rows with cp.async into a 3-stage shared
+// memory ring (rows past the context are zero-filled), so several tiles are
+// in flight per warp; fragments come out with ldmatrix (.trans for V^T) from
+// an XOR-swizzled layout (16-byte chunk c of row r at chunk c ^ (r & 7)).
+// grid = (splits, Hkv * head_groups, B), dynamic shared memory kAttnPipeSmem.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kAttnThreads)
+constexpr int kAttnStages = 3;
+constexpr uint32_t kAttnTileBytes = 16u * 256u;                 // 16 token rows x 128 fp16 (one KV head)
+constexpr uint32_t kAttnStageBytes = 2u * kAttnTileBytes;       // K + V
+constexpr uint32_t kAttnPipeSmem = (uint32_t)kAttnWarps * kAttnStages * kAttnStageBytes;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kAttnThreads, 2)
 paged_attn_f16_mma_kernel(const AttnParams p) {
     pdl_wait();
     pdl_trigger();
     constexpr int D = 128;
+    constexpr int HPC = 4 * NT;                   // query heads per CTA
+    constexpr int S = kAttnStages;
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / p.head_groups;
     const int hg = blockIdx.y % p.head_groups;
@@ -95,21 +121,59 @@ paged_attn_f16_mma_kernel(const AttnParams p) {
     const __half* kp = reinterpret_cast<const __half*>(p.k_pages);
     const __half* vp = reinterpret_cast<const __half*>(p.v_pages);
 
-    __shared__ float sm_q[4][D];                  // the CTA's (up to) 4 query heads, fp32
-    __shared__ float sm_qmax[4];
-    __shared__ float sm_p[kAttnWarps][16][4];     // p exchange, per warp
-    __shared__ float sm_ml[kAttnWarps][4][2];     // per-warp (m, l) per head
-    __shared__ float sm_o[kAttnWarps][4][D];      // per-warp unnormalized O per head
+    extern __shared__ __align__(128) unsigned char attn_smem[];   // K/V rings; O partials after the loop
+    __shared__ float sm_q[HPC][D];                // the CTA's query heads, fp32
+    __shared__ float sm_qmax[HPC];
+    __shared__ float sm_p[kAttnWarps][16][HPC];   // p exchange, per warp
+    __shared__ float sm_ml[kAttnWarps][HPC][2];   // per-warp (m, l) per head
+    __shared__ int sm_pages[kAttnMaxStagedPages];  // page ids of [t_begin, t_end)
 
-    // ---- q: load, per-head power-of-two rescale, hi/lo B fragments ----
-    for (int i = tid; i < 4 * D; i += kAttnThreads) {
+    const int first_page = t_begin / p.page_tokens;
+    const int n_pages = (t_end - 1) / p.page_tokens - first_page + 1;   // <= staged capacity (host)
+    for (int i = tid; i < n_pages; i += kAttnThreads) {
+        int page = __ldg(table + first_page + i);
+        if (page < 0 || page >= p.num_pages) {
+            atomicOr(&g_attn_page_fault, 1);
+            page = 0;
+        }
+        sm_pages[i] = page;
+    }
+    // ---- q: load, per-head power-of-two rescale ----
+    for (int i = tid; i < HPC * D; i += kAttnThreads) {
         const int hl = i / D, dd = i % D;
-        const int h = hg * 4 + hl;
-        sm_q[hl][dd] = (hl < 4 && h < group) ? p.q[((size_t)b * p.hq + (size_t)kvh * group + h) * D + dd] : 0.f;
+        const int h = hg * HPC + hl;
+        sm_q[hl][dd] = h < group ? p.q[((size_t)b * p.hq + (size_t)kvh * group + h) * D + dd] : 0.f;
     }
     __syncthreads();
+
+    // ---- this warp's tiles: start streaming K/V before anything else ----
+    const int ntiles = (t_end - t_begin + 15) / 16;
+    const int my_tiles = ntiles > warp ? (ntiles - warp + kAttnWarps - 1) / kAttnWarps : 0;
+    const uint32_t wbase = smem_u32(attn_smem) + (uint32_t)warp * S * kAttnStageBytes;
+    auto issue = [&](int it) {   // it-th tile of this warp -> stage it % S
+        const int t0 = t_begin + (warp + it * kAttnWarps) * 16;
+        const uint32_t st = wbase + (uint32_t)(it % S) * kAttnStageBytes;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = i * 32 + lane;
+            const int row = idx >> 4, ch = idx & 15;
+            const int t = t0 + row;
+            const bool valid = t < t_end;
+            const size_t ro = staged_row(sm_pages, valid ? t : t_end - 1, first_page, p.page_tokens, p.hkv, D, kvh) +
+                              (size_t)ch * 8;
+            const uint32_t off = (uint32_t)row * 256u + ((uint32_t)(ch ^ (row & 7)) << 4);
+            cp_async16(st + off, kp + ro, valid ? 16u : 0u);
+            cp_async16(st + kAttnTileBytes + off, vp + ro, valid ? 16u : 0u);
+        }
+    };
+#pragma unroll
+    for (int it = 0; it < S - 1; ++it) {
+        if (it < my_tiles) issue(it);
+        cp_async_commit();
+    }
+
     if (warp == 0) {
-        for (int hl = 0; hl < 4; ++hl) {
+        for (int hl = 0; hl < HPC; ++hl) {
             float mx = 0.f;
             for (int dd = lane; dd < D; dd += 32) mx = fmaxf(mx, fabsf(sm_q[hl][dd]));
             mx = warp_max(mx);
@@ -121,143 +185,142 @@ paged_attn_f16_mma_kernel(const AttnParams p) {
         }
     }
     __syncthreads();
-    // B fragment for k-step j: column g (head g/2, part g%2), k-slots of thread c
-    // map to dims 8c + 32(j/2) + 4(j%2) + {0,1,2,3}.
-    uint32_t qf[8][2];
-    {
-        const int hl = g >> 1;
+    // B fragment of column tile nt, k-step j: column g (head 4nt + g/2, part
+    // g%2), k rows 2c, 2c+1 and 2c+8, 2c+9 = dims 16j + {2c, 2c+1, 2c+8, 2c+9}
+    uint32_t qf[NT][8][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int hl = 4 * nt + (g >> 1);
         const bool lo = (g & 1) != 0;
         const float sc = ldexpf(1.0f, -(int)sm_qmax[hl]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int base = 8 * c + 32 * (j >> 1) + 4 * (j & 1);
+            const int dims[4] = {16 * j + 2 * c, 16 * j + 2 * c + 1, 16 * j + 2 * c + 8, 16 * j + 2 * c + 9};
             float v[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                float x = sm_q[hl][base + u] * sc;
+                float x = sm_q[hl][dims[u]] * sc;
                 if (lo) x = x - __half2float(__float2half_rn(x));
                 v[u] = x;
             }
-            qf[j][0] = pack_half2(v[0], v[1]);
-            qf[j][1] = pack_half2(v[2], v[3]);
+            qf[nt][j][0] = pack_half2(v[0], v[1]);
+            qf[nt][j][1] = pack_half2(v[2], v[3]);
         }
     }
-    // per-head score multiplier: 2^e * scale * log2(e) (exp2-domain scores)
-    const float score_mul = ldexpf(p.scale * kLog2e, (int)sm_qmax[c]);
+    // this thread's heads are 4nt + c; score multiplier 2^e * scale * log2(e)
+    float score_mul[NT], m_run[NT], l_run[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        score_mul[nt] = ldexpf(p.scale * kLog2e, (int)sm_qmax[4 * nt + c]);
+        m_run[nt] = kNegBig;
+        l_run[nt] = 0.f;
+    }
+    float oacc[NT][8][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) oacc[nt][i][0] = oacc[nt][i][1] = oacc[nt][i][2] = oacc[nt][i][3] = 0.f;
 
-    float m_run = kNegBig, l_run = 0.f;     // head c of this thread
-    float oacc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
-
-    const int ntiles = (t_end - t_begin + 15) / 16;
-    for (int tile = warp; tile < ntiles; tile += kAttnWarps) {
-        const int t0 = t_begin + tile * 16;
-        // ---- K rows g and g+8: 4 x 16 bytes each at dims 8c + 32i ----
-        uint4 kr[2][4];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int t = t0 + g + 8 * r;
-            if (t < t_end) {
-                const __half* row = kp + token_row(table, t, p.page_tokens, p.hkv, D, kvh, p.num_pages);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) kr[r][i] = ldg_nc_v4(row + 8 * c + 32 * i);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) kr[r][i] = make_uint4(0u, 0u, 0u, 0u);
-            }
-        }
-        // ---- V rows 4c..4c+3: dims [16g, 16g+16) ----
-        uint4 vr[4][2];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int t = t0 + 4 * c + r;
-            if (t < t_end) {
-                const __half* row = vp + token_row(table, t, p.page_tokens, p.hkv, D, kvh, p.num_pages);
-                vr[r][0] = ldg_nc_v4(row + 16 * g);
-                vr[r][1] = ldg_nc_v4(row + 16 * g + 8);
-            } else {
-                vr[r][0] = vr[r][1] = make_uint4(0u, 0u, 0u, 0u);
-            }
-        }
-        // ---- S = K Q^T over 8 k-steps of 16 dims ----
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
+    // ldmatrix row addresses of this lane: K (tokens x dims) and V^T (.trans)
+    const int k_row = (lane & 7) + 8 * ((lane >> 3) & 1), k_chi = lane >> 4;
+    const int v_row = (lane & 7) + 8 * (lane >> 4), v_chi = (lane >> 3) & 1;
+    for (int it = 0; it < my_tiles; ++it) {
+        cp_async_wait<S - 2>();
+        __syncwarp();   // tile it has landed; every lane is done with tile it-1 and sm_p
+        // refill the stage of tile it-1 before computing tile it
+        if (it + S - 1 < my_tiles) issue(it + S - 1);
+        cp_async_commit();
+        const int t0 = t_begin + (warp + it * kAttnWarps) * 16;
+        const uint32_t st = wbase + (uint32_t)(it % S) * kAttnStageBytes;
+        // ---- S = K Q^T over 8 k-steps of 16 dims, per column tile ----
+        float s[NT][4];
         const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int i = j >> 1, sub = j & 1;
-            const uint32_t a[4] = {u4_word(kr[0][i], 2 * sub), u4_word(kr[1][i], 2 * sub),
-                                   u4_word(kr[0][i], 2 * sub + 1), u4_word(kr[1][i], 2 * sub + 1)};
-            mma_16816_f16(s, a, qf[j][0], qf[j][1], j == 0 ? zero4 : s);
-        }
-        // scores of tokens g and g+8 for head c (hi + lo columns), exp2 domain
-        const bool v0 = (t0 + g) < t_end, v1 = (t0 + g + 8) < t_end;
-        float sc0 = v0 ? (s[0] + s[1]) * score_mul : kNegBig;
-        float sc1 = v1 ? (s[2] + s[3]) * score_mul : kNegBig;
-        float tmax = fmaxf(sc0, sc1);
-        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
-        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
-        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
-        const float m_new = fmaxf(m_run, tmax);
-        const float alpha = exp2f(m_run - m_new);
-        const float p0 = v0 ? exp2f(sc0 - m_new) : 0.f;
-        const float p1 = v1 ? exp2f(sc1 - m_new) : 0.f;
-        l_run = l_run * alpha + (p0 + p1);
-        m_run = m_new;
+            uint32_t a[4];
+            const int ch = 2 * j + k_chi;
+            ldsm_x4(st + (uint32_t)k_row * 256u + ((uint32_t)(ch ^ (k_row & 7)) << 4), a);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            oacc[i][0] *= alpha; oacc[i][1] *= alpha; oacc[i][2] *= alpha; oacc[i][3] *= alpha;
+            for (int nt = 0; nt < NT; ++nt) mma_16816_f16(s[nt], a, qf[nt][j][0], qf[nt][j][1], j == 0 ? zero4 : s[nt]);
         }
-        // ---- p exchange: thread (g,c) -> P^T B fragment of thread (g', c') ----
-        sm_p[warp][g][c] = p0 * kPScale;
-        sm_p[warp][g + 8][c] = p1 * kPScale;
+        // scores of tokens g and g+8 for heads 4nt + c (hi + lo columns), exp2 domain
+        const bool v0 = (t0 + g) < t_end, v1 = (t0 + g + 8) < t_end;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const float sc0 = v0 ? (s[nt][0] + s[nt][1]) * score_mul[nt] : kNegBig;
+            const float sc1 = v1 ? (s[nt][2] + s[nt][3]) * score_mul[nt] : kNegBig;
+            float tmax = fmaxf(sc0, sc1);
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            const float m_new = fmaxf(m_run[nt], tmax);
+            const float alpha = exp2f(m_run[nt] - m_new);
+            const float p0 = v0 ? exp2f(sc0 - m_new) : 0.f;
+            const float p1 = v1 ? exp2f(sc1 - m_new) : 0.f;
+            l_run[nt] = l_run[nt] * alpha + (p0 + p1);
+            m_run[nt] = m_new;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                oacc[nt][i][0] *= alpha; oacc[nt][i][1] *= alpha; oacc[nt][i][2] *= alpha; oacc[nt][i][3] *= alpha;
+            }
+            sm_p[warp][g][4 * nt + c] = p0 * kPScale;
+            sm_p[warp][g + 8][4 * nt + c] = p1 * kPScale;
+        }
         __syncwarp();
-        uint32_t pb0, pb1;
-        {
-            const int hl = g >> 1;
+        // P^T B fragments: column g (head 4nt + g/2, part g%2), tokens 2c, 2c+1 and 2c+8, 2c+9
+        uint32_t pb[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int hl = 4 * nt + (g >> 1);
             const bool lo = (g & 1) != 0;
+            const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
             float pv[4];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                float x = sm_p[warp][4 * c + r][hl];
+                float x = sm_p[warp][toks[r]][hl];
                 if (lo) x = x - __half2float(__float2half_rn(x));
                 pv[r] = x;
             }
-            pb0 = pack_half2(pv[0], pv[1]);
-            pb1 = pack_half2(pv[2], pv[3]);
+            pb[nt][0] = pack_half2(pv[0], pv[1]);
+            pb[nt][1] = pack_half2(pv[2], pv[3]);
         }
-        __syncwarp();
-        // ---- O^T += V^T P^T over 8 dim blocks ----
+        // ---- O^T += V^T P^T over 8 blocks of 16 dims ----
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int u = i >> 2, w = i & 3;
-            const uint32_t w0 = u4_word(vr[0][u], w), w1 = u4_word(vr[1][u], w);
-            const uint32_t w2 = u4_word(vr[2][u], w), w3 = u4_word(vr[3][u], w);
-            const uint32_t a[4] = {prmt(w0, w1, 0x5410), prmt(w0, w1, 0x7632), prmt(w2, w3, 0x5410),
-                                   prmt(w2, w3, 0x7632)};
-            mma_16816_f16(oacc[i], a, pb0, pb1, oacc[i]);
+            uint32_t a[4];
+            const int ch = 2 * i + v_chi;
+            ldsm_x4_t(st + kAttnTileBytes + (uint32_t)v_row * 256u + ((uint32_t)(ch ^ (v_row & 7)) << 4), a);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) mma_16816_f16(oacc[nt][i], a, pb[nt][0], pb[nt][1], oacc[nt][i]);
         }
     }
+    cp_async_wait<0>();
 
-    // ---- merge the warps ----
-    // l: sum of the per-thread partials over the 8 lanes of head c
-    float l_tot = l_run;
-    l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 4);
-    l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 8);
-    l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
-    if (g == 0) {
-        sm_ml[warp][c][0] = m_run;
-        sm_ml[warp][c][1] = l_tot;
-    }
+    // ---- merge the warps (O partials reuse the ring) ----
+    __syncthreads();
+    float* sm_o = reinterpret_cast<float*>(attn_smem);   // [kAttnWarps][HPC][D]
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        sm_o[warp][c][16 * g + 2 * i] = (oacc[i][0] + oacc[i][1]) * (1.0f / kPScale);
-        sm_o[warp][c][16 * g + 2 * i + 1] = (oacc[i][2] + oacc[i][3]) * (1.0f / kPScale);
+    for (int nt = 0; nt < NT; ++nt) {
+        // l: sum of the per-thread partials over the 8 lanes of head 4nt + c
+        float l_tot = l_run[nt];
+        l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 4);
+        l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 8);
+        l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
+        if (g == 0) {
+            sm_ml[warp][4 * nt + c][0] = m_run[nt];
+            sm_ml[warp][4 * nt + c][1] = l_tot;
+        }
+        float* o = sm_o + ((size_t)warp * HPC + 4 * nt + c) * D;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            o[16 * i + g] = (oacc[nt][i][0] + oacc[nt][i][1]) * (1.0f / kPScale);
+            o[16 * i + g + 8] = (oacc[nt][i][2] + oacc[nt][i][3]) * (1.0f / kPScale);
+        }
     }
     __syncthreads();
-    for (int z = tid; z < 4 * D; z += kAttnThreads) {
+    for (int z = tid; z < HPC * D; z += kAttnThreads) {
         const int hl = z / D, dd = z % D;
-        const int h_in_group = hg * 4 + hl;
+        const int h_in_group = hg * HPC + hl;
         if (h_in_group >= group) continue;
         float M = kNegBig;
         for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_ml[w][hl][0]);
@@ -265,7 +328,7 @@ paged_attn_f16_mma_kernel(const AttnParams p) {
         for (int w = 0; w < kAttnWarps; ++w) {
             const float f = exp2f(sm_ml[w][hl][0] - M);
             L += sm_ml[w][hl][1] * f;
-            O += sm_o[w][hl][dd] * f;
+            O += sm_o[((size_t)w * HPC + hl) * D + dd] * f;
         }
         const int h = kvh * group + h_in_group;
         const size_t bh = (size_t)b * p.hq + h;
@@ -413,12 +476,33 @@ int attn_read_and_clear_page_fault(int* out) {
     return VSPEC_B200_OK;
 }
 
-int attn_choose_split(int batch, int hkv, int max_ctx, int sms) {
-    long long want = (long long)batch * hkv * (long long)max_ctx / (4LL * sms);
-    int s = (int)((want + 63) / 64) * 64;
+// Context piece per CTA: enough pieces for about four CTAs per resident slot
+// (two per SM), no split at all when the (sequence, KV head group) pairs
+// alone fill the slots, pieces under 512 tokens only as far as one CTA per
+// slot needs them, and at most the staged page capacity (page_tokens <= 0:
+// the capacity for one-token pages, the most conservative).
+int attn_choose_split(int batch, int hq, int hkv, int max_ctx, int page_tokens, int sms) {
+    const int group = hkv > 0 ? hq / hkv : 1;
+    const int hpc = group <= 4 ? 4 : 8;
+    const long long pairs = (long long)batch * hkv * ((group + hpc - 1) / hpc);
+    const long long slots = 2LL * sms;
+    const int pt = page_tokens > 0 ? page_tokens : 1;
+    int cap = (kAttnMaxStagedPages - 1) * pt / 64 * 64;
+    if (cap < 64) cap = 64;
+    const long long np = pairs > 0 ? pairs : 1;
+    long long pieces = pairs >= slots ? 1 : (4 * slots + np - 1) / np;
+    long long s = ((max_ctx + pieces - 1) / pieces + 63) / 64 * 64;
+    if (s < 512) {
+        // pieces shorter than 512 tokens only as far as needed for one CTA
+        // per slot: a piece pays a fixed prologue (page ids, q fragments)
+        const long long p1 = (slots + np - 1) / np;
+        const long long s1 = ((max_ctx + p1 - 1) / p1 + 63) / 64 * 64;
+        const long long floor_s = s1 < 512 ? s1 : 512;
+        if (s < floor_s) s = floor_s;
+    }
     if (s < 64) s = 64;
-    if (s > 512) s = 512;
-    return s;
+    if (s > cap) s = cap;
+    return (int)s;
 }
 
 size_t attn_workspace_bytes(int batch, int hq, int d, int max_splits) {
@@ -430,11 +514,26 @@ int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st) {
     const int group = p.hq / p.hkv;
     const bool mma = kv_dtype == kKvF16 && p.d == 128 && p.page_tokens > 0;
     const dim3 block(kAttnThreads);
-    p.head_groups = mma ? (group + 3) / 4 : 1;
+    // 4 query heads per CTA for groups up to 4, else 8 (two column tiles)
+    const int hpc = group <= 4 ? 4 : 8;
+    p.head_groups = mma ? (group + hpc - 1) / hpc : 1;
     const dim3 grid(p.max_splits, p.hkv * p.head_groups, p.batch);
     cudaError_t e;
     if (mma) {
-        e = launch_pdl(paged_attn_f16_mma_kernel, grid, block, 0, st, p);
+        static int configured[64] = {0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev >= 0 && dev < 64 && !configured[dev]) {
+            e = cudaFuncSetAttribute(paged_attn_f16_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kAttnPipeSmem);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(paged_attn_f16_mma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kAttnPipeSmem);
+            if (e != cudaSuccess) return cuda_status(e, "paged attention smem attribute");
+            configured[dev] = 1;
+        }
+        e = hpc == 4 ? launch_pdl(paged_attn_f16_mma_kernel<1>, grid, block, kAttnPipeSmem, st, p)
+                     : launch_pdl(paged_attn_f16_mma_kernel<2>, grid, block, kAttnPipeSmem, st, p);
     } else {
         p.head_groups = 1;
         const dim3 sgrid(p.max_splits, p.hq, p.batch);

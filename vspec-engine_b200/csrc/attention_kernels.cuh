@@ -27,7 +27,7 @@ struct AttnParams {
 
 int attn_read_and_clear_page_fault(int* out);
 
-int attn_choose_split(int batch, int hkv, int max_ctx, int sms);
+int attn_choose_split(int batch, int hq, int hkv, int max_ctx, int page_tokens, int sms);
 size_t attn_workspace_bytes(int batch, int hq, int d, int max_splits);
 int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st);
 int paged_gather_launch(const void* kp, const void* vp, const int32_t* table, int ctx, int pt, int hkv, int d,
