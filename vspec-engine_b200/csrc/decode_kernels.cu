@@ -30,56 +30,72 @@ __global__ void embed_kernel(const __half* __restrict__ table, const int32_t* __
     if (t < hidden) x[(size_t)b * hidden + t] = __half2float(table[(size_t)tok[b] * hidden + t]);
 }
 
-// One block per (head, sequence): heads [0, hq) are query heads, [hq, hq+hkv)
-// key heads, [hq+hkv, hq+2hkv) value heads.  blockDim.x = head_dim (<= 256).
-__global__ void qk_norm_rope_append_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
-                                           const float* __restrict__ k_norm, const int32_t* __restrict__ pos,
-                                           int hq, int hkv, int d, float eps, float theta, float* __restrict__ q_out,
-                                           __half* __restrict__ k_pages, __half* __restrict__ v_pages,
-                                           const int32_t* __restrict__ page_table, int max_pages, int page_tokens,
-                                           int32_t* __restrict__ ctx_len) {
-    __shared__ float vals[256];
-    __shared__ float red[8];
+// One warp per (head, sequence), eight heads per block: heads [0, hq) are
+// query heads, [hq, hq+hkv) key heads, [hq+hkv, hq+2hkv) value heads.  Lane l
+// holds elements l + 32k (k < E = head_dim / 32), so both elements of every
+// rotary pair (i, i + head_dim/2) sit in the same lane.
+template <int E>
+__global__ void __launch_bounds__(256)
+qk_norm_rope_append_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
+                           const float* __restrict__ k_norm, const int32_t* __restrict__ pos, int hq, int hkv,
+                           float eps, float theta, float* __restrict__ q_out, __half* __restrict__ k_pages,
+                           __half* __restrict__ v_pages, const int32_t* __restrict__ page_table, int max_pages,
+                           int page_tokens, int32_t* __restrict__ ctx_len) {
     pdl_wait();
     pdl_trigger();
-    const int h = blockIdx.x;
+    constexpr int d = 32 * E;
+    constexpr int HE = E / 2;   // elements per lane in each half
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nh = hq + 2 * hkv;
+    const int h = blockIdx.x * 8 + warp;
     const int b = blockIdx.y;
-    const int t = threadIdx.x;
-    const int row = (hq + 2 * hkv) * d;
-    const float v = qkv[(size_t)b * row + (size_t)h * d + t];
+    if (h >= nh) return;
+    const float* src = qkv + (size_t)b * nh * d + (size_t)h * d;
+    float v[E];
+#pragma unroll
+    for (int k = 0; k < E; ++k) v[k] = src[lane + 32 * k];
     const int p = pos[b];
     const int page = page_table[(size_t)b * max_pages + p / page_tokens];
     const int slot = p % page_tokens;
     if (h >= hq + hkv) {
         // value head: straight into the page
-        const int kvh = h - hq - hkv;
-        v_pages[(((size_t)page * page_tokens + slot) * hkv + kvh) * d + t] = __float2half_rn(v);
+        __half* dst = v_pages + (((size_t)page * page_tokens + slot) * hkv + (h - hq - hkv)) * d;
+#pragma unroll
+        for (int k = 0; k < E; ++k) dst[lane + 32 * k] = __float2half_rn(v[k]);
         return;
     }
     // RMSNorm over the head
-    float ss = warp_sum(v * v);
-    if ((t & 31) == 0) red[t >> 5] = ss;
-    __syncthreads();
-    ss = 0.f;
-    for (int w = 0; w < (d + 31) / 32; ++w) ss += red[w];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < E; ++k) ss += v[k] * v[k];
+    ss = warp_sum(ss);
     const bool is_q = h < hq;
-    const float nw = is_q ? q_norm[t] : k_norm[t];
-    const float y = v / sqrtf(ss / (float)d + eps) * nw;
-    vals[t] = y;
-    __syncthreads();
-    // rotary, half split
-    const int half = d / 2;
-    const int i = t < half ? t : t - half;
-    const float inv_freq = 1.0f / powf(theta, (float)i / (float)half);
-    float sn, cs;
-    sincosf((float)p * inv_freq, &sn, &cs);
-    const float r = t < half ? vals[t] * cs - vals[t + half] * sn : vals[t - half] * sn + vals[t] * cs;
+    const float* nw = is_q ? q_norm : k_norm;
+    const float inv = 1.0f / sqrtf(ss / (float)d + eps);
+    float y[E];
+#pragma unroll
+    for (int k = 0; k < E; ++k) y[k] = v[k] * inv * nw[lane + 32 * k];
+    // rotary, half split: element i < d/2 pairs with i + d/2
+    float r[E];
+#pragma unroll
+    for (int k = 0; k < HE; ++k) {
+        const int i = lane + 32 * k;
+        const float inv_freq = 1.0f / powf(theta, (float)i / (float)(d / 2));
+        float sn, cs;
+        sincosf((float)p * inv_freq, &sn, &cs);
+        r[k] = y[k] * cs - y[k + HE] * sn;
+        r[k + HE] = y[k] * sn + y[k + HE] * cs;
+    }
     if (is_q) {
-        q_out[((size_t)b * hq + h) * d + t] = r;
+        float* dst = q_out + ((size_t)b * hq + h) * d;
+#pragma unroll
+        for (int k = 0; k < E; ++k) dst[lane + 32 * k] = r[k];
     } else {
         const int kvh = h - hq;
-        k_pages[(((size_t)page * page_tokens + slot) * hkv + kvh) * d + t] = __float2half_rn(r);
-        if (kvh == 0 && t == 0) ctx_len[b] = p + 1;
+        __half* dst = k_pages + (((size_t)page * page_tokens + slot) * hkv + kvh) * d;
+#pragma unroll
+        for (int k = 0; k < E; ++k) dst[lane + 32 * k] = __float2half_rn(r[k]);
+        if (kvh == 0 && lane == 0) ctx_len[b] = p + 1;
     }
 }
 
@@ -212,11 +228,25 @@ extern "C" int vspec_b200_decode_qk_rope_append(const float* d_qkv, const float*
         set_error("bad qk/rope/append arguments");
         return VSPEC_B200_ERR_ARG;
     }
-    const cudaError_t e = launch_pdl(qk_norm_rope_append_kernel, dim3(hq + 2 * hkv, batch), dim3(head_dim), 0,
-                                     (cudaStream_t)stream, d_qkv, d_q_norm, d_k_norm, d_pos, hq, hkv, head_dim, eps,
-                                     theta, d_q_out, reinterpret_cast<__half*>(d_k_pages),
-                                     reinterpret_cast<__half*>(d_v_pages), d_page_table, max_pages, page_tokens,
-                                     d_ctx_len);
+    const dim3 grid((hq + 2 * hkv + 7) / 8, batch);
+    __half* kpg = reinterpret_cast<__half*>(d_k_pages);
+    __half* vpg = reinterpret_cast<__half*>(d_v_pages);
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    switch (head_dim / 32) {
+        case 2: e = launch_pdl(qk_norm_rope_append_kernel<2>, grid, dim3(256), 0, st, d_qkv, d_q_norm, d_k_norm, d_pos,
+                               hq, hkv, eps, theta, d_q_out, kpg, vpg, d_page_table, max_pages, page_tokens, d_ctx_len);
+                break;
+        case 4: e = launch_pdl(qk_norm_rope_append_kernel<4>, grid, dim3(256), 0, st, d_qkv, d_q_norm, d_k_norm, d_pos,
+                               hq, hkv, eps, theta, d_q_out, kpg, vpg, d_page_table, max_pages, page_tokens, d_ctx_len);
+                break;
+        case 6: e = launch_pdl(qk_norm_rope_append_kernel<6>, grid, dim3(256), 0, st, d_qkv, d_q_norm, d_k_norm, d_pos,
+                               hq, hkv, eps, theta, d_q_out, kpg, vpg, d_page_table, max_pages, page_tokens, d_ctx_len);
+                break;
+        default: e = launch_pdl(qk_norm_rope_append_kernel<8>, grid, dim3(256), 0, st, d_qkv, d_q_norm, d_k_norm, d_pos,
+                                hq, hkv, eps, theta, d_q_out, kpg, vpg, d_page_table, max_pages, page_tokens, d_ctx_len);
+                 break;
+    }
     return e == cudaSuccess ? VSPEC_B200_OK : cuda_status(e, "qk_norm_rope_append_kernel launch");
 }
 
