@@ -124,6 +124,8 @@ gemm_prep_x_kernel(const float* __restrict__ x, const float* __restrict__ norm_w
                    __half* __restrict__ xh, float* __restrict__ xinv) {
     __shared__ float red[2][kGmPrepThreads / 32];
     pdl_wait();
+    // the GEMM may start its set-up and weight prefetch now (it waits for
+    // this grid to complete before it reads the rows)
     pdl_trigger();
     const int row = blockIdx.x;
     const float* xr = x + (size_t)row * k;
@@ -238,8 +240,11 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int G = gridDim.x;
-    // activations come from the pre-pass just before this launch
-    pdl_wait();
+    // The launch may start while the activation pre-pass still runs
+    // (programmatic dependent launch): set-up, weight tiles, scales and
+    // decoded A stages are model data; only the producer's activation loads
+    // and the epilogue's reads and writes wait for the pre-pass (and, through
+    // it, for everything before it in the stream).
     pdl_trigger();
 
     if (tid == 0) {
@@ -299,6 +304,7 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
                     if (SWIGLU) tma_load_2d(wdst + W_TILE, &wmap, kb * RB, p.half_n + wt * kGmRows, &w_full[sw]);
                     if (++sw == NSW) { sw = 0; pw ^= 1u; }
                     if (u >= NSB && !mbar_wait_sleep(&b_empty[sb], pb ^ 1u, abort_flag, kGmWaitLimit, kGmSleepNs)) { ok = false; break; }
+                    if (u == 0) pdl_wait();   // activations come from the pre-pass
                     mbar_arrive_expect_tx(&b_full[sb], B_STAGE);
                     unsigned char* bdst = bring + (size_t)sb * B_STAGE;
                     // the activation map is over bytes: k-block kb spans bytes [256 kb, 256 kb + 256)
@@ -472,6 +478,7 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
             if (!ok) break;
             // ---- epilogue of the item ----
             if (!mbar_wait_sleep(d_full, (uint32_t)(n_items & 1), abort_flag, kGmWaitLimit, kGmSleepNs)) { ok = false; break; }
+            if (n_items == 0) pdl_wait();   // x scales, residual, y and the partials follow the pre-pass
             tc_fence_after();
             const int out_n = SWIGLU ? p.half_n : p.n;
             const int col = wt * kGmRows + row;           // output column of this thread
@@ -738,10 +745,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& wm, const CUtensorMap& xm, c
         if (e != cudaSuccess) return e;
         configured[dev] = 1;
     }
-    // plain stream order: letting the next launch become resident early
-    // measured slower for this 1-CTA-per-SM kernel
-    kern<<<grid, kGmThreads, smem, st>>>(wm, xm, gp);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(grid), dim3(kGmThreads), smem, st, wm, xm, gp);
 }
 
 template <int BITS>
@@ -768,10 +772,10 @@ int gemm_tc_launch(const GemvParams& p, int bits, int unsigned_codes, cudaStream
     float* xinv = reinterpret_cast<float*>(wb + plan.xh_bytes);
     float* part = reinterpret_cast<float*>(wb + plan.xh_bytes + plan.xinv_bytes);
     const int rms = (p.flags & VSPEC_B200_F_RMSNORM) ? 1 : 0;
-    if (bits == 4) gemm_prep_x_kernel<4><<<p.m, kGmPrepThreads, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
-    else if (bits == 3) gemm_prep_x_kernel<3><<<p.m, kGmPrepThreads, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
-    else gemm_prep_x_kernel<2><<<p.m, kGmPrepThreads, 0, st>>>(p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (bits == 4) e = launch_pdl(gemm_prep_x_kernel<4>, dim3(p.m), dim3(kGmPrepThreads), 0, st, p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
+    else if (bits == 3) e = launch_pdl(gemm_prep_x_kernel<3>, dim3(p.m), dim3(kGmPrepThreads), 0, st, p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
+    else e = launch_pdl(gemm_prep_x_kernel<2>, dim3(p.m), dim3(kGmPrepThreads), 0, st, p.x, p.norm_w, p.eps, rms, p.k, xh, xinv);
     if (e != cudaSuccess) return cuda_status(e, "gemm_prep_x_kernel launch");
 
     CUtensorMap wm, xm;
