@@ -387,6 +387,55 @@ def time_decode(torch, V, world: int, rank: int, peak: float):
     }
 
 
+def time_gemm(torch, V, world: int, steps: int, peaks: dict):
+    """BASELINE config 2's M=64 and M=512 points (W4, K=4096, N=12288, group
+    128, fp16 scales, mid-range zero-point): the tcgen05 GEMM path through
+    vspec_b200_lowbit_linear, back to back in a CUDA graph over rotating
+    weight copies (> L2). TFLOP/s against the measured bf16 burst peak."""
+    out = {}
+    for m in (64, 512):
+        copies = 24
+        ws, ss = make_rotation(torch, 4, copies, seed=77 + m)
+        x = torch.randn((m, K_DIM), device="cuda", dtype=torch.float32)
+        ys = [torch.empty((m, N_DIM), device="cuda", dtype=torch.float32) for _ in range(copies)]
+        stream = torch.cuda.Stream()
+        flags = V.F_UNSIGNED | V.F_SZ_F16
+
+        def step(st):
+            for w, sc, y in zip(ws, ss, ys):
+                V.lowbit_linear(x.data_ptr(), w.data_ptr(), sc.data_ptr(), None, y.data_ptr(), m, N_DIM, K_DIM,
+                                K_DIM // GROUP, 4, flags=flags, stream=st)
+
+        with torch.cuda.stream(stream):
+            step(stream.cuda_stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step(stream.cuda_stream)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(start.elapsed_time(end), world)
+        del graph
+        us = ms * 1e3 / (steps * copies)
+        tflops = 2.0 * m * N_DIM * K_DIM / (us * 1e-6) / 1e12
+        out[f"m{m}"] = {"us_per_linear": round(us, 3), "tflops": round(tflops, 1),
+                        "frac": round(tflops / peaks["bf16_tflops"], 4),
+                        "weight_gbs": round(gemv_bytes(4, m=m) / (us * 1e-6) / 1e9, 1)}
+    out["config"] = ("config 2 M=64 and M=512 points: W4 K=4096 N=12288 group 128, fp16 scales, mid-range zero-point; "
+                     "activation pre-pass + tcgen05 GEMM (+ split-K merge) per linear; 24 rotating weight copies")
+    out["peak"] = {"bf16_tflops": peaks["bf16_tflops"], "source": "measured burst"}
+    return out
+
+
 TP_PROMPT, TP_GEN, TP_BATCH = 1024, 128, 256
 
 
@@ -564,6 +613,7 @@ def main() -> None:
     ms3, _ = time_gemv_graph(torch, V, 3, args.copies, args.steps, args.warmup, world)
     attn_steps = max(3, args.steps // 5)
     attn_ms, attn_kv, attn_other = time_attention(torch, V, attn_steps, args.warmup, world)
+    gemm = time_gemm(torch, V, world, max(3, args.steps // 5), load_peak_table())
     decode = None if args.no_decode else time_decode(torch, V, world, rank, peak)
     tp = None
     if not args.no_tp and (world > 1 or args.tp1):
@@ -619,6 +669,7 @@ def main() -> None:
                       "kv_bytes_per_step": attn_kv,
                       "config": "config 3: B=32 Hq=32 Hkv=8 d=128, ctx ~U[512,8192] (seeded), 16-token fp16 pages, "
                                 "page table = seeded permutation of the pool, one step = one decode-attention call"},
+        "gemm": gemm,
         "decode": decode,
         "decode_tp": tp if tp is not None else {
             "skipped": "config 5 is tensor-parallel over 2/4/8 GPUs; runs with --gpus >= 2 (or --tp1)"},
