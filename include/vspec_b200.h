@@ -252,6 +252,22 @@ int vspec_b200_random_fill_block(void* d_dst, size_t rows, size_t cols, size_t d
                                  size_t global_cols, size_t row0, size_t col0, float lo, float hi, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Load-time quantise + pack on the device, bit for bit the reference's
+ * _quantize_weight_rowwise (Vspec-chat/python/runtime_inference.py:708-785)
+ * on float32 weights.  d_w [n][k] fp32.  block_size: codes per scale group
+ * along k, a multiple of 32 (the reference's int4 default path, block size
+ * VSPEC_INT4_BLOCK_SIZE rounded up to 32), or 0 for whole rows (its int3 /
+ * int2 path and int4 with VSPEC_INT4_BLOCKWISE_ENABLE off).  percentile as
+ * VSPEC_QUANT_ROW_PERCENTILE (clamped to [0.95, 1]; >= 0.9999 uses min/max).
+ * Outputs: d_packed [n][ceil(k*bits/8)] signed codes LSB first, d_scales and
+ * d_zero_points [n][groups] fp32 (d_zero_points may be NULL: the reference
+ * returns no zero-points for int2, though its codes carry them).  A group is
+ * at most 46080 codes.
+ * ------------------------------------------------------------------------ */
+int vspec_b200_quantize_rowwise(const float* d_w, size_t n, size_t k, int bits, int block_size, double percentile,
+                                uint8_t* d_packed, float* d_scales, float* d_zero_points, void* stream);
+
+/* ------------------------------------------------------------------------
  * Qwen3-shape low-bit decode loop, random-init weights.
  * Host C driving the kernels above, the low-bit linears (RMSNorm / SwiGLU /
  * residual fused) and the paged attention; one decode step = one CUDA graph.

@@ -505,3 +505,99 @@ int oracle_qwen_generate(const OracleQwen* q, const int32_t* prompt, int prompt_
     free(x); free(xn); free(qkv); free(att); free(tmp); free(hbuf); free(logits); free(scores); free(kc); free(vc);
     return 0;
 }
+
+/* ---------------------------------------------------------------------------
+ * Load-time quantizer: Vspec-chat/python/runtime_inference.py:708-785
+ * (_quantize_weight_rowwise) restated with numpy's float32 semantics:
+ *   - quantiles by numpy's default 'linear' method on float32 data
+ *     (numpy/lib/_function_base_impl.py _quantile/_lerp): q cast to float32,
+ *     virtual index (n-1)*q in float32, gamma its fractional part, and
+ *     a + (b-a)*g for g < 0.5, b - (b-a)*(1-g) otherwise;
+ *   - np.min / np.max when the percentile is >= 0.9999 (:722-724);
+ *   - span = max(hi - lo, 1e-8), scale = span / levels, zp = clip(round(
+ *     min_q - lo/scale)), q = clip(round(w/scale + zp)), all float32 with
+ *     round-half-to-even (np.round), blocks along k (:734-764) or whole rows
+ *     (:766-773);
+ * and the codes packed per row (oracle_pack_rows).  block_size 0 = per row;
+ * zero_points may be NULL (the reference returns None for int2, :775-777,
+ * but the codes still carry the zero-point).  The arithmetic is kept in
+ * separate float operations (this file is built without FMA contraction).
+ * ------------------------------------------------------------------------- */
+static int cmp_f32(const void* a, const void* b) {
+    const float x = *(const float*)a, y = *(const float*)b;
+    return (x > y) - (x < y);
+}
+
+static float np_quantile_sorted_f32(const float* sorted, int n, double q) {
+    const float q32 = (float)q;
+    const float vi = (float)(n - 1) * q32;
+    if (!(vi > 0.0f)) return sorted[0];
+    if (vi >= (float)(n - 1)) return sorted[n - 1];
+    const float prev = floorf(vi);
+    const int lo = (int)prev;
+    const int hi = lo + 1 < n ? lo + 1 : n - 1;
+    const float g = vi - prev;
+    const float a = sorted[lo], b = sorted[hi];
+    const float d = b - a;
+    if (g >= 0.5f) {
+        const float t = 1.0f - g;
+        const float dt = d * t;
+        return b - dt;
+    }
+    const float dg = d * g;
+    return a + dg;
+}
+
+int oracle_quantize_rowwise(const float* w, size_t n, size_t k, int bits, int block_size, double percentile,
+                            uint8_t* packed, float* scales, float* zero_points) {
+    if (!w || !packed || !scales || n == 0 || k == 0 || bits < 2 || bits > 4 || block_size < 0) return -1;
+    double pc = percentile;
+    if (pc < 0.95) pc = 0.95;
+    if (pc > 1.0) pc = 1.0;
+    const double lo_q = 1.0 - pc;
+    const float max_q = (float)((1 << (bits - 1)) - 1);
+    const float min_q = (float)(-(1 << (bits - 1)));
+    const float levels = (max_q - min_q) > 1.0f ? (max_q - min_q) : 1.0f;
+    const size_t bs = block_size > 0 ? (size_t)block_size : k;
+    const size_t nb = (k + bs - 1) / bs;
+    float* buf = (float*)malloc(sizeof(float) * bs);
+    int8_t* codes = (int8_t*)malloc(k);
+    if (!buf || !codes) { free(buf); free(codes); return -1; }
+    const size_t rb = oracle_row_bytes(k, bits);
+    for (size_t r = 0; r < n; ++r) {
+        const float* wr = w + r * k;
+        for (size_t b = 0; b < nb; ++b) {
+            const size_t s0 = b * bs, s1 = s0 + bs < k ? s0 + bs : k;
+            const int len = (int)(s1 - s0);
+            memcpy(buf, wr + s0, sizeof(float) * (size_t)len);
+            qsort(buf, (size_t)len, sizeof(float), cmp_f32);
+            float bmin, bmax;
+            if (pc >= 0.9999) {
+                bmin = buf[0];
+                bmax = buf[len - 1];
+            } else {
+                bmin = np_quantile_sorted_f32(buf, len, lo_q);
+                bmax = np_quantile_sorted_f32(buf, len, pc);
+            }
+            float span = bmax - bmin;
+            const float floor_span = 1e-8f;
+            if (span < floor_span) span = floor_span;
+            const float scale = span / levels;
+            const float ratio = bmin / scale;
+            float zp = rintf(min_q - ratio);
+            zp = zp < min_q ? min_q : (zp > max_q ? max_q : zp);
+            for (size_t t = s0; t < s1; ++t) {
+                const float v = wr[t] / scale;
+                float qv = rintf(v + zp);
+                qv = qv < min_q ? min_q : (qv > max_q ? max_q : qv);
+                codes[t] = (int8_t)qv;
+            }
+            scales[r * nb + b] = scale;
+            if (zero_points) zero_points[r * nb + b] = zp;
+        }
+        oracle_pack_rows(codes, 1, k, bits, packed + r * rb);
+    }
+    free(buf);
+    free(codes);
+    return 0;
+}

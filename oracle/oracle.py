@@ -26,6 +26,8 @@ _o = {
     "oracle_row_bytes": ([c_size_t, c_int], c_size_t),
     "oracle_get_code": ([c_void_p, c_size_t, c_int], ctypes.c_int8),
     "oracle_pack_rows": ([c_void_p, c_size_t, c_size_t, c_int, c_void_p], None),
+    "oracle_quantize_rowwise": ([c_void_p, c_size_t, c_size_t, c_int, c_int, c_double, c_void_p, c_void_p, c_void_p],
+                                c_int),
     "oracle_unpack_rows": ([c_void_p, c_size_t, c_size_t, c_int, c_void_p], None),
     "oracle_group_of": ([c_size_t, c_size_t, c_size_t], c_size_t),
     "oracle_lowbit_matmul_f32": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_int, c_void_p, c_void_p, c_size_t,
@@ -157,6 +159,20 @@ def pack_rows(codes: np.ndarray, bits: int) -> np.ndarray:
     out = np.zeros((n, row_bytes(k, bits)), dtype=np.uint8)
     ORACLE.oracle_pack_rows(p(codes), n, k, bits, p(out))
     return out
+
+
+def quantize_rowwise(w: np.ndarray, bits: int, block_size: int, percentile: float = 0.999):
+    """C restatement of the reference quantizer (oracle_quantize_rowwise).
+    Returns (packed [n][row_bytes], scales [n*n_blocks], zero_points)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, k = w.shape
+    nb = (k + block_size - 1) // block_size if block_size > 0 else 1
+    packed = np.zeros((n, row_bytes(k, bits)), dtype=np.uint8)
+    s = np.zeros(n * nb, dtype=np.float32)
+    zp = np.zeros(n * nb, dtype=np.float32)
+    if ORACLE.oracle_quantize_rowwise(p(w), n, k, bits, block_size, percentile, p(packed), p(s), p(zp)) != 0:
+        raise RuntimeError("oracle_quantize_rowwise failed")
+    return packed, s, zp
 
 
 def unpack_rows(packed: np.ndarray, n: int, k: int, bits: int) -> np.ndarray:

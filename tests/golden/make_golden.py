@@ -13,6 +13,9 @@ Fixtures (all seeded):
   pack_rows.npz       -- runtime_inference._pack_signed_rowwise for bits 2/3/4.
   quantize_w4g128.npz -- runtime_inference._quantize_weight_rowwise with
                          VSPEC_INT4_BLOCK_SIZE=128 (config 4's quantizer).
+  quantize_variants.npz -- the same function over block sizes 32/40/64/128
+                         (a partial last block), per-row int4/int3/int2 and
+                         percentiles 0.97/0.995/0.999/1.0.
   attention_gqa.npz   -- runtime_inference._attention_cpu_batched with GQA 4:1.
 """
 from __future__ import annotations
@@ -62,6 +65,7 @@ def main() -> None:
     packed, s, zp = ri._quantize_weight_rowwise(wf, 4)
     np.savez_compressed(os.path.join(OUT, "quantize_w4g128.npz"), w=wf, packed=packed, s=s, zp=zp)
 
+
     # ---- GQA attention (Python CPU reference) ----
     hq, hkv, d, t = 8, 2, 64, 97
     q = rng.standard_normal((hq, d)).astype(np.float32)
@@ -70,6 +74,30 @@ def main() -> None:
     out = ri._attention_cpu_batched(q, keys, values, hq, hkv, False, hq // hkv, 1.0 / np.sqrt(d), 24.0)
     np.savez_compressed(os.path.join(OUT, "attention_gqa.npz"), q=q, keys=keys, values=values, out=out,
                         dims=np.array([hq, hkv, d, t], dtype=np.int64))
+    # ---- quantizer variants: block size, per-row int4/int3/int2, percentile ----
+    # (name, bits, n, k, VSPEC_INT4_BLOCKWISE_ENABLE, VSPEC_INT4_BLOCK_SIZE, VSPEC_QUANT_ROW_PERCENTILE)
+    variants = [("q4_b32", 4, 12, 320, "1", "32", "0.999"), ("q4_b128_k200", 4, 8, 200, "1", "128", "0.999"),
+                ("q4_b64_p995", 4, 8, 256, "1", "64", "0.995"), ("q4_row", 4, 8, 512, "0", "128", "0.999"),
+                ("q3_row", 3, 8, 384, "1", "128", "0.999"), ("q3_row_p1", 3, 6, 256, "1", "128", "1.0"),
+                ("q2_row", 2, 8, 256, "1", "128", "0.999"), ("q4_b40_outlier", 4, 6, 160, "1", "40", "0.97")]
+    qrng = np.random.default_rng(20261202)   # its own stream: the fixtures above stay as committed
+    qv = {}
+    for name, bits, n, k, enable, block, pct in variants:
+        os.environ["VSPEC_INT4_BLOCKWISE_ENABLE"] = enable
+        os.environ["VSPEC_INT4_BLOCK_SIZE"] = block
+        os.environ["VSPEC_QUANT_ROW_PERCENTILE"] = pct
+        wv = (qrng.standard_normal((n, k)) * 0.02).astype(np.float32)
+        wv[0, 3] = 0.5     # an outlier above the percentile
+        packed, s, zp = ri._quantize_weight_rowwise(wv, bits)
+        qv[f"{name}_w"] = wv
+        qv[f"{name}_packed"] = np.asarray(packed).reshape(n, -1)
+        qv[f"{name}_s"] = np.asarray(s, dtype=np.float32)
+        qv[f"{name}_zp"] = np.asarray(zp, dtype=np.float32) if zp is not None else np.zeros(0, np.float32)
+        qv[f"{name}_cfg"] = np.array([bits, int(enable), int(block), int(float(pct) * 1e6)], dtype=np.int64)
+    np.savez_compressed(os.path.join(OUT, "quantize_variants.npz"), **qv)
+    os.environ["VSPEC_INT4_BLOCKWISE_ENABLE"] = "1"
+    os.environ["VSPEC_INT4_BLOCK_SIZE"] = "128"
+    os.environ.pop("VSPEC_QUANT_ROW_PERCENTILE", None)
     print("fixtures written to", OUT)
 
 

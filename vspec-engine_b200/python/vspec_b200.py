@@ -146,6 +146,8 @@ _sigs = {
     "vspec_b200_random_fill": ([c_void_p, c_size_t, c_int, c_uint64, c_float, c_float, c_void_p], c_int),
     "vspec_b200_random_fill_block": ([c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_uint64, c_size_t, c_size_t,
                                       c_size_t, c_float, c_float, c_void_p], c_int),
+    "vspec_b200_quantize_rowwise": ([c_void_p, c_size_t, c_size_t, c_int, c_int, ctypes.c_double, c_void_p, c_void_p,
+                                     c_void_p, c_void_p], c_int),
     "vspec_b200_qwen_create": ([POINTER(QwenConfig), c_uint64, c_int, c_int, POINTER(c_void_p)], c_int),
     "vspec_b200_nccl_unique_id": ([c_void_p], c_int),
     "vspec_b200_qwen_create_tp": ([POINTER(QwenConfig), c_uint64, c_int, c_int, c_int, c_int, c_void_p,
