@@ -436,6 +436,56 @@ def time_gemm(torch, V, world: int, steps: int, peaks: dict):
     return out
 
 
+def time_quantize(torch, V, world: int, with_cpu: bool):
+    """Load-time quantise + pack: a 12288 x 4096 fp32
+    weight (N(0, 0.02), seeded) to W4 block 128 at the 0.999 percentile, as
+    the reference's _quantize_weight_rowwise with VSPEC_INT4_BLOCK_SIZE=128;
+    GB/s of fp32 input. CPU baseline: the C restatement on a 256-row sample."""
+    import ctypes
+    n, k, bits, block = N_DIM, K_DIM, 4, 128
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    w = torch.randn((n, k), device="cuda", generator=g) * 0.02
+    packed = torch.empty((n, k * bits // 8), dtype=torch.uint8, device="cuda")
+    s = torch.empty(n * (k // block), device="cuda")
+    zp = torch.empty(n * (k // block), device="cuda")
+    stream = torch.cuda.Stream()
+
+    def call():
+        rc = V.lib.vspec_b200_quantize_rowwise(w.data_ptr(), n, k, bits, block, ctypes.c_double(0.999),
+                                               packed.data_ptr(), s.data_ptr(), zp.data_ptr(),
+                                               ctypes.c_void_p(stream.cuda_stream))
+        if rc != 0:
+            raise RuntimeError("quantize_rowwise failed: " + V.last_error())
+
+    for _ in range(2):
+        call()
+    torch.cuda.synchronize()
+    barrier(world)
+    reps = 5
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(reps):
+            call()
+        end.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world) / reps
+    out = {"metric": "load-time W4 block-128 quantise + pack GB/s (fp32 input)", "value": round(n * k * 4 / (ms * 1e-3) / 1e9, 2),
+           "unit": "GB/s", "ms_per_matrix": round(ms, 3),
+           "config": f"{n} x {k} fp32 N(0, 0.02) -> int4 blocks of {block}, percentile 0.999 (bit-exact to the reference quantizer)"}
+    if with_cpu:
+        import oracle as O
+        rows = 256
+        wc = w[:rows].cpu().numpy()
+        t0 = time.perf_counter()
+        O.quantize_rowwise(wc, bits, block, 0.999)
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": round(rows * k * 4 / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                               "sample": f"oracle_quantize_rowwise on {rows} of {n} rows, {dt:.2f} s"}
+    return out
+
+
 TP_PROMPT, TP_GEN, TP_BATCH = 1024, 128, 256
 
 
@@ -614,6 +664,7 @@ def main() -> None:
     attn_steps = max(3, args.steps // 5)
     attn_ms, attn_kv, attn_other = time_attention(torch, V, attn_steps, args.warmup, world)
     gemm = time_gemm(torch, V, world, max(3, args.steps // 5), load_peak_table())
+    quant = time_quantize(torch, V, world, rank == 0 and not args.no_cpu)
     decode = None if args.no_decode else time_decode(torch, V, world, rank, peak)
     tp = None
     if not args.no_tp and (world > 1 or args.tp1):
@@ -670,6 +721,7 @@ def main() -> None:
                       "config": "config 3: B=32 Hq=32 Hkv=8 d=128, ctx ~U[512,8192] (seeded), 16-token fp16 pages, "
                                 "page table = seeded permutation of the pool, one step = one decode-attention call"},
         "gemm": gemm,
+        "quantize": quant,
         "decode": decode,
         "decode_tp": tp if tp is not None else {
             "skipped": "config 5 is tensor-parallel over 2/4/8 GPUs; runs with --gpus >= 2 (or --tp1)"},
