@@ -116,13 +116,18 @@ int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* args, void* stre
  *   VSPEC_B200_PATH_WARPMMA persistent split-K warp-MMA kernel, weights
  *                           streamed through registers (m <= 8)
  *   VSPEC_B200_PATH_TCGEN05 TMA + TMEM + tcgen05.mma kernel (m <= 4)
- *   VSPEC_B200_PATH_RING    TMA shared-memory ring + warp-MMA decode (m <= 8)
+ *   VSPEC_B200_PATH_RING    TMA shared-memory ring + warp-MMA decode, split-K
+ *                           across CTAs (m <= 8)
+ *   VSPEC_B200_PATH_ROWS    TMA ring + warp-MMA decode, each CTA a contiguous
+ *                           row range over all of k, no workspace (m <= 8,
+ *                           k % 1024 == 0)
  * A fast path that does not support the shape returns VSPEC_B200_ERR_UNSUPPORTED. */
 #define VSPEC_B200_PATH_AUTO 0
 #define VSPEC_B200_PATH_GENERIC 1
 #define VSPEC_B200_PATH_WARPMMA 2
 #define VSPEC_B200_PATH_TCGEN05 3
 #define VSPEC_B200_PATH_RING 4
+#define VSPEC_B200_PATH_ROWS 5
 int vspec_b200_lowbit_linear_path(const VspecB200LinearArgs* args, void* stream, int path);
 
 /* Decode every code of a packed [n][k] matrix into int8 [n][k] (bit-exact

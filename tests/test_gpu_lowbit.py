@@ -257,7 +257,7 @@ def test_workspace_too_small_is_rejected():
 
 
 
-FAST_PATHS = [V.PATH_WARPMMA, V.PATH_TCGEN05, V.PATH_RING]
+FAST_PATHS = [V.PATH_WARPMMA, V.PATH_TCGEN05, V.PATH_RING, V.PATH_ROWS]
 
 
 def test_tcgen05_path_smoke():
@@ -294,6 +294,8 @@ def test_ring_path_smoke():
 def test_fast_paths_match_oracle(path, bits, m, n, k, g):
     if path == V.PATH_TCGEN05 and m > 4:
         pytest.skip("the tcgen05 GEMV takes m <= 4")
+    if path == V.PATH_ROWS and k % 1024 != 0:
+        pytest.skip("the row-sliced GEMV takes k % 1024 == 0")
     rng = np.random.default_rng(path * 100 + bits * 10 + m + n + k)
     w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=(n % 2 == 0))
     x = rng.standard_normal((m, k)).astype(np.float32)
@@ -322,6 +324,82 @@ def test_fast_paths_fused_epilogues(path):
     gate, up = full[:, : n // 2], full[:, n // 2:]
     y = run_linear(x, w, s, zp, n, k, 4, g, flags=V.F_SWIGLU, out_cols=n // 2, path=path)
     assert rel_err(y, gate / (1.0 + np.exp(-gate)) * up) <= RTOL_F32
+
+
+def test_rows_path_smoke():
+    """One small launch of the row-sliced kernel on its own."""
+    rng = np.random.default_rng(3)
+    m, n, k, g = 1, 256, 1024, 8
+    w, s, zp = make_lowbit(rng, n, k, 4, g)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = run_linear(x, w, s, zp, n, k, 4, g, path=V.PATH_ROWS)
+    flag = __import__("ctypes").c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(__import__("ctypes").byref(flag)), "timeout flag")
+    assert flag.value == 0
+    assert rel_err(y, O.lowbit_matmul(x, w, n, k, 4, s, zp, g)) <= RTOL_F32
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("m,n,k,g,flags", [
+    (1, 24, 1024, 8, 0),                   # three CTAs of eight rows, one box each
+    (1, 80000, 1024, 8, 0),                # more than 256 rows per CTA: two row groups
+    (6, 40000, 1024, 4, 0),                # m > 4 (two activation tiles): groups of <= 128 rows
+    (2, 4104, 2048, 16, 0),                # rows per CTA not a multiple of 16
+    (5, 80000, 1024, 8, 0x10),             # SwiGLU, several gate/up group pairs per CTA
+    (3, 10000, 3072, 24, 0x4),             # residual
+    (1, 5000, 4096, 16, 0x8),              # RMSNorm input, groups of 256 codes
+])
+def test_rows_path_shapes(bits, m, n, k, g, flags):
+    """Row-sliced kernel at shapes that exercise its geometry: tiny CTAs, row
+    groups, partial 16-row blocks, every epilogue; fp32 scales + zero-points
+    (fp16 when g is a multiple of 8)."""
+    rng = np.random.default_rng(bits * 1000 + m * 10 + (n % 997) + flags)
+    w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=(g % 8 == 0))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    sf, zf = s.astype(np.float32), zp.astype(np.float32)
+    full = O.lowbit_matmul(x, w, n, k, bits, sf, zf, g).astype(np.float64)
+    if flags & V.F_SWIGLU:
+        gate, up = full[:, : n // 2], full[:, n // 2:]
+        ref = gate / (1.0 + np.exp(-gate)) * up
+        y = run_linear(x, w, s, zp, n, k, bits, g, flags=flags, out_cols=n // 2, path=V.PATH_ROWS)
+    elif flags & V.F_RESIDUAL:
+        res = rng.standard_normal((m, n)).astype(np.float32)
+        ref = full + res
+        y = run_linear(x, w, s, zp, n, k, bits, g, flags=flags, residual=res, path=V.PATH_ROWS)
+    elif flags & V.F_RMSNORM:
+        nw = rng.uniform(0.5, 1.5, k).astype(np.float32)
+        xh = (x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6)
+              * nw).astype(np.float32)
+        ref = O.lowbit_matmul(xh, w, n, k, bits, sf, zf, g)
+        y = run_linear(x, w, s, zp, n, k, bits, g, flags=flags, norm_w=nw, eps=1e-6, path=V.PATH_ROWS)
+    else:
+        ref = full
+        y = run_linear(x, w, s, zp, n, k, bits, g, path=V.PATH_ROWS)
+    flag = __import__("ctypes").c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(__import__("ctypes").byref(flag)), "timeout flag")
+    assert flag.value == 0
+    err = rel_err(y, ref)
+    print(f"rows bits={bits} m={m} n={n} k={k} flags={flags}: {err:.2e}")
+    assert err <= RTOL_F32
+
+
+def test_rows_path_deterministic_and_unsupported_shapes():
+    """Two launches give bit-identical output; shapes outside the kernel's
+    contract are refused on the host when requested explicitly."""
+    rng = np.random.default_rng(123)
+    m, n, k, g = 2, 12288, 4096, 32
+    w, s, _ = make_lowbit(rng, n, k, 4, g, sz_f16=True, zp_mode="none")
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    f = V.F_UNSIGNED | V.F_SZ_F16
+    y1 = run_linear(x, w, s, None, n, k, 4, g, flags=f, path=V.PATH_ROWS)
+    y2 = run_linear(x, w, s, None, n, k, 4, g, flags=f, path=V.PATH_ROWS)
+    assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
+    ref = x.astype(np.float64) @ dequant_np(w, n, k, 4, s.astype(np.float32), None, g, unsigned=True).T
+    assert rel_err(y1, ref) <= RTOL_F32
+    w5, s5, zp5 = make_lowbit(rng, 64, 640, 4, 5)
+    x5 = rng.standard_normal((1, 640)).astype(np.float32)
+    with pytest.raises(V.VspecB200Error, match="not supported"):
+        run_linear(x5, w5, s5, zp5, 64, 640, 4, 5, path=V.PATH_ROWS)
 
 
 @pytest.mark.parametrize("m,n", [(1, 12288), (4, 9984), (7, 12288)])

@@ -123,20 +123,22 @@ extern "C" int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* a, vo
 }
 
 extern "C" int vspec_b200_lowbit_linear_path(const VspecB200LinearArgs* a, void* stream, int path) {
-    if (path < kPathAuto || path > kPathRing) { set_error("unknown path %d", path); return VSPEC_B200_ERR_ARG; }
+    if (path < kPathAuto || path > kPathRows) { set_error("unknown path %d", path); return VSPEC_B200_ERR_ARG; }
     return linear_common(a, stream, path);
 }
 
 extern "C" int vspec_b200_gemv_timeout_flag(int* out_flag) {
     if (!out_flag) { set_error("NULL out_flag"); return VSPEC_B200_ERR_ARG; }
-    int a = 0, b = 0, c = 0;
+    int a = 0, b = 0, c = 0, d = 0;
     int rc = gemv_tc_read_and_clear_timeout(&a);
     if (rc != VSPEC_B200_OK) return rc;
     rc = gemv_ring_read_and_clear_timeout(&b);
     if (rc != VSPEC_B200_OK) return rc;
     rc = gemm_tc_read_and_clear_timeout(&c);
     if (rc != VSPEC_B200_OK) return rc;
-    *out_flag = (a || b || c) ? 1 : 0;
+    rc = gemv_rows_read_and_clear_timeout(&d);
+    if (rc != VSPEC_B200_OK) return rc;
+    *out_flag = (a || b || c || d) ? 1 : 0;
     return VSPEC_B200_OK;
 }
 

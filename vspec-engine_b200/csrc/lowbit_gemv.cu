@@ -589,6 +589,16 @@ static bool ring_path_enabled() {
     return v == 1;
 }
 
+// VSPEC_B200_GEMV_ROWS=1 makes the dispatcher prefer the row-sliced kernel.
+static bool rows_path_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_GEMV_ROWS");
+        v = (e && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
 // Library-managed workspace: one grow-only, zero-initialized buffer per device
 // and host thread (each host thread is expected to use one stream).
 struct GemvWs {
@@ -714,6 +724,23 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
     }
 
     const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
+    // The row-sliced kernel needs no workspace: it runs before any is taken (a
+    // caller workspace is still checked against the documented size).
+    if (!force_generic && (path == kPathRows || (path == kPathAuto && rows_path_enabled()))) {
+        if (gemv_rows_supported(p, bits)) {
+            if (fast && workspace && workspace_bytes < gemv_workspace_bytes(p.m, p.n, p.k, swiglu)) {
+                set_error("GEMV workspace too small (%zu < %zu)", workspace_bytes,
+                          gemv_workspace_bytes(p.m, p.n, p.k, swiglu));
+                return VSPEC_B200_ERR_ARG;
+            }
+            return gemv_rows_launch(p, bits, unsigned_codes, st, pdl_enabled());
+        }
+        if (path == kPathRows) {
+            set_error("shape not supported by the row-sliced GEMV (m <= 8, k %% 1024 == 0, groups of 128*i, "
+                      "16-byte aligned rows / scale rows, smem)");
+            return VSPEC_B200_ERR_UNSUPPORTED;
+        }
+    }
     if (!fast && (path == kPathWarpMma || path == kPathTensorCore || path == kPathRing)) {
         set_error("shape not supported by the requested fast path");
         return VSPEC_B200_ERR_UNSUPPORTED;

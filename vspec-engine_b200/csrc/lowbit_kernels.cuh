@@ -46,6 +46,7 @@ constexpr int kPathGeneric = 1;
 constexpr int kPathWarpMma = 2;
 constexpr int kPathTensorCore = 3;
 constexpr int kPathRing = 4;
+constexpr int kPathRows = 5;
 int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, int path,
                        void* workspace, size_t workspace_bytes);
 size_t gemv_workspace_bytes(int m, int n, int k, bool swiglu);
@@ -59,6 +60,10 @@ bool gemv_ring_supported(const GemvParams& p, int bits, size_t counter_slots);
 int gemv_ring_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl);
 size_t gemv_ring_scratch_floats(int m, int n, int k, bool swiglu);
 int gemv_ring_read_and_clear_timeout(int* out);
+// row-sliced TMA GEMV, no workspace (lowbit_gemv_rows.cu)
+bool gemv_rows_supported(const GemvParams& p, int bits);
+int gemv_rows_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl);
+int gemv_rows_read_and_clear_timeout(int* out);
 // tcgen05 GEMM for m > kGemvMaxM (lowbit_gemm_tc.cu)
 bool gemm_tc_supported(const GemvParams& p, int bits, size_t counter_slots);
 size_t gemm_tc_workspace_bytes(int m, int n, int k, bool swiglu);

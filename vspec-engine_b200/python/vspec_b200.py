@@ -26,7 +26,7 @@ F_RMSNORM = 0x8
 F_SWIGLU = 0x10
 KV_F32 = 0
 KV_F16 = 1
-PATH_AUTO, PATH_GENERIC, PATH_WARPMMA, PATH_TCGEN05, PATH_RING = 0, 1, 2, 3, 4
+PATH_AUTO, PATH_GENERIC, PATH_WARPMMA, PATH_TCGEN05, PATH_RING, PATH_ROWS = 0, 1, 2, 3, 4, 5
 
 
 class VspecB200Error(RuntimeError):
