@@ -110,8 +110,8 @@ int vspec_b200_lowbit_linear_static(const VspecB200LinearArgs* args, void* strea
 int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* args, void* stream);
 
 /* Same contraction through an explicit kernel family:
- *   VSPEC_B200_PATH_AUTO    the dispatcher's choice (ring, else warp-MMA,
- *                           else generic)
+ *   VSPEC_B200_PATH_AUTO    the dispatcher's choice (row-sliced where it is
+ *                           faster, else ring, else warp-MMA, else generic)
  *   VSPEC_B200_PATH_GENERIC any shape, one warp per output row
  *   VSPEC_B200_PATH_WARPMMA persistent split-K warp-MMA kernel, weights
  *                           streamed through registers (m <= 8)

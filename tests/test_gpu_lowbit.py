@@ -348,6 +348,7 @@ def test_rows_path_smoke():
     (5, 80000, 1024, 8, 0x10),             # SwiGLU, several gate/up group pairs per CTA
     (3, 10000, 3072, 24, 0x4),             # residual
     (1, 5000, 4096, 16, 0x8),              # RMSNorm input, groups of 256 codes
+    (8, 12288, 4096, 32, 0),               # m = 8: large activation fragments, a shallow ring
 ])
 def test_rows_path_shapes(bits, m, n, k, g, flags):
     """Row-sliced kernel at shapes that exercise its geometry: tiny CTAs, row

@@ -317,9 +317,9 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
             // every issued copy lands before the CTA's shared memory goes away
             const long long issued = u;
             for (long long i = (issued > NSW ? issued - NSW : 0); i < issued; ++i)
-                (void)mbar_wait_sleep(&w_full[i % NSW], (uint32_t)((i / NSW) & 1), abort_flag, kGmWaitLimit, kGmSleepNs);
+                (void)mbar_wait_drain(&w_full[i % NSW], (uint32_t)((i / NSW) & 1), kGmWaitLimit);
             for (long long i = (issued > NSB ? issued - NSB : 0); i < issued; ++i)
-                (void)mbar_wait_sleep(&b_full[i % NSB], (uint32_t)((i / NSB) & 1), abort_flag, kGmWaitLimit, kGmSleepNs);
+                (void)mbar_wait_drain(&b_full[i % NSB], (uint32_t)((i / NSB) & 1), kGmWaitLimit);
         }
     } else if (warp == kGmMmaWarp) {
         // ======================= MMA issuer ===================================

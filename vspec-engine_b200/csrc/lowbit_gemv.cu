@@ -589,14 +589,16 @@ static bool ring_path_enabled() {
     return v == 1;
 }
 
-// VSPEC_B200_GEMV_ROWS=1 makes the dispatcher prefer the row-sliced kernel.
-static bool rows_path_enabled() {
+// Row-sliced kernel in the automatic dispatch (VSPEC_B200_GEMV_ROWS): unset =
+// the shapes where it measured faster (2), "1" = every shape it supports (1),
+// "0" = never (0, A/B timing).
+static int rows_path_mode() {
     static int v = -1;
     if (v < 0) {
         const char* e = getenv("VSPEC_B200_GEMV_ROWS");
-        v = (e && e[0] == '1') ? 1 : 0;
+        v = (e && e[0] == '1') ? 1 : ((e && e[0] == '0') ? 0 : 2);
     }
-    return v == 1;
+    return v;
 }
 
 // Library-managed workspace: one grow-only, zero-initialized buffer per device
@@ -726,7 +728,10 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
     const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
     // The row-sliced kernel needs no workspace: it runs before any is taken (a
     // caller workspace is still checked against the documented size).
-    if (!force_generic && (path == kPathRows || (path == kPathAuto && rows_path_enabled()))) {
+    const int rows_mode = rows_path_mode();
+    const bool rows_auto = path == kPathAuto && (rows_mode == 1 ? gemv_rows_supported(p, bits)
+                                                 : (rows_mode == 2 && gemv_rows_preferred(p, bits)));
+    if (!force_generic && (path == kPathRows || rows_auto)) {
         if (gemv_rows_supported(p, bits)) {
             if (fast && workspace && workspace_bytes < gemv_workspace_bytes(p.m, p.n, p.k, swiglu)) {
                 set_error("GEMV workspace too small (%zu < %zu)", workspace_bytes,

@@ -774,7 +774,7 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
         // every issued copy lands before the CTA's shared memory goes away
         const int first = p_issued > NS ? p_issued - NS : 0;
         for (int i = first; i < p_issued; ++i)
-            (void)mbar_wait_sleep(&full[i % NS], (uint32_t)((i / NS) & 1), abort_flag, kRingWaitLimit, kRingSleepNs);
+            (void)mbar_wait_drain(&full[i % NS], (uint32_t)((i / NS) & 1), kRingWaitLimit);
     }
 
     if (p.cluster_merge) {

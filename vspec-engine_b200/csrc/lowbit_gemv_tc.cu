@@ -484,7 +484,7 @@ lowbit_gemv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
             // drain: every issued copy must land before the CTA's smem goes away
             const int first = p_issued > NS ? p_issued - NS : 0;
             for (int i = first; i < p_issued; ++i)
-                (void)mbar_wait(&full[i % NS], (uint32_t)((i / NS) & 1), abort_flag, kTcWaitLimit);
+                (void)mbar_wait_drain(&full[i % NS], (uint32_t)((i / NS) & 1), 1u << 16);
         }
     } else {
         // ======================= MMA issuer (warp 9) ==========================

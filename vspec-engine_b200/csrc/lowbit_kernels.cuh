@@ -62,6 +62,7 @@ size_t gemv_ring_scratch_floats(int m, int n, int k, bool swiglu);
 int gemv_ring_read_and_clear_timeout(int* out);
 // row-sliced TMA GEMV, no workspace (lowbit_gemv_rows.cu)
 bool gemv_rows_supported(const GemvParams& p, int bits);
+bool gemv_rows_preferred(const GemvParams& p, int bits);
 int gemv_rows_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st, bool pdl);
 int gemv_rows_read_and_clear_timeout(int* out);
 // tcgen05 GEMM for m > kGemvMaxM (lowbit_gemm_tc.cu)

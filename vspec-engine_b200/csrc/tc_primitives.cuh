@@ -68,6 +68,16 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
     return false;
 }
 
+// Bounded wait for the copies a CTA issued itself before it exits: unlike
+// mbar_wait_sleep it ignores the abort flag, so an aborted CTA still waits for
+// its in-flight bulk copies instead of releasing shared memory under them.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint32_t limit) {
+    if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+    return false;
+}
+
 // ---------------------------------------------------------------- TMA
 // 2-D tile load global -> shared, completion counted on `bar` (transaction bytes).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
