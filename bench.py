@@ -326,6 +326,62 @@ def time_attention(torch, V, steps: int, warmup: int, world: int):
     return ms, kv_bytes, other
 
 
+def time_attention_int3(torch, V, steps: int, warmup: int, world: int, block: int = 32):
+    """Config 3 with int3 K/V pages (kv_cache.c int3 compression, block 32):
+    the same seeded fp16 pools quantised on the GPU, then paged GQA attention
+    reading the 3-bit codes and per-block scales (128 B per token and KV head
+    for K+V instead of 512 B of fp16)."""
+    ctx, table, total, kp, vp, q = make_config3(torch)
+    rows = total * ATTN_PT
+    pb, nb = ATTN_D * 3 // 8, ATTN_D // block
+    pools = []
+    for src in (kp, vp):
+        codes = torch.empty((rows, ATTN_HKV, pb), dtype=torch.uint8, device="cuda")
+        scales = torch.empty((rows, ATTN_HKV, nb), dtype=torch.float32, device="cuda")
+        f32 = src.float()
+        V.kv_int3_quantize(f32.data_ptr(), None, rows, ATTN_HKV, ATTN_D, block, codes.data_ptr(), scales.data_ptr())
+        torch.cuda.synchronize()
+        del f32
+        pools.append((codes, scales))
+    del kp, vp
+    (kc, ks), (vc, vs) = pools
+    dt = torch.from_numpy(table).cuda()
+    dc = torch.from_numpy(ctx).cuda()
+    out = torch.empty((ATTN_B, ATTN_HQ, ATTN_D), device="cuda", dtype=torch.float32)
+    stream = torch.cuda.Stream()
+    scale = 1.0 / float(np.sqrt(ATTN_D))
+
+    def call(st):
+        V.paged_attention_int3(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), ks.data_ptr(), vs.data_ptr(), block,
+                               dt.data_ptr(), dc.data_ptr(), out.data_ptr(), ATTN_B, ATTN_HQ, ATTN_HKV, ATTN_D,
+                               ATTN_PT, table.shape[1], total, int(ctx.max()), scale, stream=st)
+
+    with torch.cuda.stream(stream):
+        call(stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        call(stream.cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    del graph
+    kv_bytes = int(ctx.astype(np.int64).sum()) * ATTN_HKV * (pb + nb * 4) * 2
+    other = q.numel() * 4 + out.numel() * 4 + table.size * 4 + ctx.size * 4
+    return ms, kv_bytes, other
+
+
 DEC_PROMPT, DEC_GEN, DEC_BATCH = 512, 256, 64
 
 
@@ -663,6 +719,7 @@ def main() -> None:
     ms3, _ = time_gemv_graph(torch, V, 3, args.copies, args.steps, args.warmup, world)
     attn_steps = max(3, args.steps // 5)
     attn_ms, attn_kv, attn_other = time_attention(torch, V, attn_steps, args.warmup, world)
+    a3_ms, a3_kv, a3_other = time_attention_int3(torch, V, attn_steps, args.warmup, world)
     gemm = time_gemm(torch, V, world, max(3, args.steps // 5), load_peak_table())
     quant = time_quantize(torch, V, world, rank == 0 and not args.no_cpu)
     decode = None if args.no_decode else time_decode(torch, V, world, rank, peak)
@@ -720,6 +777,14 @@ def main() -> None:
                       "kv_bytes_per_step": attn_kv,
                       "config": "config 3: B=32 Hq=32 Hkv=8 d=128, ctx ~U[512,8192] (seeded), 16-token fp16 pages, "
                                 "page table = seeded permutation of the pool, one step = one decode-attention call"},
+        "attention_int3": {
+            "value": round(world * attn_steps * (a3_kv + a3_other) / (a3_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(a3_ms / attn_steps, 4),
+            "frac": round((a3_kv + a3_other) / (a3_ms * 1e-3 / attn_steps) / 1e9 / peak, 4),
+            "kv_bytes_per_step": a3_kv,
+            "speedup_vs_fp16_pages": round(attn_ms / a3_ms, 3),
+            "config": "config 3 with int3 K/V pages: the fp16 pools quantised on the GPU as vspec_kv_cache_append's "
+                      "int3 compression does (block 32, percentile 99.5), 3-bit codes + fp32 block scales"},
         "gemm": gemm,
         "quantize": quant,
         "decode": decode,
@@ -727,7 +792,7 @@ def main() -> None:
             "skipped": "config 5 is tensor-parallel over 2/4/8 GPUs; runs with --gpus >= 2 (or --tp1)"},
         "cpu_baseline": cpu,
         "clocks": clocks,
-        "gpu_launches": launches * 2 + attn_steps * 2,
+        "gpu_launches": launches * 2 + attn_steps * 2 * 2,
     }
     print(json.dumps(line))
 

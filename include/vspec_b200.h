@@ -194,6 +194,30 @@ typedef struct VspecB200PagedAttnArgs {
 size_t vspec_b200_paged_attention_workspace_bytes(size_t batch, size_t num_q_heads, size_t num_kv_heads,
                                                   size_t head_dim, size_t max_ctx);
 int vspec_b200_paged_attention(const VspecB200PagedAttnArgs* args, void* stream);
+
+/* int3 KV pages (VspecKVCache int3 compression, src/attention/kv_cache.c:64-126
+ * and 160-226, dequantised in attention as src/kernel/cuda/attention_fused.cu:23-45
+ * and 232-351 do, moved onto the paged layout):
+ *   codes  [num_pages][page_tokens][num_kv_heads][head_dim*3/8] bytes, each
+ *          head row the LSB-first 3-bit bitstream of src/quant/pack.c:30-51;
+ *   scales [num_pages][page_tokens][num_kv_heads][head_dim/block_size] fp32.
+ * vspec_b200_kv_int3_quantize compresses `rows` fp32 rows [num_heads][head_dim]
+ * (one token each) into pool rows d_slots[r] (page * page_tokens + slot; r
+ * when d_slots is NULL), bit for bit as vspec_kv_cache_append with int3
+ * compression on: per block of block_size (16 or 32) dims the percentile
+ * element of the sorted |x| (the reference uses 99.5), scale = that / 4,
+ * codes lrintf(x / scale) clipped to [-4, 3].  head_dim % block_size == 0,
+ * head_dim <= 256, head_dim % 8 == 0. */
+#define VSPEC_B200_KV_INT3 2
+int vspec_b200_kv_int3_quantize(const float* d_src, const int32_t* d_slots, size_t rows, size_t num_heads,
+                                size_t head_dim, size_t block_size, float percentile, uint8_t* d_codes,
+                                float* d_scales, void* stream);
+/* Paged GQA decode attention over int3 pages: args->d_k_pages / d_v_pages are
+ * the code pools, args->kv_dtype must be VSPEC_B200_KV_INT3, head_dim 128,
+ * at most 8 query heads per KV head; pools and scale pools 16-byte aligned.
+ * Same contract as vspec_b200_paged_attention otherwise. */
+int vspec_b200_paged_attention_int3(const VspecB200PagedAttnArgs* args, const float* d_k_scales,
+                                    const float* d_v_scales, size_t block_size, void* stream);
 /* Reads and clears the out-of-range page id flag (1 = seen since last call). */
 int vspec_b200_paged_attention_page_fault(int* out_flag);
 

@@ -601,3 +601,98 @@ int oracle_quantize_rowwise(const float* w, size_t n, size_t k, int bits, int bl
     free(codes);
     return 0;
 }
+
+/* ---- int3 KV-cache compression (src/attention/kv_cache.c:32-126, 160-226) ---- */
+static int cmp_float_asc(const void* a, const void* b) {
+    const float x = *(const float*)a, y = *(const float*)b;
+    return x < y ? -1 : (x > y ? 1 : 0);
+}
+
+void oracle_kv_int3_quantize(const float* src, size_t rows, size_t heads, size_t head_dim, size_t block_size,
+                             float percentile, uint8_t* codes, float* scales) {
+    const size_t pb = oracle_row_bytes(head_dim, 3);
+    const size_t nb = (head_dim + block_size - 1) / block_size;
+    if (percentile < 50.0f) percentile = 50.0f;       /* kv_cache.c:38-43 */
+    if (percentile > 100.0f) percentile = 100.0f;
+    int8_t* q = (int8_t*)malloc(head_dim);
+    float tmp[32];
+    for (size_t r = 0; r < rows; ++r) {
+        for (size_t h = 0; h < heads; ++h) {
+            const float* x = src + (r * heads + h) * head_dim;
+            float* sc = scales + (r * heads + h) * nb;
+            for (size_t b = 0; b < nb; ++b) {
+                const size_t base = b * block_size;
+                size_t len = block_size;
+                if (base + len > head_dim) len = head_dim - base;
+                size_t n = len > 32 ? 32 : len;
+                for (size_t i = 0; i < n; ++i) tmp[i] = fabsf(x[base + i]);
+                qsort(tmp, n, sizeof(float), cmp_float_asc);
+                size_t idx = (size_t)((double)(n - 1) * ((double)percentile / 100.0));
+                if (idx >= n) idx = n - 1;
+                const float rep = n ? tmp[idx] : 0.0f;
+                float scale = rep > 0.0f ? rep / 4.0f : 1.0f;   /* qmax = 4 */
+                if (scale < 1e-6f) scale = 1e-6f;
+                sc[b] = scale;
+                for (size_t i = 0; i < len; ++i) {
+                    const long qi = lrintf(x[base + i] / scale);
+                    int v = (int8_t)qi;                          /* the int8 cast before the clip */
+                    if (v < -4) v = -4;
+                    if (v > 3) v = 3;
+                    q[base + i] = (int8_t)v;
+                }
+            }
+            oracle_pack_rows(q, 1, head_dim, 3, codes + (r * heads + h) * pb);
+        }
+    }
+    free(q);
+}
+
+void oracle_paged_int3_attention_f64(const float* q, const uint8_t* k_codes, const uint8_t* v_codes,
+                                     const float* k_scales, const float* v_scales, const int32_t* page_table,
+                                     size_t max_pages_per_seq, const int32_t* ctx_len, size_t batch,
+                                     size_t num_q_heads, size_t num_kv_heads, size_t head_dim, size_t page_tokens,
+                                     size_t block_size, float scale, double* out) {
+    const size_t group = num_q_heads / num_kv_heads;
+    const size_t pb = oracle_row_bytes(head_dim, 3);
+    const size_t nb = (head_dim + block_size - 1) / block_size;
+    float* kd = (float*)malloc(head_dim * sizeof(float));
+    float* vd = (float*)malloc(head_dim * sizeof(float));
+    for (size_t b = 0; b < batch; ++b) {
+        const size_t ctx = (size_t)ctx_len[b];
+        const int32_t* table = page_table + b * max_pages_per_seq;
+        double* scores = (double*)malloc((ctx ? ctx : 1) * sizeof(double));
+        for (size_t h = 0; h < num_q_heads; ++h) {
+            size_t kv_h = h / (group ? group : 1);
+            if (kv_h > num_kv_heads - 1) kv_h = num_kv_heads - 1;
+            const float* qh = q + (b * num_q_heads + h) * head_dim;
+            double* oh = out + (b * num_q_heads + h) * head_dim;
+            for (size_t d = 0; d < head_dim; ++d) oh[d] = 0.0;
+            if (ctx == 0) continue;
+            double max_score = -1.0e300;
+            for (size_t t = 0; t < ctx; ++t) {
+                const size_t row = ((size_t)table[t / page_tokens] * page_tokens + t % page_tokens) * num_kv_heads + kv_h;
+                for (size_t d = 0; d < head_dim; ++d)   /* attention_fused.cu:23-45: q * s[block] */
+                    kd[d] = (float)oracle_get_code(k_codes + row * pb, d, 3) * k_scales[row * nb + d / block_size];
+                double acc = 0.0;
+                for (size_t d = 0; d < head_dim; ++d) acc += (double)qh[d] * (double)kd[d];
+                scores[t] = acc * (double)scale;
+                if (scores[t] > max_score) max_score = scores[t];
+            }
+            double sum = 0.0;
+            for (size_t t = 0; t < ctx; ++t) {
+                scores[t] = exp(scores[t] - max_score);
+                sum += scores[t];
+            }
+            for (size_t t = 0; t < ctx; ++t) {
+                const size_t row = ((size_t)table[t / page_tokens] * page_tokens + t % page_tokens) * num_kv_heads + kv_h;
+                for (size_t d = 0; d < head_dim; ++d)
+                    vd[d] = (float)oracle_get_code(v_codes + row * pb, d, 3) * v_scales[row * nb + d / block_size];
+                const double pr = scores[t] / sum;
+                for (size_t d = 0; d < head_dim; ++d) oh[d] += pr * (double)vd[d];
+            }
+        }
+        free(scores);
+    }
+    free(kd);
+    free(vd);
+}

@@ -46,6 +46,9 @@ _o = {
     "oracle_paged_gqa_attention_f64": ([c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_size_t,
                                         c_size_t, c_size_t, c_size_t, c_float, c_void_p], None),
 }
+_o["oracle_kv_int3_quantize"] = ([c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_float, c_void_p, c_void_p], None)
+_o["oracle_paged_int3_attention_f64"] = ([c_void_p] * 6 + [c_size_t, c_void_p] + [c_size_t] * 6 + [c_float, c_void_p],
+                                         None)
 for _n, (_a, _r) in _o.items():
     _f = getattr(ORACLE, _n)
     _f.argtypes = _a
@@ -237,4 +240,39 @@ def paged_attention(q, k_pages, v_pages, table, ctx_len, hq, hkv, d, pt, scale, 
     out = np.zeros((b, hq, d), dtype=np.float64 if f64 else np.float32)
     fn = ORACLE.oracle_paged_gqa_attention_f64 if f64 else ORACLE.oracle_paged_gqa_attention_f32
     fn(p(q), p(kp), p(vp), p(table), table.shape[1], p(ctx), b, hq, hkv, d, pt, scale, p(out))
+    return out
+
+
+def kv_int3_quantize(x: np.ndarray, block: int, percentile: float = 99.5, reference: bool = False):
+    """int3 KV compression of rows [rows][heads][d] (kv_cache.c:32-126): codes
+    [rows][heads][ceil(3d/8)] uint8 and scales [rows][heads][d/block] fp32.
+    reference=True runs the reference's own vspec_kv_cache_append instead
+    (percentile fixed at 99.5 there)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, heads, d = x.shape
+    codes = np.zeros((rows, heads, row_bytes(d, 3)), dtype=np.uint8)
+    scales = np.zeros((rows, heads, (d + block - 1) // block), dtype=np.float32)
+    if reference:
+        if REF is None:
+            raise RuntimeError("oracle/_ref/libvspec_ref.so not built")
+        fn = REF.ref_kv_int3_quantize
+        fn.argtypes = [c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p, c_void_p]
+        fn.restype = c_int
+        if fn(p(x), rows, heads, d, block, p(codes), p(scales)) != 0:
+            raise RuntimeError("ref_kv_int3_quantize failed")
+    else:
+        ORACLE.oracle_kv_int3_quantize(p(x), rows, heads, d, block, percentile, p(codes), p(scales))
+    return codes, scales
+
+
+def paged_int3_attention(q, k_codes, v_codes, k_scales, v_scales, table, ctx_len, hq, hkv, d, pt, block, scale):
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    table = np.ascontiguousarray(table, dtype=np.int32)
+    ctx = np.ascontiguousarray(ctx_len, dtype=np.int32)
+    b = ctx.shape[0]
+    out = np.zeros((b, hq, d), dtype=np.float64)
+    ORACLE.oracle_paged_int3_attention_f64(p(q), p(np.ascontiguousarray(k_codes)), p(np.ascontiguousarray(v_codes)),
+                                           p(np.ascontiguousarray(k_scales, dtype=np.float32)),
+                                           p(np.ascontiguousarray(v_scales, dtype=np.float32)), p(table), table.shape[1],
+                                           p(ctx), b, hq, hkv, d, pt, block, scale, p(out))
     return out

@@ -137,3 +137,27 @@ int ref_paged_gather(const VspecKVPagedCache* c, uint64_t session, float* k_out,
     }
     return 1;
 }
+
+/* ---- int3 KV compression through the reference cache (src/attention/kv_cache.c) ----
+ * Appends `rows` tokens of [heads][head_dim] fp32 to a cache with int3
+ * compression on (block 16 or 32) and copies out the key codes and scales. */
+int ref_kv_int3_quantize(const float* src, size_t rows, size_t heads, size_t head_dim, size_t block_size,
+                         uint8_t* codes_out, float* scales_out) {
+    VspecKVCache c;
+    memset(&c, 0, sizeof(c));
+    const size_t n = rows * heads * head_dim;
+    float* kb = (float*)calloc(n ? n : 1, sizeof(float));
+    float* vb = (float*)calloc(n ? n : 1, sizeof(float));
+    int ok = kb && vb && vspec_kv_cache_init(&c, kb, vb, rows, heads, head_dim) &&
+             vspec_kv_cache_enable_int3_compression(&c, block_size);
+    for (size_t r = 0; ok && r < rows; ++r)
+        ok = vspec_kv_cache_append(&c, src + r * heads * head_dim, src + r * heads * head_dim);
+    if (ok) {
+        memcpy(codes_out, c.key_int3, rows * heads * c.packed_head_bytes);
+        memcpy(scales_out, c.key_scales, rows * heads * c.blocks_per_head * sizeof(float));
+    }
+    vspec_kv_cache_disable_int3_compression(&c);
+    free(kb);
+    free(vb);
+    return ok ? 0 : 1;
+}

@@ -155,6 +155,81 @@ extern "C" int vspec_b200_paged_attention(const VspecB200PagedAttnArgs* a, void*
     return paged_attention_launch(p, a->kv_dtype == VSPEC_B200_KV_F16 ? kKvF16 : kKvF32, (cudaStream_t)stream);
 }
 
+extern "C" int vspec_b200_kv_int3_quantize(const float* d_src, const int32_t* d_slots, size_t rows, size_t num_heads,
+                                           size_t head_dim, size_t block_size, float percentile, uint8_t* d_codes,
+                                           float* d_scales, void* stream) {
+    if (!d_src || !d_codes || !d_scales) { set_error("NULL pointer argument"); return VSPEC_B200_ERR_ARG; }
+    if (rows == 0 || num_heads == 0) return VSPEC_B200_OK;
+    if (block_size != 16 && block_size != 32) { set_error("block_size must be 16 or 32"); return VSPEC_B200_ERR_ARG; }
+    if (head_dim == 0 || head_dim > 256 || head_dim % block_size != 0 || head_dim % 8 != 0) {
+        set_error("head_dim must be a multiple of block_size and of 8, at most 256"); return VSPEC_B200_ERR_ARG;
+    }
+    if (rows * num_heads > (size_t)1 << 30) { set_error("too many rows"); return VSPEC_B200_ERR_ARG; }
+    return kv_int3_quantize_launch(d_src, d_slots, (int)rows, (int)num_heads, (int)head_dim, (int)block_size, percentile,
+                                   d_codes, d_scales, (cudaStream_t)stream);
+}
+
+extern "C" int vspec_b200_paged_attention_int3(const VspecB200PagedAttnArgs* a, const float* d_k_scales,
+                                               const float* d_v_scales, size_t block_size, void* stream) {
+    if (!a) { set_error("args is NULL"); return VSPEC_B200_ERR_ARG; }
+    if (!a->d_q || !a->d_k_pages || !a->d_v_pages || !a->d_page_table || !a->d_ctx_len || !a->d_out || !d_k_scales ||
+        !d_v_scales) {
+        set_error("NULL pointer argument"); return VSPEC_B200_ERR_ARG;
+    }
+    if (a->kv_dtype != VSPEC_B200_KV_INT3) { set_error("kv_dtype must be VSPEC_B200_KV_INT3"); return VSPEC_B200_ERR_ARG; }
+    if (a->batch == 0 || a->num_q_heads == 0 || a->num_kv_heads == 0 || a->page_tokens == 0 ||
+        a->max_pages_per_seq == 0 || a->num_pages == 0) {
+        set_error("zero dimension"); return VSPEC_B200_ERR_ARG;
+    }
+    if (a->head_dim != 128) { set_error("int3 pages need head_dim 128"); return VSPEC_B200_ERR_UNSUPPORTED; }
+    if (block_size != 16 && block_size != 32) { set_error("block_size must be 16 or 32"); return VSPEC_B200_ERR_ARG; }
+    if (a->num_q_heads % a->num_kv_heads != 0 || a->num_q_heads / a->num_kv_heads > 8) {
+        set_error("num_q_heads must be a multiple of num_kv_heads, at most 8 per KV head"); return VSPEC_B200_ERR_ARG;
+    }
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a->d_k_pages) | reinterpret_cast<uintptr_t>(a->d_v_pages) |
+                         reinterpret_cast<uintptr_t>(d_k_scales) | reinterpret_cast<uintptr_t>(d_v_scales);
+    if (al % 16 != 0) { set_error("int3 page pools must be 16-byte aligned"); return VSPEC_B200_ERR_ARG; }
+    if (a->max_ctx > a->max_pages_per_seq * a->page_tokens) {
+        set_error("max_ctx %zu exceeds the page table capacity %zu", a->max_ctx, a->max_pages_per_seq * a->page_tokens);
+        return VSPEC_B200_ERR_ARG;
+    }
+    const size_t max_ctx = a->max_ctx ? a->max_ctx : a->max_pages_per_seq * a->page_tokens;
+    AttnParams p;
+    memset(&p, 0, sizeof(p));
+    p.q = a->d_q;
+    p.k_pages = a->d_k_pages;
+    p.v_pages = a->d_v_pages;
+    p.k_scales = d_k_scales;
+    p.v_scales = d_v_scales;
+    p.kv_block = (int)block_size;
+    p.page_table = a->d_page_table;
+    p.ctx_len = a->d_ctx_len;
+    p.out = a->d_out;
+    p.scale = a->scale;
+    p.batch = (int)a->batch;
+    p.hq = (int)a->num_q_heads;
+    p.hkv = (int)a->num_kv_heads;
+    p.d = (int)a->head_dim;
+    p.page_tokens = (int)a->page_tokens;
+    p.max_pages = (int)a->max_pages_per_seq;
+    p.num_pages = (int)a->num_pages;
+    // the (sequence, KV head) pairs are the CTAs' unit, as for the fp16 kernel with <= 4 heads per CTA
+    p.split_tokens = attn_choose_split(p.batch, p.hkv * 4, p.hkv, (int)max_ctx, p.page_tokens, device_sm_count());
+    p.max_splits = (int)((max_ctx + p.split_tokens - 1) / p.split_tokens);
+    if (p.max_splits < 1) p.max_splits = 1;
+    const size_t need = attn_workspace_bytes(p.batch, p.hq, p.d, p.max_splits);
+    void* ws = a->d_workspace;
+    if (ws) {
+        if (a->workspace_bytes < need) { set_error("workspace too small (%zu < %zu)", a->workspace_bytes, need); return VSPEC_B200_ERR_ARG; }
+    } else {
+        ws = attn_scratch(need);
+        if (!ws) { set_error("cannot allocate %zu bytes of attention scratch", need); return VSPEC_B200_ERR_NOMEM; }
+    }
+    p.part_o = reinterpret_cast<float*>(ws);
+    p.part_ml = p.part_o + (size_t)p.batch * p.hq * p.max_splits * p.d;
+    return paged_attention_launch(p, kKvInt3, (cudaStream_t)stream);
+}
+
 extern "C" int vspec_b200_paged_attention_page_fault(int* out_flag) {
     if (!out_flag) { set_error("NULL out_flag"); return VSPEC_B200_ERR_ARG; }
     return attn_read_and_clear_page_fault(out_flag);

@@ -450,6 +450,271 @@ __global__ void paged_attn_combine_kernel(const AttnParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// int3 KV pages: per-(token, head) codes of 3 bits packed
+// LSB-first (src/quant/pack.c:30-51) with fp32 scales per block of 16 or 32
+// dims, as vspec_kv_cache_append stores them with int3 compression on
+// (src/attention/kv_cache.c:64-126,160-226).  d = 128: 48 bytes of codes and
+// 16 or 32 bytes of scales per token and head instead of 256 bytes of fp16.
+// ---------------------------------------------------------------------------
+
+// Quantisation on append: one warp per (row, head).  Per block: the
+// percentile element of the sorted |x| by rank selection across the lanes
+// (position idx = (size_t)((n-1) * percentile/100), computed on the host in
+// double like kv_cache.c:35-58), scale = rep/4 (1 for rep 0, >= 1e-6), then
+// q = lrintf(x/scale) truncated to int8 and clipped to [-4, 3]
+// (kv_cache.c:86-101); IEEE division and round-to-nearest-even as the C code.
+constexpr int kKvQuantWarps = 4;
+
+__global__ void __launch_bounds__(kKvQuantWarps * 32)
+kv_int3_quantize_kernel(const float* __restrict__ src, const int32_t* __restrict__ slots, int rows, int heads, int d,
+                        int block, int idx, uint8_t* __restrict__ codes, float* __restrict__ scales) {
+    __shared__ uint8_t sm_codes[kKvQuantWarps][256];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long item = (long long)blockIdx.x * kKvQuantWarps + warp;
+    if (item >= (long long)rows * heads) return;
+    const int r = (int)(item / heads), h = (int)(item - (long long)r * heads);
+    const float* x = src + ((size_t)r * heads + h) * d;
+    const int pb = d * 3 / 8, nb = d / block;
+    const size_t orow = (size_t)(slots ? slots[r] : r) * heads + h;
+    uint8_t* cw = sm_codes[warp];
+    const bool in_block = lane < block;
+    for (int b = 0; b < nb; ++b) {
+        const float v = in_block ? x[b * block + lane] : 0.f;
+        const float a = fabsf(v);
+        int less = 0, le = 0;
+        for (int j = 0; j < block; ++j) {
+            const float aj = __shfl_sync(0xffffffffu, a, j);
+            less += aj < a ? 1 : 0;
+            le += aj <= a ? 1 : 0;
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, in_block && less <= idx && idx < le);
+        const float rep = __shfl_sync(0xffffffffu, a, hit ? __ffs(hit) - 1 : 0);
+        float scale = rep > 0.0f ? rep * 0.25f : 1.0f;   // rep / 4, exact
+        if (scale < 1e-6f) scale = 1e-6f;
+        if (in_block) {
+            const long long qi = __float2ll_rn(__fdiv_rn(v, scale));
+            int q = (int)(signed char)(qi & 0xFF);          // the int8 cast before the clip
+            q = q < -4 ? -4 : (q > 3 ? 3 : q);
+            cw[b * block + lane] = (uint8_t)(q & 7);
+        }
+        if (lane == 0) scales[orow * nb + b] = scale;
+    }
+    __syncwarp();
+    uint8_t* crow = codes + orow * pb;
+    for (int j = lane; j < pb; j += 32) {
+        unsigned val = 0;
+        for (int i = (8 * j) / 3; i <= (8 * j + 7) / 3 && i < d; ++i) {
+            const int sh = 3 * i - 8 * j;
+            const unsigned c = cw[i];
+            val |= sh >= 0 ? (c << sh) : (c >> -sh);
+        }
+        crow[j] = (uint8_t)(val & 0xFFu);
+    }
+}
+
+// Paged GQA decode attention over int3 pages, d = 128, up to 8 query heads
+// per KV head.  grid = (splits, Hkv, B), 4 warps; each warp takes 32-token
+// chunks of the CTA's piece.  QK: lane = token, the 128 codes of its K row
+// decoded in registers against q (shared memory broadcast), block scales
+// applied per block.  Softmax online in the exp2 domain per query head.  PV:
+// the chunk's V rows staged in shared memory, lane = 4 dims, p from shared
+// memory.  Warps merge in shared memory; splits merge in
+// paged_attn_combine_kernel.  The math is the reference's dequantise-then-
+// attend (src/kernel/cuda/attention_fused.cu:23-45,232-351).
+constexpr int kInt3MaxGroup = 8;
+
+template <int NBLK, int GM>
+__global__ void __launch_bounds__(kAttnThreads, 4)
+paged_attn_int3_kernel(const AttnParams p) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int D = 128, PB = 48;
+    constexpr int BS = D / NBLK;   // dims per scale block
+    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int G = p.hq / p.hkv;
+    const int ctx = p.ctx_len[b];
+    const int t_begin = split * p.split_tokens;
+    if (t_begin >= ctx) return;
+    const int t_end = min(ctx, t_begin + p.split_tokens);
+    const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int32_t* table = p.page_table + (size_t)b * p.max_pages;
+    const uint8_t* kc = reinterpret_cast<const uint8_t*>(p.k_pages);
+    const uint8_t* vc = reinterpret_cast<const uint8_t*>(p.v_pages);
+
+    __shared__ __align__(16) float sm_q[kInt3MaxGroup][D];
+    __shared__ __align__(16) uint32_t sm_v[kAttnWarps][32][PB / 4];
+    __shared__ __align__(16) float sm_vs[kAttnWarps][32][NBLK];
+    __shared__ float sm_p[kAttnWarps][kInt3MaxGroup][32];
+    __shared__ float sm_ml[kAttnWarps][kInt3MaxGroup][2];
+    __shared__ float sm_o[kAttnWarps][kInt3MaxGroup][D];
+
+    const float qmul = p.scale * kLog2e;
+    for (int i = tid; i < G * D; i += kAttnThreads) {
+        const int g = i / D, dd = i - g * D;
+        sm_q[g][dd] = p.q[((size_t)b * p.hq + h * G + g) * D + dd] * qmul;
+    }
+    __syncthreads();
+
+    float m_run[GM], l_run[GM], o[GM][4];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+        m_run[g] = kNegBig;
+        l_run[g] = 0.f;
+        o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+    }
+    const int nchunks = (t_end - t_begin + 31) / 32;
+    for (int ch = warp; ch < nchunks; ch += kAttnWarps) {
+        const int t = t_begin + ch * 32 + lane;
+        const bool valid = t < t_end;
+        size_t row = 0;
+        if (valid) {
+            int page = __ldg(table + t / p.page_tokens);
+            if (page < 0 || page >= p.num_pages) {
+                atomicOr(&g_attn_page_fault, 1);
+                page = 0;
+            }
+            row = ((size_t)page * p.page_tokens + (size_t)(t % p.page_tokens)) * p.hkv + h;
+        }
+        // ---- QK: this lane's token ----
+        uint32_t w[12];
+        float ks[NBLK];
+        if (valid) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kc + row * PB);
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                const uint4 v4 = __ldg(kr + i);
+                w[4 * i] = v4.x; w[4 * i + 1] = v4.y; w[4 * i + 2] = v4.z; w[4 * i + 3] = v4.w;
+            }
+            const float4* sr = reinterpret_cast<const float4*>(p.k_scales + row * NBLK);
+#pragma unroll
+            for (int i = 0; i < NBLK / 4; ++i) {
+                const float4 f = __ldg(sr + i);
+                ks[4 * i] = f.x; ks[4 * i + 1] = f.y; ks[4 * i + 2] = f.z; ks[4 * i + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 12; ++i) w[i] = 0u;
+#pragma unroll
+            for (int i = 0; i < NBLK; ++i) ks[i] = 0.f;
+        }
+        float sc[GM];
+#pragma unroll
+        for (int g = 0; g < GM; ++g) sc[g] = 0.f;
+#pragma unroll
+        for (int blk = 0; blk < NBLK; ++blk) {
+            float part[GM];
+#pragma unroll
+            for (int g = 0; g < GM; ++g) part[g] = 0.f;
+#pragma unroll
+            for (int i4 = 0; i4 < BS / 4; ++i4) {
+                float kv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i = blk * BS + 4 * i4 + e;   // dim, compile-time
+                    const int bit = 3 * i, wi = bit >> 5, off = bit & 31;
+                    uint32_t c = w[wi] >> off;
+                    if (off > 29) c |= w[wi + 1] << (32 - off);
+                    // 2^23 + (code + 4) from the bits, minus 2^23 + 4: exact, no int-to-float conversion
+                    kv[e] = __int_as_float(0x4B000000 | (int)((c & 7u) ^ 4u)) - 8388612.0f;
+                }
+#pragma unroll
+                for (int g = 0; g < GM; ++g) {
+                    if (GM == 8 ? g < G : true) {
+                        const float4 qv = *reinterpret_cast<const float4*>(&sm_q[g][blk * BS + 4 * i4]);
+                        part[g] = fmaf(qv.x, kv[0], fmaf(qv.y, kv[1], fmaf(qv.z, kv[2], fmaf(qv.w, kv[3], part[g]))));
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < GM; ++g) sc[g] = fmaf(part[g], ks[blk], sc[g]);
+        }
+        // ---- V rows of the chunk into shared memory ----
+        if (valid) {
+            const uint4* vr = reinterpret_cast<const uint4*>(vc + row * PB);
+            uint4* dst = reinterpret_cast<uint4*>(&sm_v[warp][lane][0]);
+#pragma unroll
+            for (int i = 0; i < 3; ++i) dst[i] = __ldg(vr + i);
+            const float4* sr = reinterpret_cast<const float4*>(p.v_scales + row * NBLK);
+            float4* sd = reinterpret_cast<float4*>(&sm_vs[warp][lane][0]);
+#pragma unroll
+            for (int i = 0; i < NBLK / 4; ++i) sd[i] = __ldg(sr + i);
+        }
+        // ---- online softmax per query head ----
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            if (GM == 8 ? g < G : true) {
+                const float s = valid ? sc[g] : kNegBig;
+                const float cmax = warp_max(s);
+                const float m_new = fmaxf(m_run[g], cmax);
+                const float alpha = exp2f(m_run[g] - m_new);
+                const float pw = valid ? exp2f(s - m_new) : 0.f;
+                l_run[g] = l_run[g] * alpha + warp_sum(pw);
+                m_run[g] = m_new;
+                o[g][0] *= alpha; o[g][1] *= alpha; o[g][2] *= alpha; o[g][3] *= alpha;
+                sm_p[warp][g][lane] = pw;
+            }
+        }
+        __syncwarp();
+        // ---- PV: lane owns dims 4*lane .. 4*lane+3 (bits 12*lane .. +11) ----
+        const int nvalid = min(32, t_end - (t_begin + ch * 32));
+        const int bit0 = 12 * lane, w0 = bit0 >> 5, off0 = bit0 & 31;
+        const int vblk = (4 * lane) / BS;
+        for (int j = 0; j < nvalid; ++j) {
+            uint32_t c = sm_v[warp][j][w0] >> off0;
+            if (off0 > 20) c |= sm_v[warp][j][w0 + 1] << (32 - off0);
+            const float vs = sm_vs[warp][j][vblk];
+            float vv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                vv[e] = (__int_as_float(0x4B000000 | (int)(((c >> (3 * e)) & 7u) ^ 4u)) - 8388612.0f) * vs;
+#pragma unroll
+            for (int g = 0; g < GM; ++g) {
+                if (GM == 8 ? g < G : true) {
+                    const float pj = sm_p[warp][g][j];
+                    o[g][0] = fmaf(pj, vv[0], o[g][0]);
+                    o[g][1] = fmaf(pj, vv[1], o[g][1]);
+                    o[g][2] = fmaf(pj, vv[2], o[g][2]);
+                    o[g][3] = fmaf(pj, vv[3], o[g][3]);
+                }
+            }
+        }
+        __syncwarp();
+    }
+    // ---- merge the warps ----
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+        if (GM == 8 ? g < G : true) {
+            if (lane == 0) { sm_ml[warp][g][0] = m_run[g]; sm_ml[warp][g][1] = l_run[g]; }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sm_o[warp][g][4 * lane + e] = o[g][e];
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += kAttnThreads) {
+        const int g = i / D, dd = i - g * D;
+        float M = kNegBig;
+        for (int wv = 0; wv < kAttnWarps; ++wv) M = fmaxf(M, sm_ml[wv][g][0]);
+        float L = 0.f, O = 0.f;
+        for (int wv = 0; wv < kAttnWarps; ++wv) {
+            const float f = exp2f(sm_ml[wv][g][0] - M);
+            L += sm_ml[wv][g][1] * f;
+            O += sm_o[wv][g][dd] * f;
+        }
+        const size_t bh = (size_t)b * p.hq + h * G + g;
+        if (nsplit == 1) {
+            p.out[bh * D + dd] = O / fmaxf(L, 1e-12f);
+        } else {
+            p.part_o[(bh * p.max_splits + split) * D + dd] = O;
+            if (dd == 0) {
+                p.part_ml[(bh * p.max_splits + split) * 2 + 0] = M;   // exp2 domain already
+                p.part_ml[(bh * p.max_splits + split) * 2 + 1] = L;
+            }
+        }
+    }
+}
+
 // Bit-exact gather of one sequence's K/V rows (parity hook for
 // vspec_kv_paged_get_token_ptr, src/attention/kv_paged_cache.c:312-356).
 template <typename T>
@@ -510,8 +775,44 @@ size_t attn_workspace_bytes(int batch, int hq, int d, int max_splits) {
     return rows * d * sizeof(float) + rows * 2 * sizeof(float);
 }
 
+int kv_int3_quantize_launch(const float* src, const int32_t* slots, int rows, int heads, int d, int block,
+                            float percentile, uint8_t* codes, float* scales, cudaStream_t st) {
+    if (percentile < 50.0f) percentile = 50.0f;   // kv_cache.c:38-43
+    if (percentile > 100.0f) percentile = 100.0f;
+    size_t idx = (size_t)((double)(block - 1) * ((double)percentile / 100.0));
+    if (idx >= (size_t)block) idx = (size_t)block - 1;
+    const long long items = (long long)rows * heads;
+    const unsigned grid = (unsigned)((items + kKvQuantWarps - 1) / kKvQuantWarps);
+    kv_int3_quantize_kernel<<<grid, kKvQuantWarps * 32, 0, st>>>(src, slots, rows, heads, d, block, (int)idx, codes,
+                                                                 scales);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "kv_int3_quantize_kernel launch");
+    return VSPEC_B200_OK;
+}
+
 int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st) {
     const int group = p.hq / p.hkv;
+    if (kv_dtype == kKvInt3) {
+        p.head_groups = 1;
+        const dim3 grid(p.max_splits, p.hkv, p.batch);
+        // query heads per KV head: exact kernels for 1, 2 and 4, predicated up to 8 otherwise
+        const int gm = group == 1 ? 1 : (group == 2 ? 2 : (group == 4 ? 4 : 8));
+        auto pick = [&](auto k1, auto k2, auto k4, auto k8) {
+            return gm == 1 ? launch_pdl(k1, grid, dim3(kAttnThreads), 0, st, p)
+                 : gm == 2 ? launch_pdl(k2, grid, dim3(kAttnThreads), 0, st, p)
+                 : gm == 4 ? launch_pdl(k4, grid, dim3(kAttnThreads), 0, st, p)
+                           : launch_pdl(k8, grid, dim3(kAttnThreads), 0, st, p);
+        };
+        cudaError_t e = p.kv_block == 16
+            ? pick(paged_attn_int3_kernel<8, 1>, paged_attn_int3_kernel<8, 2>, paged_attn_int3_kernel<8, 4>,
+                   paged_attn_int3_kernel<8, 8>)
+            : pick(paged_attn_int3_kernel<4, 1>, paged_attn_int3_kernel<4, 2>, paged_attn_int3_kernel<4, 4>,
+                   paged_attn_int3_kernel<4, 8>);
+        if (e != cudaSuccess) return cuda_status(e, "paged int3 attention launch");
+        e = launch_pdl(paged_attn_combine_kernel, dim3(p.hq, p.batch), dim3(128), 0, st, p);
+        if (e != cudaSuccess) return cuda_status(e, "paged attention combine launch");
+        return VSPEC_B200_OK;
+    }
     const bool mma = kv_dtype == kKvF16 && p.d == 128 && p.page_tokens > 0;
     const dim3 block(kAttnThreads);
     // 4 query heads per CTA for groups up to 4, else 8 (two column tiles)

@@ -9,6 +9,7 @@ namespace vb200 {
 
 constexpr int kKvF32 = 0;
 constexpr int kKvF16 = 1;
+constexpr int kKvInt3 = 2;
 
 struct AttnParams {
     const float* q;             // [batch][hq][d]
@@ -23,6 +24,12 @@ struct AttnParams {
     int batch, hq, hkv, d, page_tokens, max_pages;
     int split_tokens, max_splits, head_groups;
     int num_pages;              // valid page ids are [0, num_pages)
+    // int3 pages (kv_dtype kKvInt3): k_pages / v_pages hold the codes
+    // [pages][page_tokens][hkv][3*d/8], these the per-block fp32 scales
+    // [pages][page_tokens][hkv][d/kv_block]
+    const float* k_scales;
+    const float* v_scales;
+    int kv_block;
 };
 
 int attn_read_and_clear_page_fault(int* out);
@@ -30,6 +37,10 @@ int attn_read_and_clear_page_fault(int* out);
 int attn_choose_split(int batch, int hq, int hkv, int max_ctx, int page_tokens, int sms);
 size_t attn_workspace_bytes(int batch, int hq, int d, int max_splits);
 int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st);
+// int3 KV compression of rows [rows][heads][d] fp32 into pool rows slots[r]
+// (rows r when slots is NULL): codes [.][heads][3*d/8], scales [.][heads][d/block].
+int kv_int3_quantize_launch(const float* src, const int32_t* slots, int rows, int heads, int d, int block,
+                            float percentile, uint8_t* codes, float* scales, cudaStream_t st);
 int paged_gather_launch(const void* kp, const void* vp, const int32_t* table, int ctx, int pt, int hkv, int d,
                         int kv_dtype, void* kout, void* vout, cudaStream_t st);
 

@@ -26,6 +26,7 @@ F_RMSNORM = 0x8
 F_SWIGLU = 0x10
 KV_F32 = 0
 KV_F16 = 1
+KV_INT3 = 2
 PATH_AUTO, PATH_GENERIC, PATH_WARPMMA, PATH_TCGEN05, PATH_RING, PATH_ROWS = 0, 1, 2, 3, 4, 5
 
 
@@ -129,6 +130,9 @@ _sigs = {
     "vspec_b200_paged_attention_workspace_bytes": ([c_size_t] * 5, c_size_t),
     "vspec_b200_paged_attention": ([POINTER(PagedAttnArgs), c_void_p], c_int),
     "vspec_b200_paged_attention_page_fault": ([POINTER(c_int)], c_int),
+    "vspec_b200_kv_int3_quantize": ([c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_float, c_void_p,
+                                     c_void_p, c_void_p], c_int),
+    "vspec_b200_paged_attention_int3": ([POINTER(PagedAttnArgs), c_void_p, c_void_p, c_size_t, c_void_p], c_int),
     "vspec_b200_paged_gather": ([c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_int, c_void_p,
                                  c_void_p, c_void_p], c_int),
     "vspec_b200_rmsnorm_f32": ([c_void_p, c_void_p, c_float, c_size_t, c_size_t, c_void_p, c_void_p], c_int),
@@ -250,6 +254,22 @@ def paged_attention(q: int, k_pages: int, v_pages: int, page_table: int, ctx_len
     a = PagedAttnArgs(q, k_pages, v_pages, page_table, ctx_len, out, batch, hq, hkv, d, page_tokens, max_pages,
                       num_pages, max_ctx, scale, kv_dtype, workspace, workspace_bytes)
     check(lib.vspec_b200_paged_attention(ctypes.byref(a), stream), "vspec_b200_paged_attention")
+
+
+def kv_int3_quantize(src: int, slots: int | None, rows: int, heads: int, head_dim: int, block: int, codes: int,
+                     scales: int, percentile: float = 99.5, stream: int = 0) -> None:
+    check(lib.vspec_b200_kv_int3_quantize(src, slots, rows, heads, head_dim, block, percentile, codes, scales, stream),
+          "vspec_b200_kv_int3_quantize")
+
+
+def paged_attention_int3(q: int, k_codes: int, v_codes: int, k_scales: int, v_scales: int, block: int,
+                         page_table: int, ctx_len: int, out: int, batch: int, hq: int, hkv: int, d: int,
+                         page_tokens: int, max_pages: int, num_pages: int, max_ctx: int, scale: float,
+                         workspace: int | None = None, workspace_bytes: int = 0, stream: int = 0) -> None:
+    a = PagedAttnArgs(q, k_codes, v_codes, page_table, ctx_len, out, batch, hq, hkv, d, page_tokens, max_pages,
+                      num_pages, max_ctx, scale, KV_INT3, workspace, workspace_bytes)
+    check(lib.vspec_b200_paged_attention_int3(ctypes.byref(a), k_scales, v_scales, block, stream),
+          "vspec_b200_paged_attention_int3")
 
 
 def page_fault_flag() -> int:
