@@ -120,7 +120,7 @@ int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* args, void* stre
  *                           across CTAs (m <= 8)
  *   VSPEC_B200_PATH_ROWS    TMA ring + warp-MMA decode, each CTA a contiguous
  *                           row range over all of k, no workspace (m <= 8,
- *                           k % 1024 == 0)
+ *                           k % 1024 == 0, int4 k % 2048 == 0)
  * A fast path that does not support the shape returns VSPEC_B200_ERR_UNSUPPORTED. */
 #define VSPEC_B200_PATH_AUTO 0
 #define VSPEC_B200_PATH_GENERIC 1

@@ -294,8 +294,8 @@ def test_ring_path_smoke():
 def test_fast_paths_match_oracle(path, bits, m, n, k, g):
     if path == V.PATH_TCGEN05 and m > 4:
         pytest.skip("the tcgen05 GEMV takes m <= 4")
-    if path == V.PATH_ROWS and k % 1024 != 0:
-        pytest.skip("the row-sliced GEMV takes k % 1024 == 0")
+    if path == V.PATH_ROWS and k % (2048 if bits == 4 else 1024) != 0:
+        pytest.skip("the row-sliced GEMV takes k % 1024 == 0 (int4: k % 2048 == 0)")
     rng = np.random.default_rng(path * 100 + bits * 10 + m + n + k)
     w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=(n % 2 == 0))
     x = rng.standard_normal((m, k)).astype(np.float32)
@@ -309,7 +309,7 @@ def test_fast_paths_match_oracle(path, bits, m, n, k, g):
 @pytest.mark.parametrize("path", FAST_PATHS)
 def test_fast_paths_fused_epilogues(path):
     rng = np.random.default_rng(70 + path)
-    m, k, g = 3, 1024, 8
+    m, k, g = (3, 2048, 16) if path == V.PATH_ROWS else (3, 1024, 8)   # row-sliced int4: k % 2048
     n = 512   # SwiGLU halves of 256 rows fill one tile of every fast path
     w, s, zp = make_lowbit(rng, n, k, 4, g)
     x = rng.standard_normal((m, k)).astype(np.float32)
@@ -329,7 +329,7 @@ def test_fast_paths_fused_epilogues(path):
 def test_rows_path_smoke():
     """One small launch of the row-sliced kernel on its own."""
     rng = np.random.default_rng(3)
-    m, n, k, g = 1, 256, 1024, 8
+    m, n, k, g = 1, 256, 2048, 16
     w, s, zp = make_lowbit(rng, n, k, 4, g)
     x = rng.standard_normal((m, k)).astype(np.float32)
     y = run_linear(x, w, s, zp, n, k, 4, g, path=V.PATH_ROWS)
@@ -341,14 +341,14 @@ def test_rows_path_smoke():
 
 @pytest.mark.parametrize("bits", [2, 3, 4])
 @pytest.mark.parametrize("m,n,k,g,flags", [
-    (1, 24, 1024, 8, 0),                   # three CTAs of eight rows, one box each
-    (1, 80000, 1024, 8, 0),                # more than 256 rows per CTA: two row groups
-    (6, 40000, 1024, 4, 0),                # m > 4 (two activation tiles): groups of <= 128 rows
+    (1, 24, 2048, 16, 0),                  # three CTAs of eight rows, one box each
+    (1, 18000, 2048, 16, 0),               # 60-61 rows per CTA: one 64-row group
+    (6, 9000, 2048, 8, 0),                 # m > 4 (two activation tiles), groups of 256 codes
     (2, 4104, 2048, 16, 0),                # rows per CTA not a multiple of 16
-    (5, 80000, 1024, 8, 0x10),             # SwiGLU, several gate/up group pairs per CTA
-    (3, 10000, 3072, 24, 0x4),             # residual
+    (2, 36000, 2048, 16, 0x10),            # SwiGLU: a gate group and its up group per CTA
+    (3, 10000, 4096, 32, 0x4),             # residual
     (1, 5000, 4096, 16, 0x8),              # RMSNorm input, groups of 256 codes
-    (8, 12288, 4096, 32, 0),               # m = 8: large activation fragments, a shallow ring
+    (8, 4096, 4096, 32, 0),                # m = 8: large activation fragments in shared memory
 ])
 def test_rows_path_shapes(bits, m, n, k, g, flags):
     """Row-sliced kernel at shapes that exercise its geometry: tiny CTAs, row
@@ -401,6 +401,13 @@ def test_rows_path_deterministic_and_unsupported_shapes():
     x5 = rng.standard_normal((1, 640)).astype(np.float32)
     with pytest.raises(V.VspecB200Error, match="not supported"):
         run_linear(x5, w5, s5, zp5, 64, 640, 4, 5, path=V.PATH_ROWS)
+    # more rows per CTA than one 64-row group: refused explicitly, the ring kernel in auto dispatch
+    wl, sl, zl = make_lowbit(rng, 40000, 2048, 4, 16)
+    xl = rng.standard_normal((1, 2048)).astype(np.float32)
+    with pytest.raises(V.VspecB200Error, match="not supported"):
+        run_linear(xl, wl, sl, zl, 40000, 2048, 4, 16, path=V.PATH_ROWS)
+    assert rel_err(run_linear(xl, wl, sl, zl, 40000, 2048, 4, 16), O.lowbit_matmul(xl, wl, 40000, 2048, 4, sl, zl, 16)) \
+        <= RTOL_F32
 
 
 @pytest.mark.parametrize("m,n", [(1, 12288), (4, 9984), (7, 12288)])

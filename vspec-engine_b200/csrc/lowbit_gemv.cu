@@ -741,8 +741,8 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
             return gemv_rows_launch(p, bits, unsigned_codes, st, pdl_enabled());
         }
         if (path == kPathRows) {
-            set_error("shape not supported by the row-sliced GEMV (m <= 8, k %% 1024 == 0, groups of 128*i, "
-                      "16-byte aligned rows / scale rows, smem)");
+            set_error("shape not supported by the row-sliced GEMV (m <= 8, k %% 1024 == 0 (int4: k %% 2048 == 0), "
+                      "groups of 128*i, 16-byte aligned rows / scale rows, smem)");
             return VSPEC_B200_ERR_UNSUPPORTED;
         }
     }

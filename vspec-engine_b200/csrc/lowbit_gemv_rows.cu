@@ -29,9 +29,9 @@ static int make_scale_map(CUtensorMap* map, const void* base, int rows, int n_gr
 }
 
 // Row-group size, ring depth and CTA count.  Two CTAs per SM when their
-// shared memory fits in half an SM, else one.  Row groups (at most 64 rows)
-// are the largest that leave a ring of at least eight units and 24 KB in
-// flight, and split a CTA's rows evenly.
+// shared memory fits in half an SM, else one.  The row group (at most 64
+// rows) holds all of a CTA's rows and leaves a ring of at least eight units
+// and 24 KB in flight.
 static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo, size_t* smem) {
     const int m = p.m, kbt = p.k / 128;
     const int n_out = swiglu ? p.n / 2 : p.n;
@@ -40,7 +40,8 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
     const int szb = (p.flags & VSPEC_B200_F_SZ_F16) ? 2 : 4;
     const int srow = p.n_groups * szb;
     const bool has_s = p.s != nullptr, has_zp = p.zp != nullptr;
-    const uint32_t rb = (uint32_t)rows_row_bytes(bits);
+    const uint32_t rb = (uint32_t)rows_unit_bytes(bits);
+    const int kut = kbt / rows_kpu(bits);
     for (int per_sm = 2; per_sm >= 1; --per_sm) {
         const uint32_t budget = per_sm == 2 ? kRowsSmemShared : kRowsSmemMax;
         const int slots = device_sm_count() * per_sm;
@@ -59,8 +60,12 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
                 if (br == 16) break;
                 continue;
             }
+            // one row group per CTA (a CTA's rows fit one box): the only geometry
+            // run back to back on B200 without a fault; shapes that would need
+            // several groups per CTA take the split-K ring kernel
+            if (rmax > br) break;
             int ns = (int)((budget - fixed) / (stage + 16u));
-            const int most = ((rmax + br - 1) / br) * S * kbt;   // the busiest CTA's units
+            const int most = ((rmax + br - 1) / br) * S * kut;   // the busiest CTA's units
             if (ns > most) ns = most;
             if (ns > kRowsMaxStages) ns = kRowsMaxStages;
             // enough in flight: a unit per consumer warp and >= 24 KB per CTA
@@ -86,7 +91,7 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
 
 bool gemv_rows_supported(const GemvParams& p, int bits) {
     if (p.m < 1 || p.m > kGemvMaxM) return false;
-    if (p.k % 1024 != 0 || p.n_groups < 1 || p.k % p.n_groups != 0 || (p.k / p.n_groups) % 128 != 0) return false;
+    if (p.k % (1024 * rows_kpu(bits)) != 0 || p.n_groups < 1 || p.k % p.n_groups != 0 || (p.k / p.n_groups) % 128 != 0) return false;
     if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || reinterpret_cast<uintptr_t>(p.x) % 16 != 0) return false;
     if ((size_t)p.row_bytes != row_bytes_for((size_t)p.k, bits)) return false;
     if ((size_t)p.row_bytes % 16 != 0) return false;   // TMA global stride
@@ -104,19 +109,16 @@ bool gemv_rows_supported(const GemvParams& p, int bits) {
 }
 
 // Where the row-sliced kernel beats the split-K ring kernel (measured on B200,
-// back-to-back launches over weights larger than L2): one activation row, no
-// SwiGLU pairing, int4 or int3, k <= 4096 and one row group of >= 48 rows per
-// CTA (boxes of >= 2.25 KB), e.g. n = 12288, k = 4096: 9.5 against 10.6 us
-// for int4, 10.7 against 12.2 us for int3.  Narrower or deeper shapes issue
-// more, smaller boxes per CTA and stay on the ring kernel.
+// back-to-back launches over weights larger than L2, us per launch, ring ->
+// rows): one activation row, int4 or int3, k <= 4096, e.g. int4 k = 4096 with
+// n = 4096: 7.11 -> 5.69, n = 6144: 7.66 -> 7.01, n = 12288: 10.63 -> 9.51,
+// SwiGLU n = 24576: 15.92 -> 13.66; int3 n = 12288: 12.18 -> 10.95.  Deeper
+// rows (k = 12288: 11.9 -> 14.1) and several activation rows (m = 4: 11.5 ->
+// 14.8) stay on the ring kernel, as do shapes with more than one row group per
+// CTA (refused by the planner).
 bool gemv_rows_preferred(const GemvParams& p, int bits) {
-    if (p.m != 1 || bits < 3 || (p.flags & VSPEC_B200_F_SWIGLU) || p.k > 4096) return false;
-    if (!gemv_rows_supported(p, bits)) return false;
-    RowsGeom geo;
-    size_t smem = 0;
-    if (!rows_plan(p, bits, false, &geo, &smem)) return false;
-    const int rmax = (geo.n_out + geo.ctas - 1) / geo.ctas;
-    return geo.br >= 48 && rmax <= geo.br;
+    if (p.m != 1 || bits < 3 || p.k > 4096) return false;
+    return gemv_rows_supported(p, bits);
 }
 
 int gemv_rows_read_and_clear_timeout(int* out) {
@@ -143,9 +145,9 @@ int gemv_rows_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st
     CUtensorMap wmap, smap, zmap;
     memset(&smap, 0, sizeof(smap));
     memset(&zmap, 0, sizeof(zmap));
-    const CUtensorMapSwizzle swz = bits == 4 ? CU_TENSOR_MAP_SWIZZLE_64B
+    const CUtensorMapSwizzle swz = bits == 4 ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : (bits == 2 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE);
-    int rc = make_row_tile_map(&wmap, p.w, p.n, p.row_bytes, rows_row_bytes(bits), geo.br, swz);
+    int rc = make_row_tile_map(&wmap, p.w, p.n, p.row_bytes, rows_unit_bytes(bits), geo.br, swz);
     if (rc != VSPEC_B200_OK) return rc;
     const int szb = (p.flags & VSPEC_B200_F_SZ_F16) ? 2 : 4;
     if (p.s) {

@@ -65,6 +65,10 @@ constexpr int kRowsMaxStages = 512;
 static __device__ int g_rows_timeout = 0;
 
 __host__ __device__ constexpr int rows_row_bytes(int bits) { return bits == 4 ? 64 : (bits == 3 ? 48 : 32); }
+// k-blocks per unit (TMA box): int4 boxes carry two 128-code k-blocks per row
+// (128 B, 128-byte swizzle), halving the boxes a CTA issues.
+__host__ __device__ constexpr int rows_kpu(int bits) { return bits == 4 ? 2 : 1; }
+__host__ __device__ constexpr int rows_unit_bytes(int bits) { return rows_row_bytes(bits) * rows_kpu(bits); }
 __host__ __device__ inline int rows_nt(int m) { return (2 * m + 7) / 8; }
 __host__ __device__ inline int rows_lanes(int m) { return 4 * (2 * m < 8 ? 2 * m : 8); }
 __host__ __device__ inline uint32_t rows_align(uint32_t v, uint32_t a) { return (v + a - 1u) & ~(a - 1u); }
@@ -86,7 +90,7 @@ struct RowsSmem {
 __host__ __device__ inline RowsSmem rows_smem_plan(int bits, int m, int kbt, int br, int ns, int srow_bytes,
                                                    bool has_s, bool has_zp, bool swiglu) {
     RowsSmem s;
-    uint32_t o = (uint32_t)ns * (uint32_t)br * (uint32_t)rows_row_bytes(bits);
+    uint32_t o = (uint32_t)ns * (uint32_t)br * (uint32_t)rows_unit_bytes(bits);
     o = rows_align(o, 128u);
     s.sbuf = o;
     if (has_s) o += 2u * (uint32_t)br * (uint32_t)srow_bytes;
@@ -146,12 +150,14 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                         const __grid_constant__ CUtensorMap zmap, const __grid_constant__ GemvParams p,
                         const RowsGeom geo) {
     constexpr int RB = rows_row_bytes(BITS);
+    constexpr int KPU = rows_kpu(BITS);
+    constexpr int UB = rows_unit_bytes(BITS);
     constexpr bool SWIGLU = EPI == kEpiSwiGLU;
     constexpr int S = SWIGLU ? 2 : 1;   // physical groups per row group (gate, up)
     constexpr int SZB = SZ16 ? 2 : 4;
     const int NS = geo.stages;
     constexpr int BR = 16 * NB;
-    const uint32_t STAGE_BYTES = (uint32_t)BR * RB;
+    const uint32_t STAGE_BYTES = (uint32_t)BR * UB;
 
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -185,8 +191,9 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
     const int r1 = (int)(((long long)(blockIdx.x + 1) * geo.n_out) / geo.ctas);
     const int n_grp = (r1 - r0 + BR - 1) / BR;
     const int n_phys = n_grp * S;
-    const int total_units = n_phys * kbt;
-    const int q_per_warp = kbt / kRowsWarps;   // kbt % 8 == 0 (host check)
+    const int kut = kbt / KPU;                   // units per physical group
+    const int total_units = n_phys * kut;
+    const int q_per_warp = kut / kRowsWarps;     // kut % 8 == 0 (host check)
     const int half_n = p.n >> 1;
     const uint32_t sbytes = (uint32_t)BR * (uint32_t)geo.srow_bytes;
     const uint32_t sz_tx = (has_s ? sbytes : 0u) + (has_zp ? sbytes : 0u);
@@ -240,9 +247,9 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                     break;
                 }
                 mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                tma_load_2d(wring + (size_t)stage * STAGE_BYTES, &wmap, kb * RB, row, &full[stage]);
+                tma_load_2d(wring + (size_t)stage * STAGE_BYTES, &wmap, kb * UB, row, &full[stage]);
                 if (++stage == NS) { stage = 0; ++use; }
-                if (++kb == kbt) {
+                if (++kb == kut) {
                     kb = 0;
                     ++pg;
                     row = r0 + (pg / S) * BR + ((SWIGLU && (pg & 1)) ? half_n : 0);
@@ -254,7 +261,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             }
             // every issued copy lands before the CTA's shared memory goes away
             // (bounded, and not cut short by the abort flag)
-            const int issued = pg * kbt + kb;
+            const int issued = pg * kut + kb;
             int i = issued > NS ? issued - NS : 0;
             int ds = i % NS;
             uint32_t dph = (uint32_t)((i / NS) & 1);
@@ -401,88 +408,118 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             const unsigned char* zg = zbuf + (size_t)par * sbytes;
             // One unit's contribution to a set of accumulators: every 16-row
             // block of the unit's stage against the k-block's activation parts.
-            auto unit_math = [&](const unsigned char* stg, int kb, float (&ac)[NB][NT][2]) {
-                const uint4* fb = frag + (size_t)kb * NT * lanes * 2;
-                uint4 bb[NT][2];
+            // One unit's contribution to a set of accumulators: every 16-row
+            // block of the unit's stage against its k-blocks' activation parts.
+            auto unit_math = [&](const unsigned char* stg, int ku, float (&ac)[NB][NT][2]) {
+                uint4 bb[KPU][NT][2];
+                float xsum[KPU][NT], coff[KPU][NT], inv[KPU][NT];
+                const unsigned char* sgc[KPU];
+                const unsigned char* zgc[KPU];
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    bb[nt][0] = bb[nt][1] = make_uint4(0u, 0u, 0u, 0u);
-                    if (lane_has_b) {
-                        bb[nt][0] = fb[(nt * lanes + lane) * 2];
-                        bb[nt][1] = fb[(nt * lanes + lane) * 2 + 1];
+                for (int h = 0; h < KPU; ++h) {
+                    const int kb = ku * KPU + h;
+                    const uint4* fb = frag + (size_t)kb * NT * lanes * 2;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        bb[h][nt][0] = bb[h][nt][1] = make_uint4(0u, 0u, 0u, 0u);
+                        if (lane_has_b) {
+                            bb[h][nt][0] = fb[(nt * lanes + lane) * 2];
+                            bb[h][nt][1] = fb[(nt * lanes + lane) * 2 + 1];
+                        }
+                        const int r = 4 * nt + c;
+                        const int ri = r < m ? r : 0;
+                        xsum[h][nt] = xs[kb * m + ri];
+                        coff[h][nt] = cs[kb * m + ri];
+                        inv[h][nt] = isc[kb * m + ri];
                     }
+                    const int col = p.kb_per_group_shift >= 0 ? (kb >> p.kb_per_group_shift) : kb / p.kb_per_group;
+                    sgc[h] = sg + (uint32_t)col * SZB;
+                    zgc[h] = zg + (uint32_t)col * SZB;
                 }
-                float xsum[NT], coff[NT], inv[NT];
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    const int r = 4 * nt + c;
-                    const int ri = r < m ? r : 0;
-                    xsum[nt] = xs[kb * m + ri];
-                    coff[nt] = cs[kb * m + ri];
-                    inv[nt] = isc[kb * m + ri];
-                }
-                const int col = p.kb_per_group_shift >= 0 ? (kb >> p.kb_per_group_shift) : kb / p.kb_per_group;
-                const unsigned char* sgc = sg + (uint32_t)col * SZB;
-                const unsigned char* zgc = zg + (uint32_t)col * SZB;
 #pragma unroll
                 for (int j = 0; j < NB; ++j) {
                     if (j < nblk) {
                         const int ra = 16 * j + g, rb2 = ra + 8;
-                        Chunk<BITS> ch0, ch1;
-                        rows_lds_chunk<BITS>(ch0, stg + rows_chunk_offset<BITS>(ra, c));
-                        rows_lds_chunk<BITS>(ch1, stg + rows_chunk_offset<BITS>(rb2, c));
-                        float sv0 = 1.0f, sv1 = 1.0f, zv0 = p.zp_const, zv1 = p.zp_const;
-                        if (has_s) {
-                            if constexpr (SZ16) {
-                                sv0 = __half2float(*reinterpret_cast<const __half*>(sgc + ra * geo.srow_bytes));
-                                sv1 = __half2float(*reinterpret_cast<const __half*>(sgc + rb2 * geo.srow_bytes));
-                            } else {
-                                sv0 = *reinterpret_cast<const float*>(sgc + ra * geo.srow_bytes);
-                                sv1 = *reinterpret_cast<const float*>(sgc + rb2 * geo.srow_bytes);
+                        Chunk<BITS> ch0[KPU], ch1[KPU];   // rows g and g+8, per k-block of the unit
+                        if constexpr (KPU == 2) {
+                            // 128-byte swizzle: chunk q of row r at (q ^ (r & 7)) * 16.  Odd rows read
+                            // the second k-block first, so each quarter-warp's two rows fall in
+                            // opposite bank halves (conflict-free).
+                            const int par = g & 1;
+                            const int qa = 4 * par + c, qb = 4 * (1 - par) + c;
+                            Chunk<BITS> a0, b0, a1, b1;
+                            rows_lds_chunk<BITS>(a0, stg + ra * UB + ((qa ^ (ra & 7)) << 4));
+                            rows_lds_chunk<BITS>(b0, stg + ra * UB + ((qb ^ (ra & 7)) << 4));
+                            rows_lds_chunk<BITS>(a1, stg + rb2 * UB + ((qa ^ (rb2 & 7)) << 4));
+                            rows_lds_chunk<BITS>(b1, stg + rb2 * UB + ((qb ^ (rb2 & 7)) << 4));
+#pragma unroll
+                            for (int wd = 0; wd < BITS; ++wd) {
+                                ch0[0].w[wd] = par ? b0.w[wd] : a0.w[wd];
+                                ch0[1].w[wd] = par ? a0.w[wd] : b0.w[wd];
+                                ch1[0].w[wd] = par ? b1.w[wd] : a1.w[wd];
+                                ch1[1].w[wd] = par ? a1.w[wd] : b1.w[wd];
                             }
+                        } else {
+                            rows_lds_chunk<BITS>(ch0[0], stg + rows_chunk_offset<BITS>(ra, c));
+                            rows_lds_chunk<BITS>(ch1[0], stg + rows_chunk_offset<BITS>(rb2, c));
                         }
-                        if (has_zp) {
-                            if constexpr (SZ16) {
-                                zv0 = __half2float(*reinterpret_cast<const __half*>(zgc + ra * geo.srow_bytes));
-                                zv1 = __half2float(*reinterpret_cast<const __half*>(zgc + rb2 * geo.srow_bytes));
-                            } else {
-                                zv0 = *reinterpret_cast<const float*>(zgc + ra * geo.srow_bytes);
-                                zv1 = *reinterpret_cast<const float*>(zgc + rb2 * geo.srow_bytes);
+#pragma unroll
+                        for (int h = 0; h < KPU; ++h) {
+                            float sv0 = 1.0f, sv1 = 1.0f, zv0 = p.zp_const, zv1 = p.zp_const;
+                            if (has_s) {
+                                if constexpr (SZ16) {
+                                    sv0 = __half2float(*reinterpret_cast<const __half*>(sgc[h] + ra * geo.srow_bytes));
+                                    sv1 = __half2float(*reinterpret_cast<const __half*>(sgc[h] + rb2 * geo.srow_bytes));
+                                } else {
+                                    sv0 = *reinterpret_cast<const float*>(sgc[h] + ra * geo.srow_bytes);
+                                    sv1 = *reinterpret_cast<const float*>(sgc[h] + rb2 * geo.srow_bytes);
+                                }
                             }
-                        }
-                        I8Words<BITS> w0, w1;
-                        i8_prepare<BITS, UNSIGNED>(ch0, w0);
-                        i8_prepare<BITS, UNSIGNED>(ch1, w1);
-                        int D[NC][NT][4];
+                            if (has_zp) {
+                                if constexpr (SZ16) {
+                                    zv0 = __half2float(*reinterpret_cast<const __half*>(zgc[h] + ra * geo.srow_bytes));
+                                    zv1 = __half2float(*reinterpret_cast<const __half*>(zgc[h] + rb2 * geo.srow_bytes));
+                                } else {
+                                    zv0 = *reinterpret_cast<const float*>(zgc[h] + ra * geo.srow_bytes);
+                                    zv1 = *reinterpret_cast<const float*>(zgc[h] + rb2 * geo.srow_bytes);
+                                }
+                            }
+                            I8Words<BITS> w0, w1;
+                            i8_prepare<BITS, UNSIGNED>(ch0[h], w0);
+                            i8_prepare<BITS, UNSIGNED>(ch1[h], w1);
+                            int D[NC][NT][4];
 #pragma unroll
-                        for (int cl = 0; cl < NC; ++cl)
+                            for (int cl = 0; cl < NC; ++cl)
 #pragma unroll
-                            for (int nt = 0; nt < NT; ++nt) D[cl][nt][0] = D[cl][nt][1] = D[cl][nt][2] = D[cl][nt][3] = 0;
+                                for (int nt = 0; nt < NT; ++nt) D[cl][nt][0] = D[cl][nt][1] = D[cl][nt][2] = D[cl][nt][3] = 0;
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const uint32_t a[4] = {i8_reg<BITS>(w0, q, 0), i8_reg<BITS>(w1, q, 0),
-                                                   i8_reg<BITS>(w0, q, 1), i8_reg<BITS>(w1, q, 1)};
+                            for (int q = 0; q < 4; ++q) {
+                                const uint32_t a[4] = {i8_reg<BITS>(w0, q, 0), i8_reg<BITS>(w1, q, 0),
+                                                       i8_reg<BITS>(w0, q, 1), i8_reg<BITS>(w1, q, 1)};
+#pragma unroll
+                                for (int nt = 0; nt < NT; ++nt) {
+                                    const uint4& b = bb[h][nt][q >> 1];
+                                    imma_16832_u8s8(D[i8_class<BITS>(q)][nt], a, (q & 1) ? b.z : b.x,
+                                                    (q & 1) ? b.w : b.y);
+                                }
+                            }
 #pragma unroll
                             for (int nt = 0; nt < NT; ++nt) {
-                                const uint4& b = bb[nt][q >> 1];
-                                imma_16832_u8s8(D[i8_class<BITS>(q)][nt], a, (q & 1) ? b.z : b.x,
-                                                (q & 1) ? b.w : b.y);
+                                int cmb[4];
+#pragma unroll
+                                for (int k4 = 0; k4 < 4; ++k4) {
+                                    int v = D[0][nt][k4];
+#pragma unroll
+                                    for (int cl = 1; cl < NC; ++cl) v += D[cl][nt][k4] >> i8_class_shift<BITS>(cl);
+                                    cmb[k4] = v;
+                                }
+                                const float e0 = (float)(cmb[0] * 256 + cmb[1]);   // xh * 256 + xl parts
+                                const float e1 = (float)(cmb[2] * 256 + cmb[3]);
+                                ac[j][nt][0] = fmaf(sv0 * inv[h][nt], e0 - fmaf(zv0, xsum[h][nt], coff[h][nt]),
+                                                    ac[j][nt][0]);
+                                ac[j][nt][1] = fmaf(sv1 * inv[h][nt], e1 - fmaf(zv1, xsum[h][nt], coff[h][nt]),
+                                                    ac[j][nt][1]);
                             }
-                        }
-#pragma unroll
-                        for (int nt = 0; nt < NT; ++nt) {
-                            int cmb[4];
-#pragma unroll
-                            for (int k4 = 0; k4 < 4; ++k4) {
-                                int v = D[0][nt][k4];
-#pragma unroll
-                                for (int cl = 1; cl < NC; ++cl) v += D[cl][nt][k4] >> i8_class_shift<BITS>(cl);
-                                cmb[k4] = v;
-                            }
-                            const float e0 = (float)(cmb[0] * 256 + cmb[1]);   // xh * 256 + xl parts
-                            const float e1 = (float)(cmb[2] * 256 + cmb[3]);
-                            ac[j][nt][0] = fmaf(sv0 * inv[nt], e0 - fmaf(zv0, xsum[nt], coff[nt]), ac[j][nt][0]);
-                            ac[j][nt][1] = fmaf(sv1 * inv[nt], e1 - fmaf(zv1, xsum[nt], coff[nt]), ac[j][nt][1]);
                         }
                     }
                 }
@@ -491,14 +528,14 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             // warp consumes its own in order, so the oldest unconsumed unit is
             // always issued and the ring cannot stall.
             for (int t = 0; t < q_per_warp; ++t) {
-                const int kb = kRowsWarps * t + warp;
+                const int ku = kRowsWarps * t + warp;   // unit (k-blocks ku*KPU ...)
                 const int cur = stage;
                 const uint32_t cur_ph = (uint32_t)(use & 1);
                 stage += kRowsWarps;
                 while (stage >= NS) { stage -= NS; ++use; }
                 if (ok && !mbar_wait_sleep(&full[cur], cur_ph, abort_flag, kRowsWaitLimit, kRowsSleepNs)) ok = false;
                 if (!ok) continue;
-                unit_math(wring + (size_t)cur * STAGE_BYTES, kb, acc);
+                unit_math(wring + (size_t)cur * STAGE_BYTES, ku, acc);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[cur]);
             }
