@@ -213,8 +213,7 @@ extern "C" int vspec_b200_paged_attention_int3(const VspecB200PagedAttnArgs* a, 
     p.page_tokens = (int)a->page_tokens;
     p.max_pages = (int)a->max_pages_per_seq;
     p.num_pages = (int)a->num_pages;
-    // the (sequence, KV head) pairs are the CTAs' unit, as for the fp16 kernel with <= 4 heads per CTA
-    p.split_tokens = attn_choose_split(p.batch, p.hkv * 4, p.hkv, (int)max_ctx, p.page_tokens, device_sm_count());
+    p.split_tokens = attn_choose_split(p.batch, p.hq, p.hkv, (int)max_ctx, p.page_tokens, device_sm_count());
     p.max_splits = (int)((max_ctx + p.split_tokens - 1) / p.split_tokens);
     if (p.max_splits < 1) p.max_splits = 1;
     const size_t need = attn_workspace_bytes(p.batch, p.hq, p.d, p.max_splits);

@@ -24,6 +24,7 @@
 #include "tc_primitives.cuh"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 namespace vb200 {
@@ -715,6 +716,338 @@ paged_attn_int3_kernel(const AttnParams p) {
     }
 }
 
+// Tensor-core kernel over int3 pages (d = 128): the fp16 kernel's pipeline
+// with a decode step.  Per warp and 16-token tile, cp.async stages the K and V
+// code rows (48 B per token) and their block scales; after they land the warp
+// turns the codes into fp16 small integers (exact) in the fp16 kernel's
+// swizzled tile layout, so QK^T and PV run as in paged_attn_f16_mma_kernel.
+// The scales stay out of the fp16 operands: QK^T accumulates per scale block
+// and multiplies each token's block partial by its K scale in fp32, and PV
+// folds each token's V scale into p (split into fp16 hi + lo parts) per block
+// of dims.  Math as the reference's dequantise-then-attend
+// (src/kernel/cuda/attention_fused.cu:23-45,232-351).
+constexpr uint32_t kI3Codes = 16u * 48u;   // 16 token rows of one head's K (or V) codes
+template <int NBLK>
+struct I3Smem {
+    static constexpr uint32_t kScales = 16u * NBLK * 4u;                   // 16 rows of fp32 block scales
+    static constexpr uint32_t kStage = 2u * kI3Codes + 2u * kScales;      // K codes, V codes, K scales, V scales
+    static constexpr uint32_t kWarp = 2u * kAttnTileBytes + kAttnStages * kStage;
+    static constexpr uint32_t kTotal = kAttnWarps * kWarp;
+};
+
+// 64 codes (bits [0, 192) of w) -> 8 chunks of 8 fp16 values (code as a small integer).
+__device__ __forceinline__ void i3_decode64(const uint32_t (&w)[6], uint4 (&out)[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint32_t h2[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t u[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int ii = 8 * k + 2 * q + e, bit = 3 * ii, wi = bit >> 5, off = bit & 31;
+                uint32_t cc = w[wi] >> off;
+                if (off > 29) cc |= w[wi + 1] << (32 - off);
+                u[e] = (cc & 7u) ^ 4u;   // code + 4
+            }
+            // fp16 1024 + (code + 4) in both halves, minus 1028: the code, exactly
+            h2[q] = hsub2_bits(0x64006400u | u[0] | (u[1] << 16), 0x64046404u);
+        }
+        out[k] = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+    }
+}
+
+template <int NT, int NBLK>
+__global__ void __launch_bounds__(kAttnThreads, 2)
+paged_attn_int3_mma_kernel(const AttnParams p) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int D = 128;
+    constexpr int HPC = 4 * NT;
+    constexpr int S = kAttnStages;
+    constexpr int KS = 8 / NBLK;                 // 16-dim k-steps per scale block
+    using SM = I3Smem<NBLK>;
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / p.head_groups;
+    const int hg = blockIdx.y % p.head_groups;
+    const int b = blockIdx.z;
+    const int group = p.hq / p.hkv;
+    const int ctx = p.ctx_len[b];
+    const int t_begin = split * p.split_tokens;
+    if (t_begin >= ctx) return;
+    const int t_end = min(ctx, t_begin + p.split_tokens);
+    const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int32_t* table = p.page_table + (size_t)b * p.max_pages;
+    const uint8_t* kc = reinterpret_cast<const uint8_t*>(p.k_pages);
+    const uint8_t* vc = reinterpret_cast<const uint8_t*>(p.v_pages);
+
+    extern __shared__ __align__(128) unsigned char attn_smem[];
+    __shared__ float sm_q[HPC][D];
+    __shared__ float sm_qmax[HPC];
+    __shared__ float sm_p[kAttnWarps][16][HPC];
+    __shared__ float sm_ml[kAttnWarps][HPC][2];
+    __shared__ int sm_pages[kAttnMaxStagedPages];
+
+    const int first_page = t_begin / p.page_tokens;
+    const int n_pages = (t_end - 1) / p.page_tokens - first_page + 1;
+    for (int i = tid; i < n_pages; i += kAttnThreads) {
+        int page = __ldg(table + first_page + i);
+        if (page < 0 || page >= p.num_pages) {
+            atomicOr(&g_attn_page_fault, 1);
+            page = 0;
+        }
+        sm_pages[i] = page;
+    }
+    for (int i = tid; i < HPC * D; i += kAttnThreads) {
+        const int hl = i / D, dd = i % D;
+        const int h = hg * HPC + hl;
+        sm_q[hl][dd] = h < group ? p.q[((size_t)b * p.hq + (size_t)kvh * group + h) * D + dd] : 0.f;
+    }
+    __syncthreads();
+
+    const int ntiles = (t_end - t_begin + 15) / 16;
+    const int my_tiles = ntiles > warp ? (ntiles - warp + kAttnWarps - 1) / kAttnWarps : 0;
+    unsigned char* wptr = attn_smem + (size_t)warp * SM::kWarp;
+    const uint32_t wbase = smem_u32(wptr);
+    const uint32_t tile_k = wbase, tile_v = wbase + kAttnTileBytes;
+    const uint32_t stage0 = wbase + 2u * kAttnTileBytes;
+    auto issue = [&](int it) {   // codes and scales of this warp's it-th tile -> stage it % S
+        const int t0 = t_begin + (warp + it * kAttnWarps) * 16;
+        const uint32_t st = stage0 + (uint32_t)(it % S) * SM::kStage;
+        for (int idx = lane; idx < 48; idx += 32) {   // 16 rows x 3 chunks of 16 B
+            const int row = idx / 3, k = idx - 3 * (idx / 3);
+            const int t = t0 + row;
+            const bool valid = t < t_end;
+            const size_t ri = staged_row(sm_pages, valid ? t : t_end - 1, first_page, p.page_tokens, p.hkv, 1, kvh);
+            cp_async16(st + (uint32_t)(row * 48 + k * 16), kc + ri * 48 + k * 16, valid ? 16u : 0u);
+            cp_async16(st + kI3Codes + (uint32_t)(row * 48 + k * 16), vc + ri * 48 + k * 16, valid ? 16u : 0u);
+        }
+        constexpr int SCH = NBLK / 4;                 // 16-byte chunks of one row's scales
+        for (int idx = lane; idx < 16 * SCH; idx += 32) {
+            const int row = idx / SCH, k = idx - SCH * (idx / SCH);
+            const int t = t0 + row;
+            const bool valid = t < t_end;
+            const size_t ri = staged_row(sm_pages, valid ? t : t_end - 1, first_page, p.page_tokens, p.hkv, 1, kvh);
+            const uint32_t so = (uint32_t)(row * NBLK * 4 + k * 16);
+            cp_async16(st + 2u * kI3Codes + so, p.k_scales + ri * NBLK + k * 4, valid ? 16u : 0u);
+            cp_async16(st + 2u * kI3Codes + SM::kScales + so, p.v_scales + ri * NBLK + k * 4, valid ? 16u : 0u);
+        }
+    };
+#pragma unroll
+    for (int it = 0; it < S - 1; ++it) {
+        if (it < my_tiles) issue(it);
+        cp_async_commit();
+    }
+
+    if (warp == 0) {
+        for (int hl = 0; hl < HPC; ++hl) {
+            float mx = 0.f;
+            for (int dd = lane; dd < D; dd += 32) mx = fmaxf(mx, fabsf(sm_q[hl][dd]));
+            mx = warp_max(mx);
+            if (lane == 0) {
+                int ex = 0;
+                if (mx > 0.f && isfinite(mx)) { (void)frexpf(mx, &ex); ex -= 14; }
+                sm_qmax[hl] = (float)ex;
+            }
+        }
+    }
+    __syncthreads();
+    uint32_t qf[NT][8][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int hl = 4 * nt + (g >> 1);
+        const bool lo = (g & 1) != 0;
+        const float sc = ldexpf(1.0f, -(int)sm_qmax[hl]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int dims[4] = {16 * j + 2 * c, 16 * j + 2 * c + 1, 16 * j + 2 * c + 8, 16 * j + 2 * c + 9};
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float x = sm_q[hl][dims[u]] * sc;
+                if (lo) x = x - __half2float(__float2half_rn(x));
+                v[u] = x;
+            }
+            qf[nt][j][0] = pack_half2(v[0], v[1]);
+            qf[nt][j][1] = pack_half2(v[2], v[3]);
+        }
+    }
+    float score_mul[NT], m_run[NT], l_run[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        score_mul[nt] = ldexpf(p.scale * kLog2e, (int)sm_qmax[4 * nt + c]);
+        m_run[nt] = kNegBig;
+        l_run[nt] = 0.f;
+    }
+    float oacc[NT][8][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) oacc[nt][i][0] = oacc[nt][i][1] = oacc[nt][i][2] = oacc[nt][i][3] = 0.f;
+
+    const int k_row = (lane & 7) + 8 * ((lane >> 3) & 1), k_chi = lane >> 4;
+    const int v_row = (lane & 7) + 8 * (lane >> 4), v_chi = (lane >> 3) & 1;
+    const int dr = lane >> 1, dh = lane & 1;      // decode: token row and half of the dims
+    for (int it = 0; it < my_tiles; ++it) {
+        cp_async_wait<S - 2>();
+        __syncwarp();   // tile it has landed; every lane is done with tile it-1 (decoded tiles, sm_p)
+        const int t0 = t_begin + (warp + it * kAttnWarps) * 16;
+        const uint32_t st = stage0 + (uint32_t)(it % S) * SM::kStage;
+        const unsigned char* stp = wptr + 2u * kAttnTileBytes + (size_t)(it % S) * SM::kStage;
+        // ---- decode the tile's K and V codes into fp16 tiles (row dr, dims 64*dh ..) ----
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv) {
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(stp + kv * kI3Codes + dr * 48 + dh * 24);
+            uint32_t w[6];
+#pragma unroll
+            for (int i = 0; i < 6; ++i) w[i] = src[i];
+            uint4 outc[8];
+            i3_decode64(w, outc);
+            unsigned char* tile = wptr + kv * kAttnTileBytes;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int ch = 8 * dh + k;
+                *reinterpret_cast<uint4*>(tile + dr * 256 + ((ch ^ (dr & 7)) << 4)) = outc[k];
+            }
+        }
+        __syncwarp();
+        // refill the stage of tile it-1 (its codes were decoded in the previous step)
+        if (it + S - 1 < my_tiles) issue(it + S - 1);
+        cp_async_commit();
+        const float* ks = reinterpret_cast<const float*>(stp + 2u * kI3Codes);
+        const float* vs = reinterpret_cast<const float*>(stp + 2u * kI3Codes + SM::kScales);
+        // ---- S = K Q^T per scale block, scaled per token in fp32 ----
+        float s[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+        const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int bl = 0; bl < NBLK; ++bl) {
+            float sb[NT][4];
+#pragma unroll
+            for (int jj = 0; jj < KS; ++jj) {
+                const int j = bl * KS + jj;
+                uint32_t a[4];
+                const int ch = 2 * j + k_chi;
+                ldsm_x4(tile_k + (uint32_t)k_row * 256u + ((uint32_t)(ch ^ (k_row & 7)) << 4), a);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    mma_16816_f16(sb[nt], a, qf[nt][j][0], qf[nt][j][1], jj == 0 ? zero4 : sb[nt]);
+            }
+            const float k0 = ks[g * NBLK + bl], k1 = ks[(g + 8) * NBLK + bl];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                s[nt][0] = fmaf(sb[nt][0], k0, s[nt][0]);
+                s[nt][1] = fmaf(sb[nt][1], k0, s[nt][1]);
+                s[nt][2] = fmaf(sb[nt][2], k1, s[nt][2]);
+                s[nt][3] = fmaf(sb[nt][3], k1, s[nt][3]);
+            }
+        }
+        const bool v0 = (t0 + g) < t_end, v1 = (t0 + g + 8) < t_end;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const float sc0 = v0 ? (s[nt][0] + s[nt][1]) * score_mul[nt] : kNegBig;
+            const float sc1 = v1 ? (s[nt][2] + s[nt][3]) * score_mul[nt] : kNegBig;
+            float tmax = fmaxf(sc0, sc1);
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            const float m_new = fmaxf(m_run[nt], tmax);
+            const float alpha = exp2f(m_run[nt] - m_new);
+            const float p0 = v0 ? exp2f(sc0 - m_new) : 0.f;
+            const float p1 = v1 ? exp2f(sc1 - m_new) : 0.f;
+            l_run[nt] = l_run[nt] * alpha + (p0 + p1);
+            m_run[nt] = m_new;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                oacc[nt][i][0] *= alpha; oacc[nt][i][1] *= alpha; oacc[nt][i][2] *= alpha; oacc[nt][i][3] *= alpha;
+            }
+            sm_p[warp][g][4 * nt + c] = p0 * kPScale;
+            sm_p[warp][g + 8][4 * nt + c] = p1 * kPScale;
+        }
+        __syncwarp();
+        // ---- O^T += V^T (P s_v)^T, per scale block of dims ----
+        const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+#pragma unroll
+        for (int bl = 0; bl < NBLK; ++bl) {
+            uint32_t pb[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int hl = 4 * nt + (g >> 1);
+                const bool lo = (g & 1) != 0;
+                float pv[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    float x = sm_p[warp][toks[r]][hl] * vs[toks[r] * NBLK + bl];
+                    if (lo) x = x - __half2float(__float2half_rn(x));
+                    pv[r] = x;
+                }
+                pb[nt][0] = pack_half2(pv[0], pv[1]);
+                pb[nt][1] = pack_half2(pv[2], pv[3]);
+            }
+#pragma unroll
+            for (int ii = 0; ii < KS; ++ii) {
+                const int i = bl * KS + ii;
+                uint32_t a[4];
+                const int ch = 2 * i + v_chi;
+                ldsm_x4_t(tile_v + (uint32_t)v_row * 256u + ((uint32_t)(ch ^ (v_row & 7)) << 4), a);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma_16816_f16(oacc[nt][i], a, pb[nt][0], pb[nt][1], oacc[nt][i]);
+            }
+        }
+    }
+    cp_async_wait<0>();
+
+    // ---- merge the warps (O partials reuse the staging area) ----
+    __syncthreads();
+    float* sm_o = reinterpret_cast<float*>(attn_smem);   // [kAttnWarps][HPC][D]
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        float l_tot = l_run[nt];
+        l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 4);
+        l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 8);
+        l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
+        if (g == 0) {
+            sm_ml[warp][4 * nt + c][0] = m_run[nt];
+            sm_ml[warp][4 * nt + c][1] = l_tot;
+        }
+        float* o = sm_o + ((size_t)warp * HPC + 4 * nt + c) * D;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            o[16 * i + g] = (oacc[nt][i][0] + oacc[nt][i][1]) * (1.0f / kPScale);
+            o[16 * i + g + 8] = (oacc[nt][i][2] + oacc[nt][i][3]) * (1.0f / kPScale);
+        }
+    }
+    __syncthreads();
+    for (int z = tid; z < HPC * D; z += kAttnThreads) {
+        const int hl = z / D, dd = z % D;
+        const int h_in_group = hg * HPC + hl;
+        if (h_in_group >= group) continue;
+        float M = kNegBig;
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_ml[w][hl][0]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = exp2f(sm_ml[w][hl][0] - M);
+            L += sm_ml[w][hl][1] * f;
+            O += sm_o[((size_t)w * HPC + hl) * D + dd] * f;
+        }
+        const int h = kvh * group + h_in_group;
+        const size_t bh = (size_t)b * p.hq + h;
+        if (nsplit == 1) {
+            p.out[bh * D + dd] = O / fmaxf(L, 1e-12f);
+        } else {
+            p.part_o[(bh * p.max_splits + split) * D + dd] = O;
+            if (dd == 0) {
+                p.part_ml[(bh * p.max_splits + split) * 2 + 0] = M;
+                p.part_ml[(bh * p.max_splits + split) * 2 + 1] = L;
+            }
+        }
+    }
+}
+
 // Bit-exact gather of one sequence's K/V rows (parity hook for
 // vspec_kv_paged_get_token_ptr, src/attention/kv_paged_cache.c:312-356).
 template <typename T>
@@ -790,8 +1123,53 @@ int kv_int3_quantize_launch(const float* src, const int32_t* slots, int rows, in
     return VSPEC_B200_OK;
 }
 
+// VSPEC_B200_INT3_ATTN_SIMT=1 runs int3 pages through the SIMT kernel (A/B timing).
+static bool int3_mma_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_INT3_ATTN_SIMT");
+        v = (e && e[0] == '1') ? 0 : 1;
+    }
+    return v == 1;
+}
+
 int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st) {
     const int group = p.hq / p.hkv;
+    if (kv_dtype == kKvInt3 && int3_mma_enabled()) {
+        const int hpc = group <= 4 ? 4 : 8;
+        p.head_groups = (group + hpc - 1) / hpc;
+        const dim3 grid(p.max_splits, p.hkv * p.head_groups, p.batch);
+        static int configured[64] = {0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaError_t e = cudaSuccess;
+        if (dev >= 0 && dev < 64 && !configured[dev]) {
+            e = cudaFuncSetAttribute(paged_attn_int3_mma_kernel<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)I3Smem<4>::kTotal);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(paged_attn_int3_mma_kernel<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)I3Smem<4>::kTotal);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(paged_attn_int3_mma_kernel<1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)I3Smem<8>::kTotal);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(paged_attn_int3_mma_kernel<2, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)I3Smem<8>::kTotal);
+            if (e != cudaSuccess) return cuda_status(e, "paged int3 attention smem attribute");
+            configured[dev] = 1;
+        }
+        const dim3 blk(kAttnThreads);
+        if (p.kv_block == 16)
+            e = hpc == 4 ? launch_pdl(paged_attn_int3_mma_kernel<1, 8>, grid, blk, I3Smem<8>::kTotal, st, p)
+                         : launch_pdl(paged_attn_int3_mma_kernel<2, 8>, grid, blk, I3Smem<8>::kTotal, st, p);
+        else
+            e = hpc == 4 ? launch_pdl(paged_attn_int3_mma_kernel<1, 4>, grid, blk, I3Smem<4>::kTotal, st, p)
+                         : launch_pdl(paged_attn_int3_mma_kernel<2, 4>, grid, blk, I3Smem<4>::kTotal, st, p);
+        if (e != cudaSuccess) return cuda_status(e, "paged int3 attention launch");
+        e = launch_pdl(paged_attn_combine_kernel, dim3(p.hq, p.batch), dim3(128), 0, st, p);
+        if (e != cudaSuccess) return cuda_status(e, "paged attention combine launch");
+        return VSPEC_B200_OK;
+    }
     if (kv_dtype == kKvInt3) {
         p.head_groups = 1;
         const dim3 grid(p.max_splits, p.hkv, p.batch);
