@@ -736,22 +736,23 @@ struct I3Smem {
 };
 
 // 64 codes (bits [0, 192) of w) -> 8 chunks of 8 fp16 values (code as a small integer).
+// Each chunk is one 24-bit group of 8 codes: one XOR turns every code into
+// its offset u = code + 4 (flip bit 2 of each field), then a pair of codes
+// becomes two fp16 1024 + u with one shift-select and one mask-or, and one
+// half2 subtraction of 1028 leaves the codes, exactly.
 __device__ __forceinline__ void i3_decode64(const uint32_t (&w)[6], uint4 (&out)[8]) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
+        const int bit = 24 * k, wi = bit >> 5, off = bit & 31;
+        uint32_t grp = w[wi] >> off;
+        if (off > 8) grp |= w[wi + 1] << (32 - off);
+        grp ^= 0x00924924u;   // bit 2 of each of the 8 three-bit fields
         uint32_t h2[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            uint32_t u[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int ii = 8 * k + 2 * q + e, bit = 3 * ii, wi = bit >> 5, off = bit & 31;
-                uint32_t cc = w[wi] >> off;
-                if (off > 29) cc |= w[wi + 1] << (32 - off);
-                u[e] = (cc & 7u) ^ 4u;   // code + 4
-            }
-            // fp16 1024 + (code + 4) in both halves, minus 1028: the code, exactly
-            h2[q] = hsub2_bits(0x64006400u | u[0] | (u[1] << 16), 0x64046404u);
+            const uint32_t lo = grp >> (6 * q);          // codes 2q (bits 0-2) and 2q+1 (bits 3-5)
+            const uint32_t t = (lo & 0xFFFFu) | ((lo << 13) & 0xFFFF0000u);   // code 2q+1 to bits 16-18
+            h2[q] = hsub2_bits((t & 0x00070007u) | 0x64006400u, 0x64046404u);
         }
         out[k] = make_uint4(h2[0], h2[1], h2[2], h2[3]);
     }
