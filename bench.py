@@ -220,6 +220,49 @@ def time_gemv_graph(torch, V, bits: int, copies: int, steps: int, warmup: int, w
     return ms, clocks
 
 
+def time_q4k(torch, V, copies: int, steps: int, warmup: int, world: int):
+    """Q4_K (GGUF-style 256-element super-blocks, q4_k.c) GEMV at the bench shape
+    K=4096 N=12288 M=1: 144 bytes per 256 weights, rotating copies > L2."""
+    nb = K_DIM // 256
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4242)
+    ws = [torch.randint(0, 256, (N_DIM, nb, 144), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+    for w in ws:   # finite fp16 d / dmin
+        w[:, :, 1] = 0x20
+        w[:, :, 3] = 0x20
+    x = torch.randn((1, K_DIM), device="cuda", dtype=torch.float32)
+    ys = [torch.empty((1, N_DIM), device="cuda", dtype=torch.float32) for _ in range(copies)]
+    stream = torch.cuda.Stream()
+
+    def step(st):
+        for w, y in zip(ws, ys):
+            V.q4k_linear(x.data_ptr(), w.data_ptr(), y.data_ptr(), 1, N_DIM, K_DIM, stream=st)
+
+    with torch.cuda.stream(stream):
+        step(stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(stream.cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    del graph
+    bytes_per_call = N_DIM * nb * 144 + K_DIM * 4 + N_DIM * 4
+    return ms, bytes_per_call
+
+
 def time_e2e_bridge(torch, V, copies: int, steps: int, warmup: int, world: int):
     """Reference host-pointer ABI: registered int4 weights (fp32 s + zp, the
     bridge's formats), host x -> host y on every call."""
@@ -721,6 +764,8 @@ def main() -> None:
     attn_ms, attn_kv, attn_other = time_attention(torch, V, attn_steps, args.warmup, world)
     a3_ms, a3_kv, a3_other = time_attention_int3(torch, V, attn_steps, args.warmup, world)
     gemm = time_gemm(torch, V, world, max(3, args.steps // 5), load_peak_table())
+    q4k_steps = max(3, args.steps // 5)
+    q4k_ms, q4k_bytes = time_q4k(torch, V, args.copies, q4k_steps, args.warmup, world)
     quant = time_quantize(torch, V, world, rank == 0 and not args.no_cpu)
     decode = None if args.no_decode else time_decode(torch, V, world, rank, peak)
     tp = None
@@ -785,6 +830,12 @@ def main() -> None:
             "speedup_vs_fp16_pages": round(attn_ms / a3_ms, 3),
             "config": "config 3 with int3 K/V pages: the fp16 pools quantised on the GPU as vspec_kv_cache_append's "
                       "int3 compression does (block 32, percentile 99.5), 3-bit codes + fp32 block scales"},
+        "q4k": {"value": round(world * q4k_steps * args.copies * q4k_bytes / (q4k_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "us_per_linear": round(q4k_ms * 1e3 / (q4k_steps * args.copies), 3),
+                "frac": round(q4k_bytes / (q4k_ms * 1e-3 / (q4k_steps * args.copies)) / 1e9 / peak, 4),
+                "bytes_per_launch": q4k_bytes,
+                "config": "Q4_K GEMV (q4_k.c 256-element super-blocks, 144 B each), K=4096 N=12288 M=1, "
+                          f"{args.copies} rotating weight copies in one CUDA graph"},
         "gemm": gemm,
         "quantize": quant,
         "decode": decode,

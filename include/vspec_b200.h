@@ -106,6 +106,15 @@ int vspec_b200_gemv_timeout_flag(int* out_flag);
  * streams, threads, concurrent graph replays) race; order them on one stream. */
 int vspec_b200_lowbit_linear_static(const VspecB200LinearArgs* args, void* stream);
 
+/* Q4_K dequant-matmul (src/quant/formats/q4_k.c:41-134,
+ * include/vspec/quant/formats/q4_k.h:7-16; the device counterpart of
+ * vspec_q4k_matmul_ref_f32): y[m][n] = x[m][k] W^T for W stored as n rows of
+ * k/256 VspecQ4KBlock (144 bytes: fp16 d, fp16 dmin, 12 bytes of sixteen 6-bit
+ * sub-scales / sub-mins, 128 bytes of 4-bit codes), element =
+ * d*(sc/63)*q - dmin*(mn/63).  k % 256 == 0; x and the blocks 16-byte aligned. */
+int vspec_b200_q4k_linear(const float* d_x, const void* d_blocks, float* d_y, size_t m, size_t n, size_t k,
+                          void* stream);
+
 /* Same contraction through the any-shape path only (testing / odd shapes). */
 int vspec_b200_lowbit_linear_generic(const VspecB200LinearArgs* args, void* stream);
 

@@ -696,3 +696,47 @@ void oracle_paged_int3_attention_f64(const float* q, const uint8_t* k_codes, con
     free(kd);
     free(vd);
 }
+
+/* ---- Q4_K (src/quant/formats/q4_k.c:41-134) ---- */
+static float q4k_half(uint16_t h) {   /* fp16 -> fp32 by the IEEE definition */
+    const int e = (h >> 10) & 0x1F, f = h & 0x3FF;
+    float v;
+    if (e == 0) v = ldexpf((float)f, -24);
+    else if (e == 31) v = f ? NAN : INFINITY;
+    else v = ldexpf((float)(f | 0x400), e - 25);
+    return (h & 0x8000) ? -v : v;
+}
+
+void oracle_q4k_matmul_f32(const float* a, size_t m, size_t k, const uint8_t* blocks, size_t n, float* c) {
+    const size_t nb = k / 256;
+    float* row = (float*)malloc(k * sizeof(float));
+    for (size_t j = 0; j < n; ++j) {
+        for (size_t b = 0; b < nb; ++b) {
+            const uint8_t* blk = blocks + (j * nb + b) * 144;
+            const float d = q4k_half((uint16_t)(blk[0] | (blk[1] << 8)));
+            const float dmin = q4k_half((uint16_t)(blk[2] | (blk[3] << 8)));
+            uint8_t sm[16];
+            for (int i = 0; i < 16; ++i) {   /* 6-bit fields, LSB first */
+                const int bit = 6 * i;
+                const unsigned v = (unsigned)blk[4 + bit / 8] | ((bit / 8 + 1 < 12) ? (unsigned)blk[4 + bit / 8 + 1] << 8 : 0u);
+                sm[i] = (uint8_t)((v >> (bit % 8)) & 0x3F);
+            }
+            for (int sb = 0; sb < 8; ++sb) {
+                const float sub_scale = d * ((float)sm[sb] / 63.0f);
+                const float sub_min = dmin * ((float)sm[8 + sb] / 63.0f);
+                for (int t = 0; t < 32; ++t) {
+                    const int local = sb * 32 + t;
+                    const uint8_t byte = blk[16 + local / 2];
+                    const float q = (float)((local & 1) ? (byte >> 4) : (byte & 0x0F));
+                    row[b * 256 + local] = (sub_scale * q) - sub_min;
+                }
+            }
+        }
+        for (size_t i = 0; i < m; ++i) {
+            float acc = 0.0f;
+            for (size_t t = 0; t < k; ++t) acc += a[i * k + t] * row[t];
+            c[i * n + j] = acc;
+        }
+    }
+    free(row);
+}

@@ -49,6 +49,7 @@ _o = {
 _o["oracle_kv_int3_quantize"] = ([c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_float, c_void_p, c_void_p], None)
 _o["oracle_paged_int3_attention_f64"] = ([c_void_p] * 6 + [c_size_t, c_void_p] + [c_size_t] * 6 + [c_float, c_void_p],
                                          None)
+_o["oracle_q4k_matmul_f32"] = ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p], None)
 for _n, (_a, _r) in _o.items():
     _f = getattr(ORACLE, _n)
     _f.argtypes = _a
@@ -276,3 +277,34 @@ def paged_int3_attention(q, k_codes, v_codes, k_scales, v_scales, table, ctx_len
                                            p(np.ascontiguousarray(v_scales, dtype=np.float32)), p(table), table.shape[1],
                                            p(ctx), b, hq, hkv, d, pt, block, scale, p(out))
     return out
+
+
+def q4k_matmul(a: np.ndarray, blocks: np.ndarray, n: int, k: int, reference: bool = False) -> np.ndarray:
+    """Q4_K dequant-matmul C = A W^T over [n][k/256] 144-byte blocks
+    (q4_k.c:41-134); reference=True runs vspec_q4k_matmul_ref_f32 itself."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    m = a.shape[0]
+    out = np.zeros((m, n), dtype=np.float32)
+    if reference:
+        if REF is None:
+            raise RuntimeError("oracle/_ref/libvspec_ref.so not built")
+        fn = REF.vspec_q4k_matmul_ref_f32
+        fn.argtypes = [c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p]
+        fn.restype = None
+        fn(p(a), m, k, p(blocks), n, p(out))
+    else:
+        ORACLE.oracle_q4k_matmul_f32(p(a), m, k, p(blocks), n, p(out))
+    return out
+
+
+def random_q4k_blocks(rng, n: int, k: int) -> np.ndarray:
+    """Seeded Q4_K rows: fp16 d ~U(0.005, 0.02), dmin ~U(0, 0.1), random 6-bit
+    sub-scales / sub-mins and nibbles."""
+    nb = k // 256
+    blk = rng.integers(0, 256, size=(n, nb, 144), dtype=np.uint8)
+    d = rng.uniform(0.005, 0.02, size=(n, nb)).astype(np.float16)
+    dmin = rng.uniform(0.0, 0.1, size=(n, nb)).astype(np.float16)
+    blk[:, :, 0:2] = d.view(np.uint8).reshape(n, nb, 2)
+    blk[:, :, 2:4] = dmin.view(np.uint8).reshape(n, nb, 2)
+    return blk

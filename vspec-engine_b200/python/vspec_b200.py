@@ -130,6 +130,7 @@ _sigs = {
     "vspec_b200_paged_attention_workspace_bytes": ([c_size_t] * 5, c_size_t),
     "vspec_b200_paged_attention": ([POINTER(PagedAttnArgs), c_void_p], c_int),
     "vspec_b200_paged_attention_page_fault": ([POINTER(c_int)], c_int),
+    "vspec_b200_q4k_linear": ([c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_void_p], c_int),
     "vspec_b200_kv_int3_quantize": ([c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_float, c_void_p,
                                      c_void_p, c_void_p], c_int),
     "vspec_b200_paged_attention_int3": ([POINTER(PagedAttnArgs), c_void_p, c_void_p, c_size_t, c_void_p], c_int),
@@ -270,6 +271,10 @@ def paged_attention_int3(q: int, k_codes: int, v_codes: int, k_scales: int, v_sc
                       num_pages, max_ctx, scale, KV_INT3, workspace, workspace_bytes)
     check(lib.vspec_b200_paged_attention_int3(ctypes.byref(a), k_scales, v_scales, block, stream),
           "vspec_b200_paged_attention_int3")
+
+
+def q4k_linear(x: int, blocks: int, y: int, m: int, n: int, k: int, stream: int = 0) -> None:
+    check(lib.vspec_b200_q4k_linear(x, blocks, y, m, n, k, stream), "vspec_b200_q4k_linear")
 
 
 def page_fault_flag() -> int:
