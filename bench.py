@@ -220,6 +220,79 @@ def time_gemv_graph(torch, V, bits: int, copies: int, steps: int, warmup: int, w
     return ms, clocks
 
 
+def time_hybrid(torch, V, copies: int, steps: int, warmup: int, world: int):
+    """ANF hybrid linear at the reference's lane-B benchmark shape
+    (tools/benchmark/anf_phase_b_cuda_laneB.c: m=1, k=4096, n=8192, 96 hot
+    columns (i*13 + step % 7) % n, one int4 scale block): int2 draft of every
+    column + int4 refine of the hot ones.  Device time over rotating weight
+    copies > L2 in one CUDA graph, and the host bridge end to end (host input,
+    output and hot list, copies inside) with the temporal rule off."""
+    m, k, n, hc = 1, 4096, 8192, 96
+    g = torch.Generator(device="cuda")
+    g.manual_seed(777)
+    w2s = [torch.randint(0, 256, (n, k // 4), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+    w4s = [torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+    s2 = torch.rand((n,), device="cuda", generator=g) * 0.04 + 0.01
+    s4 = torch.rand((n,), device="cuda", generator=g) * 0.015 + 0.005
+    zp4 = torch.zeros((n,), device="cuda")
+    x = torch.randn((m, k), device="cuda", dtype=torch.float32)
+    hot = torch.tensor([(i * 13) % n for i in range(hc)], dtype=torch.int32, device="cuda")
+    ys = [torch.empty((m, n), device="cuda", dtype=torch.float32) for _ in range(copies)]
+    stream = torch.cuda.Stream()
+
+    def step(st):
+        for w2, w4, y in zip(w2s, w4s, ys):
+            V.anf_hybrid_linear(x.data_ptr(), w2.data_ptr(), s2.data_ptr(), w4.data_ptr(), s4.data_ptr(),
+                                zp4.data_ptr(), y.data_ptr(), hot.data_ptr(), hc, m, n, k, 1, stream=st)
+
+    with torch.cuda.stream(stream):
+        step(stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(stream.cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    del graph
+    bytes_call = n * (k // 4) + n * 4 + hc * (k // 2 + 8) + m * k * 4 + m * n * 4
+    # bridge, host buffers (the lane-B benchmark's full path)
+    hx = x.cpu().numpy()
+    hw2, hs2 = w2s[0].cpu().numpy(), s2.cpu().numpy()
+    hw4, hs4, hzp = w4s[0].cpu().numpy(), s4.cpu().numpy(), zp4.cpu().numpy()
+    out = np.empty((m, n), dtype=np.float32)
+    lists = [np.array([(i * 13 + st % 7) % n for i in range(hc)], dtype=np.uint32) for st in range(7)]
+    os.environ.pop("VSPEC_ENABLE_ANF", None)
+
+    def call(i):
+        h = lists[i % 7]
+        ok = V.lib.vspec_cuda_fused_linear_hybrid_bridge(hx.ctypes.data, hw2.ctypes.data, hs2.ctypes.data,
+                                                         hw4.ctypes.data, hs4.ctypes.data, hzp.ctypes.data, m, k, n,
+                                                         h.ctypes.data, hc, 1, out.ctypes.data)
+        if ok != 1:
+            raise RuntimeError("vspec_cuda_fused_linear_hybrid_bridge failed")
+
+    for i in range(5):
+        call(i)
+    calls = 50
+    t0 = time.perf_counter()
+    for i in range(calls):
+        call(i)
+    bridge_ms = (time.perf_counter() - t0) * 1e3 / calls
+    return ms, bytes_call, bridge_ms, hc * 4 + m * k * 4, m * n * 4
+
+
 def time_q4k(torch, V, copies: int, steps: int, warmup: int, world: int):
     """Q4_K (GGUF-style 256-element super-blocks, q4_k.c) GEMV at the bench shape
     K=4096 N=12288 M=1: 144 bytes per 256 weights, rotating copies > L2."""
@@ -766,6 +839,8 @@ def main() -> None:
     gemm = time_gemm(torch, V, world, max(3, args.steps // 5), load_peak_table())
     q4k_steps = max(3, args.steps // 5)
     q4k_ms, q4k_bytes = time_q4k(torch, V, args.copies, q4k_steps, args.warmup, world)
+    hyb_ms, hyb_bytes, hyb_bridge_ms, hyb_h2d, hyb_d2h = time_hybrid(torch, V, args.copies, q4k_steps, args.warmup,
+                                                                     world)
     quant = time_quantize(torch, V, world, rank == 0 and not args.no_cpu)
     decode = None if args.no_decode else time_decode(torch, V, world, rank, peak)
     tp = None
@@ -836,6 +911,16 @@ def main() -> None:
                 "bytes_per_launch": q4k_bytes,
                 "config": "Q4_K GEMV (q4_k.c 256-element super-blocks, 144 B each), K=4096 N=12288 M=1, "
                           f"{args.copies} rotating weight copies in one CUDA graph"},
+        "anf_hybrid": {"value": round(world * q4k_steps * args.copies * hyb_bytes / (hyb_ms * 1e-3) / 1e9, 2),
+                       "unit": "GB/s", "us_per_call": round(hyb_ms * 1e3 / (q4k_steps * args.copies), 3),
+                       "frac": round(hyb_bytes / (hyb_ms * 1e-3 / (q4k_steps * args.copies)) / 1e9 / peak, 4),
+                       "bytes_per_call": hyb_bytes,
+                       "bridge_ms_per_call": round(hyb_bridge_ms, 4),
+                       "bridge_h2d_bytes": hyb_h2d, "bridge_d2h_bytes": hyb_d2h,
+                       "config": "ANF hybrid linear at the reference's lane-B shape: m=1 k=4096 n=8192, int2 draft "
+                                 "of every column + int4 refine of 96 hot columns; device time over "
+                                 f"{args.copies} rotating weight copies in one CUDA graph; bridge_ms_per_call = "
+                                 "vspec_cuda_fused_linear_hybrid_bridge with host buffers, host-timed"},
         "gemm": gemm,
         "quantize": quant,
         "decode": decode,

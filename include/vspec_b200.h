@@ -106,6 +106,25 @@ int vspec_b200_gemv_timeout_flag(int* out_flag);
  * streams, threads, concurrent graph replays) race; order them on one stream. */
 int vspec_b200_lowbit_linear_static(const VspecB200LinearArgs* args, void* stream);
 
+/* ANF hybrid linear (src/kernel/cuda/fused_linear_hybrid.cu:70-113, the
+ * device half of vspec_cuda_fused_linear_hybrid_bridge): y[m][n] = the int2
+ * draft of every column, (q - 1.5) * s2[j] with unsigned 2-bit codes
+ * (fused_linear_int2.cu:8-12), then each listed column j < n of d_hot
+ * recomputed from int4: sum_t x[t] * ((q4 - 8) * s4[j][b] + zp4[j][b]),
+ * b = min(t / ceil(k / n_blocks_int4), n_blocks_int4 - 1).  d_w4/d_s4/d_hot
+ * may be NULL (or hot_count 0): draft only.  d_zp4 may be NULL (zero).
+ * Both launches go on `stream`. */
+int vspec_b200_anf_hybrid_linear(const float* d_x, const unsigned char* d_w2, const float* d_s2,
+                                 const unsigned char* d_w4, const float* d_s4, const float* d_zp4, float* d_y,
+                                 const uint32_t* d_hot, size_t hot_count, size_t m, size_t n, size_t k,
+                                 size_t n_blocks_int4, void* stream);
+
+/* The refine half alone (fused_linear_hybrid.cu:30-68,115-153): overwrites
+ * y[r][j] for each listed column j < n with its int4 recompute. */
+int vspec_b200_refine_hot_int4(const float* d_x, const unsigned char* d_w4, const float* d_s4, const float* d_zp4,
+                               float* d_y, const uint32_t* d_hot, size_t hot_count, size_t m, size_t n, size_t k,
+                               size_t n_blocks, void* stream);
+
 /* Q4_K dequant-matmul (src/quant/formats/q4_k.c:41-134,
  * include/vspec/quant/formats/q4_k.h:7-16; the device counterpart of
  * vspec_q4k_matmul_ref_f32): y[m][n] = x[m][k] W^T for W stored as n rows of

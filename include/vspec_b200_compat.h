@@ -134,6 +134,15 @@ void vspec_cuda_dequant_int2_to_f32_device(const unsigned char* d_b_packed, cons
                                            size_t n, size_t k);             /* fused_linear_int2.cu:137-151 */
 void vspec_cuda_expand_int3_to_int4_device(const unsigned char* d_b_int3, unsigned char* d_b_int4, size_t n,
                                            size_t k);                       /* fused_linear_int4.cu:528-543 */
+void vspec_cuda_fused_linear_hybrid_device(const float* d_a, const unsigned char* d_b_int2_packed,
+                                           const float* d_s_int2, const unsigned char* d_b_int4_packed,
+                                           const float* d_s_int4, const float* d_zp_int4, float* d_c,
+                                           const uint32_t* d_hot_indices, size_t hot_count, size_t m, size_t n,
+                                           size_t k, size_t n_blocks_int4); /* fused_linear_hybrid.cu:70-113 */
+void vspec_cuda_refine_hot_int4_device(const float* d_a, const unsigned char* d_b_int4_packed,
+                                       const float* d_s_int4, const float* d_zp_int4, float* d_c,
+                                       const uint32_t* d_hot_indices, size_t hot_count, size_t m, size_t n,
+                                       size_t k, size_t n_blocks_int4);     /* fused_linear_hybrid.cu:115-153 */
 
 /* ---- include/vspec/kernel/cuda_ops.h:10-15 (host pointers, synchronous) ---- */
 void vspec_cuda_rmsnorm_f32(const float* input, const float* weight, float eps, size_t rows, size_t dim, float* output);
@@ -167,6 +176,18 @@ int vspec_cuda_fused_linear_int4_bridge(const float* input, const unsigned char*
                                         float* output);                     /* cuda_bridge.c:812-1037 */
 int vspec_cuda_fused_linear_int3_bridge(const float* input, const unsigned char* packed_weight, const float* scales,
                                         size_t m, size_t k, size_t n, float* output); /* cuda_bridge.c:1039-1158 */
+int vspec_cuda_fused_linear_hybrid_profile_bridge(const float* input, const unsigned char* packed_weight_int2,
+                                                  const float* scales_int2, const unsigned char* packed_weight_int4,
+                                                  const float* scales_int4, const float* zero_points_int4, size_t m,
+                                                  size_t k, size_t n, const uint32_t* hot_indices, size_t hot_count,
+                                                  size_t n_blocks_int4, float* output, float* out_h2d_ms,
+                                                  float* out_kernel_ms, float* out_d2h_ms,
+                                                  float* out_total_gpu_ms); /* cuda_bridge.c:1216-1683 */
+int vspec_cuda_fused_linear_hybrid_bridge(const float* input, const unsigned char* packed_weight_int2,
+                                          const float* scales_int2, const unsigned char* packed_weight_int4,
+                                          const float* scales_int4, const float* zero_points_int4, size_t m,
+                                          size_t k, size_t n, const uint32_t* hot_indices, size_t hot_count,
+                                          size_t n_blocks_int4, float* output); /* cuda_bridge.c:1180-1214 */
 void vspec_cuda_rmsnorm_f32_bridge(const float* input, const float* weight, float eps, size_t rows, size_t dim,
                                    float* output);                          /* cuda_bridge.c:677-686 */
 void vspec_cuda_linear_f32_bridge(const float* input, const float* weight, size_t m, size_t k, size_t n,

@@ -740,3 +740,43 @@ void oracle_q4k_matmul_f32(const float* a, size_t m, size_t k, const uint8_t* bl
     }
     free(row);
 }
+
+/* ---- ANF hybrid linear (src/kernel/cuda/fused_linear_hybrid.cu:7-153,
+ *      src/kernel/cuda/fused_linear_int2.cu:8-12,14-76) ---- */
+void oracle_anf_hybrid_f32(const float* a, size_t m, size_t k, const uint8_t* w2, const float* s2,
+                           const uint8_t* w4, const float* s4, const float* zp4, size_t n_blocks,
+                           const uint32_t* hot, size_t hot_count, size_t n, float* c) {
+    const size_t pk2 = (k + 3) / 4, pk4 = (k + 1) / 2;
+    for (size_t i = 0; i < m; ++i)
+        for (size_t j = 0; j < n; ++j) {
+            const float s = s2 ? s2[j] : 1.0f;
+            float acc = 0.0f;
+            for (size_t t = 0; t < k; ++t) {
+                const unsigned q = (w2[j * pk2 + (t >> 2)] >> ((t & 3) * 2)) & 3u;
+                acc += a[i * k + t] * (((float)q - 1.5f) * s);
+            }
+            c[i * n + j] = acc;
+        }
+    if (!hot || hot_count == 0 || !w4 || !s4) return;
+    if (n_blocks == 0) n_blocks = 1;
+    const size_t bs = n_blocks > 1 ? (k + n_blocks - 1) / n_blocks : k;
+    for (size_t h = 0; h < hot_count; ++h) {
+        const size_t j = hot[h];
+        if (j >= n) continue;
+        for (size_t i = 0; i < m; ++i) {
+            float acc = 0.0f;
+            for (size_t t = 0; t < k; ++t) {
+                const uint8_t byte = w4[j * pk4 + (t >> 1)];
+                const unsigned q = (t & 1) ? (byte >> 4) & 0xFu : byte & 0xFu;
+                size_t b = 0;
+                if (n_blocks > 1) {
+                    b = t / bs;
+                    if (b >= n_blocks) b = n_blocks - 1;
+                }
+                const float zp = zp4 ? zp4[j * n_blocks + b] : 0.0f;
+                acc += a[i * k + t] * (((float)q - 8.0f) * s4[j * n_blocks + b] + zp);
+            }
+            c[i * n + j] = acc;
+        }
+    }
+}

@@ -308,3 +308,51 @@ def random_q4k_blocks(rng, n: int, k: int) -> np.ndarray:
     blk[:, :, 0:2] = d.view(np.uint8).reshape(n, nb, 2)
     blk[:, :, 2:4] = dmin.view(np.uint8).reshape(n, nb, 2)
     return blk
+
+
+def anf_hybrid(a, w2, s2, w4, s4, zp4, n_blocks: int, hot, n: int, k: int) -> np.ndarray:
+    """ANF hybrid linear (fused_linear_hybrid.cu:7-153): int2 draft of every
+    column, listed hot columns recomputed from int4 (zero-point added)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    w2 = np.ascontiguousarray(w2, dtype=np.uint8)
+    s2 = np.ascontiguousarray(s2, dtype=np.float32)
+    hot_arr = np.ascontiguousarray(hot, dtype=np.uint32) if hot is not None else None
+    w4 = np.ascontiguousarray(w4, dtype=np.uint8) if w4 is not None else None
+    s4 = np.ascontiguousarray(s4, dtype=np.float32) if s4 is not None else None
+    zp4 = np.ascontiguousarray(zp4, dtype=np.float32) if zp4 is not None else None
+    m = a.shape[0]
+    out = np.zeros((m, n), dtype=np.float32)
+    fn = ORACLE.oracle_anf_hybrid_f32
+    fn.argtypes = [c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                   c_void_p, c_size_t, c_size_t, c_void_p]
+    fn.restype = None
+    hc = 0 if hot_arr is None else hot_arr.size
+    fn(p(a), m, k, p(w2), p(s2), p(w4), p(s4), p(zp4), n_blocks, p(hot_arr) if hc else None, hc, n, p(out))
+    return out
+
+
+class AnfTccState:
+    """Host-side temporal selection of the hybrid bridge
+    (src/python/cuda_bridge.c:1352-1404): with VSPEC_ENABLE_ANF, VSPEC_ANF_TCC_ENABLE
+    and VSPEC_ANF_MODE=active, after `warmup` calls only the hot columns absent
+    from the previous call's list are refined, provided they are at most
+    `max_changed_ratio` of the list and the list has at least `min_hot` entries."""
+
+    def __init__(self, warmup: int = 4, max_changed_ratio: float = 0.35, min_hot: int = 1):
+        self.warmup, self.ratio, self.min_hot = warmup, np.float32(max_changed_ratio), min_hot
+        self.steps = 0
+        self.prev = None
+
+    def select(self, hot):
+        hot = [int(v) for v in hot]
+        if not hot:
+            return hot
+        self.steps += 1
+        active = hot
+        if self.steps > self.warmup and self.prev and len(hot) >= self.min_hot:
+            prev = set(self.prev)
+            added = [v for v in hot if v not in prev]
+            if np.float32(len(added)) / np.float32(len(hot)) <= self.ratio:
+                active = added
+        self.prev = list(hot)
+        return active

@@ -420,3 +420,166 @@ int vspec_cuda_int4_tensorcore_available_bridge(void) {
     if (!vspec_cuda_device_capability_bridge(&maj, &min, &sms)) return 0;
     return maj >= 10 ? 1 : 0;
 }
+
+/* ---------------------------------------------------------------- ANF hybrid
+ * vspec_cuda_fused_linear_hybrid_(profile_)bridge (cuda_bridge.c:1160-1683):
+ * device copies of the int2 and int4 weights cached per host thread (pointers,
+ * sizes, sampled fingerprints; the int4 zero-points zero-filled when NULL), the
+ * activations and the hot list uploaded per call, int2 draft + int4 refine on
+ * the device, the result downloaded.  With VSPEC_ENABLE_ANF, VSPEC_ANF_TCC_ENABLE
+ * and VSPEC_ANF_MODE=active the temporal rule of cuda_bridge.c:1352-1404 picks
+ * which hot columns are refined: after VSPEC_ANF_TCC_WARMUP calls (default 4),
+ * only the columns absent from the previous call's list, when they are at most
+ * VSPEC_ANF_TCC_MAX_CHANGED_RATIO (0.35, clamped to [0.01, 1]) of a list of at
+ * least VSPEC_ANF_TCC_MIN_HOT (1) entries.  VSPEC_INT2_COMPUTE_MODE's TF32
+ * cuBLAS draft (cuda_bridge.c:1585-1619) is served by the same fused draft. */
+static VB_THREAD_LOCAL uint32_t* g_hot_prev = NULL;
+static VB_THREAD_LOCAL uint32_t* g_hot_added = NULL;
+static VB_THREAD_LOCAL size_t g_hot_prev_count = 0, g_hot_cap = 0, g_tcc_steps = 0;
+
+static int anf_tcc_active(void) {
+    const char* mode = getenv("VSPEC_ANF_MODE");
+    return vb_env_flag("VSPEC_ENABLE_ANF", 0) && vb_env_flag("VSPEC_ANF_TCC_ENABLE", 0) && mode &&
+           strcmp(mode, "active") == 0;
+}
+
+static float env_float_clamped(const char* name, float def, float lo, float hi) {
+    float v = vb_env_float(name, def);
+    return v < lo ? lo : (v > hi ? hi : v);
+}
+
+static size_t env_size_clamped(const char* name, size_t def, size_t lo, size_t hi) {
+    size_t v = vb_env_size(name, def);
+    return v < lo ? lo : (v > hi ? hi : v);
+}
+
+/* Returns 0 on allocation failure; otherwise sets *active / *active_count. */
+static int anf_tcc_select(const uint32_t* hot, size_t hot_count, int have_int4, const uint32_t** active,
+                          size_t* active_count) {
+    *active = hot;
+    *active_count = hot_count;
+    if (!anf_tcc_active()) {
+        g_hot_prev_count = 0;
+        g_tcc_steps = 0;
+        return 1;
+    }
+    if (hot_count == 0 || !hot || !have_int4) return 1;
+    const float max_ratio = env_float_clamped("VSPEC_ANF_TCC_MAX_CHANGED_RATIO", 0.35f, 0.01f, 1.0f);
+    const size_t warmup = env_size_clamped("VSPEC_ANF_TCC_WARMUP", 4, 0, 1024);
+    const size_t min_hot = env_size_clamped("VSPEC_ANF_TCC_MIN_HOT", 1, 1, 65536);
+    g_tcc_steps += 1;
+    if (g_hot_cap < hot_count) {
+        uint32_t* p = (uint32_t*)realloc(g_hot_prev, hot_count * sizeof(uint32_t));
+        if (!p) return 0;
+        g_hot_prev = p;
+        p = (uint32_t*)realloc(g_hot_added, hot_count * sizeof(uint32_t));
+        if (!p) return 0;
+        g_hot_added = p;
+        g_hot_cap = hot_count;
+    }
+    if (g_tcc_steps > warmup && g_hot_prev_count > 0 && hot_count >= min_hot) {
+        size_t added = 0;
+        for (size_t i = 0; i < hot_count; ++i) {
+            int seen = 0;
+            for (size_t j = 0; j < g_hot_prev_count; ++j)
+                if (g_hot_prev[j] == hot[i]) { seen = 1; break; }
+            if (!seen) g_hot_added[added++] = hot[i];
+        }
+        if ((float)added / (float)hot_count <= max_ratio) {
+            *active = g_hot_added;
+            *active_count = added;
+        }
+    }
+    memcpy(g_hot_prev, hot, hot_count * sizeof(uint32_t));
+    g_hot_prev_count = hot_count;
+    return 1;
+}
+
+int vspec_cuda_fused_linear_hybrid_profile_bridge(const float* input, const unsigned char* packed_weight_int2,
+                                                  const float* scales_int2, const unsigned char* packed_weight_int4,
+                                                  const float* scales_int4, const float* zero_points_int4, size_t m,
+                                                  size_t k, size_t n, const uint32_t* hot_indices, size_t hot_count,
+                                                  size_t n_blocks_int4, float* output, float* out_h2d_ms,
+                                                  float* out_kernel_ms, float* out_d2h_ms, float* out_total_gpu_ms) {
+    if (!input || !packed_weight_int2 || !scales_int2 || !output || m == 0 || k == 0 || n == 0) return 0;
+    if (hot_count > 0 && !hot_indices) return 0;
+    if (hot_count > 0 && (!packed_weight_int4 || !scales_int4)) return 0;
+    if (n_blocks_int4 == 0) n_blocks_int4 = 1;
+    const uint32_t* active = NULL;
+    size_t active_count = 0;
+    if (!anf_tcc_select(hot_indices, hot_count, packed_weight_int4 && scales_int4, &active, &active_count)) return 0;
+
+    const size_t bytes_w2 = n * ((k + 3) / 4), bytes_s2 = n * sizeof(float);
+    VbCacheEntry* e2 = vb_weight_cache(2, packed_weight_int2, bytes_w2, scales_int2, bytes_s2, NULL, 0, 0,
+                                       "VSPEC_HYBRID_BRIDGE_CACHE_CAP");
+    if (!e2) return 0;
+    VbCacheEntry* e4 = NULL;
+    if (hot_count > 0) {
+        const size_t bytes_w4 = n * ((k + 1) / 2), bytes_s4 = n * n_blocks_int4 * sizeof(float);
+        e4 = vb_weight_cache(4, packed_weight_int4, bytes_w4, scales_int4, bytes_s4, zero_points_int4, bytes_s4, 1,
+                             "VSPEC_HYBRID_BRIDGE_CACHE_CAP");
+        if (!e4) return 0;
+    }
+    VbXfer* x = vb_xfer();
+    if (!x) return 0;
+    const size_t bytes_in = m * k * sizeof(float), bytes_out = m * n * sizeof(float);
+    const size_t hot_off = (bytes_in + 255) & ~(size_t)255;
+    const size_t bytes_hot = active_count * sizeof(uint32_t);
+    if (!vb_ensure_device((void**)&x->d_in, &x->d_in_cap, bytes_in)) return 0;
+    if (!vb_ensure_device((void**)&x->d_out, &x->d_out_cap, bytes_out)) return 0;
+    if (bytes_hot && !vb_ensure_device((void**)&x->d_tmp, &x->d_tmp_cap, bytes_hot)) return 0;
+    /* one pinned staging buffer for the activations and the hot list */
+    if (!vb_ensure_host((void**)&x->h_in, &x->h_in_cap, hot_off + bytes_hot)) return 0;
+    memcpy(x->h_in, input, bytes_in);
+    if (bytes_hot) memcpy((char*)x->h_in + hot_off, active, bytes_hot);
+
+    cudaEvent_t ev[4] = {NULL, NULL, NULL, NULL};
+    const int profile = out_h2d_ms || out_kernel_ms || out_d2h_ms || out_total_gpu_ms;
+    int ok = 0;
+    if (profile) {
+        for (int i = 0; i < 4; ++i)
+            if (cudaEventCreate(&ev[i]) != cudaSuccess) goto done;
+        cudaEventRecord(ev[0], x->stream);
+    }
+    if (cudaMemcpyAsync(x->d_in, x->h_in, bytes_in, cudaMemcpyHostToDevice, x->stream) != cudaSuccess) goto done;
+    if (bytes_hot && cudaMemcpyAsync(x->d_tmp, (char*)x->h_in + hot_off, bytes_hot, cudaMemcpyHostToDevice,
+                                     x->stream) != cudaSuccess)
+        goto done;
+    if (profile) cudaEventRecord(ev[1], x->stream);
+    if (vspec_b200_anf_hybrid_linear(x->d_in, e2->d_w, e2->d_s, e4 ? e4->d_w : NULL, e4 ? e4->d_s : NULL,
+                                     e4 ? e4->d_zp : NULL, x->d_out, bytes_hot ? (const uint32_t*)x->d_tmp : NULL,
+                                     active_count, m, n, k, n_blocks_int4, (void*)x->stream) != VSPEC_B200_OK)
+        goto done;
+    if (profile) cudaEventRecord(ev[2], x->stream);
+    if (!vb_ensure_host((void**)&x->h_out, &x->h_out_cap, bytes_out)) goto done;
+    if (cudaMemcpyAsync(x->h_out, x->d_out, bytes_out, cudaMemcpyDeviceToHost, x->stream) != cudaSuccess) goto done;
+    if (profile) cudaEventRecord(ev[3], x->stream);
+    if (cudaStreamSynchronize(x->stream) != cudaSuccess) goto done;
+    memcpy(output, x->h_out, bytes_out);
+    if (profile) {
+        float h2d = 0.f, ker = 0.f, d2h = 0.f, tot = 0.f;
+        cudaEventElapsedTime(&h2d, ev[0], ev[1]);
+        cudaEventElapsedTime(&ker, ev[1], ev[2]);
+        cudaEventElapsedTime(&d2h, ev[2], ev[3]);
+        cudaEventElapsedTime(&tot, ev[0], ev[3]);
+        if (out_h2d_ms) *out_h2d_ms = h2d;
+        if (out_kernel_ms) *out_kernel_ms = ker;
+        if (out_d2h_ms) *out_d2h_ms = d2h;
+        if (out_total_gpu_ms) *out_total_gpu_ms = tot;
+    }
+    ok = 1;
+done:
+    for (int i = 0; i < 4; ++i)
+        if (ev[i]) cudaEventDestroy(ev[i]);
+    return ok;
+}
+
+int vspec_cuda_fused_linear_hybrid_bridge(const float* input, const unsigned char* packed_weight_int2,
+                                          const float* scales_int2, const unsigned char* packed_weight_int4,
+                                          const float* scales_int4, const float* zero_points_int4, size_t m,
+                                          size_t k, size_t n, const uint32_t* hot_indices, size_t hot_count,
+                                          size_t n_blocks_int4, float* output) {
+    return vspec_cuda_fused_linear_hybrid_profile_bridge(input, packed_weight_int2, scales_int2, packed_weight_int4,
+                                                         scales_int4, zero_points_int4, m, k, n, hot_indices,
+                                                         hot_count, n_blocks_int4, output, NULL, NULL, NULL, NULL);
+}

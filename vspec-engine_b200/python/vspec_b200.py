@@ -131,6 +131,13 @@ _sigs = {
     "vspec_b200_paged_attention": ([POINTER(PagedAttnArgs), c_void_p], c_int),
     "vspec_b200_paged_attention_page_fault": ([POINTER(c_int)], c_int),
     "vspec_b200_q4k_linear": ([c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_void_p], c_int),
+    "vspec_b200_anf_hybrid_linear": ([c_void_p] * 8 + [c_size_t] * 5 + [c_void_p], c_int),
+    "vspec_b200_refine_hot_int4": ([c_void_p] * 6 + [c_size_t] * 5 + [c_void_p], c_int),
+    "vspec_cuda_fused_linear_hybrid_device": ([c_void_p] * 8 + [c_size_t] * 5, None),
+    "vspec_cuda_fused_linear_hybrid_bridge": ([c_void_p] * 6 + [c_size_t] * 3 + [c_void_p, c_size_t, c_size_t,
+                                                                                  c_void_p], c_int),
+    "vspec_cuda_fused_linear_hybrid_profile_bridge": ([c_void_p] * 6 + [c_size_t] * 3 +
+                                                      [c_void_p, c_size_t, c_size_t] + [c_void_p] * 5, c_int),
     "vspec_b200_kv_int3_quantize": ([c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_float, c_void_p,
                                      c_void_p, c_void_p], c_int),
     "vspec_b200_paged_attention_int3": ([POINTER(PagedAttnArgs), c_void_p, c_void_p, c_size_t, c_void_p], c_int),
@@ -275,6 +282,13 @@ def paged_attention_int3(q: int, k_codes: int, v_codes: int, k_scales: int, v_sc
 
 def q4k_linear(x: int, blocks: int, y: int, m: int, n: int, k: int, stream: int = 0) -> None:
     check(lib.vspec_b200_q4k_linear(x, blocks, y, m, n, k, stream), "vspec_b200_q4k_linear")
+
+
+def anf_hybrid_linear(x: int, w2: int, s2: int, w4: int | None, s4: int | None, zp4: int | None, y: int,
+                      hot: int | None, hot_count: int, m: int, n: int, k: int, n_blocks_int4: int,
+                      stream: int = 0) -> None:
+    check(lib.vspec_b200_anf_hybrid_linear(x, w2, s2, w4, s4, zp4, y, hot, hot_count, m, n, k, n_blocks_int4, stream),
+          "vspec_b200_anf_hybrid_linear")
 
 
 def page_fault_flag() -> int:
