@@ -609,7 +609,7 @@ def time_gemm(torch, V, world: int, steps: int, peaks: dict):
 
 
 def time_quantize(torch, V, world: int, with_cpu: bool):
-    """Load-time quantise + pack (SURVEY 8(f) row 1): a 12288 x 4096 fp32
+    """Load-time quantise + pack: a 12288 x 4096 fp32
     weight (N(0, 0.02), seeded) to W4 block 128 at the 0.999 percentile, as
     the reference's _quantize_weight_rowwise with VSPEC_INT4_BLOCK_SIZE=128;
     GB/s of fp32 input. CPU baseline: the C restatement on a 256-row sample."""

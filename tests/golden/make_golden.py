@@ -1,7 +1,7 @@
 """Generate golden fixtures from Vspec-Engine's own Python runtime.
 
-Run in a checkout that has the reference tree (default /root/reference, or
-VSPEC_REFERENCE=<path>); the fixtures are committed so that machines without
+Run where the reference tree is present (its location in VSPEC_REFERENCE,
+which has a default below); the fixtures are committed so that machines without
 the tree (the GPU box) only read the .npz files.
 
     python tests/golden/make_golden.py

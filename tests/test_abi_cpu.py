@@ -61,7 +61,7 @@ def test_struct_layouts_match_reference_headers():
 def test_c_header_compiles_against_reference_headers(tmp_path):
     """vspec_b200_compat.h must coexist with the reference's own headers (it
     reuses their struct definitions when they are included first)."""
-    ref_inc = "/root/reference/include"
+    ref_inc = os.path.join(os.environ.get("VSPEC_REFERENCE", "/root/reference"), "include")
     if not os.path.isdir(ref_inc):
         pytest.skip("reference headers not present")
     src = tmp_path / "t.c"

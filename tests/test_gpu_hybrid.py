@@ -1,4 +1,4 @@
-"""ANF hybrid linear on the GPU (SURVEY row f.3): the int2 draft of every column
+"""ANF hybrid linear on the GPU: the int2 draft of every column
 plus the int4 recompute of the hot columns (src/kernel/cuda/fused_linear_hybrid.cu:7-153)
 against the C oracle and against the reference's own CUDA kernels, compiled from
 their sources into oracle/_ref/libvspec_ref_cuda.so and run on the same device

@@ -1,4 +1,4 @@
-"""int3 KV-cache compression on the GPU (SURVEY row f.2): the append-time
+"""int3 KV-cache compression on the GPU: the append-time
 quantiser bit for bit against the oracle and the reference's own
 vspec_kv_cache_append (src/attention/kv_cache.c:64-126,160-226), and paged GQA
 attention over int3 pages against the oracle's dequantise-then-attend

@@ -1,4 +1,4 @@
-"""Q4_K dequant-matmul on the GPU (SURVEY row f.4) against the oracle, which is
+"""Q4_K dequant-matmul on the GPU against the oracle, which is
 pinned bit for bit to the reference's vspec_q4k_matmul_ref_f32
 (src/quant/formats/q4_k.c:41-134), through the C ABI."""
 import numpy as np

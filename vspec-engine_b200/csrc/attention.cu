@@ -452,7 +452,7 @@ __global__ void paged_attn_combine_kernel(const AttnParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// int3 KV pages (SURVEY row f.2): per-(token, head) codes of 3 bits packed
+// int3 KV pages: per-(token, head) codes of 3 bits packed
 // LSB-first (src/quant/pack.c:30-51) with fp32 scales per block of 16 or 32
 // dims, as vspec_kv_cache_append stores them with int3 compression on
 // (src/attention/kv_cache.c:64-126,160-226).  d = 128: 48 bytes of codes and

@@ -1,4 +1,4 @@
-// hybrid.cu -- the ANF hybrid linear (SURVEY row f.3): an int2 draft of every
+// hybrid.cu -- the ANF hybrid linear: an int2 draft of every
 // output column, then the "hot" columns recomputed from int4 weights
 // (src/kernel/cuda/fused_linear_hybrid.cu:7-153).
 //

@@ -1,4 +1,4 @@
-// q4k.cu -- Q4_K dequant-matmul on the GPU (SURVEY row f.4): the reference's
+// q4k.cu -- Q4_K dequant-matmul on the GPU: the reference's
 // 256-element super-block format (src/quant/formats/q4_k.c:41-134,
 // include/vspec/quant/formats/q4_k.h:7-16) behind a decode GEMV.
 //
