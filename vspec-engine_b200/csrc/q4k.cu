@@ -30,6 +30,13 @@ __device__ __forceinline__ uint32_t q4k_field6(uint32_t w0, uint32_t w1, uint32_
     return __funnelshift_r(lo, hi, (uint32_t)off) & 0x3Fu;
 }
 
+// The low nibble of w as a float, exactly: 2^23 + q has q in its mantissa's
+// low bits, and subtracting 2^23 leaves q (a logic op and an add instead of an
+// integer-to-float conversion).
+__device__ __forceinline__ float q4k_code(uint32_t w) {
+    return __uint_as_float(0x4B000000u | (w & 0xFu)) - 8388608.0f;
+}
+
 // x is staged once per CTA in shared memory, [m][k/32][36] floats (every
 // 32-element sub-block padded by 16 bytes, so the 8 lanes of a load phase,
 // which read 8 different sub-blocks, hit different banks).  Warp w then takes
@@ -37,14 +44,17 @@ __device__ __forceinline__ uint32_t q4k_field6(uint32_t w0, uint32_t w1, uint32_
 // all of its header and code loads for the row issued before the math (a
 // double-buffered variant, 4 sub-blocks per lane and chunk with the next
 // chunk's loads issued before the current chunk's math, measured 31.9 us
-// against this kernel's 28.7 us at K=4096 N=12288 M=1).
+// against 28.7 us for this kernel with per-code conversions at K=4096
+// N=12288 M=1).
 template <int MM>
 __global__ void __launch_bounds__(kQ4kWarps * 32)
 q4k_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, float* __restrict__ y, int m, int n,
                 int k) {
     extern __shared__ __align__(16) float xs_sm[];
+    __shared__ float div63[64];   // v / 63 for the 6-bit fields, the same IEEE quotient as q4_k.c:94-95
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nb = k / 256, nsub = nb * 8;
+    if (tid < 64) div63[tid] = __fdiv_rn((float)tid, 63.0f);
     // stage x (float4 granules)
     const int nq = m * k / 4;
     for (int i = tid; i < nq; i += kQ4kWarps * 32) {
@@ -81,8 +91,8 @@ q4k_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
                     const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[u].x >> 16)));
                     const uint32_t sc = q4k_field6(hdr[u].y, hdr[u].z, hdr[u].w, sb);
                     const uint32_t mn = q4k_field6(hdr[u].y, hdr[u].z, hdr[u].w, 8 + sb);
-                    const float sub_scale = d * __fdiv_rn((float)sc, 63.0f);   // q4_k.c:94-95
-                    const float sub_min = dmin * __fdiv_rn((float)mn, 63.0f);
+                    const float sub_scale = d * div63[sc];   // q4_k.c:94-95
+                    const float sub_min = dmin * div63[mn];
                     const uint32_t qw[4] = {qv[u].x, qv[u].y, qv[u].z, qv[u].w};
 #pragma unroll
                     for (int r = 0; r < MM; ++r) {
@@ -93,10 +103,10 @@ q4k_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
                             for (int i = 0; i < 8; ++i) {
                                 const float4 v = xp[i];
                                 const uint32_t wd = qw[i >> 1] >> (16 * (i & 1));   // 4 codes, low nibble first
-                                xq = fmaf(v.x, (float)(wd & 0xFu), xq);
-                                xq = fmaf(v.y, (float)((wd >> 4) & 0xFu), xq);
-                                xq = fmaf(v.z, (float)((wd >> 8) & 0xFu), xq);
-                                xq = fmaf(v.w, (float)((wd >> 12) & 0xFu), xq);
+                                xq = fmaf(v.x, q4k_code(wd), xq);
+                                xq = fmaf(v.y, q4k_code(wd >> 4), xq);
+                                xq = fmaf(v.z, q4k_code(wd >> 8), xq);
+                                xq = fmaf(v.w, q4k_code(wd >> 12), xq);
                                 xsum += (v.x + v.y) + (v.z + v.w);
                             }
                             acc[r] = fmaf(sub_scale, xq, fmaf(-sub_min, xsum, acc[r]));
