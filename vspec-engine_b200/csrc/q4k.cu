@@ -22,6 +22,7 @@ constexpr int kQ4kMaxM = 8;
 constexpr int kQ4kRowsPerWarp = 4;
 constexpr int kQ4kSubPad = 36;   // floats per staged 32-element sub-block (+16 B: conflict-free float4 reads)
 constexpr size_t kQ4kStageMax = 96 * 1024;
+constexpr size_t kQ4kSumMax = kQ4kMaxM * (8192 / 32) * sizeof(float);   // per-sub-block sums of x
 
 __device__ __forceinline__ uint32_t q4k_field6(uint32_t w0, uint32_t w1, uint32_t w2, int idx) {
     const int bit = 6 * idx, word = bit >> 5, off = bit & 31;
@@ -63,6 +64,19 @@ q4k_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
         *reinterpret_cast<float4*>(xs_sm + ((size_t)r * nsub + (t >> 5)) * kQ4kSubPad + (t & 31)) = v;
     }
     __syncthreads();
+    // sum(x) of every staged sub-block, once per CTA (the sub-min term needs only that)
+    float* xsum_sm = xs_sm + (size_t)m * nsub * kQ4kSubPad;
+    for (int i = tid; i < m * nsub; i += kQ4kWarps * 32) {
+        const float4* xp = reinterpret_cast<const float4*>(xs_sm + (size_t)i * kQ4kSubPad);
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 v = xp[q];
+            sum += (v.x + v.y) + (v.z + v.w);
+        }
+        xsum_sm[i] = sum;
+    }
+    __syncthreads();
     constexpr int SPL = 8;   // sub-blocks per lane held in flight (k <= 8192 in one pass)
     for (int rr = 0; rr < kQ4kRowsPerWarp; ++rr) {
         const int j = (blockIdx.x * kQ4kWarps + warp) * kQ4kRowsPerWarp + rr;
@@ -98,7 +112,7 @@ q4k_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
                     for (int r = 0; r < MM; ++r) {
                         if (r < m) {
                             const float4* xp = reinterpret_cast<const float4*>(xs_sm + ((size_t)r * nsub + s) * kQ4kSubPad);
-                            float xq = 0.f, xsum = 0.f;
+                            float xq = 0.f;
 #pragma unroll
                             for (int i = 0; i < 8; ++i) {
                                 const float4 v = xp[i];
@@ -107,8 +121,8 @@ q4k_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
                                 xq = fmaf(v.y, q4k_code(wd >> 4), xq);
                                 xq = fmaf(v.z, q4k_code(wd >> 8), xq);
                                 xq = fmaf(v.w, q4k_code(wd >> 12), xq);
-                                xsum += (v.x + v.y) + (v.z + v.w);
                             }
+                            const float xsum = xsum_sm[(size_t)r * nsub + s];
                             acc[r] = fmaf(sub_scale, xq, fmaf(-sub_min, xsum, acc[r]));
                         }
                     }
@@ -152,10 +166,10 @@ extern "C" int vspec_b200_q4k_linear(const float* d_x, const void* d_blocks, flo
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
         cudaError_t e = cudaFuncSetAttribute(q4k_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)kQ4kStageMax);
+                                             (int)(kQ4kStageMax + kQ4kSumMax));
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(q4k_gemv_kernel<kQ4kMaxM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kQ4kStageMax);
+                                     (int)(kQ4kStageMax + kQ4kSumMax));
         if (e != cudaSuccess) return cuda_status(e, "q4k_gemv_kernel smem attribute");
         configured[dev] = 1;
     }
@@ -163,7 +177,7 @@ extern "C" int vspec_b200_q4k_linear(const float* d_x, const void* d_blocks, flo
         const int mm = (int)((m - i0) < mmax ? (m - i0) : mmax);
         const float* xb = d_x + i0 * k;
         float* yb = d_y + i0 * n;
-        const size_t smem = (size_t)mm * per_row;
+        const size_t smem = (size_t)mm * (per_row + (k / 32) * sizeof(float));
         if (mm == 1) q4k_gemv_kernel<1><<<grid, kQ4kWarps * 32, smem, st>>>(xb, (const uint8_t*)d_blocks, yb, mm, (int)n, (int)k);
         else q4k_gemv_kernel<kQ4kMaxM><<<grid, kQ4kWarps * 32, smem, st>>>(xb, (const uint8_t*)d_blocks, yb, mm, (int)n, (int)k);
         cudaError_t e = cudaGetLastError();
