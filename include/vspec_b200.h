@@ -271,6 +271,14 @@ int vspec_b200_mul_f32(float* d_data, const float* d_other, size_t count, void* 
  * the one after fails (n < 0 disables). */
 int vspec_b200_debug_fail_alloc_after(int n);
 
+/* Test hook: one step of the hybrid bridge's temporal hot-column rule (the
+ * selection vspec_cuda_fused_linear_hybrid_bridge makes before any device work,
+ * with the same per-thread state and environment): writes the columns that
+ * call would refine to out (capacity hot_count) and their number to *out_count.
+ * No CUDA call is made. */
+int vspec_b200_debug_anf_tcc_select(const uint32_t* hot, size_t hot_count, int have_int4, uint32_t* out,
+                                    size_t* out_count);
+
 /* Device properties used by the dispatch (filled on first use). */
 int vspec_b200_device_info(int* sm_count, int* cc_major, int* cc_minor, size_t* smem_per_block_optin);
 

@@ -58,3 +58,47 @@ def test_tcc_rule():
     assert st.select(c) == c                                # 4/10 > 0.35: full list
     assert st.select([1, 2, 3]) == [1, 2, 3]                # below min_hot: full list
     assert st.select([]) == []
+
+
+def _c_select(V, hot, have_int4=1):
+    import ctypes
+    hot = np.ascontiguousarray(hot, dtype=np.uint32)
+    out = np.zeros(max(1, hot.size), dtype=np.uint32)
+    cnt = ctypes.c_size_t(0)
+    rc = V.lib.vspec_b200_debug_anf_tcc_select(hot.ctypes.data if hot.size else None, hot.size, have_int4,
+                                               out.ctypes.data, ctypes.byref(cnt))
+    assert rc == 0
+    return [int(v) for v in out[:cnt.value]]
+
+
+@pytest.mark.parametrize("env,warmup,ratio,min_hot", [
+    ({}, 4, 0.35, 1),
+    ({"VSPEC_ANF_TCC_WARMUP": "2", "VSPEC_ANF_TCC_MIN_HOT": "4"}, 2, 0.35, 4),
+    ({"VSPEC_ANF_TCC_WARMUP": "0", "VSPEC_ANF_TCC_MAX_CHANGED_RATIO": "5"}, 4, 1.0, 1),      # 0 keeps 4; ratio clamps to 1
+    ({"VSPEC_ANF_TCC_MAX_CHANGED_RATIO": "0", "VSPEC_ANF_TCC_WARMUP": "1"}, 1, 0.01, 1),     # clamps to 0.01
+])
+def test_bridge_tcc_rule_in_c_matches_restatement(monkeypatch, env, warmup, ratio, min_hot):
+    """The C bridge's temporal rule (host code, no CUDA call) step by step
+    against AnfTccState under the same environment, including the clamps of
+    cuda_bridge.c:366-389."""
+    import vspec_b200 as V
+    monkeypatch.delenv("VSPEC_ENABLE_ANF", raising=False)
+    _c_select(V, [1, 2, 3])                      # rule off: resets the thread's state
+    for k_, v_ in env.items():
+        monkeypatch.setenv(k_, v_)
+    monkeypatch.setenv("VSPEC_ENABLE_ANF", "1")
+    monkeypatch.setenv("VSPEC_ANF_TCC_ENABLE", "y")
+    monkeypatch.setenv("VSPEC_ANF_MODE", "active")
+    st = O.AnfTccState(warmup=warmup, max_changed_ratio=ratio, min_hot=min_hot)
+    rng = np.random.default_rng(warmup * 10 + min_hot)
+    hot = list(rng.choice(500, size=20, replace=False))
+    for step in range(12):
+        if step:
+            change = [1, 3, 9, 0, 20, 2][step % 6]
+            keep = list(rng.permutation(hot)[: len(hot) - change])
+            fresh = [int(v) for v in rng.choice(np.setdiff1d(np.arange(500), hot), size=change, replace=False)]
+            hot = keep + fresh
+        assert _c_select(V, hot) == st.select(hot), step
+    assert _c_select(V, hot, have_int4=0) == [int(v) for v in hot]   # no int4 weights: full list, no state change
+    monkeypatch.setenv("VSPEC_ANF_MODE", "shadow")                     # not "active": the rule is off
+    assert _c_select(V, hot[:5]) == [int(v) for v in hot[:5]]

@@ -495,6 +495,17 @@ static int anf_tcc_select(const uint32_t* hot, size_t hot_count, int have_int4, 
     return 1;
 }
 
+int vspec_b200_debug_anf_tcc_select(const uint32_t* hot, size_t hot_count, int have_int4, uint32_t* out,
+                                    size_t* out_count) {
+    if (!out_count || (hot_count && (!hot || !out))) return VSPEC_B200_ERR_ARG;
+    const uint32_t* active = NULL;
+    size_t n = 0;
+    if (!anf_tcc_select(hot, hot_count, have_int4, &active, &n)) return VSPEC_B200_ERR_NOMEM;
+    if (n) memcpy(out, active, n * sizeof(uint32_t));
+    *out_count = n;
+    return VSPEC_B200_OK;
+}
+
 int vspec_cuda_fused_linear_hybrid_profile_bridge(const float* input, const unsigned char* packed_weight_int2,
                                                   const float* scales_int2, const unsigned char* packed_weight_int4,
                                                   const float* scales_int4, const float* zero_points_int4, size_t m,

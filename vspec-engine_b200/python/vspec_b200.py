@@ -148,6 +148,7 @@ _sigs = {
     "vspec_b200_silu_f32": ([c_void_p, c_size_t, c_void_p], c_int),
     "vspec_b200_mul_f32": ([c_void_p, c_void_p, c_size_t, c_void_p], c_int),
     "vspec_b200_debug_fail_alloc_after": ([c_int], c_int),
+    "vspec_b200_debug_anf_tcc_select": ([c_void_p, c_size_t, c_int, c_void_p, POINTER(c_size_t)], c_int),
     "vspec_b200_lowbit_linear_static": ([POINTER(LinearArgs), c_void_p], c_int),
     "vspec_b200_decode_embed": ([c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p], c_int),
     "vspec_b200_decode_qk_rope_append": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float,
