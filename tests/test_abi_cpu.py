@@ -182,3 +182,37 @@ def test_nccl_unique_id_and_later_torch_import():
     r = subprocess.run([sys.executable, "-c", code, os.path.dirname(V.__file__)], capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+
+
+def test_q4k_and_hybrid_refuse_bad_arguments_before_any_cuda_call():
+    """Argument checks of the Q4_K, hybrid and int4-refine entry points run on
+    the host first (no device is touched): status codes and messages, and the
+    hybrid bridges' 0 return (cuda_bridge.c:1323-1331)."""
+    fake = 0x10000   # never dereferenced on the host
+    assert V.lib.vspec_b200_q4k_linear(None, fake, fake, 1, 4, 256, None) == 1
+    assert V.lib.vspec_b200_q4k_linear(fake, fake, fake, 1, 4, 200, None) == 3
+    assert "multiple of 256" in V.last_error()
+    assert V.lib.vspec_b200_q4k_linear(fake + 4, fake, fake, 1, 4, 256, None) == 1
+    assert "16-byte aligned" in V.last_error()
+    assert V.lib.vspec_b200_q4k_linear(fake, fake, fake, 1, 4, 8448, None) == 3
+    assert V.lib.vspec_b200_q4k_linear(fake, fake, fake, 0, 4, 256, None) == 0   # nothing to do
+    assert V.lib.vspec_b200_refine_hot_int4(fake, fake, fake, None, fake, fake, 0, 1, 4, 64, 1, None) == 0
+    assert V.lib.vspec_b200_refine_hot_int4(fake, None, fake, None, fake, fake, 3, 1, 4, 64, 1, None) == 1
+    assert V.lib.vspec_b200_refine_hot_int4(fake, fake, fake, None, fake, fake, 3, 1, 4, 0, 1, None) == 1
+    assert V.lib.vspec_b200_anf_hybrid_linear(None, fake, fake, None, None, None, fake, None, 0, 1, 4, 64, 1,
+                                              None) == 1
+    assert V.lib.vspec_b200_anf_hybrid_linear(fake, fake, fake, None, None, None, fake, None, 0, 0, 4, 64, 1,
+                                              None) == 0
+    x = np.zeros(64, dtype=np.float32)
+    w2 = np.zeros(16, dtype=np.uint8)
+    s = np.ones(4, dtype=np.float32)
+    hot = np.array([1], dtype=np.uint32)
+    out = np.zeros(4, dtype=np.float32)
+    bridge = V.lib.vspec_cuda_fused_linear_hybrid_bridge
+    assert bridge(None, w2.ctypes.data, s.ctypes.data, None, None, None, 1, 64, 4, None, 0, 1, out.ctypes.data) == 0
+    assert bridge(x.ctypes.data, w2.ctypes.data, s.ctypes.data, None, None, None, 1, 64, 4, None, 1, 1,
+                  out.ctypes.data) == 0                        # hot_count without a hot list
+    assert bridge(x.ctypes.data, w2.ctypes.data, s.ctypes.data, None, None, None, 1, 64, 4, hot.ctypes.data, 1, 1,
+                  out.ctypes.data) == 0                        # hot list without int4 weights
+    assert bridge(x.ctypes.data, w2.ctypes.data, s.ctypes.data, None, None, None, 0, 64, 4, None, 0, 1,
+                  out.ctypes.data) == 0                        # m == 0
