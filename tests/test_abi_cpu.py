@@ -216,3 +216,24 @@ def test_q4k_and_hybrid_refuse_bad_arguments_before_any_cuda_call():
                   out.ctypes.data) == 0                        # hot list without int4 weights
     assert bridge(x.ctypes.data, w2.ctypes.data, s.ctypes.data, None, None, None, 0, 64, 4, None, 0, 1,
                   out.ctypes.data) == 0                        # m == 0
+
+
+def test_int3_kv_entry_points_refuse_bad_arguments_on_host():
+    fake = 0x10000
+    q = V.lib.vspec_b200_kv_int3_quantize
+    assert q(None, None, 1, 1, 128, 32, 99.5, fake, fake, None) == 1
+    assert q(fake, None, 0, 1, 128, 32, 99.5, fake, fake, None) == 0          # no rows: nothing to do
+    assert q(fake, None, 1, 1, 128, 24, 99.5, fake, fake, None) == 1
+    assert "block_size" in V.last_error()
+    assert q(fake, None, 1, 1, 136, 32, 99.5, fake, fake, None) == 1          # 136 % 32 != 0
+    a = V.PagedAttnArgs(fake, fake, fake, fake, fake, fake, 1, 8, 8, 128, 16, 1, 1, 16, 0.1, V.KV_F16, None, 0)
+    assert V.lib.vspec_b200_paged_attention_int3(ctypes.byref(a), fake, fake, 32, None) == 1
+    assert "KV_INT3" in V.last_error()
+    a = V.PagedAttnArgs(fake, fake, fake, fake, fake, fake, 1, 8, 8, 64, 16, 1, 1, 16, 0.1, V.KV_INT3, None, 0)
+    assert V.lib.vspec_b200_paged_attention_int3(ctypes.byref(a), fake, fake, 32, None) == 3
+    assert "head_dim 128" in V.last_error()
+    a = V.PagedAttnArgs(fake, fake, fake, fake, fake, fake, 1, 32, 2, 128, 16, 1, 1, 16, 0.1, V.KV_INT3, None, 0)
+    assert V.lib.vspec_b200_paged_attention_int3(ctypes.byref(a), fake, fake, 32, None) == 1   # 16 q heads per KV head
+    a = V.PagedAttnArgs(fake, fake, fake, fake, fake, fake, 1, 8, 8, 128, 16, 1, 1, 17, 0.1, V.KV_INT3, None, 0)
+    assert V.lib.vspec_b200_paged_attention_int3(ctypes.byref(a), fake, fake, 32, None) == 1
+    assert "exceeds" in V.last_error()
