@@ -237,3 +237,21 @@ def test_int3_kv_entry_points_refuse_bad_arguments_on_host():
     a = V.PagedAttnArgs(fake, fake, fake, fake, fake, fake, 1, 8, 8, 128, 16, 1, 1, 17, 0.1, V.KV_INT3, None, 0)
     assert V.lib.vspec_b200_paged_attention_int3(ctypes.byref(a), fake, fake, 32, None) == 1
     assert "exceeds" in V.last_error()
+
+
+def test_compat_declarations_agree_with_reference_kernel_headers(tmp_path):
+    """Every cuda_fused.h / cuda_ops.h function that vspec_b200_compat.h also
+    declares (the hybrid and refine launchers among them) must have the same
+    signature: one translation unit includes both, and gcc rejects conflicting
+    declarations."""
+    ref_inc = os.path.join(os.environ.get("VSPEC_REFERENCE", "/root/reference"), "include")
+    if not os.path.isfile(os.path.join(ref_inc, "vspec", "kernel", "cuda_fused.h")):
+        pytest.skip("reference headers not present")
+    src = tmp_path / "t2.c"
+    src.write_text('#include "vspec/kernel/cuda_fused.h"\n#include "vspec/kernel/cuda_ops.h"\n'
+                   '#include "vspec_b200_compat.h"\n'
+                   'int main(void){ return vspec_cuda_fused_linear_hybrid_device == 0 || '
+                   'vspec_cuda_refine_hot_int4_device == 0; }\n')
+    rc = os.system(f"gcc -std=gnu11 -Wall -Werror -Wno-address -c -I{ref_inc} -I{ROOT}/include {src} "
+                   f"-o {tmp_path}/t2.o")
+    assert rc == 0
