@@ -255,3 +255,26 @@ def test_compat_declarations_agree_with_reference_kernel_headers(tmp_path):
     rc = os.system(f"gcc -std=gnu11 -Wall -Werror -Wno-address -c -I{ref_inc} -I{ROOT}/include {src} "
                    f"-o {tmp_path}/t2.o")
     assert rc == 0
+
+
+def test_bridge_declarations_agree_with_reference_bridge(tmp_path):
+    """Each VSPEC_CUDA_API export of the reference's src/python/cuda_bridge.c
+    (its prototypes read as text) is declared by vspec_b200_compat.h with the
+    same signature: the reference prototypes are compiled after the compat
+    header in one translation unit."""
+    ref = os.environ.get("VSPEC_REFERENCE", "/root/reference")
+    path = os.path.join(ref, "src", "python", "cuda_bridge.c")
+    if not os.path.isfile(path):
+        pytest.skip("reference tree not present")
+    text = open(path).read()
+    protos = {}
+    for m in re.finditer(r"VSPEC_CUDA_API\s+([\w\s\*]+?)\s*\b(vspec_\w+)\s*\(([^)]*)\)", text):
+        protos.setdefault(m.group(2), f"{m.group(1).strip()} {m.group(2)}({' '.join(m.group(3).split())});")
+    assert len(protos) >= 20
+    compat = open(os.path.join(ROOT, "include", "vspec_b200_compat.h")).read()
+    assert [n for n in protos if not re.search(r"\b" + n + r"\s*\(", compat)] == []
+    src = tmp_path / "t3.c"
+    src.write_text('#include <stddef.h>\n#include <stdint.h>\n#include "vspec_b200_compat.h"\n'
+                   + "\n".join(protos.values()) + "\nint main(void){return 0;}\n")
+    rc = os.system(f"gcc -std=gnu11 -Wall -Werror -c -I{ROOT}/include {src} -o {tmp_path}/t3.o")
+    assert rc == 0
