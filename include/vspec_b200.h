@@ -100,10 +100,15 @@ int vspec_b200_gemv_timeout_flag(int* out_flag);
  * args->d_workspace must be NULL and workspace_bytes 0; shapes whose
  * vspec_b200_lowbit_linear_workspace_bytes() exceeds 16 MiB return
  * VSPEC_B200_ERR_ARG.  The first call on a device (that device current) looks
- * up the array with cudaGetSymbolAddress: make it before any stream capture.
- * The array's 64 KiB counter region is zero at module load and every launch
- * leaves it zero.  One array per device: overlapping calls on a device (other
- * streams, threads, concurrent graph replays) race; order them on one stream. */
+ * up the array with cudaGetSymbolAddress; under CUDA's default lazy module
+ * loading that lookup also reserves the 16 MiB on the device (at process start
+ * with CUDA_MODULE_LOADING=EAGER).  Make that first call before the caller's
+ * arena/pool allocator reserves the device's memory and before any stream
+ * capture.  Every call clears the array's 64 KiB counter region with a
+ * cudaMemsetAsync on `stream` before its launch, so a launch whose bounded wait
+ * gave up (vspec_b200_gemv_timeout_flag) cannot poison later calls.  One array
+ * per device: overlapping calls on a device (other streams, threads, concurrent
+ * graph replays) race; order them on one stream. */
 int vspec_b200_lowbit_linear_static(const VspecB200LinearArgs* args, void* stream);
 
 /* ANF hybrid linear (src/kernel/cuda/fused_linear_hybrid.cu:70-113, the

@@ -379,27 +379,61 @@ static void oq_rmsnorm(const float* x, int n, float eps, float* out) {
     for (int i = 0; i < n; ++i) out[i] = x[i] * inv;   /* weight = 1 */
 }
 
+/* Unsigned b-bit fields of one packed row (the LSB-first bitstream of
+ * src/quant/pack.c:53-74 read without sign), minus 2^(bits-1): the same values
+ * as (oracle_get_code + 2^bits) mod 2^bits - 2^(bits-1), a row at a time. */
+static void oq_unpack_row_centered(const uint8_t* row, int k, int bits, double* out) {
+    const int off = 1 << (bits - 1);
+    if (bits == 4) {
+        for (int t = 0; t + 1 < k; t += 2) {
+            const uint8_t b = row[t >> 1];
+            out[t] = (double)((b & 0xF) - off);
+            out[t + 1] = (double)((b >> 4) - off);
+        }
+        if (k & 1) out[k - 1] = (double)((row[(k - 1) >> 1] & 0xF) - off);
+        return;
+    }
+    int t0 = 0;
+    if (bits == 3) {
+        /* eight fields per 24-bit little-endian word */
+        for (; t0 + 8 <= k; t0 += 8) {
+            const uint8_t* p = row + (t0 / 8) * 3;
+            const uint32_t wv = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16);
+            for (int e = 0; e < 8; ++e) out[t0 + e] = (double)((int)((wv >> (3 * e)) & 7u) - off);
+        }
+    } else if (bits == 2) {
+        for (; t0 + 4 <= k; t0 += 4) {
+            const uint8_t b = row[t0 / 4];
+            for (int e = 0; e < 4; ++e) out[t0 + e] = (double)((int)((b >> (2 * e)) & 3u) - off);
+        }
+    }
+    for (int t = t0; t < k; ++t) {
+        const int code = oracle_get_code(row, (size_t)t, bits);
+        out[t] = (double)(((code + (1 << bits)) & ((1 << bits) - 1)) - off);
+    }
+}
+
 /* y[n] = sum_t x[t] * (u(n,t) - 2^(bits-1)) * s[n][t / group], double accumulate */
 static void oq_linear(const float* x, int k, const uint8_t* w, const uint16_t* s, int n, int bits, int group, float* y) {
     const size_t rb = oracle_row_bytes((size_t)k, bits);
     const int groups = k / group;
-    const int off = 1 << (bits - 1);
+    double* xd = (double*)malloc(sizeof(double) * (size_t)k);
+    double* cd = (double*)malloc(sizeof(double) * (size_t)k);
+    if (!xd || !cd) { free(xd); free(cd); for (int j = 0; j < n; ++j) y[j] = NAN; return; }
+    for (int t = 0; t < k; ++t) xd[t] = (double)x[t];
     for (int j = 0; j < n; ++j) {
-        const uint8_t* row = w + (size_t)j * rb;
+        oq_unpack_row_centered(w + (size_t)j * rb, k, bits, cd);
         double acc = 0.0;
         for (int g = 0; g < groups; ++g) {
             const double sc = (double)oracle_half_to_float(s[(size_t)j * groups + g]);
             double part = 0.0;
-            for (int t = g * group; t < (g + 1) * group; ++t) {
-                /* unsigned field: the two's-complement reading plus 2^(bits-1), mod 2^bits */
-                const int code = oracle_get_code(row, (size_t)t, bits);
-                const int u = (code + (1 << bits)) & ((1 << bits) - 1);
-                part += (double)x[t] * (double)(u - off);
-            }
+            for (int t = g * group; t < (g + 1) * group; ++t) part += xd[t] * cd[t];
             acc += part * sc;
         }
         y[j] = (float)acc;
     }
+    free(xd);
+    free(cd);
 }
 
 int oracle_qwen_generate(const OracleQwen* q, const int32_t* prompt, int prompt_len, int gen, int32_t* tokens_out,
@@ -438,9 +472,14 @@ int oracle_qwen_generate(const OracleQwen* q, const int32_t* prompt, int prompt_
                 oq_rmsnorm(v, d, q->eps, nv);
                 for (int t = 0; t < d; ++t) {
                     const int i = t < half ? t : t - half;
-                    const float inv_freq = 1.0f / powf(q->theta, (float)i / (float)half);
+                    /* runtime_inference.py:4227,1187-1191 in float32: inv_freq =
+                     * fl32(1 / fl32(theta ** fl32(i / half))), angle = fl32(pos * inv_freq),
+                     * cos / sin of the float angle; power and sin / cos correctly rounded
+                     * (evaluated in double, rounded once) */
+                    const float pw = (float)pow((double)q->theta, (double)((float)i / (float)half));
+                    const float inv_freq = 1.0f / pw;
                     const float ang = (float)pos * inv_freq;
-                    const float cs = cosf(ang), sn = sinf(ang);
+                    const float cs = (float)cos((double)ang), sn = (float)sin((double)ang);
                     v[t] = t < half ? nv[t] * cs - nv[t + half] * sn : nv[t - half] * sn + nv[t] * cs;
                 }
                 if (h >= hq) {

@@ -71,6 +71,56 @@ def test_decode_loop_matches_oracle(batch, bits, bits_mlp):
                 assert toks[b, s + 1] == _clean_argmax(ref[s], cfg["logit_clip"])
 
 
+# The layer shapes of the north star's decode configs at 2 layers (hidden 4096,
+# 32 q / 8 kv heads of 128, SwiGLU 12288, vocab 151936; and hidden 5120, 64 q /
+# 8 kv heads, SwiGLU 25600 with W4 attention and W3 MLP), so head_dim 128, the
+# real k of every linear and the 151936-row lm_head are all compared.
+QWEN3_8B_2L = dict(V.QWEN3_8B, num_layers=2)
+QWEN3_32B_2L = dict(V.QWEN3_32B, num_layers=2)
+
+
+def _oracle_logits(cfg, tensors, toks, seqs):
+    """Teacher-forced oracle logits of the listed sequences, one host thread
+    each (the C oracle releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=min(8, len(seqs))) as ex:
+        outs = list(ex.map(lambda b: O.qwen_generate(cfg, tensors, toks[b], 1)[1], seqs))
+    return dict(zip(seqs, outs))
+
+
+@pytest.mark.parametrize("name,batch,seqs", [("8b", 1, [0]), ("8b", 8, [0, 5, 7]), ("8b", 64, [0, 33, 63]),
+                                             ("32b", 2, [0, 1])])
+def test_decode_loop_real_layer_shapes(name, batch, seqs):
+    """Batch 1 and 8 run the m <= 8 GEMV kernels on every linear (m = 8 at the
+    k = 12288 down projection runs as two halves), batch 64 the tcgen05 GEMM.
+    Every step's logits are compared for the listed sequences."""
+    torch_cuda()
+    cfg = QWEN3_8B_2L if name == "8b" else QWEN3_32B_2L
+    rng = np.random.default_rng(1000 + batch)
+    plen, gen = 3, 2
+    model = V.QwenModel(cfg, seed=11, max_batch=batch, max_ctx=16)
+    try:
+        prompts = rng.integers(0, cfg["vocab"], size=(batch, plen)).astype(np.int32)
+        toks, _, logits = model.generate(prompts, gen, want_logits=True)
+        flag = __import__("ctypes").c_int(0)
+        V.check(V.lib.vspec_b200_gemv_timeout_flag(__import__("ctypes").byref(flag)), "timeout flag")
+        assert flag.value == 0 and V.page_fault_flag() == 0
+        tensors = _tensors(model, cfg)
+    finally:
+        model.close()
+    refs = _oracle_logits(cfg, tensors, toks, seqs)
+    steps = plen + gen - 1
+    # every step within the fp32 contract, the tcgen05 GEMM batch (fp16
+    # operands) included: measured on B200 1e-5 (m <= 8) and 1.7e-4 (batch 64)
+    tol_step = RTOL_F32
+    for b in seqs:
+        errs = [rel_err(logits[s, b], refs[b][s]) for s in range(steps)]
+        print(f"{name} batch={batch} seq={b} step errors: " + " ".join(f"{e:.2e}" for e in errs))
+        assert max(errs) <= tol_step, (b, errs)
+        for s in range(plen - 1, steps):
+            assert toks[b, s + 1] == _clean_argmax(logits[s, b], cfg["logit_clip"])
+
+
 def test_decode_is_deterministic_and_prompt_independent_per_sequence():
     """Same prompts give the same tokens and bit-identical logits; a sequence's
     results do not depend on the other sequences of the batch."""

@@ -448,6 +448,43 @@ def test_large_n_beyond_tile_counters():
         run_linear(x, w, s, zp, n, k, bits, g, path=V.PATH_WARPMMA)
 
 
+@pytest.mark.parametrize("m,flags", [(8, 0), (8, V.F_RESIDUAL), (7, V.F_RMSNORM), (8, V.F_SWIGLU), (5, 0)])
+def test_deep_k_many_rows_auto_dispatch(m, flags):
+    """k = 12288 (the Qwen3-8B down projection) at 5-8 activation rows: the
+    fast kernels cannot hold every k-block of all rows in shared memory, so
+    automatic dispatch runs the rows in halves on them (the one-warp-per-row
+    kernel took ~1.5 ms per call there).  Checked against the oracle with the
+    timeout flag clear."""
+    import ctypes
+    rng = np.random.default_rng(900 + m + flags)
+    n, k, g, bits = 1024, 12288, 96, 4
+    w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=True, zp_mode="none")
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    f = V.F_UNSIGNED | flags
+    deq = dequant_np(w, n, k, bits, s.astype(np.float32), None, g, unsigned=True)
+    if flags & V.F_RMSNORM:
+        nw = rng.uniform(0.5, 1.5, k).astype(np.float32)
+        xh = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6) * nw
+        y = run_linear(x, w, s, None, n, k, bits, g, flags=f, norm_w=nw)
+        ref = xh @ deq.T
+    elif flags & V.F_RESIDUAL:
+        res = rng.standard_normal((m, n)).astype(np.float32)
+        y = run_linear(x, w, s, None, n, k, bits, g, flags=f, residual=res)
+        ref = x.astype(np.float64) @ deq.T + res
+    elif flags & V.F_SWIGLU:
+        full = x.astype(np.float64) @ deq.T
+        gate, up = full[:, : n // 2], full[:, n // 2:]
+        y = run_linear(x, w, s, None, n, k, bits, g, flags=f, out_cols=n // 2)
+        ref = gate / (1.0 + np.exp(-gate)) * up
+    else:
+        y = run_linear(x, w, s, None, n, k, bits, g, flags=f)
+        ref = x.astype(np.float64) @ deq.T
+    flag = ctypes.c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(ctypes.byref(flag)), "timeout flag")
+    assert flag.value == 0
+    assert rel_err(y, ref) <= RTOL_F32
+
+
 # ---------------------------------------------------------------- tcgen05 GEMM (m > 8)
 def test_gemm_tcgen05_smoke():
     """One small launch of the tcgen05 GEMM on its own (fp16 operands, tolerance RTOL_BF16)."""

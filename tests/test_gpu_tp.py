@@ -1,6 +1,7 @@
-"""Tensor-parallel decode (BASELINE config 5 structure: column-parallel q/k/v
-and gate/up, row-parallel o-proj and down with an NCCL all-reduce) on two
-GPUs, one process per rank, against the unsharded model of the same seed.
+"""Tensor-parallel decode (the Qwen3-32B-shape config's structure:
+column-parallel q/k/v and gate/up, row-parallel o-proj and down with an NCCL
+all-reduce) on 2, 4 and 8 GPUs, one process per rank, against the unsharded
+model of the same seed.
 
 * Every rank's weight shard is, byte for byte, its slice of the unsharded
   model's packed codes and fp16 scales (bit-exact).
@@ -24,8 +25,10 @@ from test_gpu_decode import SMALL, _clean_argmax
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
 JOIN_S = 300
+# 8 KV heads and 128-code groups in every row-parallel slice up to 8 ranks
+# (q_dim / 8 = 128, intermediate / 8 = 128)
+TP8 = dict(SMALL, hidden=512, num_heads=16, num_kv_heads=8, head_dim=64, intermediate=1024)
 
 
 def _download(model, cfg):
@@ -36,14 +39,14 @@ def _download(model, cfg):
     return t
 
 
-def _rank_main(rank, nccl_id, cfg, seed, max_batch, forced, prompts, gen, barrier, out_q):
+def _rank_main(rank, world, nccl_id, cfg, seed, max_batch, forced, prompts, gen, barrier, out_q):
     """One rank of the group: build the shard, wait until every rank has one,
     then run the same two generations on all ranks."""
     try:
         import torch
         torch.cuda.set_device(rank)
         import vspec_b200 as V
-        model = V.QwenModel(cfg, seed=seed, max_batch=max_batch, max_ctx=64, tp_size=WORLD, tp_rank=rank,
+        model = V.QwenModel(cfg, seed=seed, max_batch=max_batch, max_ctx=64, tp_size=world, tp_rank=rank,
                             nccl_id=nccl_id)
         try:
             # no rank enters a collective unless every rank built its shard
@@ -66,9 +69,9 @@ def _row_bytes(k, bits):
     return (k * bits + 7) // 8
 
 
-def _expected_shard(full, cfg, rank):
-    """Slices of the unsharded tensors that rank `rank` must hold."""
-    T, g = WORLD, cfg["group"]
+def _expected_shard(full, cfg, rank, world):
+    """Slices of the unsharded tensors that rank `rank` of `world` must hold."""
+    T, g = world, cfg["group"]
     ba = cfg["bits"]
     bm = cfg["bits_mlp"] or ba
     H, d, I = cfg["hidden"], cfg["head_dim"], cfg["intermediate"]
@@ -95,13 +98,15 @@ def _expected_shard(full, cfg, rank):
     return exp
 
 
-@pytest.mark.parametrize("batch,bits_mlp", [(3, 3), (12, 0)])
-def test_tensor_parallel_matches_unsharded(batch, bits_mlp):
+@pytest.mark.parametrize("world,batch,bits_mlp", [(2, 3, 3), (2, 12, 0), (4, 3, 3), (4, 12, 0), (8, 3, 3),
+                                                  (8, 12, 0)])
+def test_tensor_parallel_matches_unsharded(world, batch, bits_mlp):
     torch = torch_cuda()
-    if torch.cuda.device_count() < WORLD:
-        pytest.skip(f"needs {WORLD} GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import vspec_b200 as V
-    cfg = dict(SMALL, bits_mlp=bits_mlp)
+    WORLD = world
+    cfg = dict(SMALL if world == 2 else TP8, bits_mlp=bits_mlp)
     seed = 21 + bits_mlp
     rng = np.random.default_rng(60 + batch)
     plen, gen = 5, 7
@@ -119,7 +124,8 @@ def test_tensor_parallel_matches_unsharded(batch, bits_mlp):
     barrier, out_q = ctx.Barrier(WORLD), ctx.Queue()
     env_old = os.environ.get("NCCL_NVLS_ENABLE")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    procs = [ctx.Process(target=_rank_main, args=(r, nccl_id, cfg, seed, batch, forced, prompts, gen, barrier, out_q))
+    procs = [ctx.Process(target=_rank_main,
+                         args=(r, WORLD, nccl_id, cfg, seed, batch, forced, prompts, gen, barrier, out_q))
              for r in range(WORLD)]
     try:
         for p in procs:
@@ -147,7 +153,7 @@ def test_tensor_parallel_matches_unsharded(batch, bits_mlp):
         assert results[r][1] is None, f"rank {r}: {results[r][1]}"
 
     for r in range(WORLD):
-        exp = _expected_shard(full, cfg, r)
+        exp = _expected_shard(full, cfg, r, WORLD)
         got = results[r][5]
         for key, want in exp.items():
             assert np.array_equal(got[key], want), (r, key)

@@ -1,6 +1,5 @@
 // api_static_scratch.cu -- the low-bit GEMV with a scratch buffer that the
-// library never allocates: a file-scope __device__ array reserved when the
-// module loads.
+// library never allocates: a file-scope __device__ array.
 //
 // Who needs it: callers that must not see a device allocation inside a call.
 //   * Runtimes whose device memory belongs to their own arena or pool
@@ -17,13 +16,21 @@
 //   * scratch: kStaticGemvScratchBytes (16 MiB) per device.  Shapes whose
 //     workspace (vspec_b200_lowbit_linear_workspace_bytes) exceeds it are
 //     rejected with VSPEC_B200_ERR_ARG before anything is launched.
-//   * what must start at zero: the first 64 KiB (split-K tile counters).  A
-//     __device__ array is zero when the module loads, and every launch leaves
-//     the counters zero again; the fp32 partials after them need no
-//     initialisation.
+//   * what must start at zero: the first 64 KiB (split-K tile counters).
+//     Every call clears them with a cudaMemsetAsync on its own stream before
+//     the launch (a memset, not an allocation).  A completed launch leaves
+//     them zero anyway, but one whose bounded wait gave up (the flag read by
+//     vspec_b200_gemv_timeout_flag) can leave a tile's count part-way, and the
+//     caller has no other way to reach this array; the clear keeps such a
+//     launch from corrupting every later call on the device.  The fp32
+//     partials after the counters need no initialisation.
 //   * set-up: the first call on a device (with that device current) looks up
 //     the array's device address with cudaGetSymbolAddress and keeps it.
-//     Make that first call before any stream capture.
+//     Under CUDA's default lazy module loading that lookup is also what loads
+//     this file's module and reserves the 16 MiB on the device (at process
+//     start with CUDA_MODULE_LOADING=EAGER).  So make that first call before
+//     the caller's arena or pool allocator reserves the device's memory, and
+//     before any stream capture; later calls allocate nothing.
 //   * one buffer per device: calls on the same device that overlap (different
 //     streams, host threads, or graphs replayed concurrently) race on the
 //     counters and partials.  Calls must be ordered on one stream.
@@ -36,6 +43,9 @@
 namespace {
 
 constexpr size_t kStaticGemvScratchBytes = 16u << 20;
+// The split-K tile counters at the start of any GEMV workspace (the fixed
+// 16384-int region the merge kernels count in).
+constexpr size_t kStaticGemvCounterBytes = 64u << 10;
 constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_static_gemv_scratch[kStaticGemvScratchBytes];
@@ -84,6 +94,10 @@ extern "C" int vspec_b200_lowbit_linear_static(const VspecB200LinearArgs* a, voi
     void* ptr = nullptr;
     const int rc = static_scratch_for_current_device(&ptr);
     if (rc != VSPEC_B200_OK) return rc;
+    // The split-K counters must start at zero; a launch that aborted on a
+    // bounded wait may have left some set.
+    cudaError_t e = cudaMemsetAsync(ptr, 0, kStaticGemvCounterBytes, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return vb200::cuda_status(e, "cudaMemsetAsync(static GEMV counters)");
     VspecB200LinearArgs b = *a;
     b.d_workspace = ptr;
     b.workspace_bytes = kStaticGemvScratchBytes;

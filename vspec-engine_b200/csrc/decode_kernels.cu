@@ -80,9 +80,18 @@ qk_norm_rope_append_kernel(const float* __restrict__ qkv, const float* __restric
 #pragma unroll
     for (int k = 0; k < HE; ++k) {
         const int i = lane + 32 * k;
-        const float inv_freq = 1.0f / powf(theta, (float)i / (float)(d / 2));
-        float sn, cs;
-        sincosf((float)p * inv_freq, &sn, &cs);
+        // The reference's float32 arithmetic (runtime_inference.py:4227,1187-1191):
+        // inv_freq = fl32(1 / fl32(theta ** fl32(i / half))), angle = fl32(pos *
+        // inv_freq), cos / sin of that float angle as float32.  The power and the
+        // sin / cos are evaluated in double and rounded once, which gives the
+        // correctly rounded float32 values numpy's float32 path aims at.
+        const float e = (float)i / (float)(d / 2);
+        const float pw = (float)pow((double)theta, (double)e);
+        const float inv_freq = 1.0f / pw;
+        const float ang = (float)p * inv_freq;
+        double snd, csd;
+        sincos((double)ang, &snd, &csd);
+        const float sn = (float)snd, cs = (float)csd;
         r[k] = y[k] * cs - y[k + HE] * sn;
         r[k + HE] = y[k] * sn + y[k + HE] * cs;
     }
@@ -127,7 +136,7 @@ __global__ void __launch_bounds__(256) next_token_kernel(const float* __restrict
     for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
         float v = lg[j];
         if (isnan(v)) v = 0.f;
-        v = fminf(fmaxf(v, -clip), clip);
+        v = fminf(fmaxf(v, -clip), clip) + 0.0f;   // -0 -> +0: equal values tie on the index
         const unsigned long long key = ((unsigned long long)ordered_bits(v) << 32) | (0xFFFFFFFFu - (uint32_t)j);
         best = key > best ? key : best;
     }

@@ -726,6 +726,28 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
     }
 
     const bool fast = !force_generic && fast_path_ok(p, bits) && (!swiglu || (p.n / 2) % 16 == 0);
+    // The fast kernels hold every k-block of the m activation rows in shared
+    // memory, so deep k at m up to 8 (e.g. k = 12288, m = 8) can exceed it
+    // while half the rows fit.  Automatic dispatch then runs the rows in two
+    // halves instead of the one-warp-per-row generic kernel (at m = 8, n = 4096,
+    // k = 12288 that is ~35 us against ~1.5 ms).
+    if (!fast && path == kPathAuto && p.m > 1) {
+        GemvParams h = p;
+        h.m = (p.m + 1) / 2;
+        if (fast_path_ok(h, bits) && (!swiglu || (p.n / 2) % 16 == 0)) {
+            const size_t out_cols = swiglu ? (size_t)p.n / 2 : (size_t)p.n;
+            for (int i0 = 0; i0 < p.m; i0 += h.m) {
+                GemvParams q = p;
+                q.m = (p.m - i0) < h.m ? (p.m - i0) : h.m;
+                q.x = p.x + (size_t)i0 * p.k;
+                q.y = p.y + (size_t)i0 * out_cols;
+                if (p.residual) q.residual = p.residual + (size_t)i0 * p.n;
+                const int rc = lowbit_gemv_launch(q, bits, unsigned_codes, st, path, workspace, workspace_bytes);
+                if (rc != VSPEC_B200_OK) return rc;
+            }
+            return VSPEC_B200_OK;
+        }
+    }
     // The row-sliced kernel needs no workspace: it runs before any is taken (a
     // caller workspace is still checked against the documented size).
     const int rows_mode = rows_path_mode();
