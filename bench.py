@@ -169,27 +169,50 @@ def max_over_ranks(v: float, world: int) -> float:
 
 
 # ------------------------------------------------------------------ GPU arm
-def make_rotation(torch, bits: int, copies: int, seed: int):
+def make_rotation(torch, bits: int, copies: int, seed: int, n: int = N_DIM, k: int = K_DIM, sz16: bool = True,
+                  zp_array: bool = False):
+    """Distinct weight copies: uniform packed codes, group-128 scales ~U(0.005,
+    0.02) (fp16, or fp32), and with zp_array an fp32 zero-point array of the
+    mid-range value 2^(bits-1) (the signed reading of the literal config)."""
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
-    rb = (K_DIM * bits + 7) // 8
-    ws = [torch.randint(0, 256, (N_DIM, rb), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
-    ss = [(torch.rand((N_DIM, K_DIM // GROUP), device="cuda", generator=g) * 0.015 + 0.005).half()
-          for _ in range(copies)]
-    return ws, ss
+    rb = (k * bits + 7) // 8
+    ws = [torch.randint(0, 256, (n, rb), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+    ss = []
+    for _ in range(copies):
+        s = torch.rand((n, k // GROUP), device="cuda", generator=g) * 0.015 + 0.005
+        ss.append(s.half() if sz16 else s)
+    zs = [torch.full((n, k // GROUP), float(1 << (bits - 1)), device="cuda") for _ in range(copies)] if zp_array \
+        else [None] * copies
+    return ws, ss, zs
 
 
-def time_gemv_graph(torch, V, bits: int, copies: int, steps: int, warmup: int, world: int, sampler=None):
-    ws, ss = make_rotation(torch, bits, copies, seed=1234 + bits)
-    x = torch.randn((1, K_DIM), device="cuda", dtype=torch.float32)
-    ys = [torch.empty((1, N_DIM), device="cuda", dtype=torch.float32) for _ in range(copies)]
+def copies_for(bytes_per_launch: int, floor: int = 8, cap: int = 96) -> int:
+    """Rotating weight copies so that one pass streams > 4x the 126 MB L2."""
+    need = (4 * 126 * 2 ** 20) // max(1, bytes_per_launch) + 1
+    return int(min(cap, max(floor, need)))
+
+
+def time_linear_graph(torch, V, *, m: int, n: int, k: int, bits: int, copies: int, steps: int, warmup: int,
+                      world: int, sz16: bool = True, zp_array: bool = False, sampler=None, soak_s: float = 0.0,
+                      seed: int = 0):
+    """One step = one low-bit linear over each of `copies` distinct weight
+    copies (> 4x L2 in total), captured once as a CUDA graph; device time of
+    `steps` replays (max over ranks).  With a sampler, nvidia-smi clocks are
+    recorded over a soak of the same graph right before the timed region and
+    through it.  Returns (ms, clocks, algorithmic bytes per launch)."""
+    ws, ss, zs = make_rotation(torch, bits, copies, seed=1234 + bits + 7 * m + n + seed, n=n, k=k, sz16=sz16,
+                               zp_array=zp_array)
+    x = torch.randn((m, k), device="cuda", dtype=torch.float32)
+    ys = [torch.empty((m, n), device="cuda", dtype=torch.float32) for _ in range(copies)]
     stream = torch.cuda.Stream()
-    flags = V.F_UNSIGNED | V.F_SZ_F16
+    # the literal reading (signed codes, zp array) or the mid-range unsigned one
+    flags = (V.F_SZ_F16 if sz16 else 0) | (0 if zp_array else V.F_UNSIGNED)
 
     def step(st):
-        for w, s, y in zip(ws, ss, ys):
-            V.lowbit_linear(x.data_ptr(), w.data_ptr(), s.data_ptr(), None, y.data_ptr(), 1, N_DIM, K_DIM,
-                            K_DIM // GROUP, bits, flags=flags, stream=st)
+        for w, s, z, y in zip(ws, ss, zs, ys):
+            V.lowbit_linear(x.data_ptr(), w.data_ptr(), s.data_ptr(), z.data_ptr() if z is not None else None,
+                            y.data_ptr(), m, n, k, k // GROUP, bits, flags=flags, stream=st)
 
     with torch.cuda.stream(stream):
         step(stream.cuda_stream)          # configures kernel attributes before capture
@@ -206,20 +229,38 @@ def time_gemv_graph(torch, V, bits: int, copies: int, steps: int, warmup: int, w
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if sampler:
         sampler.start()
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < soak_s:
+            with torch.cuda.stream(stream):
+                for _ in range(20):
+                    graph.replay()
+            torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         start.record(stream)
         for _ in range(steps):
             graph.replay()
         end.record(stream)
     torch.cuda.synchronize()
-    if sampler:
-        clocks = sampler.stop()
-    else:
-        clocks = None
+    clocks = sampler.stop() if sampler else None
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world)
+    gemv_timeout_check(V)
     del graph
-    return ms, clocks
+    szb = 2 if sz16 else 4
+    nbytes = n * ((k * bits + 7) // 8) + n * (k // GROUP) * szb * (2 if zp_array else 1) + m * k * 4 + m * n * 4
+    return ms, clocks, nbytes
+
+
+def gemv_timeout_check(V) -> None:
+    """Fail loudly when a bounded device wait of a GEMV gave up (its output is
+    then incomplete) or a paged attention call met an out-of-range page id."""
+    import ctypes
+    f = ctypes.c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(ctypes.byref(f)), "gemv timeout flag")
+    if f.value:
+        raise RuntimeError("a GEMV bounded wait gave up during the bench (timeout flag set)")
+    if V.page_fault_flag():
+        raise RuntimeError("paged attention met an out-of-range page id during the bench")
 
 
 def time_hybrid(torch, V, copies: int, steps: int, warmup: int, world: int):
@@ -540,73 +581,29 @@ def time_decode(torch, V, world: int, rank: int, peak: float):
     b64_bytes = decode_bytes_per_step(cfg, shard, ctx_mid)
     step1_s = ms1 * 1e-3 / DEC_GEN
     step64_s = ms64 * 1e-3 / DEC_GEN
-    return {
-        "metric": "Qwen3-8B-shape W4 decode tok/s",
-        "b1": {"value": round(world * DEC_GEN / (ms1 * 1e-3), 2), "unit": "tok/s", "ms_per_token": round(ms1 / DEC_GEN, 4),
-               "parallelism": f"{world} independent sequence(s), one per GPU",
-               "roofline": {"bound": "hbm", "bytes_per_step": b1_bytes,
-                            "achieved": round(b1_bytes / step1_s / 1e9, 1), "peak": peak, "unit": "GB/s",
-                            "frac": round(b1_bytes / step1_s / 1e9 / peak, 4)}},
-        "b64": {"value": round(DEC_BATCH * DEC_GEN / (ms64 * 1e-3), 2), "unit": "tok/s",
-                "ms_per_step": round(ms64 / DEC_GEN, 4), "parallelism": f"batch 64 sharded dp{world} ({shard} per GPU)",
-                "scaling": "strong",
-                "roofline": {"bound": "hbm", "bytes_per_step_per_gpu": b64_bytes,
-                             "achieved": round(b64_bytes / step64_s / 1e9, 1), "peak": peak, "unit": "GB/s",
-                             "frac": round(b64_bytes / step64_s / 1e9 / peak, 4)}},
-        "config": "config 4: 36 layers, hidden 4096, 32/8 heads x 128, q/k RMSNorm, SwiGLU 12288, vocab 151936, "
-                  "eps 1e-6, RoPE theta 1e6, W4 group 128 (fp16 scales, mid-range zero-point), random-init; "
-                  f"prompt {DEC_PROMPT} seeded random ids (prefilled by decode steps), {DEC_GEN} greedy tokens; "
-                  "fp16 paged KV, 16-token pages; one CUDA graph per step",
-        "data": "synthetic (seeded random weights and token ids)",
-    }
+    r1 = b1_bytes / step1_s / 1e9
+    r64 = b64_bytes / step64_s / 1e9
+    return {"b1": {"tok_s": round(world * DEC_GEN / (ms1 * 1e-3), 1), "ms": round(ms1 / DEC_GEN, 4),
+                   "frac": round(r1 / peak, 3)},
+            "b64": {"tok_s": round(DEC_BATCH * DEC_GEN / (ms64 * 1e-3), 1), "ms": round(ms64 / DEC_GEN, 4),
+                    "frac": round(r64 / peak, 3), "per_gpu": shard}}
 
 
 def time_gemm(torch, V, world: int, steps: int, peaks: dict):
-    """BASELINE config 2's M=64 and M=512 points (W4, K=4096, N=12288, group
-    128, fp16 scales, mid-range zero-point): the tcgen05 GEMM path through
-    vspec_b200_lowbit_linear, back to back in a CUDA graph over rotating
-    weight copies (> L2). TFLOP/s against the measured bf16 burst peak."""
+    """The M=64 and M=512 points of the dequant-matmul sweep (W4, K=4096,
+    N=12288, group 128, fp16 scales, mid-range zero-point): activation
+    pre-pass + tcgen05 GEMM (+ split-K merge) per linear through
+    vspec_b200_lowbit_linear, back to back in a CUDA graph over rotating weight
+    copies (> L2).  TFLOP/s against the measured bf16 burst peak."""
     out = {}
     for m in (64, 512):
         copies = 24
-        ws, ss = make_rotation(torch, 4, copies, seed=77 + m)
-        x = torch.randn((m, K_DIM), device="cuda", dtype=torch.float32)
-        ys = [torch.empty((m, N_DIM), device="cuda", dtype=torch.float32) for _ in range(copies)]
-        stream = torch.cuda.Stream()
-        flags = V.F_UNSIGNED | V.F_SZ_F16
-
-        def step(st):
-            for w, sc, y in zip(ws, ss, ys):
-                V.lowbit_linear(x.data_ptr(), w.data_ptr(), sc.data_ptr(), None, y.data_ptr(), m, N_DIM, K_DIM,
-                                K_DIM // GROUP, 4, flags=flags, stream=st)
-
-        with torch.cuda.stream(stream):
-            step(stream.cuda_stream)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step(stream.cuda_stream)
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize()
-        barrier(world)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(steps):
-                graph.replay()
-            end.record(stream)
-        torch.cuda.synchronize()
-        ms = max_over_ranks(start.elapsed_time(end), world)
-        del graph
+        ms, _, nbytes = time_linear_graph(torch, V, m=m, n=N_DIM, k=K_DIM, bits=4, copies=copies, steps=steps,
+                                          warmup=3, world=world, seed=77)
         us = ms * 1e3 / (steps * copies)
         tflops = 2.0 * m * N_DIM * K_DIM / (us * 1e-6) / 1e12
-        out[f"m{m}"] = {"us_per_linear": round(us, 3), "tflops": round(tflops, 1),
-                        "frac": round(tflops / peaks["bf16_tflops"], 4),
-                        "weight_gbs": round(gemv_bytes(4, m=m) / (us * 1e-6) / 1e9, 1)}
-    out["config"] = ("config 2 M=64 and M=512 points: W4 K=4096 N=12288 group 128, fp16 scales, mid-range zero-point; "
-                     "activation pre-pass + tcgen05 GEMM (+ split-K merge) per linear; 24 rotating weight copies")
-    out["peak"] = {"bf16_tflops": peaks["bf16_tflops"], "source": "measured burst"}
+        out[f"m{m}"] = {"us": round(us, 2), "tflops": round(tflops, 1), "frac": round(tflops / peaks["bf16_tflops"], 3),
+                        "w_gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
     return out
 
 
@@ -708,24 +705,52 @@ def time_decode_tp(torch, V, world: int, rank: int, peaks: dict):
     work = tp_step_work(cfg, TP_BATCH, TP_PROMPT + TP_GEN // 2, world)
     tflops = work["flops"] / step_s / 1e12
     gbs = work["hbm_bytes"] / step_s / 1e9
-    return {
-        "metric": "Qwen3-32B-shape W4/W3 tensor-parallel decode tok/s",
-        "value": round(TP_BATCH * TP_GEN / (ms * 1e-3), 2), "unit": "tok/s", "ms_per_step": round(ms / TP_GEN, 4),
-        "parallelism": f"tp{world} (NCCL all-reduce after o-proj and down, fp32 [256, 5120])",
-        "scaling": "strong",
-        "roofline": {"bound": "tensor", "flops_per_step_per_gpu": work["flops"], "achieved": round(tflops, 1),
-                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                     "frac": round(tflops / peaks["bf16_tflops_sustained"], 4),
-                     "peak_source": "measured bf16_tflops_sustained (fp16 operands, same tensor rate)",
-                     "hbm_bytes_per_step_per_gpu": round(work["hbm_bytes"]), "hbm_achieved_gbs": round(gbs, 1),
-                     "allreduce_bytes_per_step": work["allreduce_bytes"]},
-        "tokens_checksum": int(np.asarray(toks, dtype=np.int64).sum() % 1000003),
-        "config": "config 5: 64 layers, hidden 5120, 64/8 heads x 128, q/k RMSNorm, SwiGLU 25600, vocab 151936, "
-                  "attention + lm_head W4, MLP W3, group 128 (fp16 scales, mid-range zero-point), random-init; "
-                  f"batch {TP_BATCH}, prompt {TP_PROMPT} seeded random ids (prefilled by decode steps), {TP_GEN} "
-                  "greedy tokens; fp16 paged KV, 16-token pages; one CUDA graph per step",
-        "data": "synthetic (seeded random weights and token ids)",
-    }
+    return {"tok_s": round(TP_BATCH * TP_GEN / (ms * 1e-3), 1), "ms": round(ms / TP_GEN, 3),
+            "tflops": round(tflops, 1), "frac": round(tflops / peaks["bf16_tflops_sustained"], 3),
+            "hbm_gbs": round(gbs, 1), "tok_sum": int(np.asarray(toks, dtype=np.int64).sum() % 1000003)}
+
+
+# 8 KV heads and 128-code groups in every row-parallel slice up to 8 ranks;
+# attention W4, MLP W3 like the Qwen3-32B-shape config
+TP_PARITY_CFG = dict(num_layers=2, hidden=512, num_heads=16, num_kv_heads=8, head_dim=64, intermediate=1024,
+                     vocab=1000, bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16,
+                     bits_mlp=3)
+
+
+def tp_parity(torch, V, world: int, rank: int) -> dict:
+    """Tensor-parallel parity on the driver's multi-GPU runs: every rank holds
+    its shard of a small model (all ranks, NCCL all-reduce) and the same model
+    unsharded; the sharded logits teacher-forced on the unsharded tokens are
+    compared (max normwise error over steps, sequences and ranks) and the
+    free-running greedy tokens must be equal."""
+    import torch.distributed as dist
+    cfg = TP_PARITY_CFG
+    batch, plen, gen = 4, 6, 10
+    rng = np.random.default_rng(31)
+    prompts = rng.integers(0, cfg["vocab"], size=(batch, plen)).astype(np.int32)
+    ref = V.QwenModel(cfg, seed=17, max_batch=batch, max_ctx=64)
+    try:
+        toks_ref, _, _ = ref.generate(prompts, gen)
+        _, _, lg_ref = ref.generate(toks_ref, 1, want_logits=True)
+    finally:
+        ref.close()
+    nid = [V.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(nid, src=0)
+    shard = V.QwenModel(cfg, seed=17, max_batch=batch, max_ctx=64, tp_size=world, tp_rank=rank, nccl_id=nid[0])
+    try:
+        barrier(world)
+        _, _, lg_tp = shard.generate(toks_ref, 1, want_logits=True)
+        toks_tp, _, _ = shard.generate(prompts, gen)
+    finally:
+        shard.close()
+    err = 0.0
+    for st in range(lg_ref.shape[0]):
+        for b in range(batch):
+            r = lg_ref[st, b].astype(np.float64)
+            err = max(err, float(np.max(np.abs(lg_tp[st, b] - r)) / max(np.max(np.abs(r)), 1e-30)))
+    err = max_over_ranks(err, world)
+    equal = max_over_ranks(0.0 if np.array_equal(toks_tp, toks_ref) else 1.0, world) == 0.0
+    return {"max_rel_err": float(f"{err:.3g}"), "tokens_equal": bool(equal), "tp": world}
 
 
 # ------------------------------------------------------------------ CPU legs
@@ -749,8 +774,85 @@ def cpu_oracle_sample(seconds: float = 10.0) -> dict:
     frac = rows / N_DIM
     gbs = calls * gemv_bytes(4) * frac / dt / 1e9
     return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{calls} x oracle_lowbit_matmul_f16sz on {rows} of {N_DIM} rows (K=4096, W4, group 128), "
-                      f"{dt:.1f} s, bytes scaled to the rows computed"}
+            "sample": f"{calls} x oracle_lowbit_matmul_f16sz, {rows} of {N_DIM} rows, {dt:.1f} s, bytes scaled"}
+
+
+def _oracle_decode_tensors(cfg: dict, layers: int, rng) -> dict:
+    """Random packed weights of the given layer shapes for the C decode
+    restatement (values do not change its cost); a 16-row embedding slice is
+    enough for the token ids the timing uses."""
+    H, I, Vv = cfg["hidden"], cfg["intermediate"], cfg["vocab"]
+    qd, kvd = cfg["num_heads"] * cfg["head_dim"], cfg["num_kv_heads"] * cfg["head_dim"]
+    ba, bm = cfg["bits"], cfg["bits_mlp"] or cfg["bits"]
+
+    def w(n, k, b):
+        return rng.integers(0, 256, size=(n, (k * b + 7) // 8), dtype=np.uint8)
+
+    def s(n, k):
+        return np.full((n, k // cfg["group"]), 0x1c00, dtype=np.uint16)   # fp16 0.0039
+    t = {"emb": rng.integers(0x2000, 0x2400, size=(16, H), dtype=np.uint16), "w_lm": w(Vv, H, ba), "s_lm": s(Vv, H)}
+    for l in range(layers):
+        for i, (n, k, b) in enumerate([(qd + 2 * kvd, H, ba), (H, qd, ba), (2 * I, H, bm), (H, I, bm)]):
+            t[f"w{l}_{i}"], t[f"s{l}_{i}"] = w(n, k, b), s(n, k)
+    return t
+
+
+def cpu_decode_sample(cfg: dict, layers: int = 2) -> dict:
+    """The C restatement of the decode step (oracle_qwen_generate, one host
+    thread, batch 1) timed at the real layer shapes: one step with no layers
+    (embedding, final norm, lm_head, argmax) and one with `layers` layers; the
+    step at full depth is extrapolated per layer."""
+    import oracle as O
+    rng = np.random.default_rng(9)
+    times = {}
+    for L in (0, layers):
+        c = dict(cfg, num_layers=L)
+        t = _oracle_decode_tensors(c, L, rng)
+        best = None
+        for _ in range(2):
+            t0 = time.perf_counter()
+            O.qwen_generate(c, t, np.array([3], dtype=np.int32), 1)
+            dt = time.perf_counter() - t0
+            best = dt if best is None else min(best, dt)
+        times[L] = best
+        del t
+    per_layer = max(0.0, (times[layers] - times[0]) / layers)
+    step_s = times[0] + cfg["num_layers"] * per_layer
+    return {"value": round(1.0 / step_s, 4), "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": f"oracle_qwen_generate batch 1, 1 step at 0 and {layers} layers ({times[0]:.2f} / "
+                      f"{times[layers]:.2f} s), extrapolated to {cfg['num_layers']} layers"}
+
+
+def cpu_attention_sample(seconds: float = 6.0) -> dict:
+    """The GQA restatement (oracle_paged_gqa_attention_f32, flash-stub math per
+    query head, one host thread) on config-3 sequences of the seeded context
+    distribution; GB/s of the same algorithmic K+V bytes as the GPU leg."""
+    import oracle as O
+    rng = np.random.default_rng(3)
+    ctx = rng.integers(512, 8193, size=ATTN_B).astype(np.int32)[:2]
+    need = (ctx + ATTN_PT - 1) // ATTN_PT
+    total = int(need.sum())
+    table = np.zeros((len(ctx), int(need.max())), dtype=np.int32)
+    perm = rng.permutation(total).astype(np.int32)
+    off = 0
+    for b, nb in enumerate(need):
+        table[b, :nb] = perm[off:off + nb]
+        off += nb
+    kp = rng.standard_normal((total, ATTN_PT, ATTN_HKV, ATTN_D)).astype(np.float32)
+    vp = rng.standard_normal((total, ATTN_PT, ATTN_HKV, ATTN_D)).astype(np.float32)
+    q = rng.standard_normal((len(ctx), ATTN_HQ, ATTN_D)).astype(np.float32)
+    t0 = time.perf_counter()
+    calls = 0
+    while True:
+        O.paged_attention(q, kp, vp, table, ctx, ATTN_HQ, ATTN_HKV, ATTN_D, ATTN_PT, 1.0 / np.sqrt(ATTN_D))
+        calls += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    kv = int(ctx.astype(np.int64).sum()) * ATTN_HKV * ATTN_D * 2 * 2
+    return {"value": round(calls * kv / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{calls} x oracle_paged_gqa_attention_f32 over 2 of 32 sequences (ctx {ctx[0]}, {ctx[1]}), "
+                      f"{dt:.1f} s"}
 
 
 def reference_arm(args) -> None:
@@ -807,18 +909,80 @@ def reference_arm(args) -> None:
     print(json.dumps(line))
 
 
+def gemv_leg(ms: float, nbytes: int, launches: int, world: int, peak: float) -> dict:
+    """Compact line entry of a back-to-back linear leg: whole-job GB/s of
+    algorithmic bytes, per-launch microseconds, fraction of the HBM peak."""
+    per = ms * 1e-3 / launches
+    return {"gbs": round(world * nbytes / per / 1e9, 1), "us": round(per * 1e6, 2),
+            "frac": round(nbytes / per / 1e9 / peak, 3)}
+
+
+def run_legs(torch, V, args, world: int, rank: int, peak: float, peaks: dict) -> dict:
+    """Every secondary workload of the line (each its own seeded synthetic
+    input, device-timed with CUDA events, max over ranks)."""
+    legs = {}
+    ls = max(5, args.steps // 2)
+    cpu = rank == 0 and not args.no_cpu
+    # the other bit widths and activation counts of the dequant-matmul sweep
+    for key, m, bits in (("w3", 1, 3), ("w2", 1, 2), ("m8", 8, 4)):
+        ms, _, nb = time_linear_graph(torch, V, m=m, n=N_DIM, k=K_DIM, bits=bits, copies=args.copies, steps=ls,
+                                      warmup=args.warmup, world=world)
+        legs[key] = gemv_leg(ms, nb, ls * args.copies, world, peak)
+    # the literal GEMV config: 4096 x 4096, fp32 group scales and fp32 zero-point array (8), signed codes
+    nb1 = 4096 * 2048 + 2 * 4096 * 32 * 4 + 2 * 4096 * 4
+    c1 = copies_for(nb1)
+    ms, _, nb = time_linear_graph(torch, V, m=1, n=4096, k=4096, bits=4, copies=c1, steps=ls, warmup=args.warmup,
+                                  world=world, sz16=False, zp_array=True)
+    legs["cfg1"] = gemv_leg(ms, nb, ls * c1, world, peak)
+    legs["gemm"] = time_gemm(torch, V, world, max(3, args.steps // 5), peaks)
+    a_steps = max(3, args.steps // 5)
+    attn_ms, attn_kv, attn_other = time_attention(torch, V, a_steps, args.warmup, world)
+    per = attn_ms * 1e-3 / a_steps
+    legs["attn"] = {"gbs": round(world * (attn_kv + attn_other) / per / 1e9, 1), "ms": round(per * 1e3, 4),
+                    "frac": round((attn_kv + attn_other) / per / 1e9 / peak, 3)}
+    if cpu:
+        legs["attn"]["cpu"] = cpu_attention_sample()
+    a3_ms, a3_kv, a3_other = time_attention_int3(torch, V, a_steps, args.warmup, world)
+    per3 = a3_ms * 1e-3 / a_steps
+    legs["attn_i3"] = {"gbs": round(world * (a3_kv + a3_other) / per3 / 1e9, 1), "ms": round(per3 * 1e3, 4),
+                       "frac": round((a3_kv + a3_other) / per3 / 1e9 / peak, 3),
+                       "vs_fp16": round(attn_ms / a3_ms, 3)}
+    q_ms, q_bytes = time_q4k(torch, V, args.copies, a_steps, args.warmup, world)
+    legs["q4k"] = gemv_leg(q_ms, q_bytes, a_steps * args.copies, world, peak)
+    h_ms, h_bytes, h_bridge_ms, _, _ = time_hybrid(torch, V, args.copies, a_steps, args.warmup, world)
+    legs["anf"] = dict(gemv_leg(h_ms, h_bytes, a_steps * args.copies, world, peak), bridge_ms=round(h_bridge_ms, 4))
+    q = time_quantize(torch, V, world, cpu)
+    legs["quant"] = {"gbs": q["value"], "ms": q["ms_per_matrix"]}
+    if "cpu_baseline" in q:
+        legs["quant"]["cpu_gbs"] = q["cpu_baseline"]["value"]
+    if not args.no_decode:
+        d = time_decode(torch, V, world, rank, peak)
+        legs["dec"] = d
+        if cpu:
+            legs["dec"]["cpu"] = cpu_decode_sample(V.QWEN3_8B)
+    if not args.no_tp and (world > 1 or args.tp1):
+        legs["tp"] = time_decode_tp(torch, V, world, rank, peaks)
+        if world > 1:
+            legs["tp"]["parity"] = tp_parity(torch, V, world, rank)
+        if cpu:
+            legs["tp"]["cpu"] = cpu_decode_sample(V.QWEN3_32B)
+    gemv_timeout_check(V)
+    return legs
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--copies", type=int, default=24)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-legs", action="store_true", help="headline GEMV, e2e and CPU baseline only")
     ap.add_argument("--no-decode", action="store_true")
-    ap.add_argument("--no-tp", action="store_true", help="skip the config-5 tensor-parallel decode (N >= 2)")
-    ap.add_argument("--tp1", action="store_true", help="also run config 5 on one GPU (tp1)")
+    ap.add_argument("--no-tp", action="store_true", help="skip the Qwen3-32B-shape tensor-parallel decode (N >= 2)")
+    ap.add_argument("--tp1", action="store_true", help="also run the tensor-parallel decode on one GPU (tp1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -831,43 +995,22 @@ def main() -> None:
     import vspec_b200 as V
     rank, world, local = dist_setup(args.gpus)
     peak, peak_kind = load_peaks()
+    peaks = load_peak_table()
     sampler = ClockSampler(local) if rank == 0 else None
 
-    ms4, clocks = time_gemv_graph(torch, V, 4, args.copies, args.steps, args.warmup, world, sampler)
-    ms3, _ = time_gemv_graph(torch, V, 3, args.copies, args.steps, args.warmup, world)
-    attn_steps = max(3, args.steps // 5)
-    attn_ms, attn_kv, attn_other = time_attention(torch, V, attn_steps, args.warmup, world)
-    a3_ms, a3_kv, a3_other = time_attention_int3(torch, V, attn_steps, args.warmup, world)
-    gemm = time_gemm(torch, V, world, max(3, args.steps // 5), load_peak_table())
-    q4k_steps = max(3, args.steps // 5)
-    q4k_ms, q4k_bytes = time_q4k(torch, V, args.copies, q4k_steps, args.warmup, world)
-    hyb_ms, hyb_bytes, hyb_bridge_ms, hyb_h2d, hyb_d2h = time_hybrid(torch, V, args.copies, q4k_steps, args.warmup,
-                                                                     world)
-    quant = time_quantize(torch, V, world, rank == 0 and not args.no_cpu)
-    decode = None if args.no_decode else time_decode(torch, V, world, rank, peak)
-    tp = None
-    if not args.no_tp and (world > 1 or args.tp1):
-        tp = time_decode_tp(torch, V, world, rank, load_peak_table())
-    e2e_steps = max(3, args.steps // 5)
+    # headline: W4 GEMV, K=4096 N=12288 M=1, group 128, fp16 scales, mid-range zero-point
+    ms4, clocks, b4 = time_linear_graph(torch, V, m=1, n=N_DIM, k=K_DIM, bits=4, copies=args.copies, steps=args.steps,
+                                        warmup=args.warmup, world=world, sampler=sampler, soak_s=1.0)
+    launches = args.steps * args.copies
+    legs = {} if args.no_legs else run_legs(torch, V, args, world, rank, peak, peaks)
+    e2e_steps = max(3, args.steps // 10)
     e2e_ms, e2e_bytes_call, h2d_call, d2h_call = time_e2e_bridge(torch, V, args.copies, e2e_steps, 2, world)
 
-    launches = args.steps * args.copies
-    b4, b3 = gemv_bytes(4), gemv_bytes(3)
     gbs4 = world * launches * b4 / (ms4 * 1e-3) / 1e9
-    gbs3 = world * launches * b3 / (ms3 * 1e-3) / 1e9
     per_launch_s = ms4 * 1e-3 / launches
     achieved = b4 / per_launch_s / 1e9
     e2e_gbs = world * e2e_steps * args.copies * e2e_bytes_call / (e2e_ms * 1e-3) / 1e9
-    traffic = load_traffic()
-    cpu = None
-    if rank == 0 and not args.no_cpu:
-        cpu = cpu_oracle_sample(args.cpu_seconds)
-    if decode is not None and cpu is not None:
-        b1_bytes = decode["b1"]["roofline"]["bytes_per_step"]
-        decode["cpu_baseline"] = {
-            "value": round(cpu["value"] * 1e9 / b1_bytes, 5), "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
-            "sample": "extrapolated: batch-1 decode bytes per token / the oracle's measured single-thread group-wise "
-                      "W4 GEMV rate (the linears are >98 % of a decode step's bytes)"}
+    cpu = cpu_oracle_sample(args.cpu_seconds) if rank == 0 and not args.no_cpu else None
     if world > 1:
         import torch.distributed as dist
         barrier(world)
@@ -877,62 +1020,22 @@ def main() -> None:
     line = {
         "metric": METRIC, "value": round(gbs4, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms4 / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes x int8 activation parts, exact int32 block dots, fp32 accumulate",
-        "data": "synthetic (seeded uniform codes, fp16 scales ~U(0.005,0.02), x ~N(0,1))",
-        "config": {"workload": "config 2 (BASELINE.json configs[1]) M=1 points: W4 and W3 GEMV, K=4096, N=12288, "
-                               "group 128, fp16 scales, zero-point mid-range",
-                   "step": f"{args.copies} GEMVs over distinct weight copies in one CUDA graph",
-                   "l2": f"inputs larger than L2: {args.copies} copies x {b4 / 1e6:.1f} MB rotating",
-                   "parallelism": f"dp{world} replicas (independent weights per GPU)"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes x int8 activation parts, int32 dots, fp32 acc",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "W4 GEMV K=4096 N=12288 M=1 g128 fp16 scales mid zp (configs[1] M=1)",
+                   "step": f"{args.copies} GEMVs over distinct weight copies, one CUDA graph",
+                   "l2": f"inputs > L2: {args.copies} x {b4 / 1e6:.1f} MB", "parallelism": f"dp{world} replicas"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_source": f"{peak_kind} hbm_gbs (copy read+write)",
-                     "bytes_per_launch": b4, "launch_us": round(per_launch_s * 1e6, 3)},
-        "w3": {"value": round(gbs3, 2), "unit": "GB/s", "bytes_per_launch": b3,
-               "frac": round(b3 / (ms3 * 1e-3 / launches) / 1e9 / peak, 4)},
+                     "frac": round(achieved / peak, 4), "traffic": load_traffic(), "peak_src": f"{peak_kind} hbm_gbs",
+                     "bytes": b4, "launch_us": round(per_launch_s * 1e6, 3)},
         "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d_call * args.copies,
-                "d2h_bytes_per_step": d2h_call * args.copies,
-                "api": "vspec_cuda_fused_linear_int4_cached_bridge (host x / host y per call, fp32 s+zp)"},
-        "attention": {"value": round(world * attn_steps * (attn_kv + attn_other) / (attn_ms * 1e-3) / 1e9, 2),
-                      "unit": "GB/s", "ms_per_step": round(attn_ms / attn_steps, 4),
-                      "frac": round((attn_kv + attn_other) / (attn_ms * 1e-3 / attn_steps) / 1e9 / peak, 4),
-                      "kv_bytes_per_step": attn_kv,
-                      "config": "config 3: B=32 Hq=32 Hkv=8 d=128, ctx ~U[512,8192] (seeded), 16-token fp16 pages, "
-                                "page table = seeded permutation of the pool, one step = one decode-attention call"},
-        "attention_int3": {
-            "value": round(world * attn_steps * (a3_kv + a3_other) / (a3_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(a3_ms / attn_steps, 4),
-            "frac": round((a3_kv + a3_other) / (a3_ms * 1e-3 / attn_steps) / 1e9 / peak, 4),
-            "kv_bytes_per_step": a3_kv,
-            "speedup_vs_fp16_pages": round(attn_ms / a3_ms, 3),
-            "config": "config 3 with int3 K/V pages: the fp16 pools quantised on the GPU as vspec_kv_cache_append's "
-                      "int3 compression does (block 32, percentile 99.5), 3-bit codes + fp32 block scales"},
-        "q4k": {"value": round(world * q4k_steps * args.copies * q4k_bytes / (q4k_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "us_per_linear": round(q4k_ms * 1e3 / (q4k_steps * args.copies), 3),
-                "frac": round(q4k_bytes / (q4k_ms * 1e-3 / (q4k_steps * args.copies)) / 1e9 / peak, 4),
-                "bytes_per_launch": q4k_bytes,
-                "config": "Q4_K GEMV (q4_k.c 256-element super-blocks, 144 B each), K=4096 N=12288 M=1, "
-                          f"{args.copies} rotating weight copies in one CUDA graph"},
-        "anf_hybrid": {"value": round(world * q4k_steps * args.copies * hyb_bytes / (hyb_ms * 1e-3) / 1e9, 2),
-                       "unit": "GB/s", "us_per_call": round(hyb_ms * 1e3 / (q4k_steps * args.copies), 3),
-                       "frac": round(hyb_bytes / (hyb_ms * 1e-3 / (q4k_steps * args.copies)) / 1e9 / peak, 4),
-                       "bytes_per_call": hyb_bytes,
-                       "bridge_ms_per_call": round(hyb_bridge_ms, 4),
-                       "bridge_h2d_bytes": hyb_h2d, "bridge_d2h_bytes": hyb_d2h,
-                       "config": "ANF hybrid linear at the reference's lane-B shape: m=1 k=4096 n=8192, int2 draft "
-                                 "of every column + int4 refine of 96 hot columns; device time over "
-                                 f"{args.copies} rotating weight copies in one CUDA graph; bridge_ms_per_call = "
-                                 "vspec_cuda_fused_linear_hybrid_bridge with host buffers, host-timed"},
-        "gemm": gemm,
-        "quantize": quant,
-        "decode": decode,
-        "decode_tp": tp if tp is not None else {
-            "skipped": "config 5 is tensor-parallel over 2/4/8 GPUs; runs with --gpus >= 2 (or --tp1)"},
+                "d2h_bytes_per_step": d2h_call * args.copies, "api": "vspec_cuda_fused_linear_int4_cached_bridge"},
         "cpu_baseline": cpu,
         "clocks": clocks,
-        "gpu_launches": launches * 2 + attn_steps * 2 * 2,
+        "gpu_launches": launches,
+        "legs": legs,
     }
-    print(json.dumps(line))
+    print(json.dumps(line, separators=(",", ":")))
 
 
 if __name__ == "__main__":

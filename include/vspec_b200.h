@@ -254,6 +254,38 @@ int vspec_b200_paged_attention_int3(const VspecB200PagedAttnArgs* args, const fl
 /* Reads and clears the out-of-range page id flag (1 = seen since last call). */
 int vspec_b200_paged_attention_page_fault(int* out_flag);
 
+/* ---- device view of the reference's host paged KV cache ----
+ * `cache` is a VspecKVPagedCache* (include/vspec/attention/kv_paged_cache.h:7-49,
+ * layout in vspec_b200_compat.h) filled by the reference's vspec_kv_paged_append
+ * / reuse_prefix (src/attention/kv_paged_cache.c:185-310); the library only
+ * reads it.  Device pools are [pages][page_tokens][num_heads][head_dim] in fp32
+ * (VSPEC_B200_KV_F32) or fp16 (VSPEC_B200_KV_F16, rounded to nearest even), at
+ * least cache->max_pages pages, plus any spare pages the session views use.
+ *
+ * vspec_b200_kv_paged_sync: copies every allocated page whose last write is
+ * after clock step `since_step` (0: every allocated page) to the same page
+ * index of the device pools; *out_step (optional) = the cache's clock, the
+ * since_step of the next incremental call.  Returns after the copies landed. */
+int vspec_b200_kv_paged_sync(const void* cache, int kv_dtype, void* d_k_pages, void* d_v_pages, uint64_t since_step,
+                             uint64_t* out_step, void* stream);
+/* vspec_b200_kv_paged_session_view: the session's page-table row
+ * (d_page_table_row[0 .. max_pages_per_seq), unused entries 0) and context
+ * length (*d_ctx_len = its token count) for vspec_b200_paged_attention, with
+ * vspec_kv_paged_get_token_ptr's token order (kv_paged_cache.c:312-356).  While
+ * every page of the session but the last is full the row is its pages[]
+ * widened to int32.  A session that shares a partly filled prefix page and was
+ * appended past it has a short page in the middle: its tokens from that page
+ * on are gathered into the device pool pages spare_first .. spare_first +
+ * spare_count - 1 (which must lie at or beyond cache->max_pages; the pools
+ * must have room for them) and the row points there.  *out_ctx and
+ * *out_spare_used (spare pages written) are optional.  Returns after the copies
+ * landed.  An inactive session, a row too short for its tokens, or too few
+ * spare pages return VSPEC_B200_ERR_ARG. */
+int vspec_b200_kv_paged_session_view(const void* cache, uint64_t session_id, int kv_dtype, void* d_k_pages,
+                                     void* d_v_pages, size_t spare_first, size_t spare_count,
+                                     int32_t* d_page_table_row, size_t max_pages_per_seq, int32_t* d_ctx_len,
+                                     size_t* out_ctx, size_t* out_spare_used, void* stream);
+
 /* Bit-exact gather of one sequence's K and V rows in token order into
  * [ctx][num_kv_heads][head_dim] (parity hook for vspec_kv_paged_get_token_ptr,
  * src/attention/kv_paged_cache.c:312-356). */

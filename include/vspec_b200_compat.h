@@ -92,6 +92,49 @@ typedef struct VspecKVCache {
 } VspecKVCache;
 #endif
 
+/* Host paged KV cache (include/vspec/attention/kv_paged_cache.h:7-49), read by
+ * vspec_b200_kv_paged_sync / _session_view in vspec_b200.h. */
+#if !defined(VSPEC_ATTENTION_KV_PAGED_CACHE_H)
+#define VSPEC_KV_PAGED_MAX_SESSIONS 128U
+#define VSPEC_KV_PAGED_MAX_PAGES 4096U
+#define VSPEC_KV_PAGED_MAX_PAGES_PER_SESSION 1024U
+
+typedef struct VspecKVPagedStats {
+    uint64_t page_alloc_count;
+    uint64_t page_reuse_count;
+    uint64_t evict_session_count;
+    uint64_t append_token_count;
+    size_t free_pages;
+    size_t active_sessions;
+} VspecKVPagedStats;
+
+typedef struct VspecKVPagedCache {
+    float* key_pages;            /* [max_pages][page_tokens][num_heads][head_dim] */
+    float* value_pages;
+    size_t page_tokens;
+    size_t max_pages;
+    size_t num_heads;
+    size_t head_dim;
+    VspecKVPagedStats stats;
+    struct {
+        uint8_t allocated;
+        uint16_t owner_slot;
+        uint16_t used_tokens;
+        uint16_t ref_count;      /* > 1: a prefix page shared by several sessions */
+        uint64_t last_touch_step;
+    } page_meta[VSPEC_KV_PAGED_MAX_PAGES];
+    struct {
+        uint8_t active;
+        uint64_t session_id;
+        uint64_t last_touch_step;
+        size_t total_tokens;
+        size_t page_count;
+        uint16_t pages[VSPEC_KV_PAGED_MAX_PAGES_PER_SESSION];   /* in token order */
+    } sessions[VSPEC_KV_PAGED_MAX_SESSIONS];
+    uint64_t clock_step;
+} VspecKVPagedCache;
+#endif
+
 /* ---- CUDA backend (src/kernel/cuda/cuda_backend_stub.c:25-39,
  *      src/kernel/cuda/cuda_linear_int4.cu:72-114) ---- */
 int vspec_cuda_backend_available(void);

@@ -485,6 +485,47 @@ def test_deep_k_many_rows_auto_dispatch(m, flags):
     assert rel_err(y, ref) <= RTOL_F32
 
 
+@pytest.mark.parametrize("k", [5120, 6144])
+def test_ring_split_k_merge_back_to_back(k):
+    """The Qwen3-32B-shape lm_head (n = 151936) at k = 5120 / 6144 runs the ring
+    kernel's general split-K (CTA runs crossing tile boundaries, cross-CTA
+    merges through the workspace).  32 launches back to back in a CUDA graph,
+    every one against the oracle: a merge that reads a partial before it is
+    visible shows up as a few stale rows in some launches."""
+    torch = torch_cuda()
+    import ctypes
+    rng = np.random.default_rng(k)
+    m, n, g, bits, reps = 1, 151936, k // 128, 4, 32
+    w, s, _ = make_lowbit(rng, n, k, bits, g, sz_f16=True, zp_mode="none")
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    ref = O.lowbit_matmul(x, w, n, k, bits, s, None, g)
+    dx, dw, ds = to_dev(x), to_dev(w), to_dev(s)
+    ys = [empty_dev((m, n), torch.float32) for _ in range(reps)]
+    st = torch.cuda.Stream()
+
+    def step():
+        for y in ys:
+            V.lowbit_linear(dx.data_ptr(), dw.data_ptr(), ds.data_ptr(), None, y.data_ptr(), m, n, k, g, bits,
+                            flags=V.F_SZ_F16, stream=st.cuda_stream, path=V.PATH_RING)
+    with torch.cuda.stream(st):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        step()
+    for _ in range(2):
+        for y in ys:
+            y.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        errs = [rel_err(y.cpu().numpy(), ref) for y in ys]
+        assert max(errs) <= RTOL_F32, [f"{e:.1e}" for e in errs]
+    del graph
+    flag = ctypes.c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(ctypes.byref(flag)), "timeout flag")
+    assert flag.value == 0
+
+
 # ---------------------------------------------------------------- tcgen05 GEMM (m > 8)
 def test_gemm_tcgen05_smoke():
     """One small launch of the tcgen05 GEMM on its own (fp16 operands, tolerance RTOL_BF16)."""

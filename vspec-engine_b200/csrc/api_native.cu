@@ -20,6 +20,19 @@ void set_error(const char* fmt, ...) {
     va_end(ap);
 }
 
+}  // namespace vb200
+
+// The same thread-local message for the C host layer (declared in
+// host/bridge_internal.h; not part of the public headers).
+extern "C" void vb_set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(vb200::g_last_error, sizeof(vb200::g_last_error), fmt, ap);
+    va_end(ap);
+}
+
+namespace vb200 {
+
 int cuda_status(cudaError_t e, const char* what) {
     set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
     return VSPEC_B200_ERR_CUDA;

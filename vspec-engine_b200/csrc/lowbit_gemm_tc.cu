@@ -440,7 +440,10 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
                         words[h][4 * c16 + 0] = v.x; words[h][4 * c16 + 1] = v.y;
                         words[h][4 * c16 + 2] = v.z; words[h][4 * c16 + 3] = v.w;
                     }
-                mbar_arrive(&w_empty[sw]);
+                // the weight stage is released after the TMEM stores below have
+                // consumed these words (a release right after the loads let the
+                // refill land before the loads had read the stage)
+                const int sw_used = sw;
                 if (++sw == NSW) { sw = 0; pw ^= 1u; }
                 // A stage group g was last read by the MMAs of unit u - AS
                 if (u >= AS && !mbar_wait_sleep(&a_empty[g], (uint32_t)((u / AS - 1) & 1), abort_flag, kGmWaitLimit, kGmSleepNs)) { ok = false; break; }
@@ -471,6 +474,7 @@ lowbit_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
                         tmem_st_x32(tmem_base + lane_off + (uint32_t)(64 * (g * NW + h) + 32 * hh), hv);
                     }
                 }
+                mbar_arrive(&w_empty[sw_used]);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&a_full[g]);

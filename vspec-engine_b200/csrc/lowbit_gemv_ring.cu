@@ -541,18 +541,20 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                         part[r * WR + 16 * j + g + 8] = acc[j][nt][1];
                     }
                 }
-            // message passing: the warp's stores, then (lane 0) a release
-            // fence and the counter bump; the warp that completes the count
-            // acquires before it reads the other slots
+            // message passing: every lane fences its own partial stores at GPU
+            // scope before the warp barrier, lane 0 bumps the counter, and every
+            // lane of the warp that completes the count fences again before it
+            // reads the other slots.  (A fence by lane 0 alone orders only its
+            // own stores: other lanes' partials were then sometimes still in
+            // flight when the merging warp of another CTA read them, which left
+            // a few stale rows in about one launch in eight at k = 6144 or 5120.)
+            asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
             __syncwarp();
             int old = 0;
-            if (lane == 0) {
-                asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
-                old = atomicAdd(p.counters + ci, 1);
-                if (old == total - 1) asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
-            }
+            if (lane == 0) old = atomicAdd(p.counters + ci, 1);
             old = __shfl_sync(0xffffffffu, old, 0);
             if (old == total - 1) {
+                asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
                 __syncwarp();
                 const float* sbase = p.scratch + (size_t)ci * p.max_slots * (WR * m);
                 // Sum of slots [s0, s1) in slot order; the loads of a batch of
@@ -613,8 +615,10 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                             lds_chunk<BITS>(ch[j][0], stg + ring_chunk_offset<BITS>(wrow + 16 * j + g, c));
                             lds_chunk<BITS>(ch[j][1], stg + ring_chunk_offset<BITS>(wrow + 16 * j + g + 8, c));
                         }
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&empty[ring]);
+                        // the stage is released only after the MMAs that consume
+                        // these words (below): releasing it right after the loads let
+                        // the refill land before the last loads had read the stage
+                        const int stage_used = ring;
                         if (++ring == NS) { ring = 0; ring_ph ^= 1u; }
 
                         const int kb = c_kb;
@@ -718,6 +722,11 @@ lowbit_gemv_ring_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                                 e[j][nt][1] = (d[j][0][nt][2] + d[j][1][nt][2]) + (d[j][0][nt][3] + d[j][1][nt][3]);
                             }
                         }
+                        // every MMA reading this stage's words has issued (volatile
+                        // asm keeps them ahead of the arrive; the hardware issues an
+                        // MMA only once its registers, i.e. the loads, are complete)
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[stage_used]);
                         float sv[RBW][2], zv[RBW][2];
 #pragma unroll
                         for (int j = 0; j < RBW; ++j) {

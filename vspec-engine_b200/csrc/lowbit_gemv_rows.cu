@@ -28,50 +28,71 @@ static int make_scale_map(CUtensorMap* map, const void* base, int rows, int n_gr
     return VSPEC_B200_OK;
 }
 
-// Row-group size, ring depth and CTA count.  Two CTAs per SM when their
-// shared memory fits in half an SM, else one.  The row group (at most 64
-// rows) holds all of a CTA's rows and leaves a ring of at least eight units
-// and 24 KB in flight.
+// One CTA per SM per launch, each in at most half an SM
+// (VSPEC_B200_GEMV_ROWS_PAIR: "1" on, off otherwise): the CTAs of the next
+// launch in the stream then fit beside this launch's and start streaming their
+// weights as soon as programmatic dependent launch lets them in, instead of
+// after this launch's CTAs exit.
+static bool rows_pair_mode() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("VSPEC_B200_GEMV_ROWS_PAIR");
+        v = (e && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
+// Row-group size, ring depth and CTA count.  Candidate geometries, first fit
+// wins: (pair mode) one CTA per SM in half an SM, row groups up to 96 rows;
+// two CTAs per SM in half an SM each; one CTA per SM in a whole SM; the last
+// two with row groups up to 64 rows.  The row group holds all of a CTA's rows.
+// The ring holds every unit of the busiest CTA, or wraps with at least
+// kRowsWarps stages (required by the parity waits, see the kernel) and 24 KB
+// in flight.
 static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo, size_t* smem) {
     const int m = p.m, kbt = p.k / 128;
     const int n_out = swiglu ? p.n / 2 : p.n;
     const int S = swiglu ? 2 : 1;
-    const int brmax = 64;   // NB <= 4 row blocks per group (register accumulators)
     const int szb = (p.flags & VSPEC_B200_F_SZ_F16) ? 2 : 4;
     const int srow = p.n_groups * szb;
     const bool has_s = p.s != nullptr, has_zp = p.zp != nullptr;
-    const uint32_t rb = (uint32_t)rows_unit_bytes(bits);
-    const int kut = kbt / rows_kpu(bits);
-    for (int per_sm = 2; per_sm >= 1; --per_sm) {
-        const uint32_t budget = per_sm == 2 ? kRowsSmemShared : kRowsSmemMax;
-        const int slots = device_sm_count() * per_sm;
+    struct Cand { int per_sm; uint32_t budget; int brmax; };
+    Cand cands[3];
+    int nc = 0;
+    if (rows_pair_mode()) cands[nc++] = Cand{1, kRowsSmemShared, 16 * kRowsMaxNB};
+    cands[nc++] = Cand{2, kRowsSmemShared, 64};
+    cands[nc++] = Cand{1, kRowsSmemMax, 64};
+    for (int ci = 0; ci < nc; ++ci) {
+        const Cand& cd = cands[ci];
+        const int slots = device_sm_count() * cd.per_sm;
         const int min_rows = 8;
         int P = (n_out + min_rows - 1) / min_rows;
         if (P > slots) P = slots;
         if (P < 1) P = 1;
         const int rmax = (n_out + P - 1) / P;
-        for (int ngrp = (rmax + brmax - 1) / brmax; ngrp <= 64; ++ngrp) {
+        for (int ngrp = (rmax + cd.brmax - 1) / cd.brmax; ngrp <= 64; ++ngrp) {
             const int per = (rmax + ngrp - 1) / ngrp;
             const int br = 16 * ((per + 15) / 16);
-            if (br > brmax) continue;
-            const uint32_t stage = (uint32_t)br * rb;
+            if (br > cd.brmax) continue;
+            const uint32_t stage = (uint32_t)br * (uint32_t)rows_unit_bytes(bits, br);
+            const int kut = kbt / rows_kpu(bits, br);
             const uint32_t fixed = rows_smem_plan(bits, m, kbt, br, 0, srow, has_s, has_zp, swiglu).total + 1024u;
-            if (fixed + 4u * (stage + 16u) > budget) {
+            if (fixed + 4u * (stage + 16u) > cd.budget) {
                 if (br == 16) break;
                 continue;
             }
-            // one row group per CTA (a CTA's rows fit one box): the only geometry
-            // run back to back on B200 without a fault; shapes that would need
-            // several groups per CTA take the split-K ring kernel
+            // one row group per CTA (a CTA's rows fit one box); shapes that
+            // would need several groups per CTA take the split-K ring kernel
             if (rmax > br) break;
-            int ns = (int)((budget - fixed) / (stage + 16u));
+            int ns = (int)((cd.budget - fixed) / (stage + 16u));
             const int most = ((rmax + br - 1) / br) * S * kut;   // the busiest CTA's units
             if (ns > most) ns = most;
             if (ns > kRowsMaxStages) ns = kRowsMaxStages;
-            // enough in flight: a unit per consumer warp and >= 24 KB per CTA
-            // (or everything), else smaller row groups (or one CTA per SM)
+            // a ring that wraps needs kRowsWarps stages; and >= 24 KB in
+            // flight per CTA (or everything); else smaller row groups (or the
+            // next candidate)
             const uint64_t want = (uint64_t)most * stage < 24576u ? (uint64_t)most * stage : 24576u;
-            if (ns < (most < kRowsWarps ? most : kRowsWarps) || (uint64_t)ns * stage < want) {
+            if ((ns < most && ns < kRowsWarps) || (uint64_t)ns * stage < want) {
                 if (br == 16) break;
                 continue;
             }
@@ -91,7 +112,7 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
 
 bool gemv_rows_supported(const GemvParams& p, int bits) {
     if (p.m < 1 || p.m > kGemvMaxM) return false;
-    if (p.k % (1024 * rows_kpu(bits)) != 0 || p.n_groups < 1 || p.k % p.n_groups != 0 || (p.k / p.n_groups) % 128 != 0) return false;
+    if (p.k % (1024 * rows_kpu(bits, 16)) != 0 || p.n_groups < 1 || p.k % p.n_groups != 0 || (p.k / p.n_groups) % 128 != 0) return false;
     if (reinterpret_cast<uintptr_t>(p.w) % 16 != 0 || reinterpret_cast<uintptr_t>(p.x) % 16 != 0) return false;
     if ((size_t)p.row_bytes != row_bytes_for((size_t)p.k, bits)) return false;
     if ((size_t)p.row_bytes % 16 != 0) return false;   // TMA global stride
@@ -145,9 +166,12 @@ int gemv_rows_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st
     CUtensorMap wmap, smap, zmap;
     memset(&smap, 0, sizeof(smap));
     memset(&zmap, 0, sizeof(zmap));
-    const CUtensorMapSwizzle swz = bits == 4 ? CU_TENSOR_MAP_SWIZZLE_128B
+    // the swizzle the kernel's shared-memory reads assume: 128 B for two-k-block
+    // int4 boxes, 64 B for one-k-block int4 boxes, 32 B for int2, none for int3
+    const CUtensorMapSwizzle swz = bits == 4 ? (rows_kpu(bits, geo.br) == 2 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                                              : CU_TENSOR_MAP_SWIZZLE_64B)
                                  : (bits == 2 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE);
-    int rc = make_row_tile_map(&wmap, p.w, p.n, p.row_bytes, rows_unit_bytes(bits), geo.br, swz);
+    int rc = make_row_tile_map(&wmap, p.w, p.n, p.row_bytes, rows_unit_bytes(bits, geo.br), geo.br, swz);
     if (rc != VSPEC_B200_OK) return rc;
     const int szb = (p.flags & VSPEC_B200_F_SZ_F16) ? 2 : 4;
     if (p.s) {

@@ -12,7 +12,7 @@
 //     partial sum leaves the CTA, so there is no workspace, no cross-CTA
 //     merge and no merge tail, and every CTA streams the same bytes to within
 //     one row.
-//   * The rows are cut into row groups of BR = 16 * NB rows (NB <= 4, a
+//   * The rows are cut into row groups of BR = 16 * NB rows (NB <= 6, a
 //     compile-time constant, so a warp keeps its partial sums of the group's
 //     rows in registers; with SwiGLU a gate group is followed by the matching
 //     up group).  One
@@ -58,6 +58,7 @@ constexpr uint32_t kRowsSleepNs = 20000;
 constexpr uint32_t kRowsSmemShared = 113u * 1024u;   // two CTAs per SM
 constexpr uint32_t kRowsSmemMax = 227u * 1024u;
 constexpr int kRowsMaxStages = 512;
+constexpr int kRowsMaxNB = 6;                      // row groups of up to 96 rows
 
 // Set when a bounded wait of the row-sliced GEMV gave up.  The kernels are
 // instantiated per bit width in lowbit_gemv_rows_b{2,3,4}.cu (no relocatable
@@ -65,10 +66,12 @@ constexpr int kRowsMaxStages = 512;
 static __device__ int g_rows_timeout = 0;
 
 __host__ __device__ constexpr int rows_row_bytes(int bits) { return bits == 4 ? 64 : (bits == 3 ? 48 : 32); }
-// k-blocks per unit (TMA box): int4 boxes carry two 128-code k-blocks per row
-// (128 B, 128-byte swizzle), halving the boxes a CTA issues.
-__host__ __device__ constexpr int rows_kpu(int bits) { return bits == 4 ? 2 : 1; }
-__host__ __device__ constexpr int rows_unit_bytes(int bits) { return rows_row_bytes(bits) * rows_kpu(bits); }
+// k-blocks per unit (TMA box): int4 boxes of row groups up to 64 rows carry two
+// 128-code k-blocks per row (128 B, 128-byte swizzle), halving the boxes a CTA
+// issues; larger row groups keep one k-block per row (64 B, 64-byte swizzle)
+// so that a ring of at least kRowsWarps stages fits in half an SM.
+__host__ __device__ constexpr int rows_kpu(int bits, int br) { return (bits == 4 && br <= 64) ? 2 : 1; }
+__host__ __device__ constexpr int rows_unit_bytes(int bits, int br) { return rows_row_bytes(bits) * rows_kpu(bits, br); }
 __host__ __device__ inline int rows_nt(int m) { return (2 * m + 7) / 8; }
 __host__ __device__ inline int rows_lanes(int m) { return 4 * (2 * m < 8 ? 2 * m : 8); }
 __host__ __device__ inline uint32_t rows_align(uint32_t v, uint32_t a) { return (v + a - 1u) & ~(a - 1u); }
@@ -90,7 +93,7 @@ struct RowsSmem {
 __host__ __device__ inline RowsSmem rows_smem_plan(int bits, int m, int kbt, int br, int ns, int srow_bytes,
                                                    bool has_s, bool has_zp, bool swiglu) {
     RowsSmem s;
-    uint32_t o = (uint32_t)ns * (uint32_t)br * (uint32_t)rows_unit_bytes(bits);
+    uint32_t o = (uint32_t)ns * (uint32_t)br * (uint32_t)rows_unit_bytes(bits, br);
     o = rows_align(o, 128u);
     s.sbuf = o;
     if (has_s) o += 2u * (uint32_t)br * (uint32_t)srow_bytes;
@@ -150,8 +153,8 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                         const __grid_constant__ CUtensorMap zmap, const __grid_constant__ GemvParams p,
                         const RowsGeom geo) {
     constexpr int RB = rows_row_bytes(BITS);
-    constexpr int KPU = rows_kpu(BITS);
-    constexpr int UB = rows_unit_bytes(BITS);
+    constexpr int KPU = rows_kpu(BITS, 16 * NB);
+    constexpr int UB = rows_unit_bytes(BITS, 16 * NB);
     constexpr bool SWIGLU = EPI == kEpiSwiGLU;
     constexpr int S = SWIGLU ? 2 : 1;   // physical groups per row group (gate, up)
     constexpr int SZB = SZ16 ? 2 : 4;
@@ -526,7 +529,13 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             };
             // One unit per step, in order: units are issued in order and each
             // warp consumes its own in order, so the oldest unconsumed unit is
-            // always issued and the ring cannot stall.
+            // always issued and the ring cannot stall.  The parity waits need
+            // a ring of at least kRowsWarps stages whenever it wraps (the host
+            // plan guarantees it): the previous occupant of unit u's stage is
+            // then unit u - NS <= u - kRowsWarps, an earlier unit of this same
+            // warp, so the stage's full barrier is never more than one phase
+            // behind the phase awaited.  With fewer stages a warp could await a
+            // phase two ahead, which the parity test reports as complete.
             for (int t = 0; t < q_per_warp; ++t) {
                 const int ku = kRowsWarps * t + warp;   // unit (k-blocks ku*KPU ...)
                 const int cur = stage;

@@ -40,7 +40,9 @@ static cudaError_t launch_rows_nb(const CUtensorMap& wm, const CUtensorMap& sm, 
         case 1: return launch_rows_k<BITS, NT, UNS, EPI, SZ16, 1>(wm, sm, zm, p, geo, smem, st, pdl);
         case 2: return launch_rows_k<BITS, NT, UNS, EPI, SZ16, 2>(wm, sm, zm, p, geo, smem, st, pdl);
         case 3: return launch_rows_k<BITS, NT, UNS, EPI, SZ16, 3>(wm, sm, zm, p, geo, smem, st, pdl);
-        default: return launch_rows_k<BITS, NT, UNS, EPI, SZ16, 4>(wm, sm, zm, p, geo, smem, st, pdl);
+        case 4: return launch_rows_k<BITS, NT, UNS, EPI, SZ16, 4>(wm, sm, zm, p, geo, smem, st, pdl);
+        case 5: return launch_rows_k<BITS, NT, UNS, EPI, SZ16, 5>(wm, sm, zm, p, geo, smem, st, pdl);
+        default: return launch_rows_k<BITS, NT, UNS, EPI, SZ16, 6>(wm, sm, zm, p, geo, smem, st, pdl);
     }
 }
 

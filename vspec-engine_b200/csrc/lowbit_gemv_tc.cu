@@ -383,7 +383,10 @@ lowbit_gemv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
                                 words[2 * c8] = v.x; words[2 * c8 + 1] = v.y;
                             }
                         }
-                        mbar_arrive(&empty[ring]);
+                        // released after the TMEM store below has consumed the
+                        // words (a release right after the loads let the refill
+                        // land before the loads had read the stage)
+                        const int stage_used = ring;
                         if (++ring == NS) { ring = 0; ring_ph ^= 1u; }
                         if ((i & 1) == half) {
                             // scale / zero-point of this row and k-block's group, as
@@ -409,6 +412,7 @@ lowbit_gemv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_con
                                 unpack_mm<BITS, UNSIGNED>(ch, mm, hv[16 * cc + 2 * mm], hv[16 * cc + 2 * mm + 1]);
                         }
                         tmem_st_x32(tmem_base + lane_off + (uint32_t)(64 * a + 32 * half), hv);
+                        mbar_arrive(&empty[stage_used]);
                         if (++c_kb == kbt) { c_kb = 0; ++c_tile; }
                     }
                 }

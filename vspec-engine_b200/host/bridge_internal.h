@@ -63,6 +63,9 @@ typedef struct VbCacheEntry {
 VbCacheEntry* vb_weight_cache(int bits, const void* w, size_t bytes_w, const float* s, size_t bytes_s,
                               const float* zp, size_t bytes_zp, int want_zp, const char* cap_env);
 
+/* Sets the thread-local message vspec_b200_last_error() returns. */
+void vb_set_error(const char* fmt, ...);
+
 int vb_env_flag(const char* name, int fallback);
 float vb_env_float(const char* name, float fallback);
 size_t vb_env_size(const char* name, size_t fallback);

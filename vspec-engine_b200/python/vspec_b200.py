@@ -130,6 +130,9 @@ _sigs = {
     "vspec_b200_paged_attention_workspace_bytes": ([c_size_t] * 5, c_size_t),
     "vspec_b200_paged_attention": ([POINTER(PagedAttnArgs), c_void_p], c_int),
     "vspec_b200_paged_attention_page_fault": ([POINTER(c_int)], c_int),
+    "vspec_b200_kv_paged_sync": ([c_void_p, c_int, c_void_p, c_void_p, c_uint64, POINTER(c_uint64), c_void_p], c_int),
+    "vspec_b200_kv_paged_session_view": ([c_void_p, c_uint64, c_int, c_void_p, c_void_p, c_size_t, c_size_t, c_void_p,
+                                          c_size_t, c_void_p, POINTER(c_size_t), POINTER(c_size_t), c_void_p], c_int),
     "vspec_b200_q4k_linear": ([c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_void_p], c_int),
     "vspec_b200_anf_hybrid_linear": ([c_void_p] * 8 + [c_size_t] * 5 + [c_void_p], c_int),
     "vspec_b200_refine_hot_int4": ([c_void_p] * 6 + [c_size_t] * 5 + [c_void_p], c_int),
