@@ -1,6 +1,6 @@
 """Benchmark of the low-bit decode hot path on B200.
 
-Default workload (M=1 points; the metric's "W4/W3
+Default workload (the dequant-matmul sweep's M=1 point; the metric's "W4/W3
 dequant-GEMV GB/s vs HBM peak"): y = W x with W packed int4 (and int3),
 K=4096, N=12288, group 128 along K, fp16 scales, zero-point at mid-range
 (unsigned-code reading), fp32 x ~N(0,1), fp32 y.  A *step* is one GEMV over
@@ -424,7 +424,7 @@ ATTN_B, ATTN_HQ, ATTN_HKV, ATTN_D, ATTN_PT = 32, 32, 8, 128, 16
 
 
 def make_config3(torch, seed: int = 3):
-    """B=32, Hq=32, Hkv=8, d=128, ctx ~U[512,8192], 16-token
+    """Paged attention workload: B=32, Hq=32, Hkv=8, d=128, ctx ~U[512,8192], 16-token
     pages of fp16 K/V ~N(0,1), page table = seeded permutation of the shared pool."""
     rng = np.random.default_rng(seed)
     ctx = rng.integers(512, 8193, size=ATTN_B).astype(np.int32)
@@ -558,7 +558,7 @@ def decode_bytes_per_step(cfg: dict, batch: int, ctx: int) -> int:
 
 
 def time_decode(torch, V, world: int, rank: int, peak: float):
-    """Qwen3-8B shape, W4 group 128, random-init, prompts of
+    """Qwen3-8B-shape decode: W4 group 128, random-init, prompts of
     512 random ids, 256 greedy tokens; batch 1 (every rank its own sequence) and
     batch 64 sharded over the ranks.  tok/s over the generation phase (device
     time, max over ranks)."""
@@ -681,7 +681,7 @@ def tp_step_work(cfg: dict, batch: int, ctx: int, tp: int) -> dict:
 
 
 def time_decode_tp(torch, V, world: int, rank: int, peaks: dict):
-    """Qwen3-32B shape, attention projections and lm_head
+    """Qwen3-32B-shape decode: attention projections and lm_head
     W4, MLP W3, group 128, random-init; batch 256 sequences of 1024 seeded
     random prompt ids (prefilled by decode steps) + 128 greedy tokens,
     tensor-parallel over all ranks (NCCL all-reduce after o-proj and down).
@@ -1022,7 +1022,7 @@ def main() -> None:
         "warmup": args.warmup, "ms_per_step": round(ms4 / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes x int8 activation parts, int32 dots, fp32 acc",
         "data": "synthetic (seeded)",
-        "config": {"workload": "W4 GEMV K=4096 N=12288 M=1 g128 fp16 scales mid zp (configs[1] M=1)",
+        "config": {"workload": "W4 GEMV K=4096 N=12288 M=1 g128 fp16 scales mid zp",
                    "step": f"{args.copies} GEMVs over distinct weight copies, one CUDA graph",
                    "l2": f"inputs > L2: {args.copies} x {b4 / 1e6:.1f} MB", "parallelism": f"dp{world} replicas"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

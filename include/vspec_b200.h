@@ -370,7 +370,7 @@ int vspec_b200_quantize_rowwise(const float* d_w, size_t n, size_t k, int bits, 
                                 uint8_t* d_packed, float* d_scales, float* d_zero_points, void* stream);
 
 /* ------------------------------------------------------------------------
- * Qwen3-shape low-bit decode loop, random-init weights.
+ * Qwen3-shape low-bit decode loop (36 or 64 layers, hidden 4096 / 5120), random-init weights.
  * Host C driving the kernels above, the low-bit linears (RMSNorm / SwiGLU /
  * residual fused) and the paged attention; one decode step = one CUDA graph.
  * Linear weights: packed `bits`-bit codes (unsigned reading, mid-range

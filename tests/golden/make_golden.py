@@ -25,11 +25,13 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("VSPEC_REFERENCE", "/root/reference")
+REF = os.environ.get("VSPEC_REFERENCE", "")
 OUT = os.path.dirname(os.path.abspath(__file__))
 
 
 def main() -> None:
+    if not REF or not os.path.isdir(os.path.join(REF, "Vspec-chat", "python")):
+        sys.exit("set VSPEC_REFERENCE to the Vspec-Engine source tree (its Vspec-chat/python modules make the fixtures)")
     sys.path.insert(0, os.path.join(REF, "Vspec-chat", "python"))
     os.environ["VSPEC_INT4_BLOCKWISE_ENABLE"] = "1"
     os.environ["VSPEC_INT4_BLOCK_SIZE"] = "128"

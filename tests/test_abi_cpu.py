@@ -61,7 +61,7 @@ def test_struct_layouts_match_reference_headers():
 def test_c_header_compiles_against_reference_headers(tmp_path):
     """vspec_b200_compat.h must coexist with the reference's own headers (it
     reuses their struct definitions when they are included first)."""
-    ref_inc = os.path.join(os.environ.get("VSPEC_REFERENCE", "/root/reference"), "include")
+    ref_inc = os.path.join(os.environ.get("VSPEC_REFERENCE", ""), "include")
     if not os.path.isdir(ref_inc):
         pytest.skip("reference headers not present")
     src = tmp_path / "t.c"
@@ -125,7 +125,7 @@ def test_reference_python_bridge_binds_library(tmp_path):
     import shutil
     import subprocess
     import sys
-    ref = os.environ.get("VSPEC_REFERENCE", "/root/reference")
+    ref = os.environ.get("VSPEC_REFERENCE", "")
     src = os.path.join(ref, "Vspec-chat", "python", "vspec_cuda_bridge.py")
     if not os.path.exists(src):
         pytest.skip("reference tree not present")
@@ -244,7 +244,7 @@ def test_compat_declarations_agree_with_reference_kernel_headers(tmp_path):
     declares (the hybrid and refine launchers among them) must have the same
     signature: one translation unit includes both, and gcc rejects conflicting
     declarations."""
-    ref_inc = os.path.join(os.environ.get("VSPEC_REFERENCE", "/root/reference"), "include")
+    ref_inc = os.path.join(os.environ.get("VSPEC_REFERENCE", ""), "include")
     if not os.path.isfile(os.path.join(ref_inc, "vspec", "kernel", "cuda_fused.h")):
         pytest.skip("reference headers not present")
     src = tmp_path / "t2.c"
@@ -262,7 +262,7 @@ def test_bridge_declarations_agree_with_reference_bridge(tmp_path):
     (its prototypes read as text) is declared by vspec_b200_compat.h with the
     same signature: the reference prototypes are compiled after the compat
     header in one translation unit."""
-    ref = os.environ.get("VSPEC_REFERENCE", "/root/reference")
+    ref = os.environ.get("VSPEC_REFERENCE", "")
     path = os.path.join(ref, "src", "python", "cuda_bridge.c")
     if not os.path.isfile(path):
         pytest.skip("reference tree not present")
@@ -278,3 +278,23 @@ def test_bridge_declarations_agree_with_reference_bridge(tmp_path):
                    + "\n".join(protos.values()) + "\nint main(void){return 0;}\n")
     rc = os.system(f"gcc -std=gnu11 -Wall -Werror -c -I{ROOT}/include {src} -o {tmp_path}/t3.o")
     assert rc == 0
+
+
+def test_compat_paged_cache_layout_matches_reference(tmp_path):
+    """The VspecKVPagedCache restated in vspec_b200_compat.h (read by
+    vspec_b200_kv_paged_sync / _session_view) has the reference's size and
+    member offsets (include/vspec/attention/kv_paged_cache.h:20-49)."""
+    import oracle as O
+    if O.REF is None:
+        pytest.skip("oracle/_ref not built")
+    src = tmp_path / "p.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "vspec_b200_compat.h"\n'
+                   'int main(void){printf("%zu %zu %zu", sizeof(VspecKVPagedCache), '
+                   'offsetof(VspecKVPagedCache, sessions), offsetof(VspecKVPagedCache, page_meta)); return 0;}\n')
+    exe = tmp_path / "p"
+    assert os.system(f"gcc -std=gnu11 -Wall -Werror -I{ROOT}/include {src} -o {exe}") == 0
+    import subprocess
+    size, off_s, off_p = map(int, subprocess.check_output([str(exe)]).split())
+    assert size == O.REF.ref_sizeof_kv_paged_cache()
+    assert off_s == O.REF.ref_offsetof_paged_sessions()
+    assert off_p == O.REF.ref_offsetof_paged_page_meta()

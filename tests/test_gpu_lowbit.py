@@ -526,6 +526,52 @@ def test_ring_split_k_merge_back_to_back(k):
     assert flag.value == 0
 
 
+@pytest.mark.parametrize("m,n,k,bits,flags", [(1, 12288, 4096, 4, 0), (4, 24576, 4096, 4, 0x10), (2, 12288, 4096, 3, 0),
+                                              (1, 6144, 4096, 2, 0)])
+def test_rows_ring_wrap_back_to_back(m, n, k, bits, flags):
+    """Row-sliced GEMV shapes whose shared-memory ring wraps (fewer stages than
+    units), 32 launches back to back in a CUDA graph, replayed 3 times: every
+    launch matches the oracle and no bounded wait gives up.  A ring whose stage
+    count is not a multiple of the 8 consumer warps let a warp's parity wait
+    pass one phase early when TMA copies landed out of order (a timeout in a
+    few thousand launches)."""
+    torch = torch_cuda()
+    import ctypes
+    rng = np.random.default_rng(n + m + bits)
+    g, reps = k // 128, 32
+    w, s, _ = make_lowbit(rng, n, k, bits, g, sz_f16=True, zp_mode="none")
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    full = O.lowbit_matmul(x, w, n, k, bits, s, None, g).astype(np.float64)
+    swiglu = bool(flags & V.F_SWIGLU)
+    ref = full[:, : n // 2] / (1.0 + np.exp(-full[:, : n // 2])) * full[:, n // 2:] if swiglu else full
+    out_cols = n // 2 if swiglu else n
+    dx, dw, ds = to_dev(x), to_dev(w), to_dev(s)
+    ys = [empty_dev((m, out_cols), torch.float32) for _ in range(reps)]
+    st = torch.cuda.Stream()
+
+    def step():
+        for y in ys:
+            V.lowbit_linear(dx.data_ptr(), dw.data_ptr(), ds.data_ptr(), None, y.data_ptr(), m, n, k, g, bits,
+                            flags=V.F_SZ_F16 | flags, stream=st.cuda_stream, path=V.PATH_ROWS)
+    with torch.cuda.stream(st):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        step()
+    for _ in range(3):
+        for y in ys:
+            y.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        errs = [rel_err(y.cpu().numpy(), ref) for y in ys]
+        assert max(errs) <= RTOL_F32, [f"{e:.1e}" for e in errs]
+    del graph
+    flag = ctypes.c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(ctypes.byref(flag)), "timeout flag")
+    assert flag.value == 0
+
+
 # ---------------------------------------------------------------- tcgen05 GEMM (m > 8)
 def test_gemm_tcgen05_smoke():
     """One small launch of the tcgen05 GEMM on its own (fp16 operands, tolerance RTOL_BF16)."""

@@ -280,13 +280,50 @@ extern "C" int vspec_b200_mul_f32(float* d, const float* o, size_t n, void* stre
 // ============================================================================
 namespace vb200 {
 
-// Contiguous fp32 K/V [T][H][d] already on the device: a single page of T tokens.
+// Per host thread and device: grow-only device buffers and a stream for the
+// host-array attention entry points (the reference keeps grow-only static
+// buffers too, attention_fused.cu:160-195); allocating and freeing them on
+// every call cost ~10 ms per call in synchronising cudaFree.
+struct AttnHostState {
+    float *q, *k, *v, *out;
+    int32_t* meta;   // [0] page table = {0}, [1] context length
+    size_t cap_q, cap_kv;
+    cudaStream_t st;
+};
+static thread_local AttnHostState g_attn_host[64];
+
+static bool grow(float** p, size_t* cap, size_t bytes) {
+    if (*cap >= bytes) return true;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    if (cudaMalloc(p, bytes) != cudaSuccess) { *p = nullptr; return false; }
+    *cap = bytes;
+    return true;
+}
+
+static AttnHostState* attn_host_state(size_t qb, size_t kvb) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    AttnHostState& h = g_attn_host[dev];
+    if (!h.st && cudaStreamCreateWithFlags(&h.st, cudaStreamNonBlocking) != cudaSuccess) { h.st = nullptr; return nullptr; }
+    if (!h.meta && cudaMalloc(&h.meta, 2 * sizeof(int32_t)) != cudaSuccess) { h.meta = nullptr; return nullptr; }
+    size_t cq = h.cap_q, ckv = h.cap_kv, cq2 = h.cap_q, ckv2 = h.cap_kv;
+    if (!grow(&h.q, &cq, qb) || !grow(&h.out, &cq2, qb)) { h.cap_q = 0; return nullptr; }
+    if (!grow(&h.k, &ckv, kvb) || !grow(&h.v, &ckv2, kvb)) { h.cap_kv = 0; return nullptr; }
+    h.cap_q = cq < cq2 ? cq : cq2;
+    h.cap_kv = ckv < ckv2 ? ckv : ckv2;
+    return &h;
+}
+
+// Contiguous fp32 K/V [T][H][d] already on the device: a single page of T
+// tokens; d_meta holds two ints of device scratch for the page table and the
+// context length.
 static int attention_contiguous_dev(const float* d_q, const float* d_k, const float* d_v, size_t T, size_t H, size_t d,
-                                    float* d_out, cudaStream_t st) {
-    int32_t* d_meta = nullptr;  // [0] page table = {0}, [1] ctx = T
-    if (cudaMalloc(&d_meta, 2 * sizeof(int32_t)) != cudaSuccess) return VSPEC_B200_ERR_NOMEM;
+                                    float* d_out, int32_t* d_meta, cudaStream_t st) {
     const int32_t meta[2] = {0, (int32_t)T};
-    cudaMemcpyAsync(d_meta, meta, sizeof(meta), cudaMemcpyHostToDevice, st);
+    cudaError_t e = cudaMemcpyAsync(d_meta, meta, sizeof(meta), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_status(e, "attention metadata upload");
     VspecB200PagedAttnArgs a;
     memset(&a, 0, sizeof(a));
     a.d_q = d_q;
@@ -305,28 +342,25 @@ static int attention_contiguous_dev(const float* d_q, const float* d_k, const fl
     a.max_ctx = T;
     a.scale = 1.0f / sqrtf((float)d);
     a.kv_dtype = VSPEC_B200_KV_F32;
-    int rc = vspec_b200_paged_attention(&a, st);
-    cudaStreamSynchronize(st);
-    cudaFree(d_meta);
+    const int rc = vspec_b200_paged_attention(&a, st);
+    e = cudaStreamSynchronize(st);   // `meta` lives on this stack frame
+    if (rc == VSPEC_B200_OK && e != cudaSuccess) return cuda_status(e, "attention");
     return rc;
 }
 
 // Host arrays in, host array out (synchronous), like the reference launchers.
 static void attention_host(const float* q, const float* k, const float* v, size_t T, size_t H, size_t d, float* out) {
     if (!q || !k || !v || !out || T == 0 || H == 0 || d == 0) return;
-    float *dq = nullptr, *dk = nullptr, *dv = nullptr, *dout = nullptr;
     const size_t kvb = T * H * d * sizeof(float), qb = H * d * sizeof(float);
-    if (cudaMalloc(&dq, qb) != cudaSuccess || cudaMalloc(&dk, kvb) != cudaSuccess || cudaMalloc(&dv, kvb) != cudaSuccess ||
-        cudaMalloc(&dout, qb) != cudaSuccess) {
-        cudaFree(dq); cudaFree(dk); cudaFree(dv); cudaFree(dout);
+    AttnHostState* h = attn_host_state(qb, kvb);
+    if (!h) return;
+    if (cudaMemcpyAsync(h->q, q, qb, cudaMemcpyHostToDevice, h->st) != cudaSuccess ||
+        cudaMemcpyAsync(h->k, k, kvb, cudaMemcpyHostToDevice, h->st) != cudaSuccess ||
+        cudaMemcpyAsync(h->v, v, kvb, cudaMemcpyHostToDevice, h->st) != cudaSuccess)
         return;
+    if (attention_contiguous_dev(h->q, h->k, h->v, T, H, d, h->out, h->meta, h->st) == VSPEC_B200_OK) {
+        if (cudaMemcpyAsync(out, h->out, qb, cudaMemcpyDeviceToHost, h->st) == cudaSuccess) cudaStreamSynchronize(h->st);
     }
-    cudaMemcpy(dq, q, qb, cudaMemcpyHostToDevice);
-    cudaMemcpy(dk, k, kvb, cudaMemcpyHostToDevice);
-    cudaMemcpy(dv, v, kvb, cudaMemcpyHostToDevice);
-    if (attention_contiguous_dev(dq, dk, dv, T, H, d, dout, nullptr) == VSPEC_B200_OK)
-        cudaMemcpy(out, dout, qb, cudaMemcpyDeviceToHost);
-    cudaFree(dq); cudaFree(dk); cudaFree(dv); cudaFree(dout);
 }
 
 }  // namespace vb200
@@ -384,7 +418,8 @@ extern "C" void vspec_cuda_launch_attention_fused(VspecKernelContext* ctx) {
                                                           cache->blocks_per_head, cache->block_size);
         dequant_int3_kv_kernel<<<grid1d(rows * d), 256>>>(dvq, dvs, dv, rows, d, cache->packed_head_bytes,
                                                           cache->blocks_per_head, cache->block_size);
-        if (attention_contiguous_dev(dq, dk, dv, T, H, d, dout, nullptr) == VSPEC_B200_OK)
+        AttnHostState* h = attn_host_state(qb, 0);
+        if (h && attention_contiguous_dev(dq, dk, dv, T, H, d, dout, h->meta, nullptr) == VSPEC_B200_OK)
             cudaMemcpy(ctx->output, dout, qb, cudaMemcpyDeviceToHost);
     }
     cudaFree(dkq); cudaFree(dvq); cudaFree(dks); cudaFree(dvs);

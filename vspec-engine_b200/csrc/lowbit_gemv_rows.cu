@@ -29,7 +29,7 @@ static int make_scale_map(CUtensorMap* map, const void* base, int rows, int n_gr
 }
 
 // One CTA per SM per launch, each in at most half an SM
-// (VSPEC_B200_GEMV_ROWS_PAIR: "1" on, off otherwise): the CTAs of the next
+// (VSPEC_B200_GEMV_ROWS_PAIR: default on, "0" off): the CTAs of the next
 // launch in the stream then fit beside this launch's and start streaming their
 // weights as soon as programmatic dependent launch lets them in, instead of
 // after this launch's CTAs exit.
@@ -37,7 +37,7 @@ static bool rows_pair_mode() {
     static int v = -1;
     if (v < 0) {
         const char* e = getenv("VSPEC_B200_GEMV_ROWS_PAIR");
-        v = (e && e[0] == '1') ? 1 : 0;
+        v = (e && e[0] == '0') ? 0 : 1;
     }
     return v == 1;
 }
@@ -46,9 +46,8 @@ static bool rows_pair_mode() {
 // wins: (pair mode) one CTA per SM in half an SM, row groups up to 96 rows;
 // two CTAs per SM in half an SM each; one CTA per SM in a whole SM; the last
 // two with row groups up to 64 rows.  The row group holds all of a CTA's rows.
-// The ring holds every unit of the busiest CTA, or wraps with at least
-// kRowsWarps stages (required by the parity waits, see the kernel) and 24 KB
-// in flight.
+// The ring holds every unit of the busiest CTA, or wraps with at least one
+// stage per consumer warp and 24 KB in flight.
 static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo, size_t* smem) {
     const int m = p.m, kbt = p.k / 128;
     const int n_out = swiglu ? p.n / 2 : p.n;
@@ -88,7 +87,7 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
             const int most = ((rmax + br - 1) / br) * S * kut;   // the busiest CTA's units
             if (ns > most) ns = most;
             if (ns > kRowsMaxStages) ns = kRowsMaxStages;
-            // a ring that wraps needs kRowsWarps stages; and >= 24 KB in
+            // a ring that wraps keeps a stage per consumer warp and >= 24 KB in
             // flight per CTA (or everything); else smaller row groups (or the
             // next candidate)
             const uint64_t want = (uint64_t)most * stage < 24576u ? (uint64_t)most * stage : 24576u;
@@ -130,15 +129,16 @@ bool gemv_rows_supported(const GemvParams& p, int bits) {
 }
 
 // Where the row-sliced kernel beats the split-K ring kernel (measured on B200,
-// back-to-back launches over weights larger than L2, us per launch, ring ->
-// rows): one activation row, int4 or int3, k <= 4096, e.g. int4 k = 4096 with
-// n = 4096: 7.11 -> 5.69, n = 6144: 7.66 -> 7.01, n = 12288: 10.63 -> 9.51,
-// SwiGLU n = 24576: 15.92 -> 13.66; int3 n = 12288: 12.18 -> 10.95.  Deeper
-// rows (k = 12288: 11.9 -> 14.1) and several activation rows (m = 4: 11.5 ->
-// 14.8) stay on the ring kernel, as do shapes with more than one row group per
-// CTA (refused by the planner).
+// back-to-back launches in a CUDA graph over weights larger than L2, us per
+// launch, ring -> rows with one CTA per SM per launch): one activation row,
+// k <= 4096, e.g. int4 k = 4096 with n = 4096: 7.23 -> 5.44, n = 6144:
+// 8.69 -> 5.89, n = 12288: 10.6 -> 9.18; int3 n = 12288: 12.2 -> 9.93; int2
+// n = 12288: 9.71 -> 7.50.  Deeper rows (k = 12288: 12.3 -> 14.4) and several
+// activation rows (m = 4: 11.6 -> 15.0) stay on the ring kernel, as do shapes
+// with more than one row group per CTA.
 bool gemv_rows_preferred(const GemvParams& p, int bits) {
-    if (p.m != 1 || bits < 3 || p.k > 4096) return false;
+    if (p.m != 1 || p.k > 4096) return false;
+    if (bits == 2 && !rows_pair_mode()) return false;   // int2 gains only with one CTA per SM
     return gemv_rows_supported(p, bits);
 }
 

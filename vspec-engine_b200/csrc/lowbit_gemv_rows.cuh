@@ -116,7 +116,7 @@ __host__ __device__ inline RowsSmem rows_smem_plan(int bits, int m, int kbt, int
     o = rows_align(o, 8u);
     s.bars = o;                     // full[ns], empty[ns], sfull[2], sempty[2]
     o += (2u * (uint32_t)ns + 4u) * 8u;
-    s.misc = o;                     // abort flag, row norms [8]
+    s.misc = o;                     // abort flag, row norms [8], units issued
     o += 64u;
     s.total = o;
     return s;
@@ -143,6 +143,18 @@ __device__ __forceinline__ void rows_lds_chunk(Chunk<BITS>& ch, const unsigned c
         const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
         ch.w[0] = q[0]; ch.w[1] = q[1]; ch.w[2] = q[2];
     }
+}
+
+// Bounded wait until the producer thread has issued at least `want` units
+// (a volatile shared-memory counter it raises after every copy).
+__device__ __forceinline__ bool wait_issued(volatile int* issued, int want, volatile int* abort) {
+    if (*issued >= want) return true;
+    for (uint32_t i = 0; i < kRowsWaitLimit * 64u; ++i) {
+        __nanosleep(64);
+        if (*issued >= want) return true;
+        if (*abort) return false;
+    }
+    return false;
 }
 
 // NB = 16-row blocks per row group (BR = 16 * NB): a warp's partial sums of
@@ -185,6 +197,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
     uint64_t* sempty = sfull + 2;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base + plan.misc);
     float* row_norm = reinterpret_cast<float*>(base + plan.misc) + 4;   // [8]
+    volatile int* issued = reinterpret_cast<volatile int*>(base + plan.misc) + 12;   // units the producer issued
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -211,6 +224,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             mbar_init(&sempty[b], kRowsWarps);
         }
         *abort_flag = 0;
+        *issued = 0;
         mbar_fence_init();
     }
     __syncthreads();
@@ -251,6 +265,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                 }
                 mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
                 tma_load_2d(wring + (size_t)stage * STAGE_BYTES, &wmap, kb * UB, row, &full[stage]);
+                *issued = u + 1;
                 if (++stage == NS) { stage = 0; ++use; }
                 if (++kb == kut) {
                     kb = 0;
@@ -529,19 +544,23 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             };
             // One unit per step, in order: units are issued in order and each
             // warp consumes its own in order, so the oldest unconsumed unit is
-            // always issued and the ring cannot stall.  The parity waits need
-            // a ring of at least kRowsWarps stages whenever it wraps (the host
-            // plan guarantees it): the previous occupant of unit u's stage is
-            // then unit u - NS <= u - kRowsWarps, an earlier unit of this same
-            // warp, so the stage's full barrier is never more than one phase
-            // behind the phase awaited.  With fewer stages a warp could await a
-            // phase two ahead, which the parity test reports as complete.
+            // always issued and the ring cannot stall.  Before the parity wait
+            // on a unit's stage a warp checks that the producer has issued the
+            // unit: the producer issues unit u only after the stage's previous
+            // occupant, unit u - NS, was consumed (so it had landed), hence the
+            // stage's full barrier is then at most one phase behind the phase
+            // awaited.  Without that check, a stage whose previous occupant
+            // belongs to another warp and is still in flight (TMA copies land
+            // out of order) passes the parity test one phase early.
             for (int t = 0; t < q_per_warp; ++t) {
                 const int ku = kRowsWarps * t + warp;   // unit (k-blocks ku*KPU ...)
                 const int cur = stage;
                 const uint32_t cur_ph = (uint32_t)(use & 1);
                 stage += kRowsWarps;
                 while (stage >= NS) { stage -= NS; ++use; }
+                // the unit must have been issued before its stage's parity is
+                // tested (see above); usually it long has been
+                if (ok && !wait_issued(issued, pg * kut + ku + 1, abort_flag)) ok = false;
                 if (ok && !mbar_wait_sleep(&full[cur], cur_ph, abort_flag, kRowsWaitLimit, kRowsSleepNs)) ok = false;
                 if (!ok) continue;
                 unit_math(wring + (size_t)cur * STAGE_BYTES, ku, acc);

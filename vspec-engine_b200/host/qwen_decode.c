@@ -1,5 +1,5 @@
 /* qwen_decode.c -- Qwen3-shape low-bit decode loop on the B200 kernels
- * (BASELINE configs 4 and 5; the reference's GenericTransformerRuntime
+ * (Qwen3-8B and Qwen3-32B layer shapes; the reference's GenericTransformerRuntime
  * ._forward_token, Vspec-chat/python/runtime_inference.py:1245-1500, Qwen
  * profile).
  *

@@ -41,12 +41,12 @@ class QwenConfig(ctypes.Structure):
                 ("bits_mlp", c_int)]
 
 
-# BASELINE config 4 (Qwen3-8B shape, W4 group 128)
+# Qwen3-8B shape: 36 layers, hidden 4096, 32/8 heads x 128, SwiGLU 12288, W4 group 128
 QWEN3_8B = dict(num_layers=36, hidden=4096, num_heads=32, num_kv_heads=8, head_dim=128, intermediate=12288,
                 vocab=151936, bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16,
                 bits_mlp=0)
 
-# BASELINE config 5 (Qwen3-32B shape; attention projections and lm_head W4, MLP W3, group 128)
+# Qwen3-32B shape: 64 layers, hidden 5120, 64/8 heads x 128, SwiGLU 25600; attention and lm_head W4, MLP W3
 QWEN3_32B = dict(num_layers=64, hidden=5120, num_heads=64, num_kv_heads=8, head_dim=128, intermediate=25600,
                  vocab=151936, bits=4, group=128, rms_eps=1e-6, rope_theta=1e6, logit_clip=24.0, page_tokens=16,
                  bits_mlp=3)
