@@ -58,7 +58,8 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
     struct Cand { int per_sm; uint32_t budget; int brmax; };
     Cand cands[3];
     int nc = 0;
-    if (rows_pair_mode()) cands[nc++] = Cand{1, kRowsSmemShared, 16 * kRowsMaxNB};
+    // (SwiGLU gate/up pairs measured slower in it: n = 24576, k = 4096 went 15.5 -> 17.4 us)
+    if (rows_pair_mode() && !swiglu) cands[nc++] = Cand{1, kRowsSmemShared, 16 * kRowsMaxNB};
     cands[nc++] = Cand{2, kRowsSmemShared, 64};
     cands[nc++] = Cand{1, kRowsSmemMax, 64};
     for (int ci = 0; ci < nc; ++ci) {
