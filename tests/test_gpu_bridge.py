@@ -225,3 +225,29 @@ def test_allocation_failure_makes_bridges_fail_closed():
     out = np.zeros(n, dtype=np.float32)
     assert V.lib.vspec_cuda_fused_linear_int4_cached_bridge(x.ctypes.data, 1, k, h, n, out.ctypes.data) == 1
     assert rel_err(out, O.lowbit_matmul(x, w, n, k, 4, s, zp, 2)[0]) <= RTOL_F32
+
+
+def test_cached_bridge_graph_replays_follow_inputs_and_m():
+    """A registered weight's call runs directly first, then as one captured
+    graph (upload, linear, download): consecutive calls with new activations,
+    a change of activation count (recapture) and back all match the oracle,
+    and the stats count every call as a hit."""
+    torch_cuda()
+    rng = np.random.default_rng(404)
+    n, k, g = 2048, 4096, 32
+    w = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+    s = rng.uniform(0.005, 0.02, size=(n, g)).astype(np.float32)
+    zp = rng.uniform(-2.0, 2.0, size=(n, g)).astype(np.float32)
+    h = V.lib.vspec_cuda_fused_linear_int4_register_weight_bridge(w.ctypes.data, s.ctypes.data, zp.ctypes.data, k, n,
+                                                                   g)
+    assert h > 0
+    before = [ctypes.c_uint64() for _ in range(6)]
+    V.lib.vspec_cuda_int4_cached_stats_bridge(*[ctypes.byref(c) for c in before])
+    for m in (1, 1, 1, 3, 3, 1, 1):
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        out = np.full((m, n), np.nan, dtype=np.float32)
+        assert V.lib.vspec_cuda_fused_linear_int4_cached_bridge(x.ctypes.data, m, k, h, n, out.ctypes.data) == 1
+        assert rel_err(out, O.lowbit_matmul(x, w, n, k, 4, s, zp, g)) <= RTOL_F32, m
+    after = [ctypes.c_uint64() for _ in range(6)]
+    V.lib.vspec_cuda_int4_cached_stats_bridge(*[ctypes.byref(c) for c in after])
+    assert after[1].value - before[1].value == 7   # hits
