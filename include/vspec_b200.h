@@ -228,6 +228,24 @@ size_t vspec_b200_paged_attention_workspace_bytes(size_t batch, size_t num_q_hea
                                                   size_t head_dim, size_t max_ctx);
 int vspec_b200_paged_attention(const VspecB200PagedAttnArgs* args, void* stream);
 
+/* The CPU backend's attention with its semantics (replaces the device side of
+ * vspec_attention_ref_single_query, src/attention/attention_ref.c:7-88, reached
+ * through the CPU backend's launch_attention, src/kernel/cpu/cpu_backend.c:29-46):
+ * contiguous fp32 q [heads][head_dim] and K/V [tokens][heads][head_dim] (no GQA),
+ * q and each k row clamped to +-max(1e-6, 4.5 * population std), softmax with a
+ * double denominator, output summed in double.  three_bit_module: 1 = the 3-bit
+ * runtime module's arithmetic (src/runtime/three_bit_runtime_modules.c:138-361:
+ * noise reducer, block-normalised Kahan dot, qk-scale and logit clips, Kahan
+ * output), 0 = without it, -1 = decided from VSPEC_FUSED_BITS /
+ * VSPEC_3BIT_RUNTIME_MODULE at call time as the reference does.  block_size: the
+ * module's dot block, 32 or 64; 0 = VSPEC_3BIT_BLOCK_SIZE (default 64).
+ * head_dim <= 1024; d_workspace 256-byte aligned, at least
+ * vspec_b200_attention_ref_workspace_bytes() (0 for unsupported sizes). */
+size_t vspec_b200_attention_ref_workspace_bytes(size_t tokens, size_t heads, size_t head_dim);
+int vspec_b200_attention_ref_f32(const float* d_q, const float* d_keys, const float* d_values, size_t tokens,
+                                 size_t heads, size_t head_dim, int three_bit_module, size_t block_size,
+                                 void* d_workspace, size_t workspace_bytes, float* d_out, void* stream);
+
 /* int3 KV pages (VspecKVCache int3 compression, src/attention/kv_cache.c:64-126
  * and 160-226, dequantised in attention as src/kernel/cuda/attention_fused.cu:23-45
  * and 232-351 do, moved onto the paged layout):

@@ -148,6 +148,14 @@ void vspec_cuda_launch_linear_impl(VspecKernelContext* ctx);
  * plain softmax attention per head (src/kernel/cuda/attention_fused.cu:353-445). */
 void vspec_cuda_launch_attention_impl(VspecKernelContext* ctx);
 
+/* ---- The CPU backend's semantics on the device (src/kernel/cpu/cpu_backend.c:9-48) ----
+ * name "cpu-semantics-b200": launch_linear = vspec_cuda_launch_linear_impl (the CPU
+ * backend's INT4 semantics), launch_attention = vspec_b200_launch_attention_ref:
+ * vspec_attention_ref_single_query (src/attention/attention_ref.c:7-88) on a host
+ * VspecKVCache, the 3-bit runtime module decided from the environment per call. */
+VspecBackend vspec_b200_make_cpu_semantics_backend(void);
+void vspec_b200_launch_attention_ref(VspecKernelContext* ctx);
+
 /* ---- include/vspec/kernel/cuda_fused.h:10-122 ---- */
 int vspec_cuda_fused_available(void);
 /* Host-pointer context launchers (H2D, kernel, D2H, synchronous). */

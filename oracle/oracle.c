@@ -289,6 +289,122 @@ void oracle_clamp_rows_std(const float* in, size_t rows, size_t cols, float alph
     }
 }
 
+/* ---- the CPU backend's attention (src/attention/attention_ref.c:7-88) ----
+ * Per head of a contiguous [tokens][heads][d] fp32 cache: q and each k row clamped
+ * to +-max(1e-6, 4.5 * population std, std in double; three_bit_runtime_modules.c:
+ * 175-203), score = dot * (1/sqrtf(d)), softmax with a double denominator (:205-250),
+ * output = double sum of p_t * v_t[x] (:260-282).  module != 0 is the 3-bit runtime
+ * module: noise reducer (clip +-16, consecutive-delta limit 32; :138-173), dot over
+ * blocks of `block` (32 or 64) normalised by the block's max |value| with Kahan
+ * sums (:291-342), qk scale clipped to [1e-4, 32] (:344-361), logits clipped to
+ * +-24, Kahan output sums with the 1e7 limit (:260-282). */
+static float ar_clip(float x, float lo, float hi) { return x < lo ? lo : (x > hi ? hi : x); }
+
+static void ar_condition(const float* x, size_t n, int module, float* out) {
+    double mean = 0.0, var = 0.0;
+    for (size_t i = 0; i < n; ++i) mean += (double)x[i];
+    mean /= (double)n;
+    for (size_t i = 0; i < n; ++i) var += ((double)x[i] - mean) * ((double)x[i] - mean);
+    var /= (double)n;
+    const float sd = (float)sqrt(var);
+    const float th = fmaxf(1e-6f, 4.5f * sd);
+    float prev = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+        float v = ar_clip(x[i], -th, th);
+        if (module) {
+            v = ar_clip(v, -16.0f, 16.0f);
+            if (i > 0) {
+                const float delta = v - prev;
+                if (fabsf(delta) > 32.0f) v = prev + (delta > 0.0f ? 32.0f : -32.0f);
+            }
+            prev = v;
+        }
+        out[i] = v;
+    }
+}
+
+typedef struct { double sum, comp; } ArAcc;
+
+static void ar_add(ArAcc* a, float value, int module) {
+    if (!module) {
+        a->sum += (double)value;
+        return;
+    }
+    const double y = (double)value - a->comp;
+    const double t = a->sum + y;
+    a->comp = (t - a->sum) - y;
+    a->sum = t;
+    if (fabs(a->sum) > 1e7) {
+        a->sum = (double)ar_clip((float)a->sum, -1e7f, 1e7f);
+        a->comp = 0.0;
+    }
+}
+
+static float ar_dot(const float* a, const float* b, size_t n, int module, size_t block) {
+    if (!module) {
+        float s = 0.0f;
+        for (size_t i = 0; i < n; ++i) s += a[i] * b[i];
+        return s;
+    }
+    ArAcc total = {0.0, 0.0};
+    for (size_t base = 0; base < n; base += block) {
+        const size_t end = base + block < n ? base + block : n;
+        float babs = 0.0f;
+        for (size_t i = base; i < end; ++i) {
+            if (fabsf(a[i]) > babs) babs = fabsf(a[i]);
+            if (fabsf(b[i]) > babs) babs = fabsf(b[i]);
+        }
+        const float bs = fmaxf(babs, 1e-6f);
+        ArAcc local = {0.0, 0.0};
+        for (size_t i = base; i < end; ++i) ar_add(&local, (a[i] / bs) * (b[i] / bs), 1);
+        ar_add(&total, (float)local.sum * bs * bs, 1);
+    }
+    return (float)total.sum;
+}
+
+void oracle_attention_ref_f32(const float* q, const float* keys, const float* values, size_t tokens, size_t heads,
+                              size_t d, int module, size_t block, float* out) {
+    if (block != 32) block = 64;
+    float* qc = (float*)malloc(d * sizeof(float));
+    float* kc = (float*)malloc(d * sizeof(float));
+    float* sc = (float*)malloc(tokens * sizeof(float));
+    ArAcc* acc = (ArAcc*)malloc(d * sizeof(ArAcc));
+    const float inv_sqrt_d = 1.0f / sqrtf((float)d);
+    const float scale = module ? ar_clip(inv_sqrt_d, 1e-4f, 32.0f) : inv_sqrt_d;
+    for (size_t h = 0; h < heads; ++h) {
+        ar_condition(q + h * d, d, module, qc);
+        float mx = -3.402823466e38f;
+        for (size_t t = 0; t < tokens; ++t) {
+            ar_condition(keys + (t * heads + h) * d, d, module, kc);
+            float s = ar_dot(qc, kc, d, module, block) * scale;
+            if (module) s = ar_clip(s, -24.0f, 24.0f);
+            sc[t] = s;
+            if (s > mx) mx = s;
+        }
+        double den = 0.0;
+        for (size_t t = 0; t < tokens; ++t) {
+            sc[t] = expf(sc[t] - mx);
+            den += (double)sc[t];
+        }
+        if (den < (double)1e-12f) {
+            for (size_t t = 0; t < tokens; ++t) sc[t] = 1.0f / (float)tokens;
+        } else {
+            const float inv = 1.0f / (float)den;
+            for (size_t t = 0; t < tokens; ++t) sc[t] *= inv;
+        }
+        for (size_t x = 0; x < d; ++x) acc[x].sum = acc[x].comp = 0.0;
+        for (size_t t = 0; t < tokens; ++t) {
+            const float* vr = values + (t * heads + h) * d;
+            for (size_t x = 0; x < d; ++x) ar_add(&acc[x], sc[t] * vr[x], module);
+        }
+        for (size_t x = 0; x < d; ++x) out[h * d + x] = (float)acc[x].sum;
+    }
+    free(qc);
+    free(kc);
+    free(sc);
+    free(acc);
+}
+
 static float sr_uniform01(uint32_t state) {
     /* xorshift32 -> 24-bit uniform (src/kernel/cuda/fused_linear_int3.cu:68-73) */
     state ^= state << 13;

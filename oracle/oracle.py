@@ -42,6 +42,8 @@ _o = {
     "oracle_paged_gqa_attention_f32": ([c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_size_t,
                                         c_size_t, c_size_t, c_size_t, c_float, c_void_p], None),
     "oracle_clamp_rows_std": ([c_void_p, c_size_t, c_size_t, c_float, c_void_p], None),
+    "oracle_attention_ref_f32": ([c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_size_t,
+                                  c_void_p], None),
     "oracle_int3_blocknorm_f32": ([c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_int, c_void_p], None),
     "oracle_paged_gqa_attention_f64": ([c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_size_t,
                                         c_size_t, c_size_t, c_size_t, c_float, c_void_p], None),
@@ -241,6 +243,18 @@ def paged_attention(q, k_pages, v_pages, table, ctx_len, hq, hkv, d, pt, scale, 
     out = np.zeros((b, hq, d), dtype=np.float64 if f64 else np.float32)
     fn = ORACLE.oracle_paged_gqa_attention_f64 if f64 else ORACLE.oracle_paged_gqa_attention_f32
     fn(p(q), p(kp), p(vp), p(table), table.shape[1], p(ctx), b, hq, hkv, d, pt, scale, p(out))
+    return out
+
+
+def attention_ref(q, keys, values, module: int, block: int = 64) -> np.ndarray:
+    """The CPU backend's attention (attention_ref.c:7-88) on a contiguous cache:
+    q [heads][d], keys/values [tokens][heads][d]; module = the 3-bit runtime module."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(keys, dtype=np.float32)
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    t, h, d = k.shape
+    out = np.zeros((h, d), dtype=np.float32)
+    ORACLE.oracle_attention_ref_f32(p(q), p(k), p(v), t, h, d, int(module), int(block), p(out))
     return out
 
 

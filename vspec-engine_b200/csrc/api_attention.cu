@@ -426,6 +426,61 @@ extern "C" void vspec_cuda_launch_attention_fused(VspecKernelContext* ctx) {
     cudaFree(dk); cudaFree(dv); cudaFree(dq); cudaFree(dout);
 }
 
+extern "C" void vspec_b200_launch_attention_ref(VspecKernelContext* ctx) {
+    // The CPU backend's launch_attention (src/kernel/cpu/cpu_backend.c:29-46 ->
+    // src/attention/attention_ref.c:7-88) on the device.  K/V rows come from the cache as
+    // vspec_kv_cache_key_at/value_at read them (kv_cache.c:296-371): the fp32 arrays when the
+    // cache keeps them, else the int3 codes dequantised on the device.
+    if (!ctx || !ctx->input || !ctx->weight || !ctx->output) return;
+    const VspecKVCache* cache = (const VspecKVCache*)ctx->weight;
+    const size_t T = cache->current_tokens, H = cache->num_heads, d = cache->head_dim;
+    if (T == 0 || H == 0 || d == 0) return;
+    const size_t ws = vspec_b200_attention_ref_workspace_bytes(T, H, d);
+    if (ws == 0) {
+        set_error("vspec_b200_launch_attention_ref: unsupported cache sizes");
+        return;
+    }
+    const size_t rows = T * H, kvb = rows * d * sizeof(float), qb = H * d * sizeof(float);
+    AttnHostState* h = attn_host_state(qb, kvb);
+    void* w = attn_scratch(ws);
+    if (!h || !w) return;
+    const bool fp32 = cache->key && cache->value;
+    const bool int3 = cache->int3_compressed && cache->key_int3 && cache->value_int3 && cache->key_scales &&
+                      cache->value_scales && cache->packed_head_bytes && cache->blocks_per_head && cache->block_size;
+    if (fp32) {
+        if (cudaMemcpyAsync(h->k, cache->key, kvb, cudaMemcpyHostToDevice, h->st) != cudaSuccess ||
+            cudaMemcpyAsync(h->v, cache->value, kvb, cudaMemcpyHostToDevice, h->st) != cudaSuccess)
+            return;
+    } else if (int3) {
+        const size_t pb = rows * cache->packed_head_bytes, sb = rows * cache->blocks_per_head * sizeof(float);
+        uint8_t *dkq = nullptr, *dvq = nullptr;
+        float *dks = nullptr, *dvs = nullptr;
+        bool ok = cudaMalloc(&dkq, pb) == cudaSuccess && cudaMalloc(&dvq, pb) == cudaSuccess &&
+                  cudaMalloc(&dks, sb) == cudaSuccess && cudaMalloc(&dvs, sb) == cudaSuccess;
+        if (ok) {
+            ok = cudaMemcpyAsync(dkq, cache->key_int3, pb, cudaMemcpyHostToDevice, h->st) == cudaSuccess &&
+                 cudaMemcpyAsync(dvq, cache->value_int3, pb, cudaMemcpyHostToDevice, h->st) == cudaSuccess &&
+                 cudaMemcpyAsync(dks, cache->key_scales, sb, cudaMemcpyHostToDevice, h->st) == cudaSuccess &&
+                 cudaMemcpyAsync(dvs, cache->value_scales, sb, cudaMemcpyHostToDevice, h->st) == cudaSuccess;
+            if (ok) {
+                dequant_int3_kv_kernel<<<grid1d(rows * d), 256, 0, h->st>>>(
+                    dkq, dks, h->k, rows, d, cache->packed_head_bytes, cache->blocks_per_head, cache->block_size);
+                dequant_int3_kv_kernel<<<grid1d(rows * d), 256, 0, h->st>>>(
+                    dvq, dvs, h->v, rows, d, cache->packed_head_bytes, cache->blocks_per_head, cache->block_size);
+                ok = cudaStreamSynchronize(h->st) == cudaSuccess;
+            }
+        }
+        cudaFree(dkq); cudaFree(dvq); cudaFree(dks); cudaFree(dvs);
+        if (!ok) return;
+    } else {
+        return;
+    }
+    if (cudaMemcpyAsync(h->q, ctx->input, qb, cudaMemcpyHostToDevice, h->st) != cudaSuccess) return;
+    if (vspec_b200_attention_ref_f32(h->q, h->k, h->v, T, H, d, -1, 0, w, ws, h->out, h->st) != VSPEC_B200_OK) return;
+    if (cudaMemcpyAsync(ctx->output, h->out, qb, cudaMemcpyDeviceToHost, h->st) == cudaSuccess)
+        cudaStreamSynchronize(h->st);
+}
+
 // ---- include/vspec/kernel/cuda_ops.h (host pointers, synchronous) ----
 extern "C" void vspec_cuda_rmsnorm_f32(const float* input, const float* weight, float eps, size_t rows, size_t dim,
                                        float* output) {

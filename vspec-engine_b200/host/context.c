@@ -193,3 +193,15 @@ VspecBackend vspec_make_cuda_backend(void) {
     b.launch_attention = b200_launch_attention;
     return b;
 }
+
+/* The CPU backend (src/kernel/cpu/cpu_backend.c:9-48) with its arithmetic on the device:
+ * INT4 linear with mean-code zero-points, attention with attention_ref.c's clamp. */
+static void b200_launch_attention_ref(VspecKernelContext* ctx) { vspec_b200_launch_attention_ref(ctx); }
+
+VspecBackend vspec_b200_make_cpu_semantics_backend(void) {
+    VspecBackend b;
+    b.name = "cpu-semantics-b200";
+    b.launch_linear = b200_launch_linear;
+    b.launch_attention = b200_launch_attention_ref;
+    return b;
+}

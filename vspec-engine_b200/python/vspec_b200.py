@@ -19,6 +19,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.abspath(os.path.join(_HERE, "..", "lib", "libvspec_b200.so"))
 
 OK = 0
+ERR_ARG = 1
 F_SZ_F16 = 0x1
 F_UNSIGNED = 0x2
 F_RESIDUAL = 0x4
@@ -129,6 +130,9 @@ _sigs = {
     "vspec_b200_mean_code_zero_points": ([c_void_p, c_size_t, c_size_t, c_int, c_void_p, c_void_p], c_int),
     "vspec_b200_paged_attention_workspace_bytes": ([c_size_t] * 5, c_size_t),
     "vspec_b200_paged_attention": ([POINTER(PagedAttnArgs), c_void_p], c_int),
+    "vspec_b200_attention_ref_workspace_bytes": ([c_size_t, c_size_t, c_size_t], c_size_t),
+    "vspec_b200_attention_ref_f32": ([c_void_p] * 3 + [c_size_t] * 3 + [c_int, c_size_t, c_void_p, c_size_t, c_void_p,
+                                                                     c_void_p], c_int),
     "vspec_b200_paged_attention_page_fault": ([POINTER(c_int)], c_int),
     "vspec_b200_kv_paged_sync": ([c_void_p, c_int, c_void_p, c_void_p, c_uint64, POINTER(c_uint64), c_void_p], c_int),
     "vspec_b200_kv_paged_session_view": ([c_void_p, c_uint64, c_int, c_void_p, c_void_p, c_size_t, c_size_t, c_void_p,
@@ -184,6 +188,8 @@ _sigs = {
     "vspec_cuda_launch_fused_linear_int2": ([POINTER(KernelContext)], None),
     "vspec_cuda_launch_fused_linear_int3_storage": ([POINTER(KernelContext)], None),
     "vspec_cuda_launch_attention_fused": ([POINTER(KernelContext)], None),
+    "vspec_b200_make_cpu_semantics_backend": ([], Backend),
+    "vspec_b200_launch_attention_ref": ([POINTER(KernelContext)], None),
     "vspec_cuda_attention_fused_single_f32": ([c_void_p] * 3 + [c_size_t, c_size_t, c_void_p], None),
     "vspec_cuda_attention_flash_single_f32": ([c_void_p] * 3 + [c_size_t, c_size_t, c_size_t, c_void_p], None),
     "vspec_cuda_fused_linear_int4_device": ([c_void_p] * 5 + [c_size_t] * 4, None),
@@ -266,6 +272,14 @@ def paged_attention(q: int, k_pages: int, v_pages: int, page_table: int, ctx_len
     a = PagedAttnArgs(q, k_pages, v_pages, page_table, ctx_len, out, batch, hq, hkv, d, page_tokens, max_pages,
                       num_pages, max_ctx, scale, kv_dtype, workspace, workspace_bytes)
     check(lib.vspec_b200_paged_attention(ctypes.byref(a), stream), "vspec_b200_paged_attention")
+
+
+def attention_ref(q: int, keys: int, values: int, out: int, tokens: int, heads: int, d: int, module: int = -1,
+                  block: int = 0, workspace: int | None = None, workspace_bytes: int = 0, stream: int = 0) -> None:
+    """The CPU backend's attention semantics on device buffers (attention_ref.c:7-88);
+    module -1 = from the environment, block 0 = VSPEC_3BIT_BLOCK_SIZE."""
+    check(lib.vspec_b200_attention_ref_f32(q, keys, values, tokens, heads, d, module, block, workspace,
+                                           workspace_bytes, out, stream), "vspec_b200_attention_ref_f32")
 
 
 def kv_int3_quantize(src: int, slots: int | None, rows: int, heads: int, head_dim: int, block: int, codes: int,
