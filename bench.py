@@ -485,6 +485,83 @@ def time_attention(torch, V, steps: int, warmup: int, world: int):
     return ms, kv_bytes, other
 
 
+AREF_T, AREF_H, AREF_D, AREF_COPIES = 4096, 8, 128, 6
+AREF_ENV = ("VSPEC_FUSED_BITS", "VSPEC_3BIT_RUNTIME_MODULE", "VSPEC_3BIT_BLOCK_SIZE")
+
+
+def time_attention_ref(torch, V, steps: int, warmup: int, world: int) -> dict:
+    """The CPU backend's attention semantics (attention_ref.c: std clamp, double
+    softmax denominator and output; module=1 adds the 3-bit module's arithmetic)
+    at the shape the reference's CPU path is timed on, 8 heads x 4096 tokens x
+    128, over six rotating K/V copies (201 MB > L2)."""
+    t, h, d = AREF_T, AREF_H, AREF_D
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    kv = [(torch.randn((t, h, d), device="cuda", generator=g), torch.randn((t, h, d), device="cuda", generator=g))
+          for _ in range(AREF_COPIES)]
+    q = torch.randn((h, d), device="cuda", generator=g)
+    out = torch.empty((h, d), device="cuda", dtype=torch.float32)
+    ws = V.lib.vspec_b200_attention_ref_workspace_bytes(t, h, d)
+    wbuf = torch.empty((ws,), device="cuda", dtype=torch.uint8)
+    stream = torch.cuda.Stream()
+    nbytes = 2 * t * h * d * 4 + 2 * h * d * 4
+    res = {}
+    for module in (0, 1):
+        def run():
+            for kk, vv in kv:
+                V.attention_ref(q.data_ptr(), kk.data_ptr(), vv.data_ptr(), out.data_ptr(), t, h, d, module, 64,
+                                wbuf.data_ptr(), ws, stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                run()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(steps):
+                run()
+            end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        us = max_over_ranks(start.elapsed_time(end), world) * 1e3 / (steps * AREF_COPIES)
+        res[module] = us
+    return {"us": round(res[0], 2), "gbs": round(world * nbytes / res[0] / 1e3, 1), "module_us": round(res[1], 2),
+            "bytes": nbytes}
+
+
+def cpu_attention_ref_sample(seconds: float = 4.0) -> dict | None:
+    """The reference's own CPU backend attention (vspec_attention_ref_single_query
+    compiled from its sources, one host thread, 3-bit module off) at the GPU leg's
+    shape; GB/s of the same algorithmic K+V bytes."""
+    import oracle as O
+    if O.REF is None:
+        return None
+    saved = {k: os.environ.pop(k) for k in AREF_ENV if k in os.environ}
+    try:
+        rng = np.random.default_rng(11)
+        t, h, d = AREF_T, AREF_H, AREF_D
+        q = rng.standard_normal((h, d)).astype(np.float32)
+        k = rng.standard_normal((t, h, d)).astype(np.float32)
+        v = rng.standard_normal((t, h, d)).astype(np.float32)
+        out = np.zeros((h, d), dtype=np.float32)
+        t0 = time.perf_counter()
+        calls = 0
+        while True:
+            O.REF.ref_cpu_backend_attention(q.ctypes.data, k.ctypes.data, v.ctypes.data, t, h, d, out.ctypes.data)
+            calls += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+    finally:
+        os.environ.update(saved)
+    nbytes = 2 * t * h * d * 4 + 2 * h * d * 4
+    return {"value": round(calls * nbytes / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "reference",
+            "ms": round(dt * 1e3 / calls, 2),
+            "sample": f"{calls} x vspec_attention_ref_single_query (CPU backend) {h}x{t}x{d}, module off, {dt:.1f} s"}
+
+
 def time_attention_int3(torch, V, steps: int, warmup: int, world: int, block: int = 32):
     """Config 3 with int3 K/V pages (kv_cache.c int3 compression, block 32):
     the same seeded fp16 pools quantised on the GPU, then paged GQA attention
@@ -944,6 +1021,11 @@ def run_legs(torch, V, args, world: int, rank: int, peak: float, peaks: dict) ->
         legs["attn"]["cpu"] = cpu_attention_sample()
     a3_ms, a3_kv, a3_other = time_attention_int3(torch, V, a_steps, args.warmup, world)
     per3 = a3_ms * 1e-3 / a_steps
+    ar = time_attention_ref(torch, V, max(3, a_steps // 4), args.warmup, world)
+    legs["aref"] = {"us": ar["us"], "gbs": ar["gbs"], "frac": round(ar["bytes"] / ar["us"] / 1e3 / peak, 3),
+                    "module_us": ar["module_us"]}
+    if rank == 0 and world == 1:
+        legs["aref"]["cpu"] = cpu_attention_ref_sample()
     legs["attn_i3"] = {"gbs": round(world * (a3_kv + a3_other) / per3 / 1e9, 1), "ms": round(per3 * 1e3, 4),
                        "frac": round((a3_kv + a3_other) / per3 / 1e9 / peak, 3),
                        "vs_fp16": round(attn_ms / a3_ms, 3)}
