@@ -480,9 +480,28 @@ def time_attention(torch, V, steps: int, warmup: int, world: int):
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world)
     del graph
+    # end to end through the public call: each step uploads q from pinned host memory, runs the
+    # attention over the device-resident pages and reads the output back into pinned host memory
+    q_host = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    q_host.copy_(q)
+    out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            q.copy_(q_host, non_blocking=True)
+            call(stream.cuda_stream)
+            out_host.copy_(out, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
     kv_bytes = int(ctx.astype(np.int64).sum()) * ATTN_HKV * ATTN_D * 2 * 2
     other = q.numel() * 4 + out.numel() * 4 + table.size * 4 + ctx.size * 4
-    return ms, kv_bytes, other
+    return ms, kv_bytes, other, e2e_ms, q.numel() * 4, out.numel() * 4
 
 
 AREF_T, AREF_H, AREF_D, AREF_COPIES = 4096, 8, 128, 6
@@ -1013,10 +1032,15 @@ def run_legs(torch, V, args, world: int, rank: int, peak: float, peaks: dict) ->
     legs["cfg1"] = gemv_leg(ms, nb, ls * c1, world, peak)
     legs["gemm"] = time_gemm(torch, V, world, max(3, args.steps // 5), peaks)
     a_steps = max(3, args.steps // 5)
-    attn_ms, attn_kv, attn_other = time_attention(torch, V, a_steps, args.warmup, world)
+    attn_ms, attn_kv, attn_other, attn_e2e_ms, attn_h2d, attn_d2h = time_attention(torch, V, a_steps, args.warmup,
+                                                                                   world)
     per = attn_ms * 1e-3 / a_steps
+    per_e2e = attn_e2e_ms * 1e-3 / a_steps
     legs["attn"] = {"gbs": round(world * (attn_kv + attn_other) / per / 1e9, 1), "ms": round(per * 1e3, 4),
-                    "frac": round((attn_kv + attn_other) / per / 1e9 / peak, 3)}
+                    "frac": round((attn_kv + attn_other) / per / 1e9 / peak, 3),
+                    "e2e": {"gbs": round(world * (attn_kv + attn_other) / per_e2e / 1e9, 1),
+                            "ms": round(per_e2e * 1e3, 4), "h2d_bytes_per_step": attn_h2d,
+                            "d2h_bytes_per_step": attn_d2h}}
     if cpu:
         legs["attn"]["cpu"] = cpu_attention_sample()
     a3_ms, a3_kv, a3_other = time_attention_int3(torch, V, a_steps, args.warmup, world)

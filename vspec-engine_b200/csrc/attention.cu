@@ -815,27 +815,31 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
     const uint32_t wbase = smem_u32(wptr);
     const uint32_t tile_k = wbase, tile_v = wbase + kAttnTileBytes;
     const uint32_t stage0 = wbase + 2u * kAttnTileBytes;
+    // issue: lane -> one token row of the tile, K (lanes 0-15) or V (lanes 16-31): its 48 code bytes
+    // (three 16-byte chunks) and its NBLK block scales
+    const int i_row = lane & 15, i_kv = lane >> 4;
+    const bool pt_pow2 = (p.page_tokens & (p.page_tokens - 1)) == 0;
+    const int pt_shift = __ffs(p.page_tokens) - 1;
+    const uint8_t* i_codes = i_kv ? vc : kc;
+    const float* i_scales = i_kv ? p.v_scales : p.k_scales;
     auto issue = [&](int it) {   // codes and scales of this warp's it-th tile -> stage it % S
         const int t0 = t_begin + (warp + it * kAttnWarps) * 16;
         const uint32_t st = stage0 + (uint32_t)(it % S) * SM::kStage;
-        for (int idx = lane; idx < 48; idx += 32) {   // 16 rows x 3 chunks of 16 B
-            const int row = idx / 3, k = idx - 3 * (idx / 3);
-            const int t = t0 + row;
-            const bool valid = t < t_end;
-            const size_t ri = staged_row(sm_pages, valid ? t : t_end - 1, first_page, p.page_tokens, p.hkv, 1, kvh);
-            cp_async16(st + (uint32_t)(row * 48 + k * 16), kc + ri * 48 + k * 16, valid ? 16u : 0u);
-            cp_async16(st + kI3Codes + (uint32_t)(row * 48 + k * 16), vc + ri * 48 + k * 16, valid ? 16u : 0u);
-        }
-        constexpr int SCH = NBLK / 4;                 // 16-byte chunks of one row's scales
-        for (int idx = lane; idx < 16 * SCH; idx += 32) {
-            const int row = idx / SCH, k = idx - SCH * (idx / SCH);
-            const int t = t0 + row;
-            const bool valid = t < t_end;
-            const size_t ri = staged_row(sm_pages, valid ? t : t_end - 1, first_page, p.page_tokens, p.hkv, 1, kvh);
-            const uint32_t so = (uint32_t)(row * NBLK * 4 + k * 16);
-            cp_async16(st + 2u * kI3Codes + so, p.k_scales + ri * NBLK + k * 4, valid ? 16u : 0u);
-            cp_async16(st + 2u * kI3Codes + SM::kScales + so, p.v_scales + ri * NBLK + k * 4, valid ? 16u : 0u);
-        }
+        const int t = t0 + i_row;
+        const bool valid = t < t_end;
+        const int tt = valid ? t : t_end - 1;
+        const int pg = pt_pow2 ? (tt >> pt_shift) : tt / p.page_tokens;
+        const int slot = pt_pow2 ? (tt & (p.page_tokens - 1)) : tt - pg * p.page_tokens;
+        const size_t ri = ((size_t)sm_pages[pg - first_page] * p.page_tokens + (size_t)slot) * (size_t)p.hkv + kvh;
+        const uint32_t nb = valid ? 16u : 0u;
+        const uint32_t cdst = st + (uint32_t)i_kv * kI3Codes + (uint32_t)i_row * 48u;
+        const uint8_t* csrc = i_codes + ri * 48;
+        cp_async16(cdst, csrc, nb);
+        cp_async16(cdst + 16u, csrc + 16, nb);
+        cp_async16(cdst + 32u, csrc + 32, nb);
+        const uint32_t sdst = st + 2u * kI3Codes + (uint32_t)i_kv * SM::kScales + (uint32_t)i_row * (NBLK * 4u);
+#pragma unroll
+        for (int k = 0; k < NBLK / 4; ++k) cp_async16(sdst + 16u * k, i_scales + ri * NBLK + 4 * k, nb);
     };
 #pragma unroll
     for (int it = 0; it < S - 1; ++it) {
@@ -891,7 +895,8 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
 
     const int k_row = (lane & 7) + 8 * ((lane >> 3) & 1), k_chi = lane >> 4;
     const int v_row = (lane & 7) + 8 * (lane >> 4), v_chi = (lane >> 3) & 1;
-    const int dr = lane >> 1, dh = lane & 1;      // decode: token row and half of the dims
+    const int dr = lane & 15, dh = lane >> 4;     // decode: token row and half of the dims (8 lanes of a
+                                                  // 16-byte store phase write 8 distinct bank groups)
     for (int it = 0; it < my_tiles; ++it) {
         cp_async_wait<S - 2>();
         __syncwarp();   // tile it has landed; every lane is done with tile it-1 (decoded tiles, sm_p)
@@ -925,6 +930,14 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
         const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+        float ksg[NBLK], ksg8[NBLK];   // K scales of token rows g and g + 8
+#pragma unroll
+        for (int k4 = 0; k4 < NBLK / 4; ++k4) {
+            const float4 a = *reinterpret_cast<const float4*>(ks + g * NBLK + 4 * k4);
+            const float4 b = *reinterpret_cast<const float4*>(ks + (g + 8) * NBLK + 4 * k4);
+            ksg[4 * k4] = a.x; ksg[4 * k4 + 1] = a.y; ksg[4 * k4 + 2] = a.z; ksg[4 * k4 + 3] = a.w;
+            ksg8[4 * k4] = b.x; ksg8[4 * k4 + 1] = b.y; ksg8[4 * k4 + 2] = b.z; ksg8[4 * k4 + 3] = b.w;
+        }
 #pragma unroll
         for (int bl = 0; bl < NBLK; ++bl) {
             float sb[NT][4];
@@ -938,7 +951,7 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
                 for (int nt = 0; nt < NT; ++nt)
                     mma_16816_f16(sb[nt], a, qf[nt][j][0], qf[nt][j][1], jj == 0 ? zero4 : sb[nt]);
             }
-            const float k0 = ks[g * NBLK + bl], k1 = ks[(g + 8) * NBLK + bl];
+            const float k0 = ksg[bl], k1 = ksg8[bl];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 s[nt][0] = fmaf(sb[nt][0], k0, s[nt][0]);
@@ -972,17 +985,28 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
         __syncwarp();
         // ---- O^T += V^T (P s_v)^T, per scale block of dims ----
         const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+        float pt4[NT][4], vs4[4][NBLK];   // p of this lane's 4 tokens; their V scales
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) pt4[nt][r] = sm_p[warp][toks[r]][4 * nt + (g >> 1)];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int k4 = 0; k4 < NBLK / 4; ++k4) {
+                const float4 a = *reinterpret_cast<const float4*>(vs + toks[r] * NBLK + 4 * k4);
+                vs4[r][4 * k4] = a.x; vs4[r][4 * k4 + 1] = a.y; vs4[r][4 * k4 + 2] = a.z; vs4[r][4 * k4 + 3] = a.w;
+            }
 #pragma unroll
         for (int bl = 0; bl < NBLK; ++bl) {
             uint32_t pb[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const int hl = 4 * nt + (g >> 1);
                 const bool lo = (g & 1) != 0;
                 float pv[4];
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    float x = sm_p[warp][toks[r]][hl] * vs[toks[r] * NBLK + bl];
+                    float x = pt4[nt][r] * vs4[r][bl];
                     if (lo) x = x - __half2float(__float2half_rn(x));
                     pv[r] = x;
                 }
