@@ -101,7 +101,13 @@ using namespace vb200;
 extern "C" size_t vspec_b200_paged_attention_workspace_bytes(size_t batch, size_t hq, size_t hkv, size_t d,
                                                              size_t max_ctx) {
     if (batch == 0 || hq == 0 || hkv == 0 || d == 0) return 0;
-    const int split = attn_choose_split((int)batch, (int)hq, (int)hkv, (int)(max_ctx ? max_ctx : 1), 0, device_sm_count());
+    // the finer of the plans of the fp16/fp32 and the int3 kernels
+    const AttnPlanShape i3 = attn_plan_int3((int)hq, (int)hkv);
+    const int s2 = attn_choose_split((int)batch, (int)hq, (int)hkv, (int)(max_ctx ? max_ctx : 1), 0, device_sm_count(),
+                                     kAttnPlanF16.ctas_per_sm, kAttnPlanF16.max_staged_pages);
+    const int s3 = attn_choose_split((int)batch, (int)hq, (int)hkv, (int)(max_ctx ? max_ctx : 1), 0, device_sm_count(),
+                                     i3.ctas_per_sm, i3.max_staged_pages);
+    const int split = s2 < s3 ? s2 : s3;
     const int max_splits = (int)((max_ctx + split - 1) / split);
     return attn_workspace_bytes((int)batch, (int)hq, (int)d, max_splits > 0 ? max_splits : 1);
 }
@@ -139,7 +145,8 @@ extern "C" int vspec_b200_paged_attention(const VspecB200PagedAttnArgs* a, void*
     p.page_tokens = (int)a->page_tokens;
     p.max_pages = (int)a->max_pages_per_seq;
     p.num_pages = (int)a->num_pages;
-    p.split_tokens = attn_choose_split(p.batch, p.hq, p.hkv, (int)max_ctx, p.page_tokens, device_sm_count());
+    p.split_tokens = attn_choose_split(p.batch, p.hq, p.hkv, (int)max_ctx, p.page_tokens, device_sm_count(),
+                                       kAttnPlanF16.ctas_per_sm, kAttnPlanF16.max_staged_pages);
     p.max_splits = (int)((max_ctx + p.split_tokens - 1) / p.split_tokens);
     if (p.max_splits < 1) p.max_splits = 1;
     const size_t need = attn_workspace_bytes(p.batch, p.hq, p.d, p.max_splits);
@@ -213,7 +220,11 @@ extern "C" int vspec_b200_paged_attention_int3(const VspecB200PagedAttnArgs* a, 
     p.page_tokens = (int)a->page_tokens;
     p.max_pages = (int)a->max_pages_per_seq;
     p.num_pages = (int)a->num_pages;
-    p.split_tokens = attn_choose_split(p.batch, p.hq, p.hkv, (int)max_ctx, p.page_tokens, device_sm_count());
+    // the SIMT variant (VSPEC_B200_INT3_ATTN_SIMT=1) is planned like the fp16 kernel
+    const char* simt = getenv("VSPEC_B200_INT3_ATTN_SIMT");
+    const AttnPlanShape plan = (simt && simt[0] == '1') ? kAttnPlanF16 : attn_plan_int3(p.hq, p.hkv);
+    p.split_tokens = attn_choose_split(p.batch, p.hq, p.hkv, (int)max_ctx, p.page_tokens, device_sm_count(),
+                                       plan.ctas_per_sm, plan.max_staged_pages);
     p.max_splits = (int)((max_ctx + p.split_tokens - 1) / p.split_tokens);
     if (p.max_splits < 1) p.max_splits = 1;
     const size_t need = attn_workspace_bytes(p.batch, p.hq, p.d, p.max_splits);

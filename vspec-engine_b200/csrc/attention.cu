@@ -59,6 +59,7 @@ __device__ __forceinline__ size_t token_row(const int32_t* table, int t, int pt,
 // and redirected like token_row), so the K/V loads of a tile do not wait on a
 // page-table load first.
 constexpr int kAttnMaxStagedPages = 512;
+constexpr int kAttnInt3MaxStagedPages = 256;   // int3 tensor-core kernel (four CTAs per SM)
 
 __device__ __forceinline__ size_t staged_row(const int* sm_pages, int t, int first_page, int pt, int hkv, int d,
                                              int kvh) {
@@ -720,7 +721,8 @@ paged_attn_int3_kernel(const AttnParams p) {
 // with a decode step.  Per warp and 16-token tile, cp.async stages the K and V
 // code rows (48 B per token) and their block scales; after they land the warp
 // turns the codes into fp16 small integers (exact) in the fp16 kernel's
-// swizzled tile layout, so QK^T and PV run as in paged_attn_f16_mma_kernel.
+// swizzled tile layout, one tile per warp (the K codes for QK^T, then the V
+// codes for PV), so QK^T and PV run as in paged_attn_f16_mma_kernel.
 // The scales stay out of the fp16 operands: QK^T accumulates per scale block
 // and multiplies each token's block partial by its K scale in fp32, and PV
 // folds each token's V scale into p (split into fp16 hi + lo parts) per block
@@ -731,7 +733,7 @@ template <int NBLK>
 struct I3Smem {
     static constexpr uint32_t kScales = 16u * NBLK * 4u;                   // 16 rows of fp32 block scales
     static constexpr uint32_t kStage = 2u * kI3Codes + 2u * kScales;      // K codes, V codes, K scales, V scales
-    static constexpr uint32_t kWarp = 2u * kAttnTileBytes + kAttnStages * kStage;
+    static constexpr uint32_t kWarp = kAttnTileBytes + kAttnStages * kStage;   // one decoded tile, the ring
     static constexpr uint32_t kTotal = kAttnWarps * kWarp;
 };
 
@@ -759,7 +761,7 @@ __device__ __forceinline__ void i3_decode64(const uint32_t (&w)[6], uint4 (&out)
 }
 
 template <int NT, int NBLK>
-__global__ void __launch_bounds__(kAttnThreads, 2)
+__global__ void __launch_bounds__(kAttnThreads, NT == 1 ? 4 : 2)   // 4 CTAs per SM for one column tile
 paged_attn_int3_mma_kernel(const AttnParams p) {
     pdl_wait();
     pdl_trigger();
@@ -786,11 +788,13 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
     const uint8_t* vc = reinterpret_cast<const uint8_t*>(p.v_pages);
 
     extern __shared__ __align__(128) unsigned char attn_smem[];
-    __shared__ float sm_q[HPC][D];
+    // the query heads (fp32) live in warp 0's decoded-K tile until the fragments are built
+    float (*sm_q)[D] = reinterpret_cast<float (*)[D]>(attn_smem);
+    static_assert(HPC * D * sizeof(float) <= kAttnTileBytes, "query heads exceed one decoded tile");
     __shared__ float sm_qmax[HPC];
     __shared__ float sm_p[kAttnWarps][16][HPC];
     __shared__ float sm_ml[kAttnWarps][HPC][2];
-    __shared__ int sm_pages[kAttnMaxStagedPages];
+    __shared__ int sm_pages[kAttnInt3MaxStagedPages];
 
     const int first_page = t_begin / p.page_tokens;
     const int n_pages = (t_end - 1) / p.page_tokens - first_page + 1;
@@ -813,8 +817,9 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
     const int my_tiles = ntiles > warp ? (ntiles - warp + kAttnWarps - 1) / kAttnWarps : 0;
     unsigned char* wptr = attn_smem + (size_t)warp * SM::kWarp;
     const uint32_t wbase = smem_u32(wptr);
-    const uint32_t tile_k = wbase, tile_v = wbase + kAttnTileBytes;
-    const uint32_t stage0 = wbase + 2u * kAttnTileBytes;
+    // one decoded tile per warp: K for QK^T, then V for PV
+    const uint32_t tile_k = wbase, tile_v = wbase;
+    const uint32_t stage0 = wbase + kAttnTileBytes;
     // issue: lane -> one token row of the tile, K (lanes 0-15) or V (lanes 16-31): its 48 code bytes
     // (three 16-byte chunks) and its NBLK block scales
     const int i_row = lane & 15, i_kv = lane >> 4;
@@ -897,28 +902,28 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
     const int v_row = (lane & 7) + 8 * (lane >> 4), v_chi = (lane >> 3) & 1;
     const int dr = lane & 15, dh = lane >> 4;     // decode: token row and half of the dims (8 lanes of a
                                                   // 16-byte store phase write 8 distinct bank groups)
+    __syncthreads();   // every warp has its q fragments: warp 0's tile may now be overwritten
     for (int it = 0; it < my_tiles; ++it) {
         cp_async_wait<S - 2>();
         __syncwarp();   // tile it has landed; every lane is done with tile it-1 (decoded tiles, sm_p)
         const int t0 = t_begin + (warp + it * kAttnWarps) * 16;
         const uint32_t st = stage0 + (uint32_t)(it % S) * SM::kStage;
-        const unsigned char* stp = wptr + 2u * kAttnTileBytes + (size_t)(it % S) * SM::kStage;
-        // ---- decode the tile's K and V codes into fp16 tiles (row dr, dims 64*dh ..) ----
-#pragma unroll
-        for (int kv = 0; kv < 2; ++kv) {
+        const unsigned char* stp = wptr + kAttnTileBytes + (size_t)(it % S) * SM::kStage;
+        // codes of K (kv 0) or V (kv 1) -> the warp's fp16 tile (row dr, dims 64*dh ..)
+        auto decode_tile = [&](int kv) {
             const uint32_t* src = reinterpret_cast<const uint32_t*>(stp + kv * kI3Codes + dr * 48 + dh * 24);
             uint32_t w[6];
 #pragma unroll
             for (int i = 0; i < 6; ++i) w[i] = src[i];
             uint4 outc[8];
             i3_decode64(w, outc);
-            unsigned char* tile = wptr + kv * kAttnTileBytes;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const int ch = 8 * dh + k;
-                *reinterpret_cast<uint4*>(tile + dr * 256 + ((ch ^ (dr & 7)) << 4)) = outc[k];
+                *reinterpret_cast<uint4*>(wptr + dr * 256 + ((ch ^ (dr & 7)) << 4)) = outc[k];
             }
-        }
+        };
+        decode_tile(0);
         __syncwarp();
         // refill the stage of tile it-1 (its codes were decoded in the previous step)
         if (it + S - 1 < my_tiles) issue(it + S - 1);
@@ -982,6 +987,8 @@ paged_attn_int3_mma_kernel(const AttnParams p) {
             sm_p[warp][g][4 * nt + c] = p0 * kPScale;
             sm_p[warp][g + 8][4 * nt + c] = p1 * kPScale;
         }
+        __syncwarp();   // every lane's ldmatrix reads of the K tile are done: V may overwrite it
+        decode_tile(1);
         __syncwarp();
         // ---- O^T += V^T (P s_v)^T, per scale block of dims ----
         const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
@@ -1100,17 +1107,19 @@ int attn_read_and_clear_page_fault(int* out) {
 }
 
 // Context piece per CTA: enough pieces for about four CTAs per resident slot
-// (two per SM), no split at all when the (sequence, KV head group) pairs
-// alone fill the slots, pieces under 512 tokens only as far as one CTA per
-// slot needs them, and at most the staged page capacity (page_tokens <= 0:
-// the capacity for one-token pages, the most conservative).
-int attn_choose_split(int batch, int hq, int hkv, int max_ctx, int page_tokens, int sms) {
+// (ctas_per_sm per SM: the kernel's residency), no split at all when the
+// (sequence, KV head group) pairs alone fill the slots, pieces under 512
+// tokens only as far as one CTA per slot needs them, and at most the kernel's
+// staged page capacity (page_tokens <= 0: the capacity for one-token pages,
+// the most conservative).
+int attn_choose_split(int batch, int hq, int hkv, int max_ctx, int page_tokens, int sms, int ctas_per_sm,
+                      int max_staged_pages) {
     const int group = hkv > 0 ? hq / hkv : 1;
     const int hpc = group <= 4 ? 4 : 8;
     const long long pairs = (long long)batch * hkv * ((group + hpc - 1) / hpc);
-    const long long slots = 2LL * sms;
+    const long long slots = (long long)ctas_per_sm * sms;
     const int pt = page_tokens > 0 ? page_tokens : 1;
-    int cap = (kAttnMaxStagedPages - 1) * pt / 64 * 64;
+    int cap = (max_staged_pages - 1) * pt / 64 * 64;
     if (cap < 64) cap = 64;
     const long long np = pairs > 0 ? pairs : 1;
     long long pieces = pairs >= slots ? 1 : (4 * slots + np - 1) / np;
@@ -1180,6 +1189,13 @@ int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st) {
             if (e == cudaSuccess)
                 e = cudaFuncSetAttribute(paged_attn_int3_mma_kernel<2, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)I3Smem<8>::kTotal);
+            // the whole unified memory as shared memory, so four CTAs of one column tile fit per SM
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(paged_attn_int3_mma_kernel<1, 4>,
+                                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(paged_attn_int3_mma_kernel<1, 8>,
+                                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
             if (e != cudaSuccess) return cuda_status(e, "paged int3 attention smem attribute");
             configured[dev] = 1;
         }

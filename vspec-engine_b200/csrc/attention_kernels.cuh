@@ -34,7 +34,19 @@ struct AttnParams {
 
 int attn_read_and_clear_page_fault(int* out);
 
-int attn_choose_split(int batch, int hq, int hkv, int max_ctx, int page_tokens, int sms);
+int attn_choose_split(int batch, int hq, int hkv, int max_ctx, int page_tokens, int sms, int ctas_per_sm,
+                      int max_staged_pages);
+// What the planner assumes per kernel: resident CTAs per SM and staged page ids per CTA.
+struct AttnPlanShape {
+    int ctas_per_sm, max_staged_pages;
+};
+// fp16/fp32 kernels, and the SIMT int3 kernel
+constexpr AttnPlanShape kAttnPlanF16 = {2, 512};
+// int3 tensor-core kernel: four CTAs per SM with one column tile (query groups up to 4), else two
+inline AttnPlanShape attn_plan_int3(int hq, int hkv) {
+    const int group = hkv > 0 ? hq / hkv : 1;
+    return AttnPlanShape{group <= 4 ? 4 : 2, 256};
+}
 size_t attn_workspace_bytes(int batch, int hq, int d, int max_splits);
 int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st);
 // int3 KV compression of rows [rows][heads][d] fp32 into pool rows slots[r]
