@@ -113,3 +113,55 @@ def test_int3_attention_rejects_bad_arguments():
                                t.data_ptr(), z.data_ptr(), 1, 8, 8, 64, 16, 1, 1, 16, 0.1)
     with pytest.raises(V.VspecB200Error, match="block_size"):
         V.kv_int3_quantize(z.data_ptr(), None, 1, 1, 128, 24, z.data_ptr(), z.data_ptr())
+
+
+def test_int3_config3_full_size_sampled_sequences():
+    """Config 3 at full size on int3 pages (B=32, Hq=32, Hkv=8, d=128, ctx ~U[512, 8192], 16-token pages,
+    block 32, page table = seeded permutation of the shared pool): the pools are quantised on the GPU,
+    every output is finite, and the shortest, the longest and one more sequence match the oracle run on
+    just those sequences' pages."""
+    torch = torch_cuda()
+    rng = np.random.default_rng(34)
+    b, hq, hkv, d, pt, block = 32, 32, 8, 128, 16, 32
+    ctx = rng.integers(512, 8193, size=b).astype(np.int32)
+    need = (ctx + pt - 1) // pt
+    total = int(need.sum())
+    perm = rng.permutation(total).astype(np.int32)
+    table = np.zeros((b, int(need.max())), dtype=np.int32)
+    off = 0
+    for i, nb in enumerate(need):
+        table[i, :nb] = perm[off:off + nb]
+        off += nb
+    rows, pb, nbk = total * pt, d * 3 // 8, d // block
+    g = torch.Generator(device="cuda")
+    g.manual_seed(34)
+    pools = []
+    for _ in range(2):
+        f = torch.randn((rows, hkv, d), device="cuda", generator=g)
+        codes = torch.empty((rows, hkv, pb), dtype=torch.uint8, device="cuda")
+        scales = torch.empty((rows, hkv, nbk), dtype=torch.float32, device="cuda")
+        V.kv_int3_quantize(f.data_ptr(), None, rows, hkv, d, block, codes.data_ptr(), scales.data_ptr())
+        torch.cuda.synchronize()
+        del f
+        pools.append((codes, scales))
+    (kc, ks), (vc, vs) = pools
+    q = rng.standard_normal((b, hq, d)).astype(np.float32)
+    dq, dt, dctx = to_dev(q), to_dev(table), to_dev(ctx)
+    out = empty_dev((b, hq, d), torch.float32)
+    scale = 1.0 / np.sqrt(d)
+    V.paged_attention_int3(dq.data_ptr(), kc.data_ptr(), vc.data_ptr(), ks.data_ptr(), vs.data_ptr(), block,
+                           dt.data_ptr(), dctx.data_ptr(), out.data_ptr(), b, hq, hkv, d, pt, table.shape[1], total,
+                           int(ctx.max()), scale)
+    torch.cuda.synchronize()
+    assert V.page_fault_flag() == 0
+    got = out.cpu().numpy()
+    assert np.all(np.isfinite(got))
+    for i in sorted({int(np.argmin(ctx)), int(np.argmax(ctx)), 7}):
+        pages_i = table[i, :need[i]]
+        sel = torch.from_numpy((pages_i[:, None] * pt + np.arange(pt)[None, :]).reshape(-1).astype(np.int64)).cuda()
+        local = np.arange(need[i], dtype=np.int32)[None, :]
+        ref = O.paged_int3_attention(q[i:i + 1], kc[sel].cpu().numpy(), vc[sel].cpu().numpy(), ks[sel].cpu().numpy(),
+                                     vs[sel].cpu().numpy(), local, ctx[i:i + 1], hq, hkv, d, pt, block, scale)
+        err = rel_err(got[i], ref[0])
+        print(f"int3 config 3 sequence {i} (ctx {ctx[i]}): {err:.2e}")
+        assert err <= RTOL_F32
