@@ -183,7 +183,7 @@ def test_reference_host_attention_entry_points():
 
 
 def test_config3_full_size_sampled_sequences():
-    """BASELINE config 3 at full size (B=32, Hq=32, Hkv=8, d=128, ctx ~U[512,8192],
+    """The paged-attention workload at full size (B=32, Hq=32, Hkv=8, d=128, ctx ~U[512,8192],
     16-token fp16 pages, page table = seeded permutation of the shared pool):
     every output is finite, and the shortest, the longest and one more sequence
     match the f64 oracle (run on just those sequences' pages)."""

@@ -1,4 +1,4 @@
-"""Qwen3-shape decode loop (BASELINE config 4 structure) against the C
+"""Qwen3-shape decode loop (Qwen3-8B structure, W4 group 128) against the C
 restatement of the reference's _forward_token (oracle_qwen_generate), on the
 same random-init packed weights downloaded from the device.
 

@@ -63,7 +63,7 @@ def test_numpy_dequant_matches_oracle():
 # ------------------------------------------------------------- config 1
 @pytest.mark.parametrize("reading", ["literal", "unsigned"])
 def test_config1_w4_gemv(reading):
-    """x ~N(0,1) [1x4096]; 4096x4096 uniform codes 0..15 in the int4
+    """The literal 4096 x 4096 GEMV point: x ~N(0,1) [1x4096]; 4096x4096 uniform codes 0..15 in the int4
     layout; fp32 group-128 scales ~U(0.005,0.02); zero-point 8; seed 0."""
     rng = np.random.default_rng(0)
     n = k = 4096
