@@ -413,7 +413,6 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             const bool up = SWIGLU && (pg & 1);
             const int orow0 = r0 + grp * BR;
             const int rows_valid = (r1 - orow0) < BR ? (r1 - orow0) : BR;
-            const int nblk = (rows_valid + 15) >> 4;
             float acc[NB][NT][2];
 #pragma unroll
             for (int j = 0; j < NB; ++j)
@@ -454,9 +453,13 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
                     sgc[h] = sg + (uint32_t)col * SZB;
                     zgc[h] = zg + (uint32_t)col * SZB;
                 }
+                // Every 16-row block of the box, also past rows_valid (NB = BR / 16, so
+                // those rows are inside the staged box: the next CTA's rows or the
+                // zero fill past n; their sums are never stored).  Without a branch per
+                // block the blocks form one straight-line region the compiler overlaps.
 #pragma unroll
                 for (int j = 0; j < NB; ++j) {
-                    if (j < nblk) {
+                    {
                         const int ra = 16 * j + g, rb2 = ra + 8;
                         Chunk<BITS> ch0[KPU], ch1[KPU];   // rows g and g+8, per k-block of the unit
                         if constexpr (KPU == 2) {
