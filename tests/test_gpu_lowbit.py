@@ -485,6 +485,42 @@ def test_deep_k_many_rows_auto_dispatch(m, flags):
     assert rel_err(y, ref) <= RTOL_F32
 
 
+@pytest.mark.parametrize("m,n,flags", [(8, 12288, 0), (5, 12288, V.F_RESIDUAL), (6, 12288, V.F_RMSNORM),
+                                         (8, 24576, V.F_SWIGLU)])
+def test_large_weights_many_rows_run_in_halves(m, n, flags):
+    """More than four activation rows on weights of n * k >= 12288 * 4096: automatic dispatch runs the
+    rows in two halves of one MMA column tile each (faster there than one two-tile call).  Every
+    epilogue against the oracle, with the timeout flag clear."""
+    import ctypes
+    rng = np.random.default_rng(950 + m + flags)
+    k, g, bits = 4096, 32, 4
+    w, s, zp = make_lowbit(rng, n, k, bits, g, sz_f16=True, zp_mode="none")
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    f = V.F_UNSIGNED | flags
+    deq = dequant_np(w, n, k, bits, s.astype(np.float32), None, g, unsigned=True)
+    if flags & V.F_RMSNORM:
+        nw = rng.uniform(0.5, 1.5, k).astype(np.float32)
+        xh = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6) * nw
+        y = run_linear(x, w, s, None, n, k, bits, g, flags=f, norm_w=nw)
+        ref = xh @ deq.T
+    elif flags & V.F_RESIDUAL:
+        res = rng.standard_normal((m, n)).astype(np.float32)
+        y = run_linear(x, w, s, None, n, k, bits, g, flags=f, residual=res)
+        ref = x.astype(np.float64) @ deq.T + res
+    elif flags & V.F_SWIGLU:
+        full = x.astype(np.float64) @ deq.T
+        gate, up = full[:, : n // 2], full[:, n // 2:]
+        y = run_linear(x, w, s, None, n, k, bits, g, flags=f, out_cols=n // 2)
+        ref = gate / (1.0 + np.exp(-gate)) * up
+    else:
+        y = run_linear(x, w, s, None, n, k, bits, g, flags=f)
+        ref = x.astype(np.float64) @ deq.T
+    flag = ctypes.c_int(0)
+    V.check(V.lib.vspec_b200_gemv_timeout_flag(ctypes.byref(flag)), "timeout flag")
+    assert flag.value == 0
+    assert rel_err(y, ref) <= RTOL_F32
+
+
 @pytest.mark.parametrize("k", [5120, 6144])
 def test_ring_split_k_merge_back_to_back(k):
     """The Qwen3-32B-shape lm_head (n = 151936) at k = 5120 / 6144 runs the ring

@@ -731,7 +731,15 @@ int lowbit_gemv_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t 
     // while half the rows fit.  Automatic dispatch then runs the rows in two
     // halves instead of the one-warp-per-row generic kernel (at m = 8, n = 4096,
     // k = 12288 that is ~35 us against ~1.5 ms).
-    if (!fast && path == kPathAuto && p.m > 1) {
+    // Two halves also for m > 4 on large weights: past four activation rows
+    // the fast kernels run two MMA column tiles, and from n * k = 12288 * 4096
+    // on that costs 2.1-2.3x the one-tile time, more than reading the weights
+    // twice (measured, W4 k = 4096, m = 6 / 8: n = 12288 23.6 / 26.1 us against
+    // 20.9 / 21.6 in halves; SwiGLU n = 24576 43.0 / 47.1 against 35.9 / 39.4;
+    // n = 151936 168 / 173 against 138 / 145).  Below it one call is faster
+    // (n = 6144, m = 8: 15.4 against 21.5 us).
+    const bool big_halves = fast && path == kPathAuto && p.m > 4 && (long long)p.n * p.k >= 12288LL * 4096LL;
+    if ((!fast || big_halves) && path == kPathAuto && p.m > 1) {
         GemvParams h = p;
         h.m = (p.m + 1) / 2;
         if (fast_path_ok(h, bits) && (!swiglu || (p.n / 2) % 16 == 0)) {
