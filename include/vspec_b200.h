@@ -326,6 +326,12 @@ int vspec_b200_mul_f32(float* d_data, const float* d_other, size_t count, void* 
  * the one after fails (n < 0 disables). */
 int vspec_b200_debug_fail_alloc_after(int n);
 
+/* Test hook: fills the split-K counter region of the current device's static
+ * scratch (vspec_b200_lowbit_linear_static) with `byte`, the state a launch
+ * whose bounded wait gave up can leave; the next static call must still be
+ * correct.  A synchronous memset on the host's side, no kernel. */
+int vspec_b200_debug_poison_static_scratch(int byte);
+
 /* Test hook: one step of the hybrid bridge's temporal hot-column rule (the
  * selection vspec_cuda_fused_linear_hybrid_bridge makes before any device work,
  * with the same per-thread state and environment): writes the columns that

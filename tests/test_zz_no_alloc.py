@@ -138,3 +138,19 @@ def test_static_scratch_rejects_oversized_shapes_and_workspaces():
     a = V.LinearArgs(fake, fake, fake, None, 0.0, fake, None, None, 1e-6, 1, 128, 128, 1, 4, 0, fake, 1024)
     assert lib.vspec_b200_lowbit_linear_static(ctypes.byref(a), None) == 1
     assert "d_workspace must be NULL" in V.last_error()
+
+
+@pytest.mark.parametrize("byte", [0x01, 0xFF])
+def test_static_scratch_recovers_from_counters_left_part_way(byte):
+    """A launch whose bounded wait gave up can leave split-K counts part-way in
+    the static array, which the caller cannot reach.  Every call clears the
+    counter region before its launch, so the calls after such a state (made here
+    by filling the region from the host, no kernel involved) still match the
+    oracle and the workspace path."""
+    torch_cuda()
+    lib.vspec_b200_debug_poison_static_scratch.argtypes = [ctypes.c_int]
+    lib.vspec_b200_debug_poison_static_scratch.restype = ctypes.c_int
+    for c in CASES:
+        if c[-1] in ("ring: m=4, bench N", "ring: m=8", "tcgen05 GEMM with split-K"):
+            V.check(lib.vspec_b200_debug_poison_static_scratch(byte), "poison static scratch")
+            _run_case(*c[:8])

@@ -103,3 +103,13 @@ extern "C" int vspec_b200_lowbit_linear_static(const VspecB200LinearArgs* a, voi
     b.workspace_bytes = kStaticGemvScratchBytes;
     return vspec_b200_lowbit_linear(&b, stream);
 }
+
+// Test hook: the counter region of the current device's static scratch filled
+// with `byte`, the state a launch whose bounded wait gave up can leave behind.
+extern "C" int vspec_b200_debug_poison_static_scratch(int byte) {
+    void* ptr = nullptr;
+    const int rc = static_scratch_for_current_device(&ptr);
+    if (rc != VSPEC_B200_OK) return rc;
+    const cudaError_t e = cudaMemset(ptr, byte & 0xFF, kStaticGemvCounterBytes);
+    return e == cudaSuccess ? VSPEC_B200_OK : vb200::cuda_status(e, "poison static scratch");
+}

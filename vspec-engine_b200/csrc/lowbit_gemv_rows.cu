@@ -138,7 +138,15 @@ bool gemv_rows_supported(const GemvParams& p, int bits) {
 // activation rows (m = 4: 11.6 -> 15.0) stay on the ring kernel, as do shapes
 // with more than one row group per CTA.
 bool gemv_rows_preferred(const GemvParams& p, int bits) {
-    if (p.m != 1 || p.k > 4096) return false;
+    if (p.k > 4096 || p.m < 1) return false;
+    if (p.m > 1) {
+        // 2-4 activation rows, int4, no SwiGLU: faster than the ring kernel while m * n <= 16384
+        // (measured, k = 4096: n = 4096 at m = 2 / 3 / 4: 7.20 / 8.88 / 10.47 us against 8.56 /
+        // 10.18 / 11.66; n = 6144 at m = 2: 8.27 against 8.70; the ring kernel wins at n = 6144,
+        // m = 3 and at n = 12288, m >= 2)
+        if (p.m > 4 || bits != 4 || (p.flags & VSPEC_B200_F_SWIGLU) || (long long)p.m * p.n > 16384) return false;
+        return gemv_rows_supported(p, bits);
+    }
     if (bits == 2 && !rows_pair_mode()) return false;   // int2 gains only with one CTA per SM
     return gemv_rows_supported(p, bits);
 }
