@@ -761,7 +761,7 @@ __device__ __forceinline__ void i3_decode64(const uint32_t (&w)[6], uint4 (&out)
 }
 
 template <int NT, int NBLK>
-__global__ void __launch_bounds__(kAttnThreads, NT == 1 ? 4 : 2)   // 4 CTAs per SM for one column tile
+__global__ void __launch_bounds__(kAttnThreads, NT == 1 ? 4 : 3)   // 4 CTAs per SM for one column tile, 3 for two
 paged_attn_int3_mma_kernel(const AttnParams p) {
     pdl_wait();
     pdl_trigger();

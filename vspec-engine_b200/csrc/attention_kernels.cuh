@@ -42,10 +42,10 @@ struct AttnPlanShape {
 };
 // fp16/fp32 kernels, and the SIMT int3 kernel
 constexpr AttnPlanShape kAttnPlanF16 = {2, 512};
-// int3 tensor-core kernel: four CTAs per SM with one column tile (query groups up to 4), else two
+// int3 tensor-core kernel: four CTAs per SM with one column tile (query groups up to 4), else three
 inline AttnPlanShape attn_plan_int3(int hq, int hkv) {
     const int group = hkv > 0 ? hq / hkv : 1;
-    return AttnPlanShape{group <= 4 ? 4 : 2, 256};
+    return AttnPlanShape{group <= 4 ? 4 : 3, 256};
 }
 size_t attn_workspace_bytes(int batch, int hq, int d, int max_splits);
 int paged_attention_launch(AttnParams p, int kv_dtype, cudaStream_t st);
