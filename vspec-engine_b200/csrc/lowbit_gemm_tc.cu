@@ -669,13 +669,17 @@ static bool gemm_plan(int m, int n, int k, int bits, bool swiglu, GemmPlan* gp) 
     // accumulator before the next item's MMAs start), plus the merge kernel: ~3 k-blocks of launch and latency and the partial
     // bytes (items x NW x BN x 128 fp32, mostly L2-resident), ~20000 such
     // per-token columns per k-block time (calibrated on B200 at M = 64 and 256)
+    // An unsplit item on a GPU with idle SMs (fewer tiles than SMs) and a token tile above 128 costs
+    // more than the model's 3: measured at M = 256, N = 5120, K = 1024 (40 tiles of 256 tokens, 8
+    // k-blocks): 26.8 us unsplit against 14.7 us in two splits with the merge.
+    const double epi1 = (bn > 128 && tiles < sms) ? 3.0 + (bn - 128) / 16.0 : 3.0;
     int splits = 1;
     double best = -1.0;
     for (int d = 1; d <= kbt; ++d) {
         if (kbt % d != 0 || (d > 1 && kbt / d < 2)) continue;
         const long long items = (long long)tiles * d;
         const long long rounds = (items + sms - 1) / sms;
-        double cost = (double)rounds * (kbt / d + 3);
+        double cost = (double)rounds * (kbt / d + (d == 1 ? epi1 : 3.0));
         if (d > 1) cost += 3.0 + (double)items * nw * bn / 20000.0;
         if (best < 0.0 || cost < best) { best = cost; splits = d; }
     }
