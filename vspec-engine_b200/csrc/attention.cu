@@ -1132,7 +1132,10 @@ int attn_choose_split(int batch, int hq, int hkv, int max_ctx, int page_tokens, 
         const long long floor_s = s1 < 512 ? s1 : 512;
         if (s < floor_s) s = floor_s;
     }
-    if (s < 64) s = 64;
+    // at least 128 tokens a piece: a piece pays its prologue and the combine a slot, and at batch 1
+    // (8 KV heads, ctx 512 / 768 / 2048) 128-token pieces measured 8.8 / 9.5 / 11.8 us per call
+    // against 9.2 / 10.4 / 15.3 with 64
+    if (s < 128) s = 128;
     if (s > cap) s = cap;
     return (int)s;
 }
