@@ -12,7 +12,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 37, 256), (1, 4096, 4096), (3, 1000, 2048), (8, 640, 1024), (11, 300, 512),
-                                   (1, 12288, 4096), (2, 300, 8192), (1, 33, 8192)])
+                                   (1, 12288, 4096), (2, 300, 8192), (1, 33, 8192),
+                                   (1, 1, 4096), (1, 4097, 2048)])
 def test_q4k_linear_matches_oracle(m, n, k):
     torch = torch_cuda()
     rng = np.random.default_rng(m * 1000 + n + k)

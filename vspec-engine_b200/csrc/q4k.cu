@@ -41,13 +41,15 @@ __device__ __forceinline__ float q4k_code(uint32_t w) {
 // x is staged once per CTA in shared memory, [m][k/32][36] floats (every
 // 32-element sub-block padded by 16 bytes, so the 8 lanes of a load phase,
 // which read 8 different sub-blocks, hit different banks).  Warp w then takes
-// rows CTA*32 + 4w .. +3; lane l the sub-blocks l, l+32, ... of a row, with
-// all of its header and code loads for the row issued before the math (a
+// rows CTA*32 + 4w .. +3, RPS of them at a time; lane l the sub-blocks l,
+// l+32, ... of each, with all header and code loads of those RPS rows issued
+// before the math (SPL sub-blocks per lane and row; m = 1 with k <= 4096 runs
+// RPS 2 and SPL 4, the rest RPS 1 and SPL 8; a
 // double-buffered variant, 4 sub-blocks per lane and chunk with the next
 // chunk's loads issued before the current chunk's math, measured 31.9 us
 // against 28.7 us for this kernel with per-code conversions at K=4096
 // N=12288 M=1).
-template <int MM>
+template <int MM, int RPS, int SPL>
 __global__ void __launch_bounds__(kQ4kWarps * 32)
 q4k_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, float* __restrict__ y, int m, int n,
                 int k) {
@@ -77,63 +79,82 @@ q4k_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ w, floa
         xsum_sm[i] = sum;
     }
     __syncthreads();
-    constexpr int SPL = 8;   // sub-blocks per lane held in flight (k <= 8192 in one pass)
-    for (int rr = 0; rr < kQ4kRowsPerWarp; ++rr) {
-        const int j = (blockIdx.x * kQ4kWarps + warp) * kQ4kRowsPerWarp + rr;
-        if (j >= n) break;
-        const uint8_t* row = w + (size_t)j * nb * 144;
-        float acc[MM];
+    // RPS rows of a warp are streamed together: every header and code load of
+    // those rows is issued before the math, so a warp waits RPS times fewer
+    // memory round trips (SPL sub-blocks per lane and row cover k <= 32*SPL*32)
+    for (int rr = 0; rr < kQ4kRowsPerWarp; rr += RPS) {
+        int js[RPS];
+        bool vj[RPS];
 #pragma unroll
-        for (int r = 0; r < MM; ++r) acc[r] = 0.f;
+        for (int q = 0; q < RPS; ++q) {
+            js[q] = (blockIdx.x * kQ4kWarps + warp) * kQ4kRowsPerWarp + rr + q;
+            vj[q] = js[q] < n;
+        }
+        if (!vj[0]) break;
+        float acc[RPS][MM];
+#pragma unroll
+        for (int q = 0; q < RPS; ++q)
+#pragma unroll
+            for (int r = 0; r < MM; ++r) acc[q][r] = 0.f;
         for (int s0 = lane; s0 < nsub; s0 += 32 * SPL) {
-            uint4 hdr[SPL], qv[SPL];
+            uint4 hdr[RPS][SPL], qv[RPS][SPL];
 #pragma unroll
-            for (int u = 0; u < SPL; ++u) {
-                const int s = s0 + 32 * u;
-                if (s < nsub) {
-                    const uint8_t* blk = row + (size_t)(s >> 3) * 144;
-                    hdr[u] = __ldg(reinterpret_cast<const uint4*>(blk));
-                    qv[u] = __ldg(reinterpret_cast<const uint4*>(blk + 16 + (s & 7) * 16));
+            for (int q = 0; q < RPS; ++q) {
+                const uint8_t* row = w + (size_t)js[q] * nb * 144;
+#pragma unroll
+                for (int u = 0; u < SPL; ++u) {
+                    const int s = s0 + 32 * u;
+                    if (vj[q] && s < nsub) {
+                        const uint8_t* blk = row + (size_t)(s >> 3) * 144;
+                        hdr[q][u] = __ldg(reinterpret_cast<const uint4*>(blk));
+                        qv[q][u] = __ldg(reinterpret_cast<const uint4*>(blk + 16 + (s & 7) * 16));
+                    }
                 }
             }
 #pragma unroll
-            for (int u = 0; u < SPL; ++u) {
-                const int s = s0 + 32 * u;
-                if (s < nsub) {
-                    const int sb = s & 7;
-                    const float d = __half2float(__ushort_as_half((unsigned short)(hdr[u].x & 0xFFFFu)));
-                    const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[u].x >> 16)));
-                    const uint32_t sc = q4k_field6(hdr[u].y, hdr[u].z, hdr[u].w, sb);
-                    const uint32_t mn = q4k_field6(hdr[u].y, hdr[u].z, hdr[u].w, 8 + sb);
-                    const float sub_scale = d * div63[sc];   // q4_k.c:94-95
-                    const float sub_min = dmin * div63[mn];
-                    const uint32_t qw[4] = {qv[u].x, qv[u].y, qv[u].z, qv[u].w};
+            for (int q = 0; q < RPS; ++q) {
 #pragma unroll
-                    for (int r = 0; r < MM; ++r) {
-                        if (r < m) {
-                            const float4* xp = reinterpret_cast<const float4*>(xs_sm + ((size_t)r * nsub + s) * kQ4kSubPad);
-                            float xq = 0.f;
+                for (int u = 0; u < SPL; ++u) {
+                    const int s = s0 + 32 * u;
+                    if (vj[q] && s < nsub) {
+                        const int sb = s & 7;
+                        const float d = __half2float(__ushort_as_half((unsigned short)(hdr[q][u].x & 0xFFFFu)));
+                        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[q][u].x >> 16)));
+                        const uint32_t sc = q4k_field6(hdr[q][u].y, hdr[q][u].z, hdr[q][u].w, sb);
+                        const uint32_t mn = q4k_field6(hdr[q][u].y, hdr[q][u].z, hdr[q][u].w, 8 + sb);
+                        const float sub_scale = d * div63[sc];   // q4_k.c:94-95
+                        const float sub_min = dmin * div63[mn];
+                        const uint32_t qw[4] = {qv[q][u].x, qv[q][u].y, qv[q][u].z, qv[q][u].w};
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const float4 v = xp[i];
-                                const uint32_t wd = qw[i >> 1] >> (16 * (i & 1));   // 4 codes, low nibble first
-                                xq = fmaf(v.x, q4k_code(wd), xq);
-                                xq = fmaf(v.y, q4k_code(wd >> 4), xq);
-                                xq = fmaf(v.z, q4k_code(wd >> 8), xq);
-                                xq = fmaf(v.w, q4k_code(wd >> 12), xq);
+                        for (int r = 0; r < MM; ++r) {
+                            if (r < m) {
+                                const float4* xp = reinterpret_cast<const float4*>(xs_sm + ((size_t)r * nsub + s) * kQ4kSubPad);
+                                float xq = 0.f;
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) {
+                                    const float4 v = xp[i];
+                                    const uint32_t wd = qw[i >> 1] >> (16 * (i & 1));   // 4 codes, low nibble first
+                                    xq = fmaf(v.x, q4k_code(wd), xq);
+                                    xq = fmaf(v.y, q4k_code(wd >> 4), xq);
+                                    xq = fmaf(v.z, q4k_code(wd >> 8), xq);
+                                    xq = fmaf(v.w, q4k_code(wd >> 12), xq);
+                                }
+                                const float xsum = xsum_sm[(size_t)r * nsub + s];
+                                acc[q][r] = fmaf(sub_scale, xq, fmaf(-sub_min, xsum, acc[q][r]));
                             }
-                            const float xsum = xsum_sm[(size_t)r * nsub + s];
-                            acc[r] = fmaf(sub_scale, xq, fmaf(-sub_min, xsum, acc[r]));
                         }
                     }
                 }
             }
         }
 #pragma unroll
-        for (int r = 0; r < MM; ++r) {
-            if (r < m) {
-                const float v = warp_sum(acc[r]);
-                if (lane == 0) y[(size_t)r * n + j] = v;
+        for (int q = 0; q < RPS; ++q) {
+#pragma unroll
+            for (int r = 0; r < MM; ++r) {
+                if (r < m) {
+                    const float v = warp_sum(acc[q][r]);
+                    if (lane == 0 && vj[q]) y[(size_t)r * n + js[q]] = v;
+                }
             }
         }
     }
@@ -161,15 +182,21 @@ extern "C" int vspec_b200_q4k_linear(const float* d_x, const void* d_blocks, flo
     const size_t per_row = (k / 32) * kQ4kSubPad * sizeof(float);
     size_t mmax = kQ4kStageMax / per_row;
     if (mmax > (size_t)kQ4kMaxM) mmax = kQ4kMaxM;
+    // m = 1 and k <= 4096: two rows in flight per warp with 4 sub-blocks per
+    // lane each (K=4096 N=12288: 20.7 us against 23.1 us for one row); larger k
+    // and m > 1 keep one row with 8 sub-blocks per lane (two rows measured
+    // slower there: the staged-x reads, not the weight loads, bound them)
+    const bool two_rows = m == 1 && k <= 4096;
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(q4k_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)(kQ4kStageMax + kQ4kSumMax));
+        const int smax = (int)(kQ4kStageMax + kQ4kSumMax);
+        cudaError_t e = cudaFuncSetAttribute(q4k_gemv_kernel<1, 1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(q4k_gemv_kernel<kQ4kMaxM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(kQ4kStageMax + kQ4kSumMax));
+            e = cudaFuncSetAttribute(q4k_gemv_kernel<kQ4kMaxM, 1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(q4k_gemv_kernel<1, 2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax);
         if (e != cudaSuccess) return cuda_status(e, "q4k_gemv_kernel smem attribute");
         configured[dev] = 1;
     }
@@ -177,9 +204,12 @@ extern "C" int vspec_b200_q4k_linear(const float* d_x, const void* d_blocks, flo
         const int mm = (int)((m - i0) < mmax ? (m - i0) : mmax);
         const float* xb = d_x + i0 * k;
         float* yb = d_y + i0 * n;
+        const uint8_t* wb = (const uint8_t*)d_blocks;
         const size_t smem = (size_t)mm * (per_row + (k / 32) * sizeof(float));
-        if (mm == 1) q4k_gemv_kernel<1><<<grid, kQ4kWarps * 32, smem, st>>>(xb, (const uint8_t*)d_blocks, yb, mm, (int)n, (int)k);
-        else q4k_gemv_kernel<kQ4kMaxM><<<grid, kQ4kWarps * 32, smem, st>>>(xb, (const uint8_t*)d_blocks, yb, mm, (int)n, (int)k);
+        const unsigned th = kQ4kWarps * 32;
+        if (two_rows) q4k_gemv_kernel<1, 2, 4><<<grid, th, smem, st>>>(xb, wb, yb, mm, (int)n, (int)k);
+        else if (mm == 1) q4k_gemv_kernel<1, 1, 8><<<grid, th, smem, st>>>(xb, wb, yb, mm, (int)n, (int)k);
+        else q4k_gemv_kernel<kQ4kMaxM, 1, 8><<<grid, th, smem, st>>>(xb, wb, yb, mm, (int)n, (int)k);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_status(e, "q4k_gemv_kernel launch");
     }
