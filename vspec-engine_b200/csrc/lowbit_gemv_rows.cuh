@@ -95,11 +95,14 @@ __host__ __device__ inline RowsSmem rows_smem_plan(int bits, int m, int kbt, int
     RowsSmem s;
     uint32_t o = (uint32_t)ns * (uint32_t)br * (uint32_t)rows_unit_bytes(bits, br);
     o = rows_align(o, 128u);
+    // a CTA holds one row group, so without SwiGLU (gate, up: two physical
+    // groups) the scale boxes and warp partials need no second buffer
+    const uint32_t nbuf = swiglu ? 2u : 1u;
     s.sbuf = o;
-    if (has_s) o += 2u * (uint32_t)br * (uint32_t)srow_bytes;
+    if (has_s) o += nbuf * (uint32_t)br * (uint32_t)srow_bytes;
     o = rows_align(o, 128u);
     s.zbuf = o;
-    if (has_zp) o += 2u * (uint32_t)br * (uint32_t)srow_bytes;
+    if (has_zp) o += nbuf * (uint32_t)br * (uint32_t)srow_bytes;
     o = rows_align(o, 16u);
     s.frag = o;
     o += (uint32_t)kbt * (uint32_t)rows_nt(m) * (uint32_t)rows_lanes(m) * 32u;
@@ -109,8 +112,8 @@ __host__ __device__ inline RowsSmem rows_smem_plan(int bits, int m, int kbt, int
     o += (uint32_t)(kbt * m) * 4u;
     s.is = o;
     o += (uint32_t)(kbt * m) * 4u;
-    s.red = o;                      // [2][warps][m][br] fp32 warp partials
-    o += 2u * kRowsWarps * (uint32_t)m * (uint32_t)br * 4u;
+    s.red = o;                      // [nbuf][warps][m][br] fp32 warp partials
+    o += nbuf * kRowsWarps * (uint32_t)m * (uint32_t)br * 4u;
     s.gbuf = o;                     // [m][br] SwiGLU gate sums
     if (swiglu) o += (uint32_t)m * (uint32_t)br * 4u;
     o = rows_align(o, 8u);
