@@ -42,6 +42,28 @@ static bool rows_pair_mode() {
     return v == 1;
 }
 
+// Pair mode: how long a CTA's producer holds its first copies back while the
+// previous kernel still runs.  A CTA of the next launch becomes resident while
+// this launch's activation prologue reads x; its first copies then compete
+// with those reads on the SM's memory path.  600 ns measured best where the
+// prologue reads at least 16 KB of x (W4 K=4096 N=12288 8.81 -> 8.41 us, W3
+// 9.48 -> 8.90, N=8192 7.27 -> 6.85); shorter launches (K=2048: 4.44 -> 4.54)
+// keep no delay.  VSPEC_B200_ROWS_PREFETCH_DELAY_NS overrides it (0: off).
+static int rows_prefetch_delay_ns(int m, int k) {
+    static int v = -2;
+    if (v == -2) {
+        const char* e = getenv("VSPEC_B200_ROWS_PREFETCH_DELAY_NS");
+        if (e && e[0]) {
+            const int d = atoi(e);
+            v = d < 0 ? 0 : (d > 20000 ? 20000 : d);
+        } else {
+            v = -1;
+        }
+    }
+    if (v >= 0) return v;
+    return (long long)m * k >= 4096 ? 600 : 0;
+}
+
 // Row-group size, ring depth and CTA count.  Candidate geometries, first fit
 // wins: (pair mode) one CTA per SM in half an SM, row groups up to 96 rows;
 // two CTAs per SM in half an SM each; one CTA per SM in a whole SM; the last
@@ -103,6 +125,7 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
             geo->srow_bytes = srow;
             geo->has_s = has_s ? 1 : 0;
             geo->has_zp = has_zp ? 1 : 0;
+            geo->prefetch_delay_ns = (cd.per_sm == 1 && cd.budget == kRowsSmemShared) ? rows_prefetch_delay_ns(m, p.k) : 0;
             *smem = rows_smem_plan(bits, m, kbt, br, ns, srow, has_s, has_zp, swiglu).total + 1024u;
             return true;
         }

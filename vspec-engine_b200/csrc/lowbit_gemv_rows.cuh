@@ -83,6 +83,7 @@ struct RowsGeom {
     int stages;      // ring depth
     int srow_bytes;  // bytes of one scale row (n_groups * element size)
     int has_s, has_zp;
+    int prefetch_delay_ns;   // producer holds its first copies back this long unless the dependency resolved
 };
 
 struct RowsSmem {
@@ -148,6 +149,12 @@ __device__ __forceinline__ void rows_lds_chunk(Chunk<BITS>& ch, const unsigned c
     }
 }
 
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Bounded wait until the producer thread has issued at least `want` units
 // (a volatile shared-memory counter it raises after every copy).
 __device__ __forceinline__ bool wait_issued(volatile int* issued, int want, volatile int* abort) {
@@ -201,6 +208,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base + plan.misc);
     float* row_norm = reinterpret_cast<float*>(base + plan.misc) + 4;   // [8]
     volatile int* issued = reinterpret_cast<volatile int*>(base + plan.misc) + 12;   // units the producer issued
+    volatile int* dep_done = reinterpret_cast<volatile int*>(base + plan.misc) + 13;  // consumers passed the dependency wait
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -228,6 +236,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
         }
         *abort_flag = 0;
         *issued = 0;
+        *dep_done = 0;
         mbar_fence_init();
     }
     __syncthreads();
@@ -245,6 +254,14 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             tma_prefetch_desc(&wmap);
             if (has_s) tma_prefetch_desc(&smap);
             if (has_zp) tma_prefetch_desc(&zmap);
+            // While the previous kernel still runs, its activation prologue and
+            // refills share this SM's memory path with this CTA's first copies;
+            // hold them back a bounded time unless the dependency has resolved
+            if (geo.prefetch_delay_ns > 0) {
+                const unsigned long long t0 = globaltimer_ns();
+                while (!*dep_done && globaltimer_ns() - t0 < (unsigned long long)geo.prefetch_delay_ns)
+                    __nanosleep(32);
+            }
             bool ok = true;
             int pg = 0, kb = 0, stage = 0, use = 0, sz_issued = 0;
             int row = r0;
@@ -298,6 +315,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
 
     // ---- activation prologue (x may be the previous kernel's output) ----
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    if (tid == 0) *dep_done = 1;
     const int K = p.k;
     const bool rms = EPI_HAS_RMSNORM(p.flags);
     if (rms) {
