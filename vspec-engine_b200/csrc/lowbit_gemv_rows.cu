@@ -96,9 +96,12 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
             const int per = (rmax + ngrp - 1) / ngrp;
             const int br = 16 * ((per + 15) / 16);
             if (br > cd.brmax) continue;
-            const uint32_t stage = (uint32_t)br * (uint32_t)rows_unit_bytes(bits, br);
+            // a box (ring stage) covers the CTA's rows rounded up to 8 (the
+            // swizzle period), not the whole 16-row-block group
+            const int box = ((rmax + 7) / 8) * 8 < br ? ((rmax + 7) / 8) * 8 : br;
+            const uint32_t stage = (uint32_t)box * (uint32_t)rows_unit_bytes(bits, br);
             const int kut = kbt / rows_kpu(bits, br);
-            const uint32_t fixed = rows_smem_plan(bits, m, kbt, br, 0, srow, has_s, has_zp, swiglu).total + 1024u;
+            const uint32_t fixed = rows_smem_plan(bits, m, kbt, br, 0, srow, has_s, has_zp, swiglu, box).total + 1024u;
             if (fixed + 4u * (stage + 16u) > cd.budget) {
                 if (br == 16) break;
                 continue;
@@ -126,7 +129,16 @@ static bool rows_plan(const GemvParams& p, int bits, bool swiglu, RowsGeom* geo,
             geo->has_s = has_s ? 1 : 0;
             geo->has_zp = has_zp ? 1 : 0;
             geo->prefetch_delay_ns = (cd.per_sm == 1 && cd.budget == kRowsSmemShared) ? rows_prefetch_delay_ns(m, p.k) : 0;
-            *smem = rows_smem_plan(bits, m, kbt, br, ns, srow, has_s, has_zp, swiglu).total + 1024u;
+            // the last stage's MMA blocks read (br - box) rows past the ring:
+            // the buffers after it must cover them
+            const RowsSmem pl = rows_smem_plan(bits, m, kbt, br, ns, srow, has_s, has_zp, swiglu, box);
+            const uint32_t ring_end = (uint32_t)ns * stage;
+            if (pl.total - ring_end < (uint32_t)(br - box) * (uint32_t)rows_unit_bytes(bits, br)) {
+                if (br == 16) break;
+                continue;
+            }
+            geo->box_rows = box;
+            *smem = pl.total + 1024u;
             return true;
         }
     }
@@ -203,7 +215,7 @@ int gemv_rows_launch(GemvParams p, int bits, int unsigned_codes, cudaStream_t st
     const CUtensorMapSwizzle swz = bits == 4 ? (rows_kpu(bits, geo.br) == 2 ? CU_TENSOR_MAP_SWIZZLE_128B
                                                                               : CU_TENSOR_MAP_SWIZZLE_64B)
                                  : (bits == 2 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE);
-    int rc = make_row_tile_map(&wmap, p.w, p.n, p.row_bytes, rows_unit_bytes(bits, geo.br), geo.br, swz);
+    int rc = make_row_tile_map(&wmap, p.w, p.n, p.row_bytes, rows_unit_bytes(bits, geo.br), geo.box_rows, swz);
     if (rc != VSPEC_B200_OK) return rc;
     const int szb = (p.flags & VSPEC_B200_F_SZ_F16) ? 2 : 4;
     if (p.s) {

@@ -84,6 +84,7 @@ struct RowsGeom {
     int srow_bytes;  // bytes of one scale row (n_groups * element size)
     int has_s, has_zp;
     int prefetch_delay_ns;   // producer holds its first copies back this long unless the dependency resolved
+    int box_rows;            // rows of a weight box and ring stage (a CTA's rows rounded up to 8, <= br)
 };
 
 struct RowsSmem {
@@ -91,10 +92,11 @@ struct RowsSmem {
 };
 
 // Offsets from the 1024-aligned base; the ring starts at 0.
+// The ring holds ns stages of box_rows rows; the scale boxes hold br rows.
 __host__ __device__ inline RowsSmem rows_smem_plan(int bits, int m, int kbt, int br, int ns, int srow_bytes,
-                                                   bool has_s, bool has_zp, bool swiglu) {
+                                                   bool has_s, bool has_zp, bool swiglu, int box_rows) {
     RowsSmem s;
-    uint32_t o = (uint32_t)ns * (uint32_t)br * (uint32_t)rows_unit_bytes(bits, br);
+    uint32_t o = (uint32_t)ns * (uint32_t)box_rows * (uint32_t)rows_unit_bytes(bits, br);
     o = rows_align(o, 128u);
     // a CTA holds one row group, so without SwiGLU (gate, up: two physical
     // groups) the scale boxes and warp partials need no second buffer
@@ -182,7 +184,11 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
     constexpr int SZB = SZ16 ? 2 : 4;
     const int NS = geo.stages;
     constexpr int BR = 16 * NB;
-    const uint32_t STAGE_BYTES = (uint32_t)BR * UB;
+    // A stage holds geo.box_rows <= BR rows.  The 16-row MMA blocks still read
+    // BR rows: rows past the box belong to the next stage (or, for the last
+    // stage, to the buffers after the ring) and only feed output rows past the
+    // CTA's range, which are never stored.
+    const uint32_t STAGE_BYTES = (uint32_t)geo.box_rows * UB;
 
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -191,7 +197,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
     const int kbt = p.kb_total;
     const int lanes = rows_lanes(m);
     const bool has_s = geo.has_s != 0, has_zp = geo.has_zp != 0;
-    const RowsSmem plan = rows_smem_plan(BITS, m, kbt, BR, NS, geo.srow_bytes, has_s, has_zp, SWIGLU);
+    const RowsSmem plan = rows_smem_plan(BITS, m, kbt, BR, NS, geo.srow_bytes, has_s, has_zp, SWIGLU, geo.box_rows);
     unsigned char* wring = base;
     unsigned char* sbuf = base + plan.sbuf;
     unsigned char* zbuf = base + plan.zbuf;
