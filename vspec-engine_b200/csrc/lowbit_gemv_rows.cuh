@@ -355,17 +355,23 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
         unsigned char* fbase = base + plan.frag;
         constexpr int NW = kRowsWarps;
         constexpr int QB = 4;
-        const int npairs = kbt * m;
-        for (int pr0 = warp; pr0 < npairs; pr0 += QB * NW) {
+        // Each warp quantises the (k-block, row) pairs of exactly the k-blocks
+        // its consumer units use (units w, w+8, ... of KPU k-blocks each), so no
+        // other warp reads what it writes and a warp-level sync ends the
+        // prologue: every warp starts its first unit as soon as its own parts
+        // are ready.  kut % 8 == 0 gives every warp the same number of pairs.
+        const int per_warp = kbt * m / NW;
+        for (int i0 = 0; i0 < per_warp; i0 += QB) {
             float4 v[QB];
             int kbq[QB], rq[QB];
 #pragma unroll
             for (int q = 0; q < QB; ++q) {
-                const int pr = pr0 + q * NW;
-                rq[q] = pr % m;
-                kbq[q] = pr / m;
+                const int i = i0 + q;
+                const int j = i / m;
+                rq[q] = i - j * m;
+                kbq[q] = (warp + NW * (j / KPU)) * KPU + (j % KPU);
                 v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (pr < npairs) {
+                if (i < per_warp) {
                     const int t = kbq[q] * 128 + lane * 4;
                     v[q] = *reinterpret_cast<const float4*>(p.x + (size_t)rq[q] * K + t);
                     if (rms) {
@@ -402,7 +408,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             for (int q = 0; q < QB; ++q) xsum[q] = __reduce_add_sync(0xffffffffu, xsum[q]);
 #pragma unroll
             for (int q = 0; q < QB; ++q) {
-                if (pr0 + q * NW < npairs) {
+                if (i0 + q < per_warp) {
                     const int kb = kbq[q], r = rq[q];
                     if (lane == 0) {
                         const float X = (float)xsum[q];
@@ -423,7 +429,7 @@ lowbit_gemv_rows_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_c
             }
         }
     }
-    named_bar_sync(1, kRowsWarps * 32);
+    __syncwarp();
 
     {
         // ======================= consumer warps ===============================
