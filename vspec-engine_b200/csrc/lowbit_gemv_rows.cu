@@ -175,11 +175,13 @@ bool gemv_rows_supported(const GemvParams& p, int bits) {
 bool gemv_rows_preferred(const GemvParams& p, int bits) {
     if (p.k > 4096 || p.m < 1) return false;
     if (p.m > 1) {
-        // 2-4 activation rows, int4, no SwiGLU: faster than the ring kernel while m * n <= 16384
-        // (measured, k = 4096: n = 4096 at m = 2 / 3 / 4: 7.20 / 8.88 / 10.47 us against 8.56 /
-        // 10.18 / 11.66; n = 6144 at m = 2: 8.27 against 8.70; the ring kernel wins at n = 6144,
-        // m = 3 and at n = 12288, m >= 2)
-        if (p.m > 4 || bits != 4 || (p.flags & VSPEC_B200_F_SWIGLU) || (long long)p.m * p.n > 16384) return false;
+        // 2-4 activation rows, int4, no SwiGLU: faster than the ring kernel while m * n <= 24576
+        // for m <= 3 and m * n <= 16384 for m = 4 (measured, k = 4096, rows / ring us: n = 4096 at
+        // m = 2 / 3 / 4: 6.71 / - / 9.96 against 8.56 / 10.18 / 11.66; n = 6144 at m = 3: 9.28
+        // against 9.88; n = 12288 at m = 2: 10.08 against 10.67; the ring kernel wins at m = 4 for
+        // n = 6144 (10.98 against 11.19) and n = 12288 (11.44 against 13.77))
+        if (p.m > 4 || bits != 4 || (p.flags & VSPEC_B200_F_SWIGLU)) return false;
+        if ((long long)p.m * p.n > (p.m <= 3 ? 24576 : 16384)) return false;
         return gemv_rows_supported(p, bits);
     }
     if (bits == 2 && !rows_pair_mode()) return false;   // int2 gains only with one CTA per SM
